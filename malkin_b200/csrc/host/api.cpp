@@ -1,0 +1,358 @@
+// The C ABI (include/malkin_b200.h): status codes instead of exceptions, thread-local error text.
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <random>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../../include/malkin_b200.h"
+#include "gguf.hpp"
+#include "layout.hpp"
+#include "model.hpp"
+#include "repack.hpp"
+#include "synth.hpp"
+
+struct mk_ctx {
+  std::unique_ptr<mkb::Model> model;
+};
+
+struct mk_weight {
+  mkb::DevWeight w;
+  mkb::DevBuf buf;
+  int device = 0;
+};
+
+static_assert(sizeof(mk_batch_token) == 24, "mk_batch_token must match malkin::BatchToken");
+
+namespace {
+
+thread_local std::string g_error;
+
+template <typename F>
+int guard(int io_code, F&& f) {
+  try {
+    g_error.clear();
+    f();
+    return MK_OK;
+  } catch (const mkb::ArgError& e) {
+    g_error = e.what();
+    return MK_ERR_ARG;
+  } catch (const mkb::UnsupportedError& e) {
+    g_error = e.what();
+    return MK_ERR_UNSUPPORTED;
+  } catch (const mkb::StateError& e) {
+    g_error = e.what();
+    return MK_ERR_STATE;
+  } catch (const mkb::CudaError& e) {
+    g_error = e.what();
+    return MK_ERR_CUDA;
+  } catch (const mkb::NcclError& e) {
+    g_error = e.what();
+    return MK_ERR_NCCL;
+  } catch (const std::exception& e) {
+    g_error = e.what();
+    return io_code;
+  } catch (...) {
+    g_error = "unknown error";
+    return io_code;
+  }
+}
+
+mkb::Model& model_of(mk_ctx* c) {
+  if (!c || !c->model) throw mkb::StateError("null context");
+  return *c->model;
+}
+
+cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+int current_device() {
+  int d = 0;
+  mkb::cuda_check(cudaGetDevice(&d), "cudaGetDevice");
+  return d;
+}
+
+// Temporary quantized-activation buffers for the kernel-level entry points.
+struct TmpAct {
+  mkb::DevBuf buf;
+  mkb::ActQ act;
+  TmpAct(int n, int64_t K) {
+    const int nt8 = (n + 7) / 8, npad = nt8 * 8;
+    const int64_t blocks = K / 32;
+    const size_t qx = static_cast<size_t>(blocks) * npad * 32, f = static_cast<size_t>(blocks) * npad * 4;
+    buf = mkb::DevBuf(qx + 3 * f + 256);
+    auto* p = buf.get<uint8_t>();
+    act.qx = p;
+    act.dx = reinterpret_cast<float*>(p + qx);
+    act.dsx = act.dx + blocks * npad;
+    act.sh = reinterpret_cast<uint32_t*>(act.dsx + blocks * npad);
+    act.nt8 = nt8;
+  }
+};
+
+}  // namespace
+
+extern "C" {
+
+const char* mk_last_error(void) { return g_error.c_str(); }
+
+const char* mk_version(void) { return "malkin_b200 0.1.0 (sm_100a)"; }
+
+int mk_synth_gguf(const char* path, const mk_synth_spec* spec, int n_threads) {
+  return guard(MK_ERR_IO, [&] {
+    if (!path || !spec) throw mkb::ArgError("synth: null argument");
+    mkb::SynthSpec s{spec->n_layer,   spec->n_embd,    spec->n_ff,         spec->n_head,
+                     spec->n_head_kv, spec->head_dim,  spec->n_vocab,      spec->n_ctx_train,
+                     spec->rope_base, spec->rms_eps,   spec->tied,         static_cast<uint32_t>(spec->type_default),
+                     static_cast<uint32_t>(spec->type_attn_v), static_cast<uint32_t>(spec->type_ffn_down),
+                     static_cast<uint32_t>(spec->type_output), static_cast<uint32_t>(spec->type_embd), spec->sigma,
+                     spec->seed};
+    mkb::write_synth_gguf(path, s, n_threads);
+  });
+}
+
+int mk_nccl_unique_id(void* out128) {
+  return guard(MK_ERR_NCCL, [&] {
+    if (!out128) throw mkb::ArgError("null id buffer");
+    ncclUniqueId id;
+    if (ncclGetUniqueId(&id) != ncclSuccess) throw mkb::NcclError("ncclGetUniqueId failed");
+    static_assert(sizeof(id) == 128, "ncclUniqueId size");
+    std::memcpy(out128, &id, sizeof id);
+  });
+}
+
+int mk_init(int device, int tp_rank, int tp_size, const void* nccl_id, mk_ctx** out) {
+  return guard(MK_ERR_CUDA, [&] {
+    if (!out) throw mkb::ArgError("null output");
+    *out = nullptr;
+    auto c = std::make_unique<mk_ctx>();
+    c->model = std::make_unique<mkb::Model>(device, tp_rank, tp_size, nccl_id);
+    *out = c.release();
+  });
+}
+
+int mk_shutdown(mk_ctx* ctx) {
+  return guard(MK_ERR_CUDA, [&] { delete ctx; });
+}
+
+int mk_load_gguf(mk_ctx* ctx, const char* path) {
+  return guard(MK_ERR_IO, [&] {
+    if (!path) throw mkb::ArgError("null path");
+    model_of(ctx).load(path);
+  });
+}
+
+int mk_alloc_kv(mk_ctx* ctx, int n_ctx, int n_seq, int max_batch) {
+  return guard(MK_ERR_ARG, [&] { model_of(ctx).alloc_kv(n_ctx, n_seq, max_batch); });
+}
+
+int mk_model_config_get(const mk_ctx* ctx, mk_model_config* out) {
+  return guard(MK_ERR_ARG, [&] {
+    if (!out) throw mkb::ArgError("null output");
+    const mkb::Model& m = model_of(const_cast<mk_ctx*>(ctx));
+    const mkb::ModelCfg& c = m.cfg();
+    *out = mk_model_config{c.n_layer, c.n_embd, c.n_ff, c.n_head, c.n_head_kv, c.head_dim, c.n_ctx_train, c.n_vocab,
+                           c.rope_base, c.rms_eps, m.n_ctx(), m.n_seq(), m.tp_rank(), m.tp_size(), m.weight_bytes()};
+  });
+}
+
+int mk_forward(mk_ctx* ctx, const mk_batch_token* batch, int n, float* host_logits) {
+  return guard(MK_ERR_ARG, [&] {
+    if (!batch && n > 0) throw mkb::ArgError("null batch");
+    model_of(ctx).forward(batch, n, host_logits);
+  });
+}
+
+int mk_move_kv(mk_ctx* ctx, int from, int to, int seq) {
+  return guard(MK_ERR_ARG, [&] { model_of(ctx).move_kv(from, to, seq); });
+}
+
+int mk_accept(mk_ctx* ctx, const mk_proposal* props, int n_props, mk_accept_result* out) {
+  return guard(MK_ERR_ARG, [&] {
+    if (n_props > 0 && (!props || !out)) throw mkb::ArgError("null proposals / results");
+    model_of(ctx).accept(props, n_props, out);
+  });
+}
+
+int mk_verify_step(mk_ctx* ctx, const mk_batch_token* batch, int n, const mk_proposal* props, int n_props,
+                   mk_accept_result* out) {
+  return guard(MK_ERR_ARG, [&] {
+    mkb::Model& m = model_of(ctx);
+    if (!batch) throw mkb::ArgError("null batch");
+    m.forward(batch, n, nullptr);
+    if (n_props > 0) {
+      if (!props || !out) throw mkb::ArgError("null proposals / results");
+      m.accept(props, n_props, out);
+    }
+  });
+}
+
+int mk_rng_uniforms(uint64_t seed, int64_t skip, int n, double* out) {
+  return guard(MK_ERR_ARG, [&] {
+    if (n < 0 || skip < 0 || (n > 0 && !out)) throw mkb::ArgError("rng: bad argument");
+    std::mt19937_64 rng(seed);
+    std::uniform_real_distribution<double> u(0.0, 1.0);
+    for (int64_t i = 0; i < skip; ++i) (void)u(rng);
+    for (int i = 0; i < n; ++i) out[i] = u(rng);
+  });
+}
+
+int mk_set_profile(mk_ctx* ctx, int on) {
+  return guard(MK_ERR_ARG, [&] { model_of(ctx).set_profile(on != 0); });
+}
+
+int mk_stage_times(const mk_ctx* ctx, float* ms8) {
+  return guard(MK_ERR_ARG, [&] {
+    const float* s = model_of(const_cast<mk_ctx*>(ctx)).stage_ms();
+    for (int i = 0; i < 8; ++i) ms8[i] = s[i];
+  });
+}
+
+int64_t mk_last_launch_count(const mk_ctx* ctx) {
+  if (!ctx || !ctx->model) return -1;
+  return ctx->model->last_launches();
+}
+
+void* mk_stream(const mk_ctx* ctx) {
+  if (!ctx || !ctx->model) return nullptr;
+  return ctx->model->stream();
+}
+
+// ---- kernel-level entry points ----
+
+int mk_weight_upload(int type, const void* host_rows, int64_t rows, int64_t cols, mk_weight** out) {
+  return guard(MK_ERR_ARG, [&] {
+    if (!host_rows || !out || rows <= 0 || cols <= 0) throw mkb::ArgError("weight_upload: bad argument");
+    if (!mkb::repack_supported(static_cast<uint32_t>(type))) throw mkb::UnsupportedError("weight_upload: unsupported type");
+    const int u = mkb::kunit_values(static_cast<uint32_t>(type));
+    if (cols % u) throw mkb::ArgError("weight_upload: cols not a multiple of the block");
+    auto w = std::make_unique<mk_weight>();
+    w->device = current_device();
+    const size_t rb = mkb::row_bytes(static_cast<uint32_t>(type), cols);
+    const size_t bytes = mkb::repack_bytes(static_cast<uint32_t>(type), rows, cols / u);
+    std::vector<uint8_t> staging(bytes);
+    mkb::repack(static_cast<uint32_t>(type), static_cast<const uint8_t*>(host_rows), rb, rows, 0, cols / u,
+                staging.data(), 0);
+    w->buf = mkb::DevBuf(bytes);
+    mkb::cuda_check(cudaMemcpy(w->buf.get(), staging.data(), bytes, cudaMemcpyHostToDevice), "upload");
+    w->w.type = static_cast<uint32_t>(type);
+    w->w.data = w->buf.get<uint8_t>();
+    w->w.rows = rows;
+    w->w.cols = cols;
+    w->w.panels = (rows + mkb::kPanelRows - 1) / mkb::kPanelRows;
+    w->w.kunits = static_cast<int>(cols / u);
+    *out = w.release();
+  });
+}
+
+int mk_weight_free(mk_weight* w) {
+  return guard(MK_ERR_CUDA, [&] { delete w; });
+}
+
+int64_t mk_weight_device_bytes(const mk_weight* w) { return w ? static_cast<int64_t>(w->buf.size()) : -1; }
+
+int mk_quantize_q8(const float* dev_x, int n, int64_t k, void* dev_blocks, void* stream) {
+  return guard(MK_ERR_ARG, [&] {
+    if (n <= 0 || k <= 0 || k % 32) throw mkb::ArgError("quantize_q8: bad shape");
+    mkb::launch_quant_blockq8(dev_x, n, k, dev_blocks, as_stream(stream));
+    mkb::cuda_check(cudaGetLastError(), "quantize_q8");
+  });
+}
+
+int mk_matmul(const mk_weight* w, const float* dev_x, int n, float* dev_y, int split_k, void* stream) {
+  return guard(MK_ERR_ARG, [&] {
+    if (!w || n <= 0) throw mkb::ArgError("matmul: bad argument");
+    cudaStream_t s = as_stream(stream);
+    TmpAct t(n, w->w.cols);
+    mkb::launch_quant_rows(dev_x, w->w.cols, n, static_cast<int>(w->w.cols), t.act, s);
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int split = split_k > 0 ? split_k : mkb::gemm_auto_split(w->w, n, sms);
+    if (split > 1)
+      mkb::cuda_check(cudaMemsetAsync(dev_y, 0, static_cast<size_t>(n) * w->w.rows * 4, s), "memset");
+    mkb::launch_gemm(w->w, t.act, n, dev_y, w->w.rows, split, split > 1, s);
+    mkb::cuda_check(cudaGetLastError(), "matmul");
+    mkb::cuda_check(cudaStreamSynchronize(s), "matmul");
+  });
+}
+
+int mk_block_dots(const mk_weight* w, const float* dev_x, int n, int32_t* dev_out, void* stream) {
+  return guard(MK_ERR_ARG, [&] {
+    if (!w || n <= 0) throw mkb::ArgError("block_dots: bad argument");
+    cudaStream_t s = as_stream(stream);
+    TmpAct t(n, w->w.cols);
+    mkb::launch_quant_rows(dev_x, w->w.cols, n, static_cast<int>(w->w.cols), t.act, s);
+    mkb::launch_block_dots(w->w, t.act, n, dev_out, s);
+    mkb::cuda_check(cudaGetLastError(), "block_dots");
+    mkb::cuda_check(cudaStreamSynchronize(s), "block_dots");
+  });
+}
+
+int mk_quantize_i8(const float* dev_x, int n, int len, int8_t* dev_q, float* dev_scale, void* stream) {
+  return guard(MK_ERR_ARG, [&] {
+    if (n <= 0 || len <= 0) throw mkb::ArgError("quantize_i8: bad shape");
+    mkb::launch_quant_i8(dev_x, n, len, dev_q, dev_scale, as_stream(stream));
+    mkb::cuda_check(cudaGetLastError(), "quantize_i8");
+  });
+}
+
+int mk_silu_mul(float* dev_g, const float* dev_u, int64_t n, void* stream) {
+  return guard(MK_ERR_ARG, [&] {
+    if (n <= 0) throw mkb::ArgError("silu_mul: bad length");
+    mkb::launch_silu_mul(dev_g, dev_u, n, as_stream(stream));
+    mkb::cuda_check(cudaGetLastError(), "silu_mul");
+  });
+}
+
+int mk_attention(const float* dev_q, int n, int H, int KV, int D, const int8_t* dev_k, const int8_t* dev_v,
+                 const float* dev_ks, const float* dev_vs, int64_t n_rows, const int32_t* dev_kv_base,
+                 const int32_t* dev_n_keys, const int32_t* dev_anc_off, const int32_t* dev_anc, float* dev_out,
+                 void* stream) {
+  return guard(MK_ERR_ARG, [&] {
+    if (n <= 0 || H <= 0 || KV <= 0 || H % KV || (D != 64 && D != 128 && D != 256))
+      throw mkb::ArgError("attention: bad shape");
+    cudaStream_t s = as_stream(stream);
+    std::vector<int32_t> kvb(n), nk(n);
+    mkb::cuda_check(cudaMemcpy(kvb.data(), dev_kv_base, n * 4, cudaMemcpyDeviceToHost), "attention");
+    mkb::cuda_check(cudaMemcpy(nk.data(), dev_n_keys, n * 4, cudaMemcpyDeviceToHost), "attention");
+    const int G = H / KV, rows = std::max(1, mkb::attn_qmax() / G);
+    std::vector<int32_t> sgf, tsg(n);
+    int maxk = 1;
+    for (int t = 0; t < n; ++t) {
+      if (t == 0 || kvb[t] != kvb[t - 1] || t - sgf.back() >= rows) sgf.push_back(t);
+      tsg[t] = static_cast<int32_t>(sgf.size()) - 1;
+      maxk = std::max(maxk, nk[t]);
+    }
+    const int n_sg = static_cast<int>(sgf.size());
+    sgf.push_back(n);
+    mkb::AttnPlan p;
+    p.n = n;
+    p.n_sg = n_sg;
+    p.chunk = 256;
+    p.n_chunks = (maxk + p.chunk - 1) / p.chunk;
+    mkb::DevBuf tabs((sgf.size() + tsg.size()) * 4);
+    mkb::cuda_check(cudaMemcpy(tabs.get(), sgf.data(), sgf.size() * 4, cudaMemcpyHostToDevice), "attention");
+    mkb::cuda_check(cudaMemcpy(tabs.get<int32_t>() + sgf.size(), tsg.data(), tsg.size() * 4, cudaMemcpyHostToDevice),
+                    "attention");
+    mkb::DevBuf part(mkb::attn_part_floats(n_sg, p.n_chunks, KV, D) * 4);
+    p.sg_first = tabs.get<int32_t>();
+    p.tok_sg = tabs.get<int32_t>() + sgf.size();
+    p.kv_base = dev_kv_base;
+    p.n_keys = dev_n_keys;
+    p.anc_off = dev_anc_off;
+    p.anc = dev_anc;
+    p.part = part.get<float>();
+    mkb::AttnLayer L{const_cast<int8_t*>(dev_k), const_cast<int8_t*>(dev_v), const_cast<float*>(dev_ks),
+                     const_cast<float*>(dev_vs), n_rows};
+    mkb::launch_attention(dev_q, H, KV, D, 1.0f / std::sqrt(static_cast<float>(D)), L, p, dev_out, s);
+    mkb::cuda_check(cudaGetLastError(), "attention");
+    mkb::cuda_check(cudaStreamSynchronize(s), "attention");
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,785 @@
+#include "model.hpp"
+
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+
+#include "gguf.hpp"
+#include "layout.hpp"
+#include "repack.hpp"
+
+namespace mkb {
+
+void cuda_check(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) throw CudaError(std::string("cuda: ") + what + ": " + cudaGetErrorString(e));
+}
+
+namespace {
+
+void nccl_check(ncclResult_t r, const char* what) {
+  if (r != ncclSuccess) throw NcclError(std::string("nccl: ") + what + ": " + ncclGetErrorString(r));
+}
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+}  // namespace
+
+DevBuf::DevBuf(size_t bytes) {
+  if (bytes) cuda_check(cudaMalloc(&p_, bytes), "cudaMalloc");
+  n_ = bytes;
+}
+
+DevBuf::~DevBuf() {
+  if (p_) cudaFree(p_);
+}
+
+DevBuf& DevBuf::operator=(DevBuf&& o) noexcept {
+  if (this != &o) {
+    if (p_) cudaFree(p_);
+    p_ = o.p_;
+    n_ = o.n_;
+    o.p_ = nullptr;
+    o.n_ = 0;
+  }
+  return *this;
+}
+
+Model::Model(int device, int tp_rank, int tp_size, const void* nccl_id)
+    : device_(device), tp_rank_(tp_rank), tp_size_(tp_size) {
+  if (tp_size < 1 || tp_size > 8 || tp_rank < 0 || tp_rank >= tp_size) throw ArgError("init: bad tensor-parallel rank");
+  cuda_check(cudaSetDevice(device), "cudaSetDevice");
+  cuda_check(cudaDeviceGetAttribute(&num_sms_, cudaDevAttrMultiProcessorCount, device), "sm count");
+  cuda_check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "stream");
+  for (auto& e : ev_) cuda_check(cudaEventCreate(&e), "event");
+  if (tp_size > 1) {
+    if (!nccl_id) throw ArgError("init: tensor parallel needs an NCCL unique id");
+    ncclUniqueId id;
+    std::memcpy(&id, nccl_id, sizeof id);
+    ncclComm_t comm;
+    nccl_check(ncclCommInitRank(&comm, tp_size, id, tp_rank), "ncclCommInitRank");
+    nccl_ = comm;
+  }
+}
+
+Model::~Model() {
+  cudaSetDevice(device_);
+  for (auto& [k, g] : graphs_) cudaGraphExecDestroy(g);
+  graphs_.clear();
+  if (nccl_) ncclCommDestroy(static_cast<ncclComm_t>(nccl_));
+  if (meta_host_) cudaFreeHost(meta_host_);
+  if (acc_host_) cudaFreeHost(acc_host_);
+  for (auto& e : ev_)
+    if (e) cudaEventDestroy(e);
+  if (stream_) cudaStreamDestroy(stream_);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// load: read_config (model.cpp:177-200) + Model::Model (model.cpp:211-251) + pack (model.cpp:262-277), per shard.
+// ---------------------------------------------------------------------------------------------------------------
+void Model::load(const std::string& path) {
+  cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+  Gguf f(path);
+  const std::string arch = f.get_str("general.architecture").value_or("");
+  if (arch != "qwen3") throw ArgError("architecture '" + arch + "' unsupported (supported: qwen3)");
+  auto need = [&](const std::string& k) {
+    auto v = f.get_int("qwen3." + k);
+    if (!v) throw ArgError("model: metadata qwen3." + k + " missing");
+    return static_cast<int>(*v);
+  };
+  ModelCfg c;
+  c.n_layer = need("block_count");
+  c.n_embd = need("embedding_length");
+  c.n_ff = need("feed_forward_length");
+  c.n_head = need("attention.head_count");
+  c.n_head_kv = static_cast<int>(f.get_int("qwen3.attention.head_count_kv").value_or(c.n_head));
+  c.head_dim = static_cast<int>(f.get_int("qwen3.attention.key_length").value_or(c.n_embd / c.n_head));
+  c.n_ctx_train = static_cast<int>(f.get_int("qwen3.context_length").value_or(4096));
+  c.rope_base = static_cast<float>(f.get_float("qwen3.rope.freq_base").value_or(10000.0));
+  c.rms_eps = static_cast<float>(f.get_float("qwen3.attention.layer_norm_rms_epsilon").value_or(1e-6));
+  if (c.head_dim % 32 || c.n_head % c.n_head_kv) throw ArgError("model: unsupported head layout");
+  if (c.head_dim != 64 && c.head_dim != 128 && c.head_dim != 256)
+    throw UnsupportedError("unsupported: head_dim " + std::to_string(c.head_dim) + " (64, 128, 256)");
+
+  auto weight = [&](const std::string& name, bool required) -> const Tensor* {
+    const Tensor* t = f.tensor(name);
+    if (!t) {
+      if (required) throw ArgError("model: tensor " + name + " missing");
+      return nullptr;
+    }
+    return t;
+  };
+  auto norm = [&](const std::string& name, int64_t n) {
+    const Tensor* t = f.tensor(name);
+    if (!t) throw ArgError("model: tensor " + name + " missing");
+    if (t->type != kF32 || t->nelements() != n)
+      throw ArgError("model: norm " + name + " not F32[" + std::to_string(n) + "]");
+    return t;
+  };
+  const Tensor* tok = weight("token_embd.weight", true);
+  const Tensor* out = weight("output.weight", false);
+  if (!out) out = tok;  // tied embeddings
+  c.n_vocab = static_cast<int>(out->rows());
+  cfg_ = c;
+  const int tp = tp_size_, r = tp_rank_;
+  const int D = c.head_dim, E = c.n_embd;
+  if (c.n_head % tp || c.n_head_kv % tp)
+    throw ArgError("tensor parallel: " + std::to_string(tp) + " ranks do not divide the heads");
+  Hl_ = c.n_head / tp;
+  KVl_ = c.n_head_kv / tp;
+
+  auto check_mat = [&](const Tensor* t) {
+    if (!repack_supported(t->type))
+      throw UnsupportedError(std::string("unsupported: tensor ") + t->name + " has type " + type_name(t->type) +
+                               " (this path streams Q8_0 Q4_K Q6_K)");
+  };
+  // ffn split in whole k-units of ffn_down (32 or 256 values)
+  const Tensor* down0 = weight("blk.0.ffn_down.weight", true);
+  check_mat(down0);
+  const int fu = kunit_values(down0->type);
+  if (c.n_ff % fu) throw ArgError("model: n_ff not a multiple of the ffn_down block");
+  const int nfu = c.n_ff / fu;
+  const int fu0 = static_cast<int>(static_cast<int64_t>(r) * nfu / tp), fu1 = static_cast<int>(static_cast<int64_t>(r + 1) * nfu / tp);
+  F0_ = fu0 * fu;
+  Fl_ = (fu1 - fu0) * fu;
+  V0_ = static_cast<int64_t>(r) * c.n_vocab / tp;
+  Vl_ = static_cast<int64_t>(r + 1) * c.n_vocab / tp - V0_;
+  const int64_t HDl = static_cast<int64_t>(Hl_) * D, KDl = static_cast<int64_t>(KVl_) * D;
+
+  // Device byte plan.
+  struct Piece {
+    const Tensor* t;
+    int64_t r0, nr, c0, nc;
+    size_t off;  // in wbuf
+  };
+  std::vector<Piece> pieces;
+  size_t total = 0;
+  auto add_piece = [&](const Tensor* t, int64_t r0, int64_t nr, int64_t c0, int64_t nc) -> size_t {
+    check_mat(t);
+    const int u = kunit_values(t->type);
+    if (c0 % u || nc % u) throw ArgError("tensor parallel: shard of " + t->name + " not block aligned");
+    total = align_up(total, 256);
+    pieces.push_back({t, r0, nr, c0, nc, total});
+    total += repack_bytes(t->type, nr, nc / u);
+    weight_bytes_ += static_cast<int64_t>(nr) * static_cast<int64_t>(row_bytes(t->type, nc));
+    return pieces.size() - 1;
+  };
+  weight_bytes_ = 0;
+  struct LayerPlan {
+    int qkv[3], nqkv, wo, gu[2], ngu, down;
+    const Tensor *an, *fn, *qn, *kn;
+  };
+  std::vector<LayerPlan> lp(static_cast<size_t>(c.n_layer));
+  for (int i = 0; i < c.n_layer; ++i) {
+    const std::string p = "blk." + std::to_string(i) + ".";
+    LayerPlan& L = lp[static_cast<size_t>(i)];
+    L.an = norm(p + "attn_norm.weight", E);
+    L.fn = norm(p + "ffn_norm.weight", E);
+    L.qn = norm(p + "attn_q_norm.weight", D);
+    L.kn = norm(p + "attn_k_norm.weight", D);
+    const Tensor* wq = weight(p + "attn_q.weight", true);
+    const Tensor* wk = weight(p + "attn_k.weight", true);
+    const Tensor* wv = weight(p + "attn_v.weight", true);
+    const Tensor* wo = weight(p + "attn_output.weight", true);
+    const Tensor* wg = weight(p + "ffn_gate.weight", true);
+    const Tensor* wu = weight(p + "ffn_up.weight", true);
+    const Tensor* wd = weight(p + "ffn_down.weight", true);
+    if (wq->cols() != E || wk->cols() != E || wv->cols() != E || wg->cols() != E || wu->cols() != E ||
+        wo->cols() != static_cast<int64_t>(c.n_head) * D || wd->cols() != c.n_ff || wq->rows() != static_cast<int64_t>(c.n_head) * D ||
+        wk->rows() != static_cast<int64_t>(c.n_head_kv) * D || wv->rows() != static_cast<int64_t>(c.n_head_kv) * D ||
+        wg->rows() != c.n_ff || wu->rows() != c.n_ff || wo->rows() != E || wd->rows() != E)
+      throw ArgError("model: layer " + std::to_string(i) + " tensor shapes do not match the config");
+    if (wd->type != down0->type) throw UnsupportedError("unsupported: ffn_down types differ across layers");
+    L.qkv[0] = static_cast<int>(add_piece(wq, r * HDl, HDl, 0, E));
+    L.qkv[1] = static_cast<int>(add_piece(wk, r * KDl, KDl, 0, E));
+    L.qkv[2] = static_cast<int>(add_piece(wv, r * KDl, KDl, 0, E));
+    L.nqkv = 3;
+    L.wo = static_cast<int>(add_piece(wo, 0, E, r * HDl, HDl));
+    L.gu[0] = static_cast<int>(add_piece(wg, F0_, Fl_, 0, E));
+    L.gu[1] = static_cast<int>(add_piece(wu, F0_, Fl_, 0, E));
+    L.ngu = 2;
+    L.down = static_cast<int>(add_piece(wd, 0, E, F0_, Fl_));
+  }
+  const int lm_piece = static_cast<int>(add_piece(out, V0_, Vl_, 0, E));
+  // Embedding table (GGUF rows, replicated) and norms (F32) after the matrices.
+  total = align_up(total, 256);
+  const size_t embd_off = total;
+  embd_type_ = tok->type;
+  if (type_size(embd_type_).block == 0 || (embd_type_ != kF32 && embd_type_ != kF16 && !repack_supported(embd_type_)))
+    throw UnsupportedError(std::string("unsupported: token_embd type ") + type_name(embd_type_));
+  embd_row_bytes_ = row_bytes(tok->type, tok->cols());
+  if (tok->cols() != E) throw ArgError("model: token_embd width != n_embd");
+  total += tok->nbytes;
+  const Tensor* onorm = norm("output_norm.weight", E);
+  total = align_up(total, 256);
+  const size_t norm_off = total;
+  total += static_cast<size_t>(c.n_layer) * (2 * E + 2 * D) * 4 + static_cast<size_t>(E) * 4;
+
+  wbuf_ = DevBuf(total);
+  uint8_t* base = wbuf_.get<uint8_t>();
+  std::vector<uint8_t> staging;
+  for (const Piece& pc : pieces) {
+    const int u = kunit_values(pc.t->type);
+    const size_t rb = row_bytes(pc.t->type, pc.t->cols());
+    const size_t nbytes = repack_bytes(pc.t->type, pc.nr, pc.nc / u);
+    staging.resize(nbytes);
+    repack(pc.t->type, pc.t->data + static_cast<size_t>(pc.r0) * rb, rb, pc.nr, pc.c0 / u, pc.nc / u, staging.data(), 0);
+    cuda_check(cudaMemcpy(base + pc.off, staging.data(), nbytes, cudaMemcpyHostToDevice), "upload weights");
+  }
+  cuda_check(cudaMemcpy(base + embd_off, tok->data, tok->nbytes, cudaMemcpyHostToDevice), "upload embeddings");
+  embd_ = base + embd_off;
+  float* nb = reinterpret_cast<float*>(base + norm_off);
+  auto put_norm = [&](const Tensor* t, int64_t n) {
+    cuda_check(cudaMemcpy(nb, t->data, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice), "upload norms");
+    const float* p = nb;
+    nb += n;
+    return p;
+  };
+  auto dev = [&](int idx) {
+    const Piece& pc = pieces[static_cast<size_t>(idx)];
+    DevWeight w;
+    w.type = pc.t->type;
+    w.data = base + pc.off;
+    w.rows = pc.nr;
+    w.cols = pc.nc;
+    w.panels = (pc.nr + kPanelRows - 1) / kPanelRows;
+    w.kunits = static_cast<int>(pc.nc / kunit_values(pc.t->type));
+    return w;
+  };
+  // Fuse consecutive same-type pieces (q|k|v, gate|up) into one weight: their panels are adjacent in wbuf.
+  auto fuse = [&](const int* idx, int cnt, DevWeight* outw, int64_t* cols, int& nout) {
+    nout = 0;
+    int64_t col = 0;
+    for (int i = 0; i < cnt; ++i) {
+      DevWeight w = dev(idx[i]);
+      const bool adjacent = nout > 0 && outw[nout - 1].type == w.type &&
+                            outw[nout - 1].data + repack_bytes(w.type, outw[nout - 1].rows, w.kunits) == w.data &&
+                            outw[nout - 1].rows % kPanelRows == 0;
+      if (adjacent) {
+        outw[nout - 1].rows += w.rows;
+        outw[nout - 1].panels = (outw[nout - 1].rows + kPanelRows - 1) / kPanelRows;
+      } else {
+        outw[nout] = w;
+        cols[nout] = col;
+        ++nout;
+      }
+      col += w.rows;
+    }
+  };
+  layers_.assign(static_cast<size_t>(c.n_layer), Layer{});
+  for (int i = 0; i < c.n_layer; ++i) {
+    const LayerPlan& P = lp[static_cast<size_t>(i)];
+    Layer& L = layers_[static_cast<size_t>(i)];
+    fuse(P.qkv, P.nqkv, L.qkv, L.qkv_col, L.n_qkv);
+    L.wo = dev(P.wo);
+    fuse(P.gu, P.ngu, L.gu, L.gu_col, L.n_gu);
+    L.down = dev(P.down);
+    L.attn_norm = put_norm(P.an, E);
+    L.ffn_norm = put_norm(P.fn, E);
+    L.q_norm = put_norm(P.qn, D);
+    L.k_norm = put_norm(P.kn, D);
+  }
+  out_norm_ = put_norm(onorm, E);
+  lm_head_ = dev(lm_piece);
+  qkv_ld_ = HDl + 2 * KDl;
+  inv_freq_.clear();
+  for (int i = 0; i < D / 2; ++i) inv_freq_.push_back(std::pow(c.rope_base, -2.0f * static_cast<float>(i) / static_cast<float>(D)));
+  loaded_ = true;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// alloc_kv (model.cpp:296-301) + scratch for max_batch tokens (model.cpp:239-250).
+// ---------------------------------------------------------------------------------------------------------------
+void Model::alloc_kv(int n_ctx, int n_seq, int max_batch) {
+  if (!loaded_) throw StateError("alloc_kv before load");
+  if (n_ctx <= 0 || n_seq <= 0) throw ArgError("alloc_kv: n_ctx and n_seq must be positive");
+  if (max_batch <= 0) max_batch = 256;
+  cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+  for (auto& [k, g] : graphs_) cudaGraphExecDestroy(g);
+  graphs_.clear();
+  const ModelCfg& c = cfg_;
+  const int D = c.head_dim, E = c.n_embd;
+  n_ctx_ = n_ctx;
+  n_seq_ = n_seq;
+  max_batch_ = max_batch;
+  const int64_t R = static_cast<int64_t>(n_seq) * n_ctx;
+  const size_t plane = static_cast<size_t>(c.n_layer) * KVl_ * R;
+  kv_ = DevBuf(plane * (2 * static_cast<size_t>(D) + 2 * sizeof(float)));
+  cuda_check(cudaMemset(kv_.get(), 0, kv_.size()), "kv memset");
+  int8_t* kbase = kv_.get<int8_t>();
+  int8_t* vbase = kbase + plane * D;
+  float* ksb = reinterpret_cast<float*>(vbase + plane * D);
+  float* vsb = ksb + plane;
+  kv_layers_.resize(static_cast<size_t>(c.n_layer));
+  for (int il = 0; il < c.n_layer; ++il) {
+    const size_t lo = static_cast<size_t>(il) * KVl_ * R;
+    kv_layers_[static_cast<size_t>(il)] = {kbase + lo * D, vbase + lo * D, ksb + lo, vsb + lo, R};
+  }
+  // RoPE table [pos][cos D/2 | sin D/2], the reference's float angles and libm cos / sin (model.cpp:434-440).
+  {
+    std::vector<float> tab(static_cast<size_t>(n_ctx) * D);
+    for (int p = 0; p < n_ctx; ++p) {
+      for (int i = 0; i < D / 2; ++i) {
+        const float a = static_cast<float>(p) * inv_freq_[static_cast<size_t>(i)];
+        tab[static_cast<size_t>(p) * D + i] = std::cos(a);
+        tab[static_cast<size_t>(p) * D + D / 2 + i] = std::sin(a);
+      }
+    }
+    rope_ = DevBuf(tab.size() * 4);
+    cuda_check(cudaMemcpy(rope_.get(), tab.data(), tab.size() * 4, cudaMemcpyHostToDevice), "rope table");
+  }
+  const int NB = static_cast<int>(align_up(static_cast<size_t>(max_batch), 8));
+  const int64_t HD = static_cast<int64_t>(Hl_) * D;
+  const int64_t kmax = std::max<int64_t>({E, HD, Fl_});
+  const int64_t blocks = kmax / 32;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align_up(off + bytes, 256);
+    return o;
+  };
+  const size_t o_x = take(static_cast<size_t>(NB) * E * 4), o_y = take(static_cast<size_t>(NB) * qkv_ld_ * 4),
+               o_q = take(static_cast<size_t>(NB) * HD * 4), o_att = take(static_cast<size_t>(NB) * HD * 4),
+               o_gu = take(static_cast<size_t>(NB) * 2 * Fl_ * 4), o_p = take(static_cast<size_t>(NB) * E * 4),
+               o_lg = take(static_cast<size_t>(NB) * Vl_ * 4), o_qx = take(static_cast<size_t>(blocks) * NB * 32),
+               o_dx = take(static_cast<size_t>(blocks) * NB * 4), o_dsx = take(static_cast<size_t>(blocks) * NB * 4),
+               o_sh = take(static_cast<size_t>(blocks) * NB * 4),
+               o_cv = take(static_cast<size_t>(NB) * MK_TOPK_CAP * 4), o_ci = take(static_cast<size_t>(NB) * MK_TOPK_CAP * 4),
+               o_gv = take(static_cast<size_t>(tp_size_) * NB * MK_TOPK_CAP * 4),
+               o_gi = take(static_cast<size_t>(tp_size_) * NB * MK_TOPK_CAP * 4);
+  scratch_ = DevBuf(off);
+  cuda_check(cudaMemset(scratch_.get(), 0, off), "scratch memset");
+  uint8_t* sb = scratch_.get<uint8_t>();
+  x_ = reinterpret_cast<float*>(sb + o_x);
+  yqkv_ = reinterpret_cast<float*>(sb + o_y);
+  q_ = reinterpret_cast<float*>(sb + o_q);
+  att_ = reinterpret_cast<float*>(sb + o_att);
+  ygu_ = reinterpret_cast<float*>(sb + o_gu);
+  p_ = reinterpret_cast<float*>(sb + o_p);
+  logits_ = reinterpret_cast<float*>(sb + o_lg);
+  act_.qx = sb + o_qx;
+  act_.dx = reinterpret_cast<float*>(sb + o_dx);
+  act_.dsx = reinterpret_cast<float*>(sb + o_dsx);
+  act_.sh = reinterpret_cast<uint32_t*>(sb + o_sh);
+  cand_v_ = reinterpret_cast<float*>(sb + o_cv);
+  cand_i_ = reinterpret_cast<int32_t*>(sb + o_ci);
+  gath_v_ = reinterpret_cast<float*>(sb + o_gv);
+  gath_i_ = reinterpret_cast<int32_t*>(sb + o_gi);
+  // attention plan geometry
+  const int G = c.n_head / c.n_head_kv;
+  sg_rows_ = std::max(1, attn_qmax() / G);
+  chunk_ = 256;
+  n_chunks_ = (n_ctx + chunk_ - 1) / chunk_;
+  max_sg_ = 0;
+  attn_part_ = DevBuf();
+  meta_cap_ = 0;
+  ensure_meta(static_cast<size_t>(max_batch) * 16);
+}
+
+void Model::ensure_meta(size_t anc_cap) {
+  const size_t MB = static_cast<size_t>(max_batch_);
+  const size_t need = 9 * MB + 2 + anc_cap;
+  if (need <= meta_cap_) return;
+  for (auto& [k, g] : graphs_) cudaGraphExecDestroy(g);
+  graphs_.clear();
+  const size_t cap = std::max(need, meta_cap_ * 2);
+  meta_ = DevBuf(cap * 4);
+  if (meta_host_) cudaFreeHost(meta_host_);
+  meta_host_ = nullptr;
+  cuda_check(cudaMallocHost(reinterpret_cast<void**>(&meta_host_), cap * 4), "pinned meta");
+  meta_cap_ = cap;
+  int32_t* m = meta_.get<int32_t>();
+  d_ids_ = m;
+  d_rpos_ = m + MB;
+  d_kvat_ = m + 2 * MB;
+  d_kvbase_ = m + 3 * MB;
+  d_nkeys_ = m + 4 * MB;
+  d_ancoff_ = m + 5 * MB;
+  d_sgfirst_ = m + 6 * MB + 1;
+  d_toksg_ = m + 7 * MB + 2;
+  d_outrows_ = m + 8 * MB + 2;
+  d_anc_ = m + 9 * MB + 2;
+}
+
+void Model::stage(int i) {
+  if (!profile_) return;
+  cudaEventRecord(ev_[i + 1], stream_);
+  cur_stage_ = i;
+}
+
+void Model::allreduce(float* buf, size_t count) {
+  nccl_check(ncclAllReduce(buf, buf, count, ncclFloat, ncclSum, static_cast<ncclComm_t>(nccl_), stream_),
+             "allreduce");
+}
+
+// y (+)= W x. accumulate: y holds the addend (red.add); else y is overwritten (zeroed first when split).
+void Model::gemm(const DevWeight& w, int n, float* y, int64_t ldy, bool accumulate) {
+  const int split = gemm_auto_split(w, n, num_sms_);
+  if (!accumulate && split > 1)
+    cuda_check(cudaMemset2DAsync(y, static_cast<size_t>(ldy) * 4, 0, static_cast<size_t>(w.rows) * 4, n, stream_),
+               "memset");
+  launch_gemm(w, act_, n, y, ldy, split, accumulate || split > 1, stream_);
+}
+
+void Model::run_forward(int n, int m) {
+  const ModelCfg& c = cfg_;
+  const int D = c.head_dim, E = c.n_embd;
+  const int64_t HD = static_cast<int64_t>(Hl_) * D;
+  const float scale = 1.0f / std::sqrt(static_cast<float>(D));
+  const int nt8 = (n + 7) / 8;
+  if (profile_) cudaEventRecord(ev_[0], stream_);
+  launch_embed(embd_, embd_type_, embd_row_bytes_, E, d_ids_, n, x_, stream_);
+  const bool tp = tp_size_ > 1;
+  for (int il = 0; il < c.n_layer; ++il) {
+    const Layer& L = layers_[static_cast<size_t>(il)];
+    act_.nt8 = nt8;
+    launch_rmsnorm_quant(x_, E, tp && il > 0 ? p_ : nullptr, nullptr, L.attn_norm, c.rms_eps, n, E, act_, stream_);
+    for (int i = 0; i < L.n_qkv; ++i) gemm(L.qkv[i], n, yqkv_ + L.qkv_col[i], qkv_ld_, false);
+    stage(0);
+    launch_qkv_post(yqkv_, qkv_ld_, n, Hl_, KVl_, D, L.q_norm, L.k_norm, c.rms_eps, rope_.get<float>(), d_rpos_, d_kvat_,
+                    q_, kv_layers_[static_cast<size_t>(il)], stream_);
+    stage(1);
+    launch_attention(q_, Hl_, KVl_, D, scale, kv_layers_[static_cast<size_t>(il)], plan_, att_, stream_);
+    stage(2);
+    launch_quant_rows(att_, HD, n, static_cast<int>(HD), act_, stream_);
+    if (tp) {
+      gemm(L.wo, n, p_, E, false);
+      allreduce(p_, static_cast<size_t>(n) * E);
+    } else {
+      gemm(L.wo, n, x_, E, true);
+    }
+    launch_rmsnorm_quant(x_, E, tp ? p_ : nullptr, nullptr, L.ffn_norm, c.rms_eps, n, E, act_, stream_);
+    stage(3);
+    for (int i = 0; i < L.n_gu; ++i) gemm(L.gu[i], n, ygu_ + L.gu_col[i], 2 * static_cast<int64_t>(Fl_), false);
+    stage(4);
+    launch_silu_quant(ygu_, 2 * static_cast<int64_t>(Fl_), Fl_, n, act_, stream_);
+    stage(5);
+    if (tp) {
+      gemm(L.down, n, p_, E, false);
+      allreduce(p_, static_cast<size_t>(n) * E);
+    } else {
+      gemm(L.down, n, x_, E, true);
+    }
+    stage(6);
+  }
+  if (m > 0) {
+    act_.nt8 = (m + 7) / 8;
+    launch_rmsnorm_quant(x_, E, tp ? p_ : nullptr, d_outrows_, out_norm_, c.rms_eps, m, E, act_, stream_);
+    gemm(lm_head_, m, logits_, Vl_, false);
+  }
+  stage(7);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// forward (model.cpp:379-422)
+// ---------------------------------------------------------------------------------------------------------------
+void Model::forward(const mk_batch_token* batch, int n, float* host_logits) {
+  if (!loaded_ || n_ctx_ == 0) throw StateError("forward before load / alloc_kv");
+  if (n <= 0 || n > max_batch_) throw ArgError("forward: batch size out of range");
+  cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+  const ModelCfg& c = cfg_;
+  std::vector<int32_t> ids(n), rpos(n), kvat(n), kvbase(n), nkeys(n), ancoff(n + 1), toksg(n), outrows;
+  std::vector<int32_t> anc, sgfirst;
+  lrow_.assign(static_cast<size_t>(n), -1);
+  for (int t = 0; t < n; ++t) {
+    const mk_batch_token& b = batch[t];
+    const int kv = b.parent < 0 ? b.pos : b.kv;
+    if (b.seq < 0 || b.seq >= n_seq_ || b.pos < 0 || b.pos >= n_ctx_ || kv < 0 || kv >= n_ctx_)
+      throw ArgError("forward: bad slot");
+    if (b.parent >= t || (b.parent >= 0 && batch[b.parent].seq != b.seq)) throw ArgError("forward: bad tree parent");
+    if (b.id < 0 || b.id >= c.n_vocab) throw ArgError("forward: token id out of range");
+    ids[t] = b.id;
+    rpos[t] = b.pos;
+    kvbase[t] = b.seq * n_ctx_;
+    kvat[t] = kvbase[t] + kv;
+    if (b.logits) {
+      lrow_[static_cast<size_t>(t)] = static_cast<int>(outrows.size());
+      outrows.push_back(t);
+    }
+  }
+  for (int t = 0; t < n; ++t) {
+    const mk_batch_token& b = batch[t];
+    ancoff[t] = static_cast<int32_t>(anc.size());
+    if (b.parent < 0) {
+      nkeys[t] = b.pos + 1;
+    } else {
+      nkeys[t] = nkeys[b.parent];
+      for (int i = ancoff[b.parent]; i < ancoff[b.parent + 1]; ++i) anc.push_back(anc[static_cast<size_t>(i)]);
+      anc.push_back(kvat[t] - kvbase[t]);
+    }
+    ancoff[t + 1] = static_cast<int32_t>(anc.size());
+  }
+  // attention sub-groups: runs of one sequence, at most sg_rows_ rows
+  for (int t = 0; t < n; ++t) {
+    if (t == 0 || kvbase[t] != kvbase[t - 1] || t - sgfirst.back() >= sg_rows_) sgfirst.push_back(t);
+    toksg[t] = static_cast<int32_t>(sgfirst.size()) - 1;
+  }
+  const int n_sg = static_cast<int>(sgfirst.size());
+  sgfirst.push_back(n);
+  const int m = static_cast<int>(outrows.size());
+  ensure_meta(anc.size());
+  if (n_sg > max_sg_) {
+    for (auto& [k, g] : graphs_) cudaGraphExecDestroy(g);
+    graphs_.clear();
+    max_sg_ = std::max(n_sg, max_sg_ * 2);
+    max_sg_ = std::min(max_sg_, max_batch_);
+    max_sg_ = std::max(max_sg_, n_sg);
+    attn_part_ = DevBuf(attn_part_floats(max_sg_, n_chunks_, KVl_, c.head_dim) * 4);
+  }
+  // pinned staging -> one copy
+  const size_t MB = static_cast<size_t>(max_batch_);
+  int32_t* h = meta_host_;
+  std::copy(ids.begin(), ids.end(), h);
+  std::copy(rpos.begin(), rpos.end(), h + MB);
+  std::copy(kvat.begin(), kvat.end(), h + 2 * MB);
+  std::copy(kvbase.begin(), kvbase.end(), h + 3 * MB);
+  std::copy(nkeys.begin(), nkeys.end(), h + 4 * MB);
+  std::copy(ancoff.begin(), ancoff.end(), h + 5 * MB);
+  std::copy(sgfirst.begin(), sgfirst.end(), h + 6 * MB + 1);
+  std::copy(toksg.begin(), toksg.end(), h + 7 * MB + 2);
+  std::copy(outrows.begin(), outrows.end(), h + 8 * MB + 2);
+  std::copy(anc.begin(), anc.end(), h + 9 * MB + 2);
+  cuda_check(cudaMemcpyAsync(meta_.get(), h, (9 * MB + 2 + anc.size()) * 4, cudaMemcpyHostToDevice, stream_),
+             "meta upload");
+  plan_.n = n;
+  plan_.n_sg = n_sg;
+  plan_.chunk = chunk_;
+  plan_.n_chunks = n_chunks_;
+  plan_.sg_first = d_sgfirst_;
+  plan_.kv_base = d_kvbase_;
+  plan_.n_keys = d_nkeys_;
+  plan_.anc_off = d_ancoff_;
+  plan_.anc = d_anc_;
+  plan_.tok_sg = d_toksg_;
+  plan_.part = attn_part_.get<float>();
+
+  if (profile_) {
+    run_forward(n, m);
+    cuda_check(cudaStreamSynchronize(stream_), "forward");
+    for (int i = 0; i < 8; ++i) {
+      float ms = 0;
+      cudaEventElapsedTime(&ms, ev_[i], ev_[i + 1]);
+      stage_ms_[i] = ms;
+    }
+    last_launches_ = -1;
+  } else {
+    const auto key = std::make_tuple(n, m, n_sg);
+    auto it = graphs_.find(key);
+    if (it == graphs_.end()) {
+      cudaGraph_t g;
+      cuda_check(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), "begin capture");
+      try {
+        run_forward(n, m);
+      } catch (...) {
+        cudaStreamEndCapture(stream_, &g);
+        if (g) cudaGraphDestroy(g);
+        throw;
+      }
+      cuda_check(cudaStreamEndCapture(stream_, &g), "end capture");
+      cudaGraphExec_t ge;
+      cuda_check(cudaGraphInstantiate(&ge, g, 0), "graph instantiate");
+      size_t nodes = 0;
+      cudaGraphGetNodes(g, nullptr, &nodes);
+      cudaGraphDestroy(g);
+      if (graphs_.size() >= 16) {
+        cudaGraphExecDestroy(graphs_.begin()->second);
+        graphs_.erase(graphs_.begin());
+      }
+      it = graphs_.emplace(key, ge).first;
+      graph_nodes_[key] = static_cast<int64_t>(nodes);
+    }
+    cuda_check(cudaGraphLaunch(it->second, stream_), "graph launch");
+    last_launches_ = graph_nodes_[key];
+  }
+  last_n_ = n;
+  last_m_ = m;
+  if (host_logits && m > 0) {
+    if (tp_size_ == 1) {
+      cuda_check(cudaMemcpyAsync(host_logits, logits_, static_cast<size_t>(m) * c.n_vocab * 4, cudaMemcpyDeviceToHost,
+                                 stream_),
+                 "logits download");
+      cuda_check(cudaStreamSynchronize(stream_), "forward");
+    } else {
+      // gather every rank's vocab shard: [rank][m][Vl_r] -> host rows of n_vocab
+      cuda_check(cudaStreamSynchronize(stream_), "forward");
+      const int64_t vmax = (c.n_vocab + tp_size_ - 1) / tp_size_ + 1;
+      DevBuf gb(static_cast<size_t>(tp_size_) * m * vmax * 4), sb(static_cast<size_t>(m) * vmax * 4);
+      cuda_check(cudaMemset(sb.get(), 0, sb.size()), "memset");
+      cuda_check(cudaMemcpy2D(sb.get(), vmax * 4, logits_, Vl_ * 4, Vl_ * 4, m, cudaMemcpyDeviceToDevice), "pack");
+      nccl_check(ncclAllGather(sb.get(), gb.get(), static_cast<size_t>(m) * vmax, ncclFloat,
+                               static_cast<ncclComm_t>(nccl_), stream_),
+                 "allgather logits");
+      cuda_check(cudaStreamSynchronize(stream_), "allgather");
+      std::vector<float> all(static_cast<size_t>(tp_size_) * m * vmax);
+      cuda_check(cudaMemcpy(all.data(), gb.get(), all.size() * 4, cudaMemcpyDeviceToHost), "logits download");
+      for (int rk = 0; rk < tp_size_; ++rk) {
+        const int64_t v0 = static_cast<int64_t>(rk) * c.n_vocab / tp_size_;
+        const int64_t vl = static_cast<int64_t>(rk + 1) * c.n_vocab / tp_size_ - v0;
+        for (int row = 0; row < m; ++row)
+          std::memcpy(host_logits + static_cast<size_t>(row) * c.n_vocab + v0,
+                      all.data() + (static_cast<size_t>(rk) * m + row) * vmax, static_cast<size_t>(vl) * 4);
+      }
+    }
+  }
+}
+
+void Model::move_kv(int from, int to, int seq) {
+  if (n_ctx_ == 0) throw StateError("move_kv before alloc_kv");
+  if (seq < 0 || seq >= n_seq_ || from < 0 || from >= n_ctx_ || to < 0 || to >= n_ctx_) throw ArgError("move_kv: bad row");
+  if (from == to) return;
+  cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+  int32_t h[3] = {seq * n_ctx_ + from, seq * n_ctx_ + to, 1};
+  DevBuf d(sizeof h);
+  cuda_check(cudaMemcpyAsync(d.get(), h, sizeof h, cudaMemcpyHostToDevice, stream_), "move_kv");
+  KvCacheRef kc{kv_layers_[0].k, kv_layers_[0].v, kv_layers_[0].ks, kv_layers_[0].vs, cfg_.n_layer, KVl_, cfg_.head_dim,
+                static_cast<int64_t>(n_seq_) * n_ctx_};
+  int32_t* dp = d.get<int32_t>();
+  launch_move_kv(kc, dp, dp + 1, dp + 2, 1, 1, stream_);
+  cuda_check(cudaStreamSynchronize(stream_), "move_kv");
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// accept: Engine::accept_greedy / accept_sampled on device (engine.cpp:441-507)
+// ---------------------------------------------------------------------------------------------------------------
+void Model::accept(const mk_proposal* props, int np, mk_accept_result* res) {
+  if (last_n_ == 0) throw StateError("accept before forward");
+  if (np <= 0) return;
+  cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+  bool any_sampled = false;
+  int K = 1;
+  size_t n_chain = 0, n_q = 0, n_qn = 0, n_u = 0;
+  for (int i = 0; i < np; ++i) {
+    const mk_proposal& p = props[i];
+    const bool greedy = p.sampling.temperature <= 0.0f;
+    if (p.sampling.presence_penalty != 0.0f || p.sampling.frequency_penalty != 0.0f)
+      throw UnsupportedError("unsupported: presence / frequency penalties on the device accept path");
+    if (p.seq < 0 || p.seq >= n_seq_) throw ArgError("accept: bad sequence");
+    if (p.kk < 0 || p.kk > MK_MAX_DRAFT) throw ArgError("accept: draft length out of range");
+    if (p.cache_len < 0 || p.cache_len + 1 + p.kk > n_ctx_) throw ArgError("accept: context full");
+    const int rows = greedy ? 2 * p.kk + 1 : p.kk + 1;
+    if (p.root < 0 || p.root + rows > last_n_) throw ArgError("accept: proposal rows outside the last batch");
+    const int r0 = lrow_[static_cast<size_t>(p.root)];
+    for (int t = 0; t < rows; ++t)
+      if (r0 < 0 || lrow_[static_cast<size_t>(p.root + t)] != r0 + t) throw ArgError("accept: proposal rows without logits");
+    if (p.kk > 0 && !p.chain) throw ArgError("accept: missing chain");
+    if (greedy && p.kk > 0 && !p.alt) throw ArgError("accept: missing alt");
+    if (!greedy) {
+      any_sampled = true;
+      if (p.sampling.top_k <= 0 || p.sampling.top_k > MK_MAX_TOPK)
+        throw UnsupportedError("unsupported: top_k outside 1.." + std::to_string(MK_MAX_TOPK) + " on the device path");
+      K = std::max(K, p.sampling.top_k);
+      if (p.kk > 0 && (!p.q_p || !p.q_id || !p.q_n)) throw ArgError("accept: missing draft distributions");
+      for (int j = 0; j < p.kk; ++j) n_q += static_cast<size_t>(p.q_n[j]);
+      n_qn += static_cast<size_t>(p.kk);
+      if (p.n_uniforms > 0 && !p.uniforms) throw ArgError("accept: missing uniforms");
+      n_u += static_cast<size_t>(std::max(0, p.n_uniforms));
+    }
+    n_chain += static_cast<size_t>(p.kk);
+  }
+  K = std::min<int64_t>(K, Vl_);
+  constexpr int kc = MK_TOPK_CAP;
+  const int m = last_m_;
+  if (any_sampled)
+    launch_topk(logits_, Vl_, m, static_cast<int>(Vl_), static_cast<int>(V0_), K, kc, cand_v_, cand_i_, stream_);
+  else
+    launch_argmax_kc(logits_, Vl_, m, static_cast<int>(Vl_), static_cast<int>(V0_), kc, cand_v_, cand_i_, stream_);
+  if (tp_size_ > 1) {
+    const int kk = any_sampled ? K : 1;
+    auto comm = static_cast<ncclComm_t>(nccl_);
+    nccl_check(ncclGroupStart(), "group");
+    nccl_check(ncclAllGather(cand_v_, gath_v_, static_cast<size_t>(m) * kc, ncclFloat, comm, stream_), "allgather");
+    nccl_check(ncclAllGather(cand_i_, gath_i_, static_cast<size_t>(m) * kc, ncclInt32, comm, stream_), "allgather");
+    nccl_check(ncclGroupEnd(), "group");
+    launch_merge_cand(gath_v_, gath_i_, tp_size_, m, kk, kc, cand_v_, cand_i_, stream_);
+  }
+  // tables: reqs | outs | from | to | count | chain | alt | q_n | q_id | q_p | uniforms
+  const size_t o_req = 0, o_out = align_up(o_req + np * sizeof(AcceptReq), 16),
+               o_from = align_up(o_out + np * sizeof(AcceptOut), 16), o_to = o_from + np * 32 * 4,
+               o_cnt = o_to + np * 32 * 4, o_chain = align_up(o_cnt + np * 4, 16), o_alt = o_chain + n_chain * 4,
+               o_qn = o_alt + n_chain * 4, o_qid = o_qn + n_qn * 4, o_qp = o_qid + n_q * 4,
+               o_u = align_up(o_qp + n_q * 4, 16), total = align_up(o_u + n_u * 8 + 16, 256);
+  if (total > acc_cap_) {
+    acc_dev_ = DevBuf(total * 2);
+    if (acc_host_) cudaFreeHost(acc_host_);
+    acc_host_ = nullptr;
+    cuda_check(cudaMallocHost(&acc_host_, total * 2), "pinned accept");
+    acc_cap_ = total * 2;
+  }
+  auto* hb = static_cast<uint8_t*>(acc_host_);
+  auto* reqs = reinterpret_cast<AcceptReq*>(hb + o_req);
+  auto* chain = reinterpret_cast<int32_t*>(hb + o_chain);
+  auto* alt = reinterpret_cast<int32_t*>(hb + o_alt);
+  auto* qn = reinterpret_cast<int32_t*>(hb + o_qn);
+  auto* qid = reinterpret_cast<int32_t*>(hb + o_qid);
+  auto* qp = reinterpret_cast<float*>(hb + o_qp);
+  auto* uu = reinterpret_cast<double*>(hb + o_u);
+  size_t ci = 0, qi = 0, qni = 0, ui = 0;
+  for (int i = 0; i < np; ++i) {
+    const mk_proposal& p = props[i];
+    AcceptReq& R = reqs[i];
+    R.kk = p.kk;
+    R.greedy = p.sampling.temperature <= 0.0f ? 1 : 0;
+    R.seq = p.seq;
+    R.cache_len = p.cache_len;
+    R.row0 = lrow_[static_cast<size_t>(p.root)];
+    R.chain_off = static_cast<int32_t>(ci);
+    R.q_off = static_cast<int32_t>(qi);
+    R.qn_off = static_cast<int32_t>(qni);
+    R.u_off = static_cast<int32_t>(ui);
+    R.n_u = R.greedy ? 0 : std::max(0, p.n_uniforms);
+    R.top_k = std::min<int>(p.sampling.top_k, static_cast<int>(Vl_ * tp_size_));
+    R.temperature = p.sampling.temperature;
+    R.top_p = p.sampling.top_p;
+    R.min_p = p.sampling.min_p;
+    for (int j = 0; j < p.kk; ++j) {
+      chain[ci + static_cast<size_t>(j)] = p.chain[j];
+      alt[ci + static_cast<size_t>(j)] = R.greedy ? p.alt[j] : -1;
+    }
+    ci += static_cast<size_t>(p.kk);
+    if (!R.greedy) {
+      for (int j = 0; j < p.kk; ++j) {
+        qn[qni++] = p.q_n[j];
+        for (int e = 0; e < p.q_n[j]; ++e) {
+          qp[qi] = p.q_p[qi - static_cast<size_t>(R.q_off) + 0];
+          qid[qi] = p.q_id[qi - static_cast<size_t>(R.q_off)];
+          ++qi;
+        }
+      }
+      for (int j = 0; j < R.n_u; ++j) uu[ui++] = p.uniforms[j];
+    }
+  }
+  uint8_t* db = acc_dev_.get<uint8_t>();
+  cuda_check(cudaMemcpyAsync(db, hb, total, cudaMemcpyHostToDevice, stream_), "accept upload");
+  auto* d_out = reinterpret_cast<AcceptOut*>(db + o_out);
+  auto* d_from = reinterpret_cast<int32_t*>(db + o_from);
+  auto* d_to = reinterpret_cast<int32_t*>(db + o_to);
+  auto* d_cnt = reinterpret_cast<int32_t*>(db + o_cnt);
+  launch_accept(reinterpret_cast<AcceptReq*>(db + o_req), np, cand_v_, cand_i_, kc,
+                reinterpret_cast<int32_t*>(db + o_chain), reinterpret_cast<int32_t*>(db + o_alt),
+                reinterpret_cast<float*>(db + o_qp), reinterpret_cast<int32_t*>(db + o_qid),
+                reinterpret_cast<int32_t*>(db + o_qn), reinterpret_cast<double*>(db + o_u), n_ctx_, d_out, d_from, d_to,
+                d_cnt, stream_);
+  KvCacheRef kc_ref{kv_layers_[0].k, kv_layers_[0].v, kv_layers_[0].ks, kv_layers_[0].vs, cfg_.n_layer, KVl_,
+                    cfg_.head_dim, static_cast<int64_t>(n_seq_) * n_ctx_};
+  launch_move_kv(kc_ref, d_from, d_to, d_cnt, np, 32, stream_);
+  auto* h_out = reinterpret_cast<AcceptOut*>(hb + o_out);
+  cuda_check(cudaMemcpyAsync(h_out, d_out, np * sizeof(AcceptOut), cudaMemcpyDeviceToHost, stream_), "accept download");
+  cuda_check(cudaStreamSynchronize(stream_), "accept");
+  for (int i = 0; i < np; ++i) {
+    const AcceptOut& o = h_out[i];
+    if (o.status != 0) throw ArgError("accept: uniform stream too short for request " + std::to_string(i));
+    mk_accept_result& r = res[i];
+    r.n_accepted = o.n_acc;
+    for (int j = 0; j < o.n_acc; ++j) r.accepted[j] = o.ids[j];
+    r.next = o.next;
+    r.cache_len = o.cache_len;
+    r.uniforms_used = o.u_used;
+    r.last_node = o.last_node;
+  }
+}
+
+}  // namespace mkb

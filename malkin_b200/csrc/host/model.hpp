@@ -1,0 +1,170 @@
+// Qwen3 dense decoder on one B200 (one tensor-parallel rank): the B200 counterpart of malkin::Model
+// (model.h:33-97). Weights live in HBM in the device panel layout; the int8 KV cache is HBM-resident; a forward
+// pass is a fixed kernel sequence replayed as a CUDA graph per batch shape.
+#pragma once
+#include <cuda_runtime_api.h>
+
+#include <cstdint>
+#include <map>
+#include <memory>
+#include <string>
+#include <stdexcept>
+#include <tuple>
+#include <vector>
+
+#include "../../../include/malkin_b200.h"
+#include "../kernels/kernels.hpp"
+
+namespace mkb {
+
+struct ModelCfg {
+  int n_layer = 0, n_embd = 0, n_ff = 0, n_head = 0, n_head_kv = 0, head_dim = 0, n_ctx_train = 0, n_vocab = 0;
+  float rope_base = 10000.0f, rms_eps = 1e-6f;
+};
+
+// cudaMalloc'd bytes, freed on destruction.
+class DevBuf {
+ public:
+  DevBuf() = default;
+  explicit DevBuf(size_t bytes);
+  ~DevBuf();
+  DevBuf(const DevBuf&) = delete;
+  DevBuf& operator=(const DevBuf&) = delete;
+  DevBuf(DevBuf&& o) noexcept : p_(o.p_), n_(o.n_) { o.p_ = nullptr, o.n_ = 0; }
+  DevBuf& operator=(DevBuf&& o) noexcept;
+  template <typename T = void>
+  T* get() const {
+    return static_cast<T*>(p_);
+  }
+  size_t size() const { return n_; }
+
+ private:
+  void* p_ = nullptr;
+  size_t n_ = 0;
+};
+
+// Error kinds, mapped to the C ABI status codes by api.cpp.
+struct ArgError : std::runtime_error {          // MK_ERR_ARG: malkin throws for the same inputs
+  using std::runtime_error::runtime_error;
+};
+struct UnsupportedError : std::runtime_error {  // MK_ERR_UNSUPPORTED
+  using std::runtime_error::runtime_error;
+};
+struct StateError : std::runtime_error {        // MK_ERR_STATE
+  using std::runtime_error::runtime_error;
+};
+struct CudaError : std::runtime_error {         // MK_ERR_CUDA
+  using std::runtime_error::runtime_error;
+};
+struct NcclError : std::runtime_error {         // MK_ERR_NCCL
+  using std::runtime_error::runtime_error;
+};
+
+// Throws CudaError with the CUDA error string.
+void cuda_check(cudaError_t e, const char* what);
+
+class Model {
+ public:
+  Model(int device, int tp_rank, int tp_size, const void* nccl_id);
+  ~Model();
+
+  void load(const std::string& path);
+  void alloc_kv(int n_ctx, int n_seq, int max_batch);
+  void forward(const mk_batch_token* batch, int n, float* host_logits);
+  void move_kv(int from, int to, int seq);
+  void accept(const mk_proposal* props, int n_props, mk_accept_result* out);
+
+  const ModelCfg& cfg() const { return cfg_; }
+  int n_ctx() const { return n_ctx_; }
+  int n_seq() const { return n_seq_; }
+  int tp_rank() const { return tp_rank_; }
+  int tp_size() const { return tp_size_; }
+  int64_t weight_bytes() const { return weight_bytes_; }
+  cudaStream_t stream() const { return stream_; }
+  void set_profile(bool on) { profile_ = on; }
+  const float* stage_ms() const { return stage_ms_; }
+  int64_t last_launches() const { return last_launches_; }
+
+ private:
+  struct Layer {
+    DevWeight qkv[3];
+    int64_t qkv_col[3] = {0, 0, 0};
+    int n_qkv = 0;
+    DevWeight wo;
+    DevWeight gu[2];
+    int64_t gu_col[2] = {0, 0};
+    int n_gu = 0;
+    DevWeight down;
+    const float *attn_norm = nullptr, *ffn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+  };
+
+  void run_forward(int n, int m);               // kernel sequence (captured or direct)
+  void gemm(const DevWeight& w, int n, float* y, int64_t ldy, bool accumulate);
+  void allreduce(float* buf, size_t count);
+  void stage(int i);                             // profile lap
+  void ensure_meta(size_t anc_cap);
+
+  ModelCfg cfg_;
+  int device_ = 0, tp_rank_ = 0, tp_size_ = 1, num_sms_ = 148;
+  void* nccl_ = nullptr;  // ncclComm_t
+  cudaStream_t stream_ = nullptr;
+  bool loaded_ = false;
+
+  // shard geometry
+  int Hl_ = 0, KVl_ = 0, Fl_ = 0, F0_ = 0;  // local q heads, kv heads, ffn rows and first ffn row
+  int64_t Vl_ = 0, V0_ = 0;                  // local vocab rows, first row
+  int64_t qkv_ld_ = 0;                       // columns of y_qkv
+  int64_t weight_bytes_ = 0;
+
+  // weights
+  DevBuf wbuf_;
+  std::vector<Layer> layers_;
+  DevWeight lm_head_;
+  const float* out_norm_ = nullptr;
+  const uint8_t* embd_ = nullptr;
+  uint32_t embd_type_ = 0;
+  size_t embd_row_bytes_ = 0;
+  std::vector<float> inv_freq_;
+
+  // KV cache + activations
+  int n_ctx_ = 0, n_seq_ = 0, max_batch_ = 0;
+  DevBuf kv_, rope_, scratch_;
+  std::vector<AttnLayer> kv_layers_;
+  float *x_ = nullptr, *yqkv_ = nullptr, *q_ = nullptr, *att_ = nullptr, *ygu_ = nullptr, *p_ = nullptr,
+        *logits_ = nullptr;
+  ActQ act_;
+  float* cand_v_ = nullptr;
+  int32_t* cand_i_ = nullptr;
+  float* gath_v_ = nullptr;
+  int32_t* gath_i_ = nullptr;
+
+  // per-forward metadata (device + pinned host staging, one copy per forward)
+  DevBuf meta_;
+  int32_t* meta_host_ = nullptr;
+  size_t meta_cap_ = 0;  // int32 entries
+  int32_t *d_ids_ = nullptr, *d_rpos_ = nullptr, *d_kvat_ = nullptr, *d_kvbase_ = nullptr, *d_nkeys_ = nullptr,
+          *d_ancoff_ = nullptr, *d_sgfirst_ = nullptr, *d_toksg_ = nullptr, *d_outrows_ = nullptr, *d_anc_ = nullptr;
+  DevBuf attn_part_;
+  AttnPlan plan_;
+  int n_chunks_ = 0, chunk_ = 256, sg_rows_ = 0, max_sg_ = 0;
+
+  // last forward: logits row of each batch index (-1: none), tokens
+  std::vector<int> lrow_;
+  int last_n_ = 0, last_m_ = 0;
+
+  // accept tables
+  DevBuf acc_dev_;
+  void* acc_host_ = nullptr;
+  size_t acc_cap_ = 0;
+
+  // graphs keyed by (n, m, n_sg)
+  std::map<std::tuple<int, int, int>, cudaGraphExec_t> graphs_;
+  std::map<std::tuple<int, int, int>, int64_t> graph_nodes_;
+  bool profile_ = false;
+  cudaEvent_t ev_[9] = {};
+  float stage_ms_[8] = {};
+  int64_t last_launches_ = 0;
+  int cur_stage_ = 0;
+};
+
+}  // namespace mkb

@@ -1,0 +1,136 @@
+// Host repack of GGUF rows into the device panel layout (layout.hpp); the B200 counterpart of malkin's
+// pack_weight_into / kern::pack_panel (quant.cpp:300-311, gemm_avx512.cpp:376-544). Rows beyond the source are
+// zero-filled (they contribute exactly 0: zero scales), so matrices of any row count pad to whole panels.
+#include "repack.hpp"
+
+#include <algorithm>
+#include <atomic>
+#include <cstring>
+#include <stdexcept>
+#include <thread>
+#include <vector>
+
+#include "gguf.hpp"
+#include "layout.hpp"
+
+namespace mkb {
+
+namespace {
+
+// 6-bit value k (0..255) of a Q6_K super-block, stored +32 (quant.cpp:190-210 layout).
+inline int q6_at(const uint8_t* s, int k) {
+  const int n = k / 128, rem = k % 128, c = rem / 32, l = rem % 32;
+  const uint8_t lo = s[64 * n + l + (c & 1) * 32];
+  const int nib = c >= 2 ? lo >> 4 : lo & 0xF;
+  const int hb = (s[128 + 32 * n + l] >> (2 * c)) & 3;
+  return nib | (hb << 4);
+}
+
+// Q4_K nibble k (0..255) of a super-block.
+inline int q4_at(const uint8_t* s, int k) {
+  const int j = k / 32, l = k % 32;
+  const uint8_t b = s[16 + 32 * (j / 2) + l];
+  return (j & 1) ? b >> 4 : b & 0xF;
+}
+
+void pack_chunk(uint32_t type, const uint8_t* const rows[16], size_t unit_off, uint8_t* dst) {
+  switch (type) {
+    case kQ8_0: {
+      std::memset(dst, 0, kChunkQ8_0);
+      for (int L = 0; L < 32; ++L) {
+        const int g = L / 4, c = L % 4;
+        uint8_t* o = dst + 16 * L;
+        const int rr[4] = {g, g + 8, g, g + 8};
+        const int kk[4] = {4 * c, 4 * c, 16 + 4 * c, 16 + 4 * c};
+        for (int w = 0; w < 4; ++w) {
+          const uint8_t* s = rows[rr[w]];
+          if (!s) continue;
+          std::memcpy(o + 4 * w, s + unit_off + 2 + kk[w], 4);
+        }
+      }
+      for (int g = 0; g < 8; ++g) {
+        if (rows[g]) std::memcpy(dst + 512 + 4 * g, rows[g] + unit_off, 2);
+        if (rows[g + 8]) std::memcpy(dst + 512 + 4 * g + 2, rows[g + 8] + unit_off, 2);
+      }
+      return;
+    }
+    case kQ4_K:
+    case kQ6_K: {
+      const bool q6 = type == kQ6_K;
+      std::memset(dst, 0, q6 ? kChunkQ6_K : kChunkQ4_K);
+      auto val = [&](int r, int k) -> int {
+        const uint8_t* s = rows[r];
+        if (!s) return 0;
+        return q6 ? q6_at(s + unit_off, k) : q4_at(s + unit_off, k);
+      };
+      for (int j = 0; j < 8; ++j) {
+        for (int L = 0; L < 32; ++L) {
+          const int g = L / 4, c = L % 4;
+          uint8_t* nib = dst + 256 * j + 8 * L;
+          for (int i = 0; i < 4; ++i) {
+            const int a0 = val(g, 32 * j + 4 * c + i), a1 = val(g + 8, 32 * j + 4 * c + i);
+            const int a2 = val(g, 32 * j + 16 + 4 * c + i), a3 = val(g + 8, 32 * j + 16 + 4 * c + i);
+            nib[i] = static_cast<uint8_t>((a0 & 0xF) | ((a2 & 0xF) << 4));
+            nib[4 + i] = static_cast<uint8_t>((a1 & 0xF) | ((a3 & 0xF) << 4));
+            if (q6) {
+              dst[2048 + 128 * j + 4 * L + i] =
+                  static_cast<uint8_t>((a0 >> 4) | ((a1 >> 4) << 2) | ((a2 >> 4) << 4) | ((a3 >> 4) << 6));
+            }
+          }
+        }
+      }
+      for (int g = 0; g < 8; ++g) {
+        for (int h = 0; h < 2; ++h) {
+          const uint8_t* s = rows[g + 8 * h];
+          if (!s) continue;
+          if (q6) {
+            std::memcpy(dst + 3072 + 32 * g + 16 * h, s + unit_off + 192, 16);
+            std::memcpy(dst + 3328 + 4 * g + 2 * h, s + unit_off + 208, 2);
+          } else {
+            std::memcpy(dst + 2048 + 32 * g + 16 * h, s + unit_off, 16);
+          }
+        }
+      }
+      return;
+    }
+    default:
+      throw std::runtime_error("repack: unsupported weight type");
+  }
+}
+
+}  // namespace
+
+bool repack_supported(uint32_t type) { return type == kQ8_0 || type == kQ4_K || type == kQ6_K; }
+
+size_t repack_bytes(uint32_t type, int64_t rows, int64_t units) {
+  const int64_t panels = (rows + kPanelRows - 1) / kPanelRows;
+  return static_cast<size_t>(panels) * static_cast<size_t>(units) * chunk_bytes(type);
+}
+
+void repack(uint32_t type, const uint8_t* src, size_t src_stride, int64_t rows, int64_t unit0, int64_t units,
+            uint8_t* dst, int n_threads) {
+  if (!repack_supported(type)) throw std::runtime_error(std::string("repack: unsupported type ") + type_name(type));
+  const size_t cb = chunk_bytes(type);
+  const size_t unit_src = type_size(type).bytes;  // GGUF bytes of one k-unit of one row
+  const int64_t panels = (rows + kPanelRows - 1) / kPanelRows;
+  std::atomic<int64_t> next{0};
+  auto worker = [&] {
+    for (int64_t p; (p = next.fetch_add(1)) < panels;) {
+      const uint8_t* rp[16];
+      for (int r = 0; r < 16; ++r) {
+        const int64_t row = p * kPanelRows + r;
+        rp[r] = row < rows ? src + static_cast<size_t>(row) * src_stride : nullptr;
+      }
+      for (int64_t u = 0; u < units; ++u)
+        pack_chunk(type, rp, static_cast<size_t>(unit0 + u) * unit_src, dst + (static_cast<size_t>(p) * units + u) * cb);
+    }
+  };
+  int nt = n_threads > 0 ? n_threads : static_cast<int>(std::thread::hardware_concurrency());
+  nt = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(nt, panels)));
+  std::vector<std::thread> pool;
+  for (int i = 1; i < nt; ++i) pool.emplace_back(worker);
+  worker();
+  for (auto& t : pool) t.join();
+}
+
+}  // namespace mkb

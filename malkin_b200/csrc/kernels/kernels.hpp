@@ -1,0 +1,141 @@
+// Host-side launchers of the CUDA kernels (plain C++ signatures, usable from g++-compiled host code).
+#pragma once
+#include <cuda_runtime_api.h>
+
+#include <cstddef>
+#include <cstdint>
+
+#define MK_TOPK_CAP 64
+
+namespace mkb {
+
+// Quantized activations in the GEMM layout (layout.hpp). nt8 = token tiles of the current batch (layout stride).
+struct ActQ {
+  uint8_t* qx = nullptr;
+  float* dx = nullptr;
+  float* dsx = nullptr;
+  uint32_t* sh = nullptr;
+  int nt8 = 0;
+};
+
+// Device weight in the panel layout.
+struct DevWeight {
+  uint32_t type = 0;
+  const uint8_t* data = nullptr;
+  int64_t rows = 0;    // valid rows
+  int64_t cols = 0;    // values per row (this shard)
+  int64_t panels = 0;  // ceil(rows / 16)
+  int kunits = 0;      // cols / 32 (Q8_0) or cols / 256 (K-quants)
+};
+
+// ---- quantization (quant.cu) ----
+// x rows [n][ldx] -> act (blocks of K values); rows n..npad-1 zero-filled. K % 32 == 0.
+void launch_quant_rows(const float* x, int64_t ldx, int n, int K, const ActQ& act, cudaStream_t s);
+// rmsnorm (model.cpp:145-148) then quantize. rows: row indices into x (nullptr = 0..n-1). add (nullable): residual
+// partial added into x first (x[r] += add[r], written back; tensor-parallel allreduce result).
+void launch_rmsnorm_quant(float* x, int64_t ldx, const float* add, const int32_t* rows, const float* w, float eps, int n,
+                          int K, const ActQ& act, cudaStream_t s);
+// gu rows [n][ld]: gate at [0, F), up at [F, 2F): SiLU(gate) * up (kernels_avx512.cpp:271-280), quantized.
+void launch_silu_quant(const float* gu, int64_t ld, int F, int n, const ActQ& act, cudaStream_t s);
+// malkin BlockQ8 output (40-byte blocks) for tests.
+void launch_quant_blockq8(const float* x, int n, int64_t K, void* blocks, cudaStream_t s);
+// quantize_i8 rows (quant.cpp:216-222).
+void launch_quant_i8(const float* x, int n, int len, int8_t* q, float* scale, cudaStream_t s);
+void launch_silu_mul(float* g, const float* u, int64_t n, cudaStream_t s);
+
+// ---- GEMM (gemm.cu) ----
+// y[t * ldy + r] (+)= W[r] . x[t] for t < n, r < rows. split: k-unit ranges per CTA column (1 = whole K, malkin's
+// block order); atomic: accumulate with red.add (required when split > 1; y must hold the addend).
+void launch_gemm(const DevWeight& w, const ActQ& act, int n, float* y, int64_t ldy, int split, bool atomic,
+                 cudaStream_t s);
+// Split that fills the GPU for this weight (>= 1).
+int gemm_auto_split(const DevWeight& w, int n, int num_sms);
+// out[(r * n + t) * nblk + b]: exact int dot of block b (Q6_K: 16-value halves).
+void launch_block_dots(const DevWeight& w, const ActQ& act, int n, int32_t* out, cudaStream_t s);
+
+// ---- attention (attention.cu) ----
+struct AttnLayer {
+  int8_t* k;   // [kvh][n_rows][D]
+  int8_t* v;
+  float* ks;   // [kvh][n_rows]
+  float* vs;
+  int64_t n_rows;  // rows per head (n_seq * n_ctx)
+};
+// Per token: RoPE table row rpos, KV row kv_at (absolute). y: [n][ldy] = q heads | k heads | v heads.
+void launch_qkv_post(const float* y, int64_t ldy, int n, int H, int KV, int D, const float* q_norm, const float* k_norm,
+                     float eps, const float* rope_cs, const int32_t* rpos, const int32_t* kv_at, float* q_out,
+                     const AttnLayer& L, cudaStream_t s);
+
+// Attention work description (host-built, device tables).
+struct AttnPlan {
+  int n = 0;                    // tokens
+  int n_sg = 0;                 // query sub-groups (consecutive tokens of one sequence)
+  int chunk = 256;              // keys per partial CTA
+  int n_chunks = 0;             // chunk slots per sub-group (grid)
+  const int32_t* sg_first = nullptr;  // [n_sg + 1] token ranges
+  const int32_t* kv_base = nullptr;   // [n]
+  const int32_t* n_keys = nullptr;    // [n]
+  const int32_t* anc_off = nullptr;   // [n + 1]
+  const int32_t* anc = nullptr;       // extra key rows (relative to kv_base)
+  const int32_t* tok_sg = nullptr;    // [n] sub-group of each token
+  float* part = nullptr;              // partials workspace (attn_part_floats)
+};
+// Query vectors (rows x G) one sub-group may hold.
+int attn_qmax();
+size_t attn_part_floats(int n_sg, int n_chunks, int KV, int D);
+void launch_attention(const float* q, int H, int KV, int D, float scale, const AttnLayer& L, const AttnPlan& p,
+                      float* out, cudaStream_t s);
+
+// ---- misc (misc.cu) ----
+// Token embedding rows (GGUF Q8_0 / Q4_K / Q6_K / F32 / F16 rows) -> x [n][E].
+void launch_embed(const uint8_t* tab, uint32_t type, size_t row_bytes, int E, const int32_t* ids, int n, float* x,
+                  cudaStream_t s);
+// Sequential KV row moves (Model::move_kv semantics, in list order) for every layer and head.
+struct KvCacheRef {
+  int8_t* k;
+  int8_t* v;
+  float* ks;
+  float* vs;
+  int n_layer, kvh, D;
+  int64_t n_rows;  // per head per layer
+};
+// n_lists move lists (list l: count[l] moves from[l * stride + m] -> to[l * stride + m], absolute rows).
+void launch_move_kv(const KvCacheRef& c, const int32_t* from, const int32_t* to, const int32_t* count, int n_lists,
+                    int stride, cudaStream_t s);
+
+// ---- accept (accept.cu) ----
+// Per logits row: (max value, lowest index of it) over V values, index offset vbase (vocab shard).
+void launch_argmax(const float* logits, int64_t ld, int m, int V, int vbase, float* best_v, int32_t* best_i,
+                   cudaStream_t s);
+// Same, written at row * kc (candidate-list layout).
+void launch_argmax_kc(const float* logits, int64_t ld, int m, int V, int vbase, int kc, float* best_v,
+                      int32_t* best_i, cudaStream_t s);
+// Per logits row: top-k (value desc, index asc) candidates, stride kc per row; k <= 64.
+void launch_topk(const float* logits, int64_t ld, int m, int V, int vbase, int k, int kc, float* cand_v,
+                 int32_t* cand_i, cudaStream_t s);
+// Tensor parallel: per row, merge tp lists of k candidates ([rank][row][kc]) into the top k ([row][kc]).
+void launch_merge_cand(const float* in_v, const int32_t* in_i, int tp, int m, int k, int kc, float* out_v,
+                       int32_t* out_i, cudaStream_t s);
+
+// One request of mk_accept, device side.
+struct AcceptReq {
+  int32_t kk, greedy, seq, cache_len;
+  int32_t row0;                // logits row of the root; tree node t at row0 + t (rows contiguous)
+  int32_t chain_off;           // into chain / alt
+  int32_t q_off, qn_off;       // into q_p / q_id, q_n
+  int32_t u_off, n_u;          // into uniforms
+  int32_t top_k;
+  float temperature, top_p, min_p;
+};
+struct AcceptOut {
+  int32_t n_acc, next, cache_len, u_used, last_node, status;
+  int32_t ids[32];
+};
+// Greedy / sampled acceptance of n_req requests over per-row candidates (cand_v / cand_i, kc per row, sorted
+// value desc, index asc). Greedy requests emit their KV moves into from/to/count (list r, stride 32) with
+// sequence row base seq * n_ctx.
+void launch_accept(const AcceptReq* reqs, int n_req, const float* cand_v, const int32_t* cand_i, int kc,
+                   const int32_t* chain, const int32_t* alt, const float* q_p, const int32_t* q_id, const int32_t* q_n,
+                   const double* uniforms, int n_ctx, AcceptOut* out, int32_t* from, int32_t* to, int32_t* count,
+                   cudaStream_t s);
+}  // namespace mkb

@@ -1,0 +1,204 @@
+// Activation quantization to Q8 blocks (kern::quantize_row_q8, kernels_avx512.cpp:66-80), fused with the ops that
+// produce the activations: RMSNorm (model.cpp:145-148) and SiLU(gate) * up (kernels_avx512.cpp:271-280).
+// One warp quantizes one 32-value block: lane i holds value i.
+//
+// Bit-exactness with malkin's BlockQ8 given the same float input: d = amax / 127 (IEEE division), id = 1 / d
+// (0 when d == 0), q = round-half-even(x * id) saturated to int8, s[0] / s[1] = integer sums of the two 16-value
+// halves of the unsaturated ints.
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "kernels.hpp"
+
+namespace mkb {
+
+namespace {
+
+struct QBlock {
+  int q;     // saturated int8 value of this lane
+  float d;
+  int s0, s1;
+};
+
+__device__ __forceinline__ QBlock quant_block32(float v, int lane) {
+  QBlock r;
+  const float amax = warp_max(fabsf(v));
+  r.d = __fdiv_rn(amax, 127.0f);
+  const float id = r.d != 0.0f ? __fdiv_rn(1.0f, r.d) : 0.0f;
+  const int qi = __float2int_rn(__fmul_rn(v, id));
+  r.q = max(-128, min(127, qi));
+  int h = qi;
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) h += __shfl_xor_sync(0xffffffffu, h, o);  // sums within 16-lane halves
+  r.s0 = __shfl_sync(0xffffffffu, h, 0);
+  r.s1 = __shfl_sync(0xffffffffu, h, 16);
+  (void)lane;
+  return r;
+}
+
+// Writes block b of token t (this warp's lane values already quantized) into the GEMM layout.
+__device__ __forceinline__ void store_act(const ActQ& a, int b, int t, const QBlock& qb, int lane) {
+  const int npad = a.nt8 * 8;
+  // Gather 4 consecutive lanes' bytes into one word at lane 4m.
+  const uint32_t byte = static_cast<uint32_t>(qb.q) & 0xFFu;
+  const uint32_t b1 = __shfl_down_sync(0xffffffffu, byte, 1);
+  const uint32_t b2 = __shfl_down_sync(0xffffffffu, byte, 2);
+  const uint32_t b3 = __shfl_down_sync(0xffffffffu, byte, 3);
+  if ((lane & 3) == 0) {
+    const uint32_t word = byte | (b1 << 8) | (b2 << 16) | (b3 << 24);
+    const int m = lane >> 2;  // k = 4m .. 4m+3
+    const int c = m & 3, hi = m >> 2;
+    const int j = t >> 3, g = t & 7;
+    uint8_t* dst = a.qx + (static_cast<size_t>(b) * a.nt8 + j) * 256 + (g * 4 + c) * 8 + hi * 4;
+    *reinterpret_cast<uint32_t*>(dst) = word;
+  }
+  if (lane == 0) {
+    const size_t o = static_cast<size_t>(b) * npad + t;
+    a.dx[o] = qb.d;
+    if (a.dsx) a.dsx[o] = __fmul_rn(qb.d, static_cast<float>(qb.s0 + qb.s1));
+    if (a.sh) a.sh[o] = (static_cast<uint32_t>(qb.s0) & 0xFFFFu) | (static_cast<uint32_t>(qb.s1) << 16);
+  }
+}
+
+__device__ __forceinline__ void store_zero(const ActQ& a, int b, int t, int lane) {
+  QBlock z{0, 0.0f, 0, 0};
+  store_act(a, b, t, z, lane);
+}
+
+// grid (ceil(nb / 8), npad), block 256: warp w quantizes block blockIdx.x * 8 + w of token blockIdx.y.
+__global__ void k_quant_rows(const float* __restrict__ x, int64_t ldx, int n, int nb, ActQ a) {
+  const int lane = threadIdx.x & 31, b = blockIdx.x * 8 + (threadIdx.x >> 5), t = blockIdx.y;
+  if (b >= nb) return;
+  if (t >= n) {
+    store_zero(a, b, t, lane);
+    return;
+  }
+  const float v = x[static_cast<size_t>(t) * ldx + b * 32 + lane];
+  store_act(a, b, t, quant_block32(v, lane), lane);
+}
+
+// grid (npad), block 256: one token row. y = x * s * w, s = 1 / sqrt(dot(x, x) / K + eps).
+__global__ void k_rmsnorm_quant(float* __restrict__ x, int64_t ldx, const float* __restrict__ add,
+                                const int32_t* __restrict__ rows, const float* __restrict__ w, float eps, int n, int K,
+                                ActQ a) {
+  const int t = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nb = K / 32;
+  if (t >= n) {
+    for (int b = warp; b < nb; b += 8) store_zero(a, b, t, lane);
+    return;
+  }
+  const int r = rows ? rows[t] : t;
+  float* xr = x + static_cast<size_t>(r) * ldx;
+  __shared__ float red[8];
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < K; i += blockDim.x) {
+    float v = xr[i];
+    if (add) {
+      v = __fadd_rn(v, add[static_cast<size_t>(r) * ldx + i]);
+      xr[i] = v;
+    }
+    ss = __fmaf_rn(v, v, ss);
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  float tot = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) tot += red[i];
+  const float s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(K)), eps)));
+  for (int b = warp; b < nb; b += 8) {
+    const int i = b * 32 + lane;
+    const float v = __fmul_rn(__fmul_rn(xr[i], s), w[i]);
+    store_act(a, b, t, quant_block32(v, lane), lane);
+  }
+}
+
+// grid (ceil(nb / 8), npad), block 256.
+__global__ void k_silu_quant(const float* __restrict__ gu, int64_t ld, int F, int n, ActQ a) {
+  const int lane = threadIdx.x & 31, b = blockIdx.x * 8 + (threadIdx.x >> 5), t = blockIdx.y;
+  const int nb = F / 32;
+  if (b >= nb) return;
+  if (t >= n) {
+    store_zero(a, b, t, lane);
+    return;
+  }
+  const float* row = gu + static_cast<size_t>(t) * ld;
+  const float g = row[b * 32 + lane], u = row[F + b * 32 + lane];
+  const float e = exp_malkin(__fsub_rn(0.0f, g));
+  const float h = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, e)), u);
+  store_act(a, b, t, quant_block32(h, lane), lane);
+}
+
+// malkin BlockQ8 {float d; int16 s[2]; int8 qs[32]} output. grid (ceil(nb / 8), n), block 256.
+__global__ void k_quant_blockq8(const float* __restrict__ x, int64_t K, uint8_t* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nb = K / 32, b = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int t = blockIdx.y;
+  if (b >= nb) return;
+  const QBlock q = quant_block32(x[static_cast<size_t>(t) * K + b * 32 + lane], lane);
+  uint8_t* o = out + (static_cast<size_t>(t) * nb + b) * 40;
+  o[8 + lane] = static_cast<uint8_t>(static_cast<int8_t>(q.q));
+  if (lane == 0) {
+    *reinterpret_cast<float*>(o) = q.d;
+    reinterpret_cast<int16_t*>(o + 4)[0] = static_cast<int16_t>(q.s0);
+    reinterpret_cast<int16_t*>(o + 4)[1] = static_cast<int16_t>(q.s1);
+  }
+}
+
+// quantize_i8 (quant.cpp:216-222) of one row per warp: d = amax / 127, q = lrintf(x * (1 / d)).
+__global__ void k_quant_i8(const float* __restrict__ x, int n, int len, int8_t* __restrict__ q, float* __restrict__ sc) {
+  const int lane = threadIdx.x & 31, r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (r >= n) return;
+  const float* xr = x + static_cast<size_t>(r) * len;
+  float amax = 0.0f;
+  for (int i = lane; i < len; i += 32) amax = fmaxf(amax, fabsf(xr[i]));
+  amax = warp_max(amax);
+  const float d = __fdiv_rn(amax, 127.0f), id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+  for (int i = lane; i < len; i += 32) q[static_cast<size_t>(r) * len + i] = static_cast<int8_t>(__float2int_rn(__fmul_rn(xr[i], id)));
+  if (lane == 0) sc[r] = d;
+}
+
+__global__ void k_silu_mul(float* __restrict__ g, const float* __restrict__ u, int64_t n) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float x = g[i];
+    const float e = exp_malkin(__fsub_rn(0.0f, x));
+    g[i] = __fmul_rn(__fdiv_rn(x, __fadd_rn(1.0f, e)), u[i]);
+  }
+}
+
+}  // namespace
+
+void launch_quant_rows(const float* x, int64_t ldx, int n, int K, const ActQ& act, cudaStream_t s) {
+  const int nb = K / 32;
+  dim3 grid((nb + 7) / 8, act.nt8 * 8);
+  k_quant_rows<<<grid, 256, 0, s>>>(x, ldx, n, nb, act);
+}
+
+void launch_rmsnorm_quant(float* x, int64_t ldx, const float* add, const int32_t* rows, const float* w, float eps, int n,
+                          int K, const ActQ& act, cudaStream_t s) {
+  k_rmsnorm_quant<<<act.nt8 * 8, 256, 0, s>>>(x, ldx, add, rows, w, eps, n, K, act);
+}
+
+void launch_silu_quant(const float* gu, int64_t ld, int F, int n, const ActQ& act, cudaStream_t s) {
+  const int nb = F / 32;
+  dim3 grid((nb + 7) / 8, act.nt8 * 8);
+  k_silu_quant<<<grid, 256, 0, s>>>(gu, ld, F, n, act);
+}
+
+void launch_quant_blockq8(const float* x, int n, int64_t K, void* blocks, cudaStream_t s) {
+  const int64_t nb = K / 32;
+  dim3 grid(static_cast<unsigned>((nb + 7) / 8), n);
+  k_quant_blockq8<<<grid, 256, 0, s>>>(x, K, static_cast<uint8_t*>(blocks));
+}
+
+void launch_quant_i8(const float* x, int n, int len, int8_t* q, float* scale, cudaStream_t s) {
+  k_quant_i8<<<(n + 7) / 8, 256, 0, s>>>(x, n, len, q, scale);
+}
+
+void launch_silu_mul(float* g, const float* u, int64_t n, cudaStream_t s) {
+  const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, 4096));
+  k_silu_mul<<<blocks > 0 ? blocks : 1, 256, 0, s>>>(g, u, n);
+}
+
+}  // namespace mkb
