@@ -1,0 +1,428 @@
+"""Speculative-verify benchmark: accepted tok/s of malkin's tree-verify step (target forward over every request's
+draft tree + greedy acceptance + KV compaction) for a synthetic Qwen3 model, on 1..8 B200s (tensor parallel).
+
+    python bench.py [--gpus N --steps K --warmup W --config 8b]            # this repository's CUDA path
+    python bench.py --impl reference [...]                                  # malkin's own CPU path (oracle/_ref)
+    torchrun --nproc-per-node N bench.py --gpus N ...                       # N > 1: one rank per GPU
+
+One JSON line on rank 0. A step = one verify pass (forward + accept + move_kv) over a fixed state: every request has
+`prompt` tokens of KV (prefilled on the GPU) and the same drafted tree each step, so every step does identical work.
+Drafts follow the configuration's rule: at each depth the chain token is the target's greedy token with probability
+0.55 (seeded coin flips), otherwise uniform; siblings are uniform. The accepted count per step is therefore fixed by
+the seed (accepted = the leading run of matching flips per request, + 1 bonus token each).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "accepted tok/s, Qwen3-8B-arch Q8_0, 8 req x 16-node trees, 1/2/4/8 B200; HBM GB/s"
+
+Q8_0, Q4_K, Q6_K = 8, 12, 14
+CONFIGS = {
+    # name: model shape, weight types, requests, prompt tokens, draft depth (tree = root + chain + siblings)
+    "0.6b": dict(model=dict(n_layer=28, n_embd=1024, n_ff=3072, n_head=16, n_head_kv=8, tied=True,
+                            type_default=Q8_0), requests=1, prompt=512, kk=8),
+    "4b": dict(model=dict(n_layer=36, n_embd=2560, n_ff=9728, n_head=32, n_head_kv=8, tied=True, type_default=Q4_K,
+                          type_attn_v=Q6_K, type_ffn_down=Q6_K, type_output=Q6_K), requests=1, prompt=4096, kk=8),
+    "8b": dict(model=dict(n_layer=36, n_embd=4096, n_ff=12288, n_head=32, n_head_kv=8, tied=False,
+                          type_default=Q8_0), requests=8, prompt=2048, kk=8),
+    "14b": dict(model=dict(n_layer=40, n_embd=5120, n_ff=17408, n_head=40, n_head_kv=8, tied=False,
+                           type_default=Q6_K), requests=4, prompt=8192, kk=16),
+    "32b": dict(model=dict(n_layer=64, n_embd=5120, n_ff=25600, n_head=64, n_head_kv=8, tied=False,
+                           type_default=Q4_K), requests=32, prompt=8192, kk=8),
+    # small case for quick checks and profiling captures
+    "tiny": dict(model=dict(n_layer=4, n_embd=1024, n_ff=3072, n_head=16, n_head_kv=8, tied=False,
+                            type_default=Q8_0), requests=2, prompt=256, kk=8),
+}
+BLOCK = {Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210)}
+
+
+def model_path(name: str) -> str:
+    """Synthetic model file: MALKIN_B200_MODEL_DIR, else /dev/shm when it has room, else the temp dir."""
+    import shutil
+    d = os.environ.get("MALKIN_B200_MODEL_DIR")
+    if not d:
+        need = 2.5 * weight_bytes_of(CONFIGS[name])["total"]
+        d = os.path.join(tempfile.gettempdir(), "malkin_b200")
+        try:
+            if os.path.isdir("/dev/shm") and shutil.disk_usage("/dev/shm").free > need:
+                d = "/dev/shm/malkin_b200"
+        except OSError:
+            pass
+    os.makedirs(d, exist_ok=True)
+    return os.path.join(d, f"qwen3-{name}-synthetic-seed0.gguf")
+
+
+def spec_of(cfg: dict) -> dict:
+    m = dict(cfg["model"])
+    return dict(head_dim=128, n_vocab=151936, n_ctx_train=40960, rope_base=1e6, sigma=0.02, seed=0, **m)
+
+
+def ensure_model(name: str) -> str:
+    """Writes the synthetic GGUF once per box (rank 0); other ranks wait on the marker file."""
+    import malkin_b200 as mk
+    path = model_path(name)
+    if not os.path.exists(path + ".done"):
+        tmp = path + f".tmp{os.getpid()}"
+        mk.synth_gguf(tmp, **spec_of(CONFIGS[name]))
+        os.replace(tmp, path)
+        open(path + ".done", "w").close()
+    return path
+
+
+def weight_bytes_of(cfg: dict) -> dict:
+    """GGUF bytes of the streamed matrices (incl. LM head), per layer group and total."""
+    m = spec_of(cfg)
+    E, F, HD, KD, V, L = m["n_embd"], m["n_ff"], m["n_head"] * 128, m["n_head_kv"] * 128, m["n_vocab"], m["n_layer"]
+    td = m["type_default"]
+    tv, tdn = m.get("type_attn_v", td), m.get("type_ffn_down", td)
+    tout = m.get("type_output", td)
+
+    def rb(t, rows, cols):
+        b, s = BLOCK[t]
+        return rows * (cols // b) * s
+    qkv = rb(td, HD + KD, E) + rb(tv, KD, E)
+    wo = rb(td, E, HD)
+    gu = 2 * rb(td, F, E)
+    down = rb(tdn, E, F)
+    out = rb(tout, V, E)
+    return dict(qkv=qkv * L, wo=wo * L, gate_up=gu * L, down=down * L, output=out, total=(qkv + wo + gu + down) * L + out)
+
+
+def kv_bytes_per_token(cfg: dict) -> int:
+    m = spec_of(cfg)
+    return m["n_layer"] * 2 * m["n_head_kv"] * (128 + 4)
+
+
+def build_tree(reqs, kk):
+    """Engine::build_batch greedy layout (engine.cpp:362-379): per request [next, c0, a0, c1, a1, ...]."""
+    rows, roots = [], []
+    for seq, P, nxt, chain, alt in reqs:
+        root = len(rows)
+        roots.append(root)
+        rows.append((nxt, seq, P, 1, -1, -1))
+        for i in range(kk):
+            par = root if i == 0 else root + 2 * i - 1
+            rows.append((int(chain[i]), seq, P + 1 + i, 1, P + 1 + 2 * i, par))
+            rows.append((int(alt[i]), seq, P + 1 + i, 1, P + 2 + 2 * i, par))
+    return rows, roots
+
+
+def draft_plan(cfg: dict, V: int):
+    """Seeded coin flips (p = 0.55) and uniform fallback / sibling tokens; expected accepted tokens per step."""
+    rng = np.random.default_rng(2)
+    R, kk = cfg["requests"], cfg["kk"]
+    flips = rng.random((R, kk)) < 0.55
+    chains = rng.integers(0, V, (R, kk))
+    alts = rng.integers(0, V, (R, kk))
+    lead = [int(np.argmin(np.append(f, False))) for f in flips]  # leading run of True
+    return flips, chains, alts, sum(lead) + R
+
+
+def clocks_start():
+    try:
+        out = open(os.path.join(tempfile.gettempdir(), f"clocks{os.getpid()}.csv"), "w")
+        p = subprocess.Popen(["nvidia-smi", "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,"
+                              "clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+                              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                              "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "100"],
+                             stdout=out, stderr=subprocess.DEVNULL)
+        return p, out
+    except Exception:
+        return None, None
+
+
+def clocks_stop(handle, device: int):
+    p, out = handle
+    if p is None:
+        return None
+    p.terminate()
+    p.wait()
+    out.close()
+    sm, mx, reasons = [], 0.0, set()
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    for line in open(out.name):
+        f = [x.strip() for x in line.split(",")]
+        if len(f) < 9 or f[0] != str(device):
+            continue
+        try:
+            sm.append(float(f[1]))
+            mx = float(f[2])
+        except ValueError:
+            continue
+        for n, v in zip(names, f[5:9]):
+            if v.lower() == "active":
+                reasons.add(n)
+    os.unlink(out.name)
+    if not sm:
+        return None
+    return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def peaks():
+    try:
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))), "of measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "of fallback"
+
+
+def cpu_baseline_sample(path: str, cfg: dict, accepted_per_step: int, steps: int = 1):
+    """malkin's own CPU path (oracle/_ref) on the same weights and tree shape, all physical cores; KV prefix rows
+    exist but are not prefilled (attention reads the same number of keys)."""
+    from oracle import Ref, RefModel
+    why = Ref.available()
+    if why:
+        return None, why
+    r = Ref()
+    cores = r.physical_cores()
+    r.set_threads(cores)
+    R, P, kk = cfg["requests"], cfg["prompt"], cfg["kk"]
+    V = spec_of(cfg)["n_vocab"]
+    n_ctx = P + 2 * kk + 8
+    t0 = time.perf_counter()
+    m = RefModel(r, path, n_ctx, R)
+    load_s = time.perf_counter() - t0
+    _, chains, alts, _ = draft_plan(cfg, V)
+    rng = np.random.default_rng(3)
+    reqs = [(s, P, int(rng.integers(0, V)), chains[s], alts[s]) for s in range(R)]
+    rows, roots = build_tree(reqs, kk)
+    # malkin caps a forward at kMaxBatch = 256 rows: larger trees batches split on whole requests
+    per = max(1, 256 // (2 * kk + 1))
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        for s0 in range(0, R, per):
+            sub = [rw for rw in rows if s0 <= rw[1] < s0 + per]
+            base = min(i for i, rw in enumerate(rows) if rw[1] == s0)
+            sub = [(a, b, c, d, e, (f - base if f >= 0 else f)) for (a, b, c, d, e, f) in sub]
+            lg = m.forward(sub)
+            s = r.sampler(temperature=0.0, seed=1)
+            for j, seq in enumerate(range(s0, min(R, s0 + per))):
+                rt = j * (2 * kk + 1)
+                r.accept_greedy(s, lg[rt:rt + 2 * kk + 1], chains[seq], alts[seq], model=None)
+            r.free_sampler(s)
+        times.append(time.perf_counter() - t0)
+    t = min(times)
+    return dict(value=accepted_per_step / t, unit="tok/s", cores=cores, kind="reference",
+                sample=f"{steps} verify step(s) of the {R}x{2 * kk + 1}-row tree batch (ms/step {t * 1e3:.1f}, "
+                       f"model load {load_s:.1f} s), prefix KV not prefilled, accepted/step from the seeded draft "
+                       f"rule"), None
+
+
+def run_reference(args, cfg):
+    """--impl reference: malkin's CPU path on this config (rank 0 only)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    V = spec_of(cfg)["n_vocab"]
+    _, _, _, A = draft_plan(cfg, V)
+    path = ensure_model(args.config)
+    base, why = cpu_baseline_sample(path, cfg, A, steps=max(1, min(args.steps, 2)))
+    line = {"impl": "reference", "metric": METRIC, "unit": "tok/s", "higher_is_better": True,
+            "n_gpus": args.gpus, "steps": max(1, min(args.steps, 2)), "warmup": 0, "dtype": "int8 x int8 -> fp32",
+            "data": "synthetic", "config": config_json(args, cfg)}
+    if base is None:
+        line.update({"unavailable": f"malkin CPU path cannot run here: {why}"})
+    else:
+        line.update({"value": base["value"], "ms_per_step": A / base["value"] * 1e3, "cpu_baseline": base,
+                     "e2e": {"value": base["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
+                             "d2h_bytes_per_step": 0}})
+    print(json.dumps(line), flush=True)
+
+
+def config_json(args, cfg):
+    m = spec_of(cfg)
+    return {"workload": f"qwen3-{args.config} synthetic, {cfg['requests']} req x {2 * cfg['kk']}-node trees "
+                        f"(chain {cfg['kk']} + siblings), {cfg['prompt']}-token KV prefix, greedy accept",
+            "model": f"Qwen3-{args.config} architecture", "weights": "Q8_0" if m["type_default"] == Q8_0 else
+            ("Q4_K" if m["type_default"] == Q4_K else "Q6_K"), "requests": cfg["requests"],
+            "rows_per_step": cfg["requests"] * (2 * cfg["kk"] + 1), "prompt": cfg["prompt"],
+            "parallelism": f"tp{args.gpus}", "l2": "inputs larger than L2 (weights stream from HBM every step)"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="8b", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="malkin_b200", choices=["malkin_b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        return run_reference(args, cfg)
+
+    import torch
+    import torch.distributed as dist
+
+    import malkin_b200 as mk
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("gloo", timeout=timedelta(seconds=300))
+    # model file (rank 0 writes, everyone waits)
+    if rank == 0:
+        path = ensure_model(args.config)
+    if world > 1:
+        dist.barrier()
+    path = model_path(args.config)
+    nid = None
+    if world > 1:
+        obj = [mk.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nid = obj[0]
+    R, P, kk = cfg["requests"], cfg["prompt"], cfg["kk"]
+    rows_per_step = R * (2 * kk + 1)
+    n_ctx = P + 2 * kk + 8
+    max_batch = max(256, rows_per_step)
+    t0 = time.perf_counter()
+    m = mk.Model(local, rank, world, nid).load(path).alloc_kv(n_ctx, R, max_batch)
+    load_s = time.perf_counter() - t0
+    mc = m.config()
+    V = mc.n_vocab
+    # prefill: seeded prompts, chunks of max_batch tokens, logits for each prompt's last token
+    rng = np.random.default_rng(1)
+    prompts = rng.integers(0, V, (R, P))
+    toks = [(int(prompts[s, i]), s, i, int(i == P - 1), -1, -1) for s in range(R) for i in range(P)]
+    nexts = {}
+    t0 = time.perf_counter()
+    for c0 in range(0, len(toks), max_batch):
+        chunk = toks[c0:c0 + max_batch]
+        lg = m.forward([mk.BatchToken(*r) for r in chunk])
+        j = 0
+        for r in chunk:
+            if r[3]:
+                nexts[r[1]] = int(np.argmax(lg[j]))
+                j += 1
+    prefill_s = time.perf_counter() - t0
+    # drafts by the 0.55 greedy-match rule: depth by depth, the target's greedy token at the chain node above
+    flips, chains, alts, A_pred = draft_plan(cfg, V)
+    chains = chains.copy()
+    for d in range(kk):
+        reqs = [(s, P, nexts[s], chains[s], alts[s]) for s in range(R)]
+        rows, roots = build_tree(reqs, kk)
+        lg = m.forward([mk.BatchToken(*r) for r in rows])
+        for s in range(R):
+            node = 0 if d == 0 else 2 * d - 1
+            if flips[s, d]:
+                chains[s, d] = int(np.argmax(lg[roots[s] + node]))
+    reqs = [(s, P, nexts[s], chains[s], alts[s]) for s in range(R)]
+    rows, roots = build_tree(reqs, kk)
+    batch = mk.make_batch(mk.BatchToken(*r) for r in rows)
+    props = [mk.Proposal(seq=s, root=roots[s], cache_len=P, chain=chains[s], alt=alts[s]) for s in range(R)]
+
+    res = m.verify_step(batch, props)
+    A = sum(r.n_accepted + 1 for r in res)
+    for _ in range(args.warmup):
+        m.verify_step(batch, props)
+    stream = torch.cuda.ExternalStream(m.stream)
+    # timed: device events on the library's stream, K steps, max over ranks
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clk = clocks_start() if rank == 0 else (None, None)
+    launches = 0
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        res = m.verify_step(batch, props)
+        launches += m.last_launch_count() + 3  # forward graph kernels + candidates, accept, move_kv
+    ev1.record(stream)
+    ev1.synchronize()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = clocks_stop(clk, local) if rank == 0 else None
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    A_step = sum(r.n_accepted + 1 for r in res)
+    ms_step = ms / args.steps
+    value = A_step / (ms_step / 1e3)
+    # e2e: the same steps through the public API from host inputs, host wall clock (inputs rebuilt every step)
+    m.io_bytes()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        b = mk.make_batch(mk.BatchToken(*r) for r in rows)
+        ps = [mk.Proposal(seq=s, root=roots[s], cache_len=P, chain=chains[s], alt=alts[s]) for s in range(R)]
+        res2 = m.verify_step(b, ps)
+    e2e_s = time.perf_counter() - t0
+    h2d, d2h = m.io_bytes()
+    if world > 1:
+        t = torch.tensor([e2e_s], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    # roofline: stage-profiled forwards (CUDA events per stage on the launching stream)
+    m.set_profile(True)
+    st = np.zeros(8)
+    for _ in range(3):
+        m.forward(batch, want_logits=False)
+        st += np.asarray(m.stage_times())
+    st /= 3
+    m.set_profile(False)
+    wb = weight_bytes_of(cfg)
+    pk, pk_src = peaks()
+    gu_bytes = wb["gate_up"] / world
+    gu_gbs = gu_bytes / (st[4] / 1e3) / 1e9 if st[4] > 0 else None
+    step_bytes = wb["total"] / world + (R * P + rows_per_step) * kv_bytes_per_token(cfg) / world + \
+        rows_per_step * V * 4 / world
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8 x int8 -> fp32 (Q8 activations, GGUF weights)",
+        "data": "synthetic (seeded N(0,0.02) weights, seeded prompts and drafts)", "config": config_json(args, cfg),
+        "accepted_per_step": A_step, "accepted_predicted": A_pred, "verified_rows_per_s": rows_per_step / ms_step * 1e3,
+        "step_hbm_gbs": step_bytes * world / (ms_step / 1e3) / 1e9,
+        "e2e": {"value": A_step * args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": h2d // args.steps,
+                "d2h_bytes_per_step": d2h // args.steps},
+        "gpu_launches": launches,
+        "roofline": {"kernel": "gate+up weight-streaming GEMM (k_gemm_q8_0)", "bound": "hbm", "achieved": gu_gbs,
+                     "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": (gu_gbs / pk["hbm_gbs"]) if gu_gbs else None,
+                     "peak_source": pk_src, "traffic": None,
+                     "algorithmic_bytes_per_launch": gu_bytes / spec_of(cfg)["n_layer"],
+                     "stage_ms": {k: float(v) for k, v in zip(
+                         ["norm+qkv", "qk-norm/rope/kv", "attention", "wo+res+norm", "gate+up", "silu+quant", "down",
+                          "output"], st)}},
+        "roofline_step": {"bytes_per_step": step_bytes * world, "roofline_ms": step_bytes / (pk["hbm_gbs"] * 1e9) * 1e3,
+                          "frac": (step_bytes / (pk["hbm_gbs"] * 1e9)) / (ms_step / 1e3)},
+        "clocks": clocks, "load_s": load_s, "prefill_s": prefill_s,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            base, why = cpu_baseline_sample(path, cfg, A_step)
+        except Exception as e:  # the baseline is reported, never fatal
+            base, why = None, str(e)
+        line["cpu_baseline"] = base if base else {"value": None, "unit": "tok/s", "kind": "reference",
+                                                  "sample": f"unavailable: {why}"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    m.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -180,6 +180,8 @@ int mk_set_profile(mk_ctx* ctx, int on);
 int mk_stage_times(const mk_ctx* ctx, float* ms8);
 /* Kernel launches issued by the last mk_forward / mk_accept / mk_verify_step (graph nodes counted). */
 int64_t mk_last_launch_count(const mk_ctx* ctx);
+/* Host->device and device->host bytes the context copied since the previous call of this function. */
+int mk_last_io_bytes(mk_ctx* ctx, int64_t* h2d, int64_t* d2h);
 /* The CUDA stream the context launches on (cudaStream_t), for callers that time with events. */
 void* mk_stream(const mk_ctx* ctx);
 

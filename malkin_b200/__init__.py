@@ -164,6 +164,7 @@ lib.mk_set_profile.argtypes = [_vp, ctypes.c_int]
 lib.mk_stage_times.argtypes = [_vp, _P_F32]
 lib.mk_last_launch_count.argtypes = [_vp]
 lib.mk_last_launch_count.restype = ctypes.c_int64
+lib.mk_last_io_bytes.argtypes = [_vp, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64)]
 lib.mk_stream.argtypes = [_vp]
 lib.mk_stream.restype = _vp
 lib.mk_weight_upload.argtypes = [ctypes.c_int, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.POINTER(_vp)]
@@ -182,7 +183,7 @@ lib.mk_attention.argtypes = [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctyp
 EXPORTS = ("mk_last_error", "mk_version", "mk_synth_gguf", "mk_init", "mk_nccl_unique_id", "mk_shutdown",
            "mk_load_gguf", "mk_alloc_kv", "mk_model_config_get", "mk_forward", "mk_move_kv", "mk_accept",
            "mk_rng_uniforms", "mk_verify_step", "mk_set_profile", "mk_stage_times", "mk_last_launch_count",
-           "mk_stream", "mk_weight_upload", "mk_weight_free", "mk_weight_device_bytes", "mk_quantize_q8",
+           "mk_stream", "mk_last_io_bytes", "mk_weight_upload", "mk_weight_free", "mk_weight_device_bytes", "mk_quantize_q8",
            "mk_matmul", "mk_block_dots", "mk_quantize_i8", "mk_silu_mul", "mk_attention")
 
 
@@ -296,6 +297,12 @@ class Model:
 
     def last_launch_count(self) -> int:
         return int(lib.mk_last_launch_count(self._h))
+
+    def io_bytes(self):
+        """(host->device, device->host) bytes copied since the previous call."""
+        h, d = ctypes.c_int64(), ctypes.c_int64()
+        _check(lib.mk_last_io_bytes(self._h, ctypes.byref(h), ctypes.byref(d)))
+        return h.value, d.value
 
     @property
     def stream(self) -> int:

@@ -1,6 +1,5 @@
 // The C ABI (include/malkin_b200.h): status codes instead of exceptions, thread-local error text.
 #include <cuda_runtime.h>
-#include <nccl.h>
 
 #include <cmath>
 #include <cstring>
@@ -14,6 +13,7 @@
 #include "gguf.hpp"
 #include "layout.hpp"
 #include "model.hpp"
+#include "nccl_dl.hpp"
 #include "repack.hpp"
 #include "synth.hpp"
 
@@ -119,7 +119,7 @@ int mk_nccl_unique_id(void* out128) {
   return guard(MK_ERR_NCCL, [&] {
     if (!out128) throw mkb::ArgError("null id buffer");
     ncclUniqueId id;
-    if (ncclGetUniqueId(&id) != ncclSuccess) throw mkb::NcclError("ncclGetUniqueId failed");
+    if (mkb::dl_get_unique_id(&id) != ncclSuccess) throw mkb::NcclError("ncclGetUniqueId failed");
     static_assert(sizeof(id) == 128, "ncclUniqueId size");
     std::memcpy(out128, &id, sizeof id);
   });
@@ -215,6 +215,13 @@ int mk_stage_times(const mk_ctx* ctx, float* ms8) {
 int64_t mk_last_launch_count(const mk_ctx* ctx) {
   if (!ctx || !ctx->model) return -1;
   return ctx->model->last_launches();
+}
+
+int mk_last_io_bytes(mk_ctx* ctx, int64_t* h2d, int64_t* d2h) {
+  return guard(MK_ERR_ARG, [&] {
+    if (!h2d || !d2h) throw mkb::ArgError("null output");
+    model_of(ctx).io_bytes(h2d, d2h);
+  });
 }
 
 void* mk_stream(const mk_ctx* ctx) {

@@ -1,7 +1,6 @@
 #include "model.hpp"
 
 #include <cuda_runtime.h>
-#include <nccl.h>
 
 #include <algorithm>
 #include <cmath>
@@ -11,6 +10,7 @@
 
 #include "gguf.hpp"
 #include "layout.hpp"
+#include "nccl_dl.hpp"
 #include "repack.hpp"
 
 namespace mkb {
@@ -22,7 +22,7 @@ void cuda_check(cudaError_t e, const char* what) {
 namespace {
 
 void nccl_check(ncclResult_t r, const char* what) {
-  if (r != ncclSuccess) throw NcclError(std::string("nccl: ") + what + ": " + ncclGetErrorString(r));
+  if (r != ncclSuccess) throw NcclError(std::string("nccl: ") + what + ": " + dl_error_string(r));
 }
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -55,13 +55,12 @@ Model::Model(int device, int tp_rank, int tp_size, const void* nccl_id)
   cuda_check(cudaSetDevice(device), "cudaSetDevice");
   cuda_check(cudaDeviceGetAttribute(&num_sms_, cudaDevAttrMultiProcessorCount, device), "sm count");
   cuda_check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "stream");
-  for (auto& e : ev_) cuda_check(cudaEventCreate(&e), "event");
   if (tp_size > 1) {
     if (!nccl_id) throw ArgError("init: tensor parallel needs an NCCL unique id");
     ncclUniqueId id;
     std::memcpy(&id, nccl_id, sizeof id);
     ncclComm_t comm;
-    nccl_check(ncclCommInitRank(&comm, tp_size, id, tp_rank), "ncclCommInitRank");
+    nccl_check(dl_comm_init_rank(&comm, tp_size, id, tp_rank), "ncclCommInitRank");
     nccl_ = comm;
   }
 }
@@ -70,10 +69,10 @@ Model::~Model() {
   cudaSetDevice(device_);
   for (auto& [k, g] : graphs_) cudaGraphExecDestroy(g);
   graphs_.clear();
-  if (nccl_) ncclCommDestroy(static_cast<ncclComm_t>(nccl_));
+  if (nccl_) dl_comm_destroy(static_cast<ncclComm_t>(nccl_));
   if (meta_host_) cudaFreeHost(meta_host_);
   if (acc_host_) cudaFreeHost(acc_host_);
-  for (auto& e : ev_)
+  for (auto& e : pev_)
     if (e) cudaEventDestroy(e);
   if (stream_) cudaStreamDestroy(stream_);
 }
@@ -407,12 +406,18 @@ void Model::ensure_meta(size_t anc_cap) {
 
 void Model::stage(int i) {
   if (!profile_) return;
-  cudaEventRecord(ev_[i + 1], stream_);
-  cur_stage_ = i;
+  if (pk_ == pev_.size()) {
+    cudaEvent_t e;
+    cuda_check(cudaEventCreate(&e), "event");
+    pev_.push_back(e);
+    pstage_.push_back(-1);
+  }
+  cuda_check(cudaEventRecord(pev_[pk_], stream_), "event record");
+  pstage_[pk_++] = i;
 }
 
 void Model::allreduce(float* buf, size_t count) {
-  nccl_check(ncclAllReduce(buf, buf, count, ncclFloat, ncclSum, static_cast<ncclComm_t>(nccl_), stream_),
+  nccl_check(dl_all_reduce(buf, buf, count, ncclFloat, ncclSum, static_cast<ncclComm_t>(nccl_), stream_),
              "allreduce");
 }
 
@@ -431,7 +436,10 @@ void Model::run_forward(int n, int m) {
   const int64_t HD = static_cast<int64_t>(Hl_) * D;
   const float scale = 1.0f / std::sqrt(static_cast<float>(D));
   const int nt8 = (n + 7) / 8;
-  if (profile_) cudaEventRecord(ev_[0], stream_);
+  if (profile_) {
+    pk_ = 0;
+    stage(-1);
+  }
   launch_embed(embd_, embd_type_, embd_row_bytes_, E, d_ids_, n, x_, stream_);
   const bool tp = tp_size_ > 1;
   for (int il = 0; il < c.n_layer; ++il) {
@@ -545,6 +553,7 @@ void Model::forward(const mk_batch_token* batch, int n, float* host_logits) {
   std::copy(anc.begin(), anc.end(), h + 9 * MB + 2);
   cuda_check(cudaMemcpyAsync(meta_.get(), h, (9 * MB + 2 + anc.size()) * 4, cudaMemcpyHostToDevice, stream_),
              "meta upload");
+  h2d_bytes_ += static_cast<int64_t>((9 * MB + 2 + anc.size()) * 4);
   plan_.n = n;
   plan_.n_sg = n_sg;
   plan_.chunk = chunk_;
@@ -560,10 +569,11 @@ void Model::forward(const mk_batch_token* batch, int n, float* host_logits) {
   if (profile_) {
     run_forward(n, m);
     cuda_check(cudaStreamSynchronize(stream_), "forward");
-    for (int i = 0; i < 8; ++i) {
+    for (float& v : stage_ms_) v = 0.0f;
+    for (size_t k = 1; k < pk_; ++k) {
       float ms = 0;
-      cudaEventElapsedTime(&ms, ev_[i], ev_[i + 1]);
-      stage_ms_[i] = ms;
+      cuda_check(cudaEventElapsedTime(&ms, pev_[k - 1], pev_[k]), "event time");
+      if (pstage_[k] >= 0 && pstage_[k] < 8) stage_ms_[pstage_[k]] += ms;
     }
     last_launches_ = -1;
   } else {
@@ -584,6 +594,14 @@ void Model::forward(const mk_batch_token* batch, int n, float* host_logits) {
       cuda_check(cudaGraphInstantiate(&ge, g, 0), "graph instantiate");
       size_t nodes = 0;
       cudaGraphGetNodes(g, nullptr, &nodes);
+      std::vector<cudaGraphNode_t> nv(nodes);
+      cudaGraphGetNodes(g, nv.data(), &nodes);
+      size_t kernels = 0;
+      for (auto nd : nv) {
+        cudaGraphNodeType ty;
+        if (cudaGraphNodeGetType(nd, &ty) == cudaSuccess && ty == cudaGraphNodeTypeKernel) ++kernels;
+      }
+      nodes = kernels;
       cudaGraphDestroy(g);
       if (graphs_.size() >= 16) {
         cudaGraphExecDestroy(graphs_.begin()->second);
@@ -602,6 +620,7 @@ void Model::forward(const mk_batch_token* batch, int n, float* host_logits) {
       cuda_check(cudaMemcpyAsync(host_logits, logits_, static_cast<size_t>(m) * c.n_vocab * 4, cudaMemcpyDeviceToHost,
                                  stream_),
                  "logits download");
+      d2h_bytes_ += static_cast<int64_t>(m) * c.n_vocab * 4;
       cuda_check(cudaStreamSynchronize(stream_), "forward");
     } else {
       // gather every rank's vocab shard: [rank][m][Vl_r] -> host rows of n_vocab
@@ -610,7 +629,7 @@ void Model::forward(const mk_batch_token* batch, int n, float* host_logits) {
       DevBuf gb(static_cast<size_t>(tp_size_) * m * vmax * 4), sb(static_cast<size_t>(m) * vmax * 4);
       cuda_check(cudaMemset(sb.get(), 0, sb.size()), "memset");
       cuda_check(cudaMemcpy2D(sb.get(), vmax * 4, logits_, Vl_ * 4, Vl_ * 4, m, cudaMemcpyDeviceToDevice), "pack");
-      nccl_check(ncclAllGather(sb.get(), gb.get(), static_cast<size_t>(m) * vmax, ncclFloat,
+      nccl_check(dl_all_gather(sb.get(), gb.get(), static_cast<size_t>(m) * vmax, ncclFloat,
                                static_cast<ncclComm_t>(nccl_), stream_),
                  "allgather logits");
       cuda_check(cudaStreamSynchronize(stream_), "allgather");
@@ -690,10 +709,10 @@ void Model::accept(const mk_proposal* props, int np, mk_accept_result* res) {
   if (tp_size_ > 1) {
     const int kk = any_sampled ? K : 1;
     auto comm = static_cast<ncclComm_t>(nccl_);
-    nccl_check(ncclGroupStart(), "group");
-    nccl_check(ncclAllGather(cand_v_, gath_v_, static_cast<size_t>(m) * kc, ncclFloat, comm, stream_), "allgather");
-    nccl_check(ncclAllGather(cand_i_, gath_i_, static_cast<size_t>(m) * kc, ncclInt32, comm, stream_), "allgather");
-    nccl_check(ncclGroupEnd(), "group");
+    nccl_check(dl_group_start(), "group");
+    nccl_check(dl_all_gather(cand_v_, gath_v_, static_cast<size_t>(m) * kc, ncclFloat, comm, stream_), "allgather");
+    nccl_check(dl_all_gather(cand_i_, gath_i_, static_cast<size_t>(m) * kc, ncclInt32, comm, stream_), "allgather");
+    nccl_check(dl_group_end(), "group");
     launch_merge_cand(gath_v_, gath_i_, tp_size_, m, kk, kc, cand_v_, cand_i_, stream_);
   }
   // tables: reqs | outs | from | to | count | chain | alt | q_n | q_id | q_p | uniforms
@@ -754,6 +773,7 @@ void Model::accept(const mk_proposal* props, int np, mk_accept_result* res) {
   }
   uint8_t* db = acc_dev_.get<uint8_t>();
   cuda_check(cudaMemcpyAsync(db, hb, total, cudaMemcpyHostToDevice, stream_), "accept upload");
+  h2d_bytes_ += static_cast<int64_t>(total);
   auto* d_out = reinterpret_cast<AcceptOut*>(db + o_out);
   auto* d_from = reinterpret_cast<int32_t*>(db + o_from);
   auto* d_to = reinterpret_cast<int32_t*>(db + o_to);
@@ -768,6 +788,7 @@ void Model::accept(const mk_proposal* props, int np, mk_accept_result* res) {
   launch_move_kv(kc_ref, d_from, d_to, d_cnt, np, 32, stream_);
   auto* h_out = reinterpret_cast<AcceptOut*>(hb + o_out);
   cuda_check(cudaMemcpyAsync(h_out, d_out, np * sizeof(AcceptOut), cudaMemcpyDeviceToHost, stream_), "accept download");
+  d2h_bytes_ += static_cast<int64_t>(np * sizeof(AcceptOut));
   cuda_check(cudaStreamSynchronize(stream_), "accept");
   for (int i = 0; i < np; ++i) {
     const AcceptOut& o = h_out[i];

@@ -84,6 +84,12 @@ class Model {
   void set_profile(bool on) { profile_ = on; }
   const float* stage_ms() const { return stage_ms_; }
   int64_t last_launches() const { return last_launches_; }
+  // Host->device and device->host bytes copied since the previous call (then reset).
+  void io_bytes(int64_t* h2d, int64_t* d2h) {
+    *h2d = h2d_bytes_;
+    *d2h = d2h_bytes_;
+    h2d_bytes_ = d2h_bytes_ = 0;
+  }
 
  private:
   struct Layer {
@@ -161,10 +167,12 @@ class Model {
   std::map<std::tuple<int, int, int>, cudaGraphExec_t> graphs_;
   std::map<std::tuple<int, int, int>, int64_t> graph_nodes_;
   bool profile_ = false;
-  cudaEvent_t ev_[9] = {};
+  std::vector<cudaEvent_t> pev_;  // profile: one event per stage boundary of every layer
+  std::vector<int> pstage_;
+  size_t pk_ = 0;
   float stage_ms_[8] = {};
   int64_t last_launches_ = 0;
-  int cur_stage_ = 0;
+  int64_t h2d_bytes_ = 0, d2h_bytes_ = 0;  // host <-> device bytes since the last io_bytes() read
 };
 
 }  // namespace mkb

@@ -224,6 +224,7 @@ class Ref:
         L.ref_attend_gqa.argtypes = [_vp, ctypes.c_int, ctypes.c_int, _vp, _vp, ctypes.c_int64, ctypes.c_int64,
                                      ctypes.c_int, ctypes.c_float, _vp, _vp, ctypes.c_int]
         L.ref_silu_mul.argtypes = [ctypes.c_int64, _vp, _vp]
+        L.ref_uniforms.argtypes = [ctypes.c_uint64, ctypes.c_int, _vp]
         L.ref_sampler_new.argtypes = [ctypes.c_float, ctypes.c_float, ctypes.c_int, ctypes.c_float, ctypes.c_float,
                                       ctypes.c_float, ctypes.c_uint64]
         L.ref_sampler_new.restype = _vp
@@ -295,6 +296,11 @@ class Ref:
         out = np.zeros(G * D, dtype=np.float32)
         self.lib.ref_attend_gqa(q.ctypes.data, G, D, kb.ctypes.data, vb.ctypes.data, stride, D + 4, n, scale,
                                 out.ctypes.data, extra.ctypes.data if extra.size else None, int(extra.size))
+        return out
+
+    def uniforms(self, seed: int, n: int) -> np.ndarray:
+        out = np.zeros(n, dtype=np.float64)
+        self.lib.ref_uniforms(seed, n, out.ctypes.data)
         return out
 
     def sampler(self, temperature=0.8, top_p=0.95, top_k=40, min_p=0.05, seed=1) -> int:

@@ -16,6 +16,7 @@
 #include <cstdint>
 #include <cstring>
 #include <memory>
+#include <random>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -179,6 +180,13 @@ void ref_attend_gqa(const float* q, int G, int D, const int8_t* k, const int8_t*
 void ref_silu_mul(int64_t n, float* g, const float* u) { kern::silu_mul(n, g, u); }
 
 // ---- sampler.h ----
+
+// The uniform stream Sampler draws from (sampler.h:39, sampler.cpp:110 / 126): n values of
+// std::uniform_real_distribution<double>(0, 1) over std::mt19937_64(seed).
+void ref_uniforms(uint64_t seed, int n, double* out) {
+  std::mt19937_64 rng(seed);
+  for (int i = 0; i < n; ++i) out[i] = std::uniform_real_distribution<double>(0.0, 1.0)(rng);
+}
 
 void* ref_sampler_new(float temp, float top_p, int top_k, float min_p, float pres, float freq, uint64_t seed) {
   return new Sampler(params_of(temp, top_p, top_k, min_p, pres, freq, seed));

@@ -1,0 +1,156 @@
+"""Kernel-level parity of the sm_100a path (through the C ABI) against the oracle and malkin's golden outputs."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+TYPES = (8, 12, 14)
+
+
+def dev(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def test_quantize_q8_bit_exact(mk, golden, torch_cuda):
+    """BlockQ8 bit-identical to kern::quantize_row_q8 given the same floats (kernels_avx512.cpp:66-80)."""
+    torch = torch_cuda
+    x = golden["q8_x"]
+    xd = dev(torch, x)
+    out = torch.zeros(x.shape[0] * x.shape[1] // 32 * 40, dtype=torch.uint8, device="cuda")
+    mk.quantize_q8(xd.data_ptr(), x.shape[0], x.shape[1], out.data_ptr())
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy(), golden["q8_blocks"].reshape(-1))
+
+
+def test_quantize_i8_bit_exact(mk, golden, torch_cuda):
+    torch = torch_cuda
+    x = golden["i8_x"]
+    q = torch.zeros(x.shape, dtype=torch.int8, device="cuda")
+    d = torch.zeros(x.shape[0], dtype=torch.float32, device="cuda")
+    mk.quantize_i8(dev(torch, x).data_ptr(), x.shape[0], x.shape[1], q.data_ptr(), d.data_ptr())
+    torch.cuda.synchronize()
+    assert np.array_equal(q.cpu().numpy(), golden["i8_q"]) and np.array_equal(d.cpu().numpy(), golden["i8_d"])
+
+
+@pytest.mark.parametrize("t", TYPES)
+def test_block_dots_bit_exact(mk, oracle, golden, torch_cuda, t):
+    """Exact int8 block dot products (gemm_avx512.cpp:83-98, 130-141, 179-199): identical to the oracle's."""
+    torch = torch_cuda
+    w, x = golden[f"mm{t}_w"], golden[f"mm{t}_x"]
+    W = mk.Weight(t, w, 35, 512)
+    nblk = 512 // 32 * (2 if t == 14 else 1)
+    out = torch.zeros((35, x.shape[0], nblk), dtype=torch.int32, device="cuda")
+    W.block_dots(dev(torch, x).data_ptr(), x.shape[0], out.data_ptr())
+    assert np.array_equal(out.cpu().numpy(), oracle.block_dots(t, w, 35, 512, x))
+
+
+@pytest.mark.parametrize("t", TYPES)
+def test_matmul_bit_exact_split1(mk, golden, torch_cuda, t):
+    """split_k = 1 keeps malkin's block order per (row, token): y bit-identical to its compact panel kernels."""
+    torch = torch_cuda
+    w, x = golden[f"mm{t}_w"], golden[f"mm{t}_x"]
+    W = mk.Weight(t, w, 35, 512)
+    assert W.device_bytes == ((35 + 15) // 16) * 16 * mk.row_bytes(t, 512)
+    y = torch.full((x.shape[0], 35), np.nan, dtype=torch.float32, device="cuda")
+    W.matmul(dev(torch, x).data_ptr(), x.shape[0], y.data_ptr(), split_k=1)
+    assert np.array_equal(y.cpu().numpy(), golden[f"mm{t}_y"])
+
+
+@pytest.mark.parametrize("t", TYPES)
+def test_matmul_split_k(mk, golden, torch_cuda, t):
+    """Split-K reassociates the block sum: same values within float rounding."""
+    torch = torch_cuda
+    w, x = golden[f"mm{t}_w"], golden[f"mm{t}_x"]
+    W = mk.Weight(t, w, 35, 512)
+    ref = golden[f"mm{t}_y"]
+    for split in (2, 3, 0):
+        y = torch.zeros((x.shape[0], 35), dtype=torch.float32, device="cuda")
+        W.matmul(dev(torch, x).data_ptr(), x.shape[0], y.data_ptr(), split_k=split)
+        assert np.abs(y.cpu().numpy() - ref).max() <= 1e-5 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("t", TYPES)
+@pytest.mark.parametrize("n", [1, 7, 8, 136, 150, 300])
+def test_matmul_shapes_vs_oracle(mk, oracle, torch_cuda, t, n):
+    """Ragged rows (not a multiple of 16), token counts across the 8-token tiles and the 144-token passes."""
+    torch = torch_cuda
+    from make_golden import random_rows
+    rng = np.random.default_rng(n * 31 + t)
+    rows, cols = 53, 1024
+    w = random_rows(rng, t, rows, cols)
+    x = rng.uniform(-3, 3, (n, cols)).astype(np.float32)
+    W = mk.Weight(t, w, rows, cols)
+    y = torch.zeros((n, rows), dtype=torch.float32, device="cuda")
+    W.matmul(dev(torch, x).data_ptr(), n, y.data_ptr(), split_k=1)
+    assert np.array_equal(y.cpu().numpy(), oracle.matmul(t, w, rows, cols, x))
+
+
+def test_silu(mk, golden, torch_cuda):
+    torch = torch_cuda
+    g = dev(torch, golden["silu_g"])
+    mk.silu_mul(g.data_ptr(), dev(torch, golden["silu_u"]).data_ptr(), g.numel())
+    np.testing.assert_allclose(g.cpu().numpy(), golden["silu_y"], rtol=1e-6, atol=1e-7)
+
+
+def _attention(mk, torch, q, H, KV, D, k, v, ks, vs, kv_base, n_keys, anc):
+    """q [n, H*D]; k / v [KV, rows, D]; ks / vs [KV, rows]; anc: per token list of extra rows."""
+    n = q.shape[0]
+    off = np.zeros(n + 1, dtype=np.int32)
+    flat = []
+    for i, a in enumerate(anc):
+        flat += list(a)
+        off[i + 1] = len(flat)
+    out = torch.zeros((n, H * D), dtype=torch.float32, device="cuda")
+    tens = [dev(torch, a) for a in (q, k, v, ks, vs, np.asarray(kv_base, np.int32), np.asarray(n_keys, np.int32), off,
+                                    np.asarray(flat or [0], np.int32))]
+    mk.attention(tens[0].data_ptr(), n, H, KV, D, tens[1].data_ptr(), tens[2].data_ptr(), tens[3].data_ptr(),
+                 tens[4].data_ptr(), k.shape[1], tens[5].data_ptr(), tens[6].data_ptr(), tens[7].data_ptr(),
+                 tens[8].data_ptr(), out.data_ptr())
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+def test_attention_golden(mk, golden, torch_cuda):
+    """Tree-masked GQA vs malkin's attend_gqa (extra ancestor keys after the prefix)."""
+    torch = torch_cuda
+    for i in range(4):
+        G, D, n = map(int, golden[f"att{i}_shape"])
+        k, v = golden[f"att{i}_k"], golden[f"att{i}_v"]
+        out = _attention(mk, torch, golden[f"att{i}_q"].reshape(1, -1), G, 1, D, k[None], v[None],
+                         golden[f"att{i}_ks"][None], golden[f"att{i}_vs"][None], [0], [n], [golden[f"att{i}_extra"]])
+        np.testing.assert_allclose(out.reshape(-1), golden[f"att{i}_out"], rtol=2e-4, atol=2e-5)
+
+
+def test_attention_tree_batch_vs_oracle(mk, oracle, torch_cuda):
+    """Two sequences, a 9-node tree on one and a 5-token prompt chunk on the other, long prefix (several chunks)."""
+    torch = torch_cuda
+    rng = np.random.default_rng(5)
+    H, KV, D, n_ctx = 8, 2, 128, 700
+    G = H // KV
+    rows = 2 * n_ctx
+    k = rng.integers(-127, 128, (KV, rows, D)).astype(np.int8)
+    v = rng.integers(-127, 128, (KV, rows, D)).astype(np.int8)
+    ks = rng.uniform(0.005, 0.03, (KV, rows)).astype(np.float32)
+    vs = rng.uniform(0.005, 0.03, (KV, rows)).astype(np.float32)
+    P = 600
+    toks = []  # (kv_base, n_keys, anc)
+    toks.append((0, P + 1, []))
+    par = {0: []}
+    for i in range(4):
+        parent = 0 if i == 0 else 2 * i - 1
+        for j, row in ((2 * i + 1, P + 1 + 2 * i), (2 * i + 2, P + 2 + 2 * i)):
+            a = par[parent] + [row]
+            par[j] = a
+            toks.append((0, P + 1, a))
+    for p in range(300, 305):
+        toks.append((n_ctx, p + 1, []))
+    n = len(toks)
+    q = rng.uniform(-2, 2, (n, H * D)).astype(np.float32)
+    out = _attention(mk, torch, q, H, KV, D, k, v, ks, vs, [t[0] for t in toks], [t[1] for t in toks],
+                     [t[2] for t in toks])
+    scale = np.float32(1.0 / np.sqrt(D))
+    for t, (base, nk, anc) in enumerate(toks):
+        for g in range(KV):
+            want = oracle.attend(q[t, g * G * D:(g + 1) * G * D], G, D, k[g, base:], v[g, base:], ks[g, base:],
+                                 vs[g, base:], nk, anc, scale)
+            np.testing.assert_allclose(out[t, g * G * D:(g + 1) * G * D], want, rtol=3e-4, atol=3e-5)
