@@ -41,7 +41,10 @@ CONFIGS = {
                            type_default=Q6_K), requests=4, prompt=8192, kk=16),
     "32b": dict(model=dict(n_layer=64, n_embd=5120, n_ff=25600, n_head=64, n_head_kv=8, tied=False,
                            type_default=Q4_K), requests=32, prompt=8192, kk=8),
-    # small case for quick checks and profiling captures
+    # two layers of the 8B shapes (full vocabulary): the small case for ncu captures of the 8B kernels
+    "8b-l2": dict(model=dict(n_layer=2, n_embd=4096, n_ff=12288, n_head=32, n_head_kv=8, tied=False,
+                             type_default=Q8_0), requests=8, prompt=2048, kk=8),
+    # small case for quick checks
     "tiny": dict(model=dict(n_layer=4, n_embd=1024, n_ff=3072, n_head=16, n_head_kv=8, tied=False,
                             type_default=Q8_0), requests=2, prompt=256, kk=8),
 }

@@ -54,6 +54,9 @@ int guard(int io_code, F&& f) {
   } catch (const mkb::NcclError& e) {
     g_error = e.what();
     return MK_ERR_NCCL;
+  } catch (const mkb::TimeoutError& e) {
+    g_error = e.what();
+    return MK_ERR_TIMEOUT;
   } catch (const std::exception& e) {
     g_error = e.what();
     return io_code;
@@ -81,7 +84,7 @@ struct TmpAct {
   mkb::DevBuf buf;
   mkb::ActQ act;
   TmpAct(int n, int64_t K) {
-    const int nt8 = (n + 7) / 8, npad = nt8 * 8;
+    const int nt8 = mkb::act_tiles(n), npad = nt8 * 8;
     const int64_t blocks = K / 32;
     const size_t qx = static_cast<size_t>(blocks) * npad * 32, f = static_cast<size_t>(blocks) * npad * 4;
     buf = mkb::DevBuf(qx + 3 * f + 256);
@@ -279,12 +282,19 @@ int mk_matmul(const mk_weight* w, const float* dev_x, int n, float* dev_y, int s
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int split = split_k > 0 ? split_k : mkb::gemm_auto_split(w->w, n, sms);
-    if (split > 1)
-      mkb::cuda_check(cudaMemsetAsync(dev_y, 0, static_cast<size_t>(n) * w->w.rows * 4, s), "memset");
-    mkb::launch_gemm(w->w, t.act, n, dev_y, w->w.rows, split, split > 1, s);
+    const int split = mkb::gemm_slices(w->w, split_k > 0 ? split_k : mkb::gemm_split_for(w->w, sms));
+    const int64_t slice = static_cast<int64_t>(n) * w->w.rows;
+    mkb::DevBuf status(sizeof(int));
+    mkb::cuda_check(cudaMemsetAsync(status.get(), 0, sizeof(int), s), "memset");
+    mkb::DevBuf slices(split > 1 ? static_cast<size_t>(split) * slice * 4 : 0);
+    float* out = split > 1 ? slices.get<float>() : dev_y;
+    mkb::launch_gemm(w->w, t.act, n, out, w->w.rows, slice, split, status.get<int>(), s);
+    if (split > 1) mkb::launch_sum_slices(mkb::Slices{out, split, slice}, w->w.rows, n, static_cast<int>(w->w.rows), dev_y, s);
     mkb::cuda_check(cudaGetLastError(), "matmul");
+    int st = 0;
+    mkb::cuda_check(cudaMemcpyAsync(&st, status.get(), sizeof st, cudaMemcpyDeviceToHost, s), "status");
     mkb::cuda_check(cudaStreamSynchronize(s), "matmul");
+    if (st != 0) throw mkb::TimeoutError("matmul: device pipeline wait gave up");
   });
 }
 
@@ -328,11 +338,15 @@ int mk_attention(const float* dev_q, int n, int H, int KV, int D, const int8_t* 
     mkb::cuda_check(cudaMemcpy(kvb.data(), dev_kv_base, n * 4, cudaMemcpyDeviceToHost), "attention");
     mkb::cuda_check(cudaMemcpy(nk.data(), dev_n_keys, n * 4, cudaMemcpyDeviceToHost), "attention");
     const int G = H / KV, rows = std::max(1, mkb::attn_qmax() / G);
-    std::vector<int32_t> sgf, tsg(n);
+    std::vector<int32_t> sgf, tsg(n), sgm;
     int maxk = 1;
     for (int t = 0; t < n; ++t) {
-      if (t == 0 || kvb[t] != kvb[t - 1] || t - sgf.back() >= rows) sgf.push_back(t);
+      if (t == 0 || kvb[t] != kvb[t - 1] || t - sgf.back() >= rows) {
+        sgf.push_back(t);
+        sgm.push_back(0);
+      }
       tsg[t] = static_cast<int32_t>(sgf.size()) - 1;
+      sgm.back() = std::max(sgm.back(), nk[t]);
       maxk = std::max(maxk, nk[t]);
     }
     const int n_sg = static_cast<int>(sgf.size());
@@ -342,13 +356,17 @@ int mk_attention(const float* dev_q, int n, int H, int KV, int D, const int8_t* 
     p.n_sg = n_sg;
     p.chunk = 256;
     p.n_chunks = (maxk + p.chunk - 1) / p.chunk;
-    mkb::DevBuf tabs((sgf.size() + tsg.size()) * 4);
+    mkb::DevBuf tabs((sgf.size() + tsg.size() + sgm.size()) * 4);
     mkb::cuda_check(cudaMemcpy(tabs.get(), sgf.data(), sgf.size() * 4, cudaMemcpyHostToDevice), "attention");
     mkb::cuda_check(cudaMemcpy(tabs.get<int32_t>() + sgf.size(), tsg.data(), tsg.size() * 4, cudaMemcpyHostToDevice),
+                    "attention");
+    mkb::cuda_check(cudaMemcpy(tabs.get<int32_t>() + sgf.size() + tsg.size(), sgm.data(), sgm.size() * 4,
+                               cudaMemcpyHostToDevice),
                     "attention");
     mkb::DevBuf part(mkb::attn_part_floats(n_sg, p.n_chunks, KV, D) * 4);
     p.sg_first = tabs.get<int32_t>();
     p.tok_sg = tabs.get<int32_t>() + sgf.size();
+    p.sg_maxk = tabs.get<int32_t>() + sgf.size() + tsg.size();
     p.kv_base = dev_kv_base;
     p.n_keys = dev_n_keys;
     p.anc_off = dev_anc_off;

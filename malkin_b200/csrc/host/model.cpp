@@ -274,9 +274,14 @@ void Model::load(const std::string& path) {
     const LayerPlan& P = lp[static_cast<size_t>(i)];
     Layer& L = layers_[static_cast<size_t>(i)];
     fuse(P.qkv, P.nqkv, L.qkv, L.qkv_col, L.n_qkv);
+    for (int j = 0; j < L.n_qkv; ++j) L.qkv_split[j] = gemm_split_for(L.qkv[j], num_sms_);
+    if (L.n_qkv == 3) L.qkv_split[1] = L.qkv_split[0];  // q and k columns are summed with one slice count
     L.wo = dev(P.wo);
+    L.wo_split = gemm_split_for(L.wo, num_sms_);
     fuse(P.gu, P.ngu, L.gu, L.gu_col, L.n_gu);
+    for (int j = 0; j < L.n_gu; ++j) L.gu_split[j] = gemm_split_for(L.gu[j], num_sms_);
     L.down = dev(P.down);
+    L.down_split = gemm_split_for(L.down, num_sms_);
     L.attn_norm = put_norm(P.an, E);
     L.ffn_norm = put_norm(P.fn, E);
     L.q_norm = put_norm(P.qn, D);
@@ -331,25 +336,36 @@ void Model::alloc_kv(int n_ctx, int n_seq, int max_batch) {
     rope_ = DevBuf(tab.size() * 4);
     cuda_check(cudaMemcpy(rope_.get(), tab.data(), tab.size() * 4, cudaMemcpyHostToDevice), "rope table");
   }
-  const int NB = static_cast<int>(align_up(static_cast<size_t>(max_batch), 8));
+  const int NT8 = act_tiles(max_batch);
+  const int NB = NT8 * 8;  // token rows of the activation buffers (whole GEMM passes)
   const int64_t HD = static_cast<int64_t>(Hl_) * D;
   const int64_t kmax = std::max<int64_t>({E, HD, Fl_});
   const int64_t blocks = kmax / 32;
+  int s_qkv = 1, s_gu = 1, s_part = 1;
+  for (const Layer& L : layers_) {
+    for (int j = 0; j < L.n_qkv; ++j) s_qkv = std::max(s_qkv, L.qkv_split[j]);
+    for (int j = 0; j < L.n_gu; ++j) s_gu = std::max(s_gu, L.gu_split[j]);
+    s_part = std::max({s_part, L.wo_split, L.down_split});
+  }
+  qkv_slice_ = static_cast<int64_t>(NB) * qkv_ld_;
+  gu_slice_ = static_cast<int64_t>(NB) * 2 * Fl_;
+  part_slice_ = static_cast<int64_t>(NB) * E;
   size_t off = 0;
   auto take = [&](size_t bytes) {
     const size_t o = off;
     off = align_up(off + bytes, 256);
     return o;
   };
-  const size_t o_x = take(static_cast<size_t>(NB) * E * 4), o_y = take(static_cast<size_t>(NB) * qkv_ld_ * 4),
+  const size_t o_x = take(static_cast<size_t>(NB) * E * 4), o_y = take(static_cast<size_t>(s_qkv) * qkv_slice_ * 4),
                o_q = take(static_cast<size_t>(NB) * HD * 4), o_att = take(static_cast<size_t>(NB) * HD * 4),
-               o_gu = take(static_cast<size_t>(NB) * 2 * Fl_ * 4), o_p = take(static_cast<size_t>(NB) * E * 4),
+               o_gu = take(static_cast<size_t>(s_gu) * gu_slice_ * 4), o_p = take(static_cast<size_t>(NB) * E * 4),
+               o_part = take(static_cast<size_t>(s_part) * part_slice_ * 4),
                o_lg = take(static_cast<size_t>(NB) * Vl_ * 4), o_qx = take(static_cast<size_t>(blocks) * NB * 32),
                o_dx = take(static_cast<size_t>(blocks) * NB * 4), o_dsx = take(static_cast<size_t>(blocks) * NB * 4),
                o_sh = take(static_cast<size_t>(blocks) * NB * 4),
                o_cv = take(static_cast<size_t>(NB) * MK_TOPK_CAP * 4), o_ci = take(static_cast<size_t>(NB) * MK_TOPK_CAP * 4),
                o_gv = take(static_cast<size_t>(tp_size_) * NB * MK_TOPK_CAP * 4),
-               o_gi = take(static_cast<size_t>(tp_size_) * NB * MK_TOPK_CAP * 4);
+               o_gi = take(static_cast<size_t>(tp_size_) * NB * MK_TOPK_CAP * 4), o_st = take(256);
   scratch_ = DevBuf(off);
   cuda_check(cudaMemset(scratch_.get(), 0, off), "scratch memset");
   uint8_t* sb = scratch_.get<uint8_t>();
@@ -359,6 +375,7 @@ void Model::alloc_kv(int n_ctx, int n_seq, int max_batch) {
   att_ = reinterpret_cast<float*>(sb + o_att);
   ygu_ = reinterpret_cast<float*>(sb + o_gu);
   p_ = reinterpret_cast<float*>(sb + o_p);
+  part_ = reinterpret_cast<float*>(sb + o_part);
   logits_ = reinterpret_cast<float*>(sb + o_lg);
   act_.qx = sb + o_qx;
   act_.dx = reinterpret_cast<float*>(sb + o_dx);
@@ -368,6 +385,7 @@ void Model::alloc_kv(int n_ctx, int n_seq, int max_batch) {
   cand_i_ = reinterpret_cast<int32_t*>(sb + o_ci);
   gath_v_ = reinterpret_cast<float*>(sb + o_gv);
   gath_i_ = reinterpret_cast<int32_t*>(sb + o_gi);
+  status_ = reinterpret_cast<int*>(sb + o_st);
   // attention plan geometry
   const int G = c.n_head / c.n_head_kv;
   sg_rows_ = std::max(1, attn_qmax() / G);
@@ -381,7 +399,7 @@ void Model::alloc_kv(int n_ctx, int n_seq, int max_batch) {
 
 void Model::ensure_meta(size_t anc_cap) {
   const size_t MB = static_cast<size_t>(max_batch_);
-  const size_t need = 9 * MB + 2 + anc_cap;
+  const size_t need = 10 * MB + 2 + anc_cap;
   if (need <= meta_cap_) return;
   for (auto& [k, g] : graphs_) cudaGraphExecDestroy(g);
   graphs_.clear();
@@ -401,7 +419,8 @@ void Model::ensure_meta(size_t anc_cap) {
   d_sgfirst_ = m + 6 * MB + 1;
   d_toksg_ = m + 7 * MB + 2;
   d_outrows_ = m + 8 * MB + 2;
-  d_anc_ = m + 9 * MB + 2;
+  d_sgmaxk_ = m + 9 * MB + 2;
+  d_anc_ = m + 10 * MB + 2;
 }
 
 void Model::stage(int i) {
@@ -421,13 +440,8 @@ void Model::allreduce(float* buf, size_t count) {
              "allreduce");
 }
 
-// y (+)= W x. accumulate: y holds the addend (red.add); else y is overwritten (zeroed first when split).
-void Model::gemm(const DevWeight& w, int n, float* y, int64_t ldy, bool accumulate) {
-  const int split = gemm_auto_split(w, n, num_sms_);
-  if (!accumulate && split > 1)
-    cuda_check(cudaMemset2DAsync(y, static_cast<size_t>(ldy) * 4, 0, static_cast<size_t>(w.rows) * 4, n, stream_),
-               "memset");
-  launch_gemm(w, act_, n, y, ldy, split, accumulate || split > 1, stream_);
+void Model::gemm(const DevWeight& w, int split, int n, float* y, int64_t ldy, int64_t slice) {
+  launch_gemm(w, act_, n, y, ldy, slice, split, status_, stream_);
 }
 
 void Model::run_forward(int n, int m) {
@@ -435,49 +449,56 @@ void Model::run_forward(int n, int m) {
   const int D = c.head_dim, E = c.n_embd;
   const int64_t HD = static_cast<int64_t>(Hl_) * D;
   const float scale = 1.0f / std::sqrt(static_cast<float>(D));
-  const int nt8 = (n + 7) / 8;
+  const int nt8 = act_tiles(n);
   if (profile_) {
     pk_ = 0;
     stage(-1);
   }
   launch_embed(embd_, embd_type_, embd_row_bytes_, E, d_ids_, n, x_, stream_);
   const bool tp = tp_size_ > 1;
+  Slices pending;  // residual contributions not yet added into x (the previous down projection)
   for (int il = 0; il < c.n_layer; ++il) {
     const Layer& L = layers_[static_cast<size_t>(il)];
     act_.nt8 = nt8;
-    launch_rmsnorm_quant(x_, E, tp && il > 0 ? p_ : nullptr, nullptr, L.attn_norm, c.rms_eps, n, E, act_, stream_);
-    for (int i = 0; i < L.n_qkv; ++i) gemm(L.qkv[i], n, yqkv_ + L.qkv_col[i], qkv_ld_, false);
+    launch_rmsnorm_quant(x_, E, pending, nullptr, L.attn_norm, c.rms_eps, n, E, act_, stream_);
+    for (int i = 0; i < L.n_qkv; ++i) gemm(L.qkv[i], L.qkv_split[i], n, yqkv_ + L.qkv_col[i], qkv_ld_, qkv_slice_);
     stage(0);
-    launch_qkv_post(yqkv_, qkv_ld_, n, Hl_, KVl_, D, L.q_norm, L.k_norm, c.rms_eps, rope_.get<float>(), d_rpos_, d_kvat_,
-                    q_, kv_layers_[static_cast<size_t>(il)], stream_);
+    // q / k columns come from the first weight (fused q|k|v, or q then k), v from the last
+    const int64_t v_col0 = L.n_qkv == 3 ? L.qkv_col[2] : (L.n_qkv == 2 ? L.qkv_col[1] : qkv_ld_);
+    const int v_n = L.n_qkv >= 2 ? L.qkv_split[L.n_qkv - 1] : L.qkv_split[0];
+    launch_qkv_post(Slices{yqkv_, L.qkv_split[0], qkv_slice_}, v_n, v_col0, qkv_ld_, n, Hl_, KVl_, D, L.q_norm,
+                    L.k_norm, c.rms_eps, rope_.get<float>(), d_rpos_, d_kvat_, q_, kv_layers_[static_cast<size_t>(il)],
+                    stream_);
     stage(1);
     launch_attention(q_, Hl_, KVl_, D, scale, kv_layers_[static_cast<size_t>(il)], plan_, att_, stream_);
     stage(2);
     launch_quant_rows(att_, HD, n, static_cast<int>(HD), act_, stream_);
+    gemm(L.wo, L.wo_split, n, part_, E, part_slice_);
+    Slices wo_add{part_, L.wo_split, part_slice_};
     if (tp) {
-      gemm(L.wo, n, p_, E, false);
+      launch_sum_slices(wo_add, E, n, E, p_, stream_);
       allreduce(p_, static_cast<size_t>(n) * E);
-    } else {
-      gemm(L.wo, n, x_, E, true);
+      wo_add = Slices{p_, 1, 0};
     }
-    launch_rmsnorm_quant(x_, E, tp ? p_ : nullptr, nullptr, L.ffn_norm, c.rms_eps, n, E, act_, stream_);
+    launch_rmsnorm_quant(x_, E, wo_add, nullptr, L.ffn_norm, c.rms_eps, n, E, act_, stream_);
     stage(3);
-    for (int i = 0; i < L.n_gu; ++i) gemm(L.gu[i], n, ygu_ + L.gu_col[i], 2 * static_cast<int64_t>(Fl_), false);
+    for (int i = 0; i < L.n_gu; ++i) gemm(L.gu[i], L.gu_split[i], n, ygu_ + L.gu_col[i], 2 * static_cast<int64_t>(Fl_), gu_slice_);
     stage(4);
-    launch_silu_quant(ygu_, 2 * static_cast<int64_t>(Fl_), Fl_, n, act_, stream_);
+    launch_silu_quant(Slices{ygu_, L.gu_split[0], gu_slice_}, 2 * static_cast<int64_t>(Fl_), Fl_, n, act_, stream_);
     stage(5);
+    gemm(L.down, L.down_split, n, part_, E, part_slice_);
+    pending = Slices{part_, L.down_split, part_slice_};
     if (tp) {
-      gemm(L.down, n, p_, E, false);
+      launch_sum_slices(pending, E, n, E, p_, stream_);
       allreduce(p_, static_cast<size_t>(n) * E);
-    } else {
-      gemm(L.down, n, x_, E, true);
+      pending = Slices{p_, 1, 0};
     }
     stage(6);
   }
   if (m > 0) {
-    act_.nt8 = (m + 7) / 8;
-    launch_rmsnorm_quant(x_, E, tp ? p_ : nullptr, d_outrows_, out_norm_, c.rms_eps, m, E, act_, stream_);
-    gemm(lm_head_, m, logits_, Vl_, false);
+    act_.nt8 = act_tiles(m);
+    launch_rmsnorm_quant(x_, E, pending, d_outrows_, out_norm_, c.rms_eps, m, E, act_, stream_);
+    gemm(lm_head_, 1, m, logits_, Vl_, 0);
   }
   stage(7);
 }
@@ -522,9 +543,14 @@ void Model::forward(const mk_batch_token* batch, int n, float* host_logits) {
     ancoff[t + 1] = static_cast<int32_t>(anc.size());
   }
   // attention sub-groups: runs of one sequence, at most sg_rows_ rows
+  std::vector<int32_t> sgmaxk;
   for (int t = 0; t < n; ++t) {
-    if (t == 0 || kvbase[t] != kvbase[t - 1] || t - sgfirst.back() >= sg_rows_) sgfirst.push_back(t);
+    if (t == 0 || kvbase[t] != kvbase[t - 1] || t - sgfirst.back() >= sg_rows_) {
+      sgfirst.push_back(t);
+      sgmaxk.push_back(0);
+    }
     toksg[t] = static_cast<int32_t>(sgfirst.size()) - 1;
+    sgmaxk.back() = std::max(sgmaxk.back(), nkeys[t]);
   }
   const int n_sg = static_cast<int>(sgfirst.size());
   sgfirst.push_back(n);
@@ -550,10 +576,11 @@ void Model::forward(const mk_batch_token* batch, int n, float* host_logits) {
   std::copy(sgfirst.begin(), sgfirst.end(), h + 6 * MB + 1);
   std::copy(toksg.begin(), toksg.end(), h + 7 * MB + 2);
   std::copy(outrows.begin(), outrows.end(), h + 8 * MB + 2);
-  std::copy(anc.begin(), anc.end(), h + 9 * MB + 2);
-  cuda_check(cudaMemcpyAsync(meta_.get(), h, (9 * MB + 2 + anc.size()) * 4, cudaMemcpyHostToDevice, stream_),
+  std::copy(sgmaxk.begin(), sgmaxk.end(), h + 9 * MB + 2);
+  std::copy(anc.begin(), anc.end(), h + 10 * MB + 2);
+  cuda_check(cudaMemcpyAsync(meta_.get(), h, (10 * MB + 2 + anc.size()) * 4, cudaMemcpyHostToDevice, stream_),
              "meta upload");
-  h2d_bytes_ += static_cast<int64_t>((9 * MB + 2 + anc.size()) * 4);
+  h2d_bytes_ += static_cast<int64_t>((10 * MB + 2 + anc.size()) * 4);
   plan_.n = n;
   plan_.n_sg = n_sg;
   plan_.chunk = chunk_;
@@ -564,6 +591,7 @@ void Model::forward(const mk_batch_token* batch, int n, float* host_logits) {
   plan_.anc_off = d_ancoff_;
   plan_.anc = d_anc_;
   plan_.tok_sg = d_toksg_;
+  plan_.sg_maxk = d_sgmaxk_;
   plan_.part = attn_part_.get<float>();
 
   if (profile_) {
@@ -622,6 +650,7 @@ void Model::forward(const mk_batch_token* batch, int n, float* host_logits) {
                  "logits download");
       d2h_bytes_ += static_cast<int64_t>(m) * c.n_vocab * 4;
       cuda_check(cudaStreamSynchronize(stream_), "forward");
+      check_status();
     } else {
       // gather every rank's vocab shard: [rank][m][Vl_r] -> host rows of n_vocab
       cuda_check(cudaStreamSynchronize(stream_), "forward");
@@ -643,6 +672,15 @@ void Model::forward(const mk_batch_token* batch, int n, float* host_logits) {
                       all.data() + (static_cast<size_t>(rk) * m + row) * vmax, static_cast<size_t>(vl) * 4);
       }
     }
+  }
+}
+
+void Model::check_status() {
+  int st = 0;
+  cuda_check(cudaMemcpy(&st, status_, sizeof st, cudaMemcpyDeviceToHost), "status");
+  if (st != 0) {
+    cuda_check(cudaMemset(status_, 0, sizeof st), "status reset");
+    throw TimeoutError("device pipeline wait gave up (code " + std::to_string(st) + "): results of this step are invalid");
   }
 }
 
@@ -788,8 +826,15 @@ void Model::accept(const mk_proposal* props, int np, mk_accept_result* res) {
   launch_move_kv(kc_ref, d_from, d_to, d_cnt, np, 32, stream_);
   auto* h_out = reinterpret_cast<AcceptOut*>(hb + o_out);
   cuda_check(cudaMemcpyAsync(h_out, d_out, np * sizeof(AcceptOut), cudaMemcpyDeviceToHost, stream_), "accept download");
+  auto* h_status = reinterpret_cast<int*>(hb + o_cnt);  // the count region is free on the host side
+  cuda_check(cudaMemcpyAsync(h_status, status_, sizeof(int), cudaMemcpyDeviceToHost, stream_), "status download");
   d2h_bytes_ += static_cast<int64_t>(np * sizeof(AcceptOut));
   cuda_check(cudaStreamSynchronize(stream_), "accept");
+  if (*h_status != 0) {
+    const int code = *h_status;
+    cuda_check(cudaMemset(status_, 0, sizeof(int)), "status reset");
+    throw TimeoutError("device pipeline wait gave up (code " + std::to_string(code) + "): results of this step are invalid");
+  }
   for (int i = 0; i < np; ++i) {
     const AcceptOut& o = h_out[i];
     if (o.status != 0) throw ArgError("accept: uniform stream too short for request " + std::to_string(i));

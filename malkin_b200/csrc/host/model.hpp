@@ -59,6 +59,9 @@ struct CudaError : std::runtime_error {         // MK_ERR_CUDA
 struct NcclError : std::runtime_error {         // MK_ERR_NCCL
   using std::runtime_error::runtime_error;
 };
+struct TimeoutError : std::runtime_error {      // MK_ERR_TIMEOUT: a device-side bounded wait gave up
+  using std::runtime_error::runtime_error;
+};
 
 // Throws CudaError with the CUDA error string.
 void cuda_check(cudaError_t e, const char* what);
@@ -95,20 +98,26 @@ class Model {
   struct Layer {
     DevWeight qkv[3];
     int64_t qkv_col[3] = {0, 0, 0};
+    int qkv_split[3] = {1, 1, 1};  // split-K slices of each GEMM (fixed per weight)
     int n_qkv = 0;
     DevWeight wo;
+    int wo_split = 1;
     DevWeight gu[2];
     int64_t gu_col[2] = {0, 0};
+    int gu_split[2] = {1, 1};
     int n_gu = 0;
     DevWeight down;
+    int down_split = 1;
     const float *attn_norm = nullptr, *ffn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
   };
 
   void run_forward(int n, int m);               // kernel sequence (captured or direct)
-  void gemm(const DevWeight& w, int n, float* y, int64_t ldy, bool accumulate);
+  // y slices = W x: slice s at y + s * slice (split-K partial sums, summed in order by the consumer)
+  void gemm(const DevWeight& w, int split, int n, float* y, int64_t ldy, int64_t slice);
   void allreduce(float* buf, size_t count);
   void stage(int i);                             // profile lap
   void ensure_meta(size_t anc_cap);
+  void check_status();  // throws TimeoutError if a kernel recorded a failed bounded wait
 
   ModelCfg cfg_;
   int device_ = 0, tp_rank_ = 0, tp_size_ = 1, num_sms_ = 148;
@@ -137,7 +146,9 @@ class Model {
   DevBuf kv_, rope_, scratch_;
   std::vector<AttnLayer> kv_layers_;
   float *x_ = nullptr, *yqkv_ = nullptr, *q_ = nullptr, *att_ = nullptr, *ygu_ = nullptr, *p_ = nullptr,
-        *logits_ = nullptr;
+        *part_ = nullptr, *logits_ = nullptr;
+  int64_t qkv_slice_ = 0, gu_slice_ = 0, part_slice_ = 0;  // floats between split-K slices
+  int* status_ = nullptr;                                  // device word: bounded-wait failures
   ActQ act_;
   float* cand_v_ = nullptr;
   int32_t* cand_i_ = nullptr;
@@ -149,7 +160,7 @@ class Model {
   int32_t* meta_host_ = nullptr;
   size_t meta_cap_ = 0;  // int32 entries
   int32_t *d_ids_ = nullptr, *d_rpos_ = nullptr, *d_kvat_ = nullptr, *d_kvbase_ = nullptr, *d_nkeys_ = nullptr,
-          *d_ancoff_ = nullptr, *d_sgfirst_ = nullptr, *d_toksg_ = nullptr, *d_outrows_ = nullptr, *d_anc_ = nullptr;
+          *d_ancoff_ = nullptr, *d_sgfirst_ = nullptr, *d_toksg_ = nullptr, *d_outrows_ = nullptr, *d_sgmaxk_ = nullptr, *d_anc_ = nullptr;
   DevBuf attn_part_;
   AttnPlan plan_;
   int n_chunks_ = 0, chunk_ = 256, sg_rows_ = 0, max_sg_ = 0;

@@ -9,12 +9,14 @@
 // Per chunk it keeps an online softmax (running max m, sum l, weighted values o); the combine kernel merges the
 // chunks and the extra rows. Arithmetic: score = (q . k_int8) * (k_scale * 1/sqrt(D)); p = exp(score - max)
 // with malkin's exp; out = (sum p * v_scale * v_int8) / sum p.
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cfloat>
 
 #include "common.cuh"
 #include "kernels.hpp"
+#include "pipeline.cuh"
 
 namespace mkb {
 
@@ -23,7 +25,7 @@ namespace {
 // ---------------- q/k norm + RoPE + KV write ----------------
 // grid (n, ceil((H + 2 KV) / 4)), block 128: one warp per head. D % 64 == 0, D <= 256.
 template <int D>
-__global__ void k_qkv_post(const float* __restrict__ y, int64_t ldy, int n, int H, int KV,
+__global__ void k_qkv_post(Slices qk, int v_n, int64_t v_col0, int64_t ldy, int n, int H, int KV,
                            const float* __restrict__ q_norm, const float* __restrict__ k_norm, float eps,
                            const float* __restrict__ rope_cs, const int32_t* __restrict__ rpos,
                            const int32_t* __restrict__ kv_at, float* __restrict__ q_out, AttnLayer L) {
@@ -31,10 +33,12 @@ __global__ void k_qkv_post(const float* __restrict__ y, int64_t ldy, int n, int 
   const int t = blockIdx.x, lane = threadIdx.x & 31;
   const int head = blockIdx.y * 4 + (threadIdx.x >> 5);
   if (head >= H + 2 * KV) return;
-  const float* src = y + static_cast<size_t>(t) * ldy + static_cast<size_t>(head) * D;
+  const int64_t col = static_cast<int64_t>(head) * D;
+  const int ns = col >= v_col0 ? v_n : qk.n;  // GEMM slices of this head's columns, summed in slice order
+  const float* src = qk.p + static_cast<size_t>(t) * ldy + col;
   float v[PER];
 #pragma unroll
-  for (int m = 0; m < PER; ++m) v[m] = src[lane + 32 * m];
+  for (int m = 0; m < PER; ++m) v[m] = sum_strided16(src + lane + 32 * m, ns, qk.stride);
   const bool is_q = head < H, is_k = !is_q && head < H + KV;
   if (is_q || is_k) {
     const float* w = is_q ? q_norm : k_norm;
@@ -76,10 +80,18 @@ __global__ void k_qkv_post(const float* __restrict__ y, int64_t ldy, int n, int 
   if (lane == 0) (is_k ? L.ks : L.vs)[row] = d;
 }
 
-// ---------------- partial attention over a key chunk ----------------
-constexpr int kQMax = 72;   // query vectors per sub-group
-constexpr int kKT = 32;     // keys per tile
-constexpr int kThreads = 256;
+// ---------------- partial attention over a key chunk (tensor cores) ----------------
+// One CTA = (sub-group, KV head, key chunk). Query vectors (sub-group rows x G heads, at most kQMax) are split into
+// m16 tiles, one per warp. Per tile of 64 keys: S = Q K^T with mma.sync m16n8k16 (fp16 in, fp32 accumulate) where Q
+// is split into fp16 hi + lo parts (q = hi + lo to ~22 bits) and int8 K converts to fp16 exactly; then the online
+// softmax in registers (a row lives in one quad of lanes); then O += P V with P' = p * v_scale * 2^12 split into fp16
+// hi + lo (the power-of-two scale keeps P' in fp16's normal range; it is divided out exactly at the end) and int8 V
+// in fp16. K / V int8 tiles for the next 64 keys are prefetched into registers while the current tile computes.
+constexpr int kQMax = 96;   // query vectors per sub-group (6 warps x 16)
+constexpr int kKT = 64;     // keys per tile
+constexpr int kAttWarps = kQMax / 16;
+constexpr int kThreads = kAttWarps * 32;
+constexpr float kPScale = 4096.0f;
 
 struct PartArgs {
   const float* q;  // [n][H][D]
@@ -89,168 +101,279 @@ struct PartArgs {
   AttnPlan p;
 };
 
+__device__ __forceinline__ uint32_t pack_h2(__half a, __half b) {
+  return static_cast<uint32_t>(__half_as_ushort(a)) | (static_cast<uint32_t>(__half_as_ushort(b)) << 16);
+}
+
+// x = hi + lo in fp16 (both round to nearest).
+__device__ __forceinline__ void split_h(float x, __half& hi, __half& lo) {
+  hi = __float2half_rn(x);
+  lo = __float2half_rn(__fsub_rn(x, __half2float(hi)));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_addr(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_addr(p)));
+}
+
+__device__ __forceinline__ void mma_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <int D>
+struct AttSmem {
+  static constexpr int DP = D + 8;  // padded fp16 row (conflict-free ldmatrix)
+  static constexpr size_t QH = 0, QL = QH + sizeof(__half) * kQMax * DP, K = QL + sizeof(__half) * kQMax * DP,
+                          V = K + sizeof(__half) * kKT * DP, KS = V + sizeof(__half) * kKT * DP, VS = KS + 4 * kKT,
+                          NK = VS + 4 * kKT, BYTES = NK + 4 * kQMax;
+};
+
 template <int D>
 __global__ void __launch_bounds__(kThreads) k_attn_part(PartArgs a) {
-  constexpr int DP = D + 4;            // padded smem row (floats)
-  constexpr int DV = D / 4;            // threads per query for the PV product (4 dims each)
-  constexpr int QG = kThreads / DV;    // query groups in PV
-  constexpr int QI = (kQMax + QG - 1) / QG;
-  constexpr int SI = kQMax / 8;        // queries per thread in the score product (8 warps)
-  extern __shared__ float smem[];
-  float* Qs = smem;                      // [kQMax][DP]
-  float* Kf = Qs + kQMax * DP;           // [kKT][DP]
-  float* Vf = Kf + kKT * DP;             // [kKT][DP]
-  float* Ps = Vf + kKT * DP;             // [kQMax][kKT + 4]   p * v_scale
-  float* Ms = Ps + kQMax * (kKT + 4);    // [kQMax] running max
-  float* Ls = Ms + kQMax;                // [kQMax] running sum
-  float* Al = Ls + kQMax;                // [kQMax] rescale of this tile
-  int* Nk = reinterpret_cast<int*>(Al + kQMax);  // [kQMax] keys of the query's token
+  using SM = AttSmem<D>;
+  constexpr int DP = SM::DP;
+  constexpr int NDT = D / 8;          // d tiles (n8) of O
+  constexpr int CH = D / 16;          // 16-byte int8 chunks per key row
+  constexpr int PF = (2 * kKT * CH + kThreads - 1) / kThreads;  // prefetch chunks per thread (K and V)
+  extern __shared__ __align__(128) uint8_t sm[];
+  __half* Qh = reinterpret_cast<__half*>(sm + SM::QH);
+  __half* Ql = reinterpret_cast<__half*>(sm + SM::QL);
+  __half* Kh = reinterpret_cast<__half*>(sm + SM::K);
+  __half* Vh = reinterpret_cast<__half*>(sm + SM::V);
+  float* ksc = reinterpret_cast<float*>(sm + SM::KS);
+  float* vsc = reinterpret_cast<float*>(sm + SM::VS);
+  int* Nk = reinterpret_cast<int*>(sm + SM::NK);
 
   const int chunk = blockIdx.x, sg = blockIdx.y, kvh = blockIdx.z;
   const int t0 = a.p.sg_first[sg], t1 = a.p.sg_first[sg + 1];
   const int nq = (t1 - t0) * a.G;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  // Keys of this sub-group: the longest prefix among its rows.
-  int maxk = 0;
-  for (int t = t0; t < t1; ++t) maxk = max(maxk, a.p.n_keys[t]);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, c = lane & 3;
+  const int maxk = a.p.sg_maxk[sg];
   const int k0 = chunk * a.p.chunk;
   if (k0 >= maxk) return;
   const int k1 = min(maxk, k0 + a.p.chunk);
   const int base = a.p.kv_base[t0];
 
-  for (int i = tid; i < nq * D; i += kThreads) {
-    const int qi = i / D, d = i % D;
-    const int t = t0 + qi / a.G, h = kvh * a.G + qi % a.G;
-    Qs[qi * DP + d] = a.q[(static_cast<size_t>(t) * a.H + h) * D + d];
-  }
-  for (int qi = tid; qi < kQMax; qi += kThreads) {
-    Ms[qi] = -INFINITY;
-    Ls[qi] = 0.0f;
-    Nk[qi] = qi < nq ? a.p.n_keys[t0 + qi / a.G] : 0;
-  }
-  float o[QI][4];
+  // Q (hi / lo fp16), zero rows past nq: warp w loads its 16 query vectors, lanes over d (independent loads first)
+  {
+    constexpr int PL = D / 32;  // values per lane
+    float qv[16][PL];
 #pragma unroll
-  for (int i = 0; i < QI; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
+    for (int i = 0; i < 16; ++i) {
+      const int qi = warp * 16 + i;
+      const int t = t0 + qi / a.G, h = kvh * a.G + qi % a.G;
+      const float* src = a.q + (static_cast<size_t>(t) * a.H + h) * D;
+#pragma unroll
+      for (int m = 0; m < PL; ++m) qv[i][m] = qi < nq ? src[lane + 32 * m] : 0.0f;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int qi = warp * 16 + i;
+#pragma unroll
+      for (int m = 0; m < PL; ++m) {
+        __half hi, lo;
+        split_h(qv[i][m], hi, lo);
+        Qh[qi * DP + lane + 32 * m] = hi;
+        Ql[qi * DP + lane + 32 * m] = lo;
+      }
+    }
+  }
+  for (int qi = tid; qi < kQMax; qi += kThreads) Nk[qi] = qi < nq ? a.p.n_keys[t0 + qi / a.G] : 0;
+
   const int8_t* kh = a.L.k + (static_cast<size_t>(kvh) * a.L.n_rows + base) * D;
   const int8_t* vh = a.L.v + (static_cast<size_t>(kvh) * a.L.n_rows + base) * D;
   const float* ksh = a.L.ks + static_cast<size_t>(kvh) * a.L.n_rows + base;
   const float* vsh = a.L.vs + static_cast<size_t>(kvh) * a.L.n_rows + base;
+
+  // register prefetch of one 64-key tile: chunk i < kKT*CH is K, else V
+  int4 pre[PF];
+  float pks = 0.0f, pvs = 0.0f;
+  auto fetch = [&](int kt) {
+    const int nk = min(kKT, k1 - kt);
+#pragma unroll
+    for (int u = 0; u < PF; ++u) {
+      const int i = tid + u * kThreads;
+      int4 v = make_int4(0, 0, 0, 0);
+      if (i < 2 * kKT * CH) {
+        const bool isv = i >= kKT * CH;
+        const int ii = isv ? i - kKT * CH : i;
+        const int j = ii / CH, ch = ii % CH;
+        if (j < nk) v = *reinterpret_cast<const int4*>((isv ? vh : kh) + static_cast<size_t>(kt + j) * D + ch * 16);
+      }
+      pre[u] = v;
+    }
+    if (tid < kKT) {
+      pks = tid < nk ? __fmul_rn(ksh[kt + tid], a.scale) : 0.0f;
+      pvs = tid < nk ? __fmul_rn(vsh[kt + tid], kPScale) : 0.0f;
+    }
+  };
+  auto commit = [&]() {
+#pragma unroll
+    for (int u = 0; u < PF; ++u) {
+      const int i = tid + u * kThreads;
+      if (i < 2 * kKT * CH) {
+        const bool isv = i >= kKT * CH;
+        const int ii = isv ? i - kKT * CH : i;
+        const int j = ii / CH, ch = ii % CH;
+        const int8_t* b = reinterpret_cast<const int8_t*>(&pre[u]);
+        __half* dst = (isv ? Vh : Kh) + j * DP + ch * 16;
+#pragma unroll
+        for (int e = 0; e < 16; e += 2)
+          *reinterpret_cast<uint32_t*>(dst + e) =
+              pack_h2(__int2half_rn(static_cast<int>(b[e])), __int2half_rn(static_cast<int>(b[e + 1])));
+      }
+    }
+    if (tid < kKT) {
+      ksc[tid] = pks;
+      vsc[tid] = pvs;
+    }
+  };
+
+  const int r0 = warp * 16;
+  const bool active = r0 < nq;
+  float o[NDT][4];
+#pragma unroll
+  for (int j = 0; j < NDT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+  float mA = -INFINITY, mB = -INFINITY, lA = 0.0f, lB = 0.0f;
+  fetch(k0);
   __syncthreads();
+  const int nkA = Nk[min(r0 + g, kQMax - 1)], nkB = Nk[min(r0 + g + 8, kQMax - 1)];
 
   for (int kt = k0; kt < k1; kt += kKT) {
-    const int nk = min(kKT, k1 - kt);
-    // int8 K / V tile -> float smem (unscaled), 4 values per thread-iteration.
-    for (int i = tid; i < kKT * D / 4; i += kThreads) {
-      const int j = i / (D / 4), d4 = (i % (D / 4)) * 4;
-      char4 kv = make_char4(0, 0, 0, 0), vv = make_char4(0, 0, 0, 0);
-      if (j < nk) {
-        kv = *reinterpret_cast<const char4*>(kh + static_cast<size_t>(kt + j) * D + d4);
-        vv = *reinterpret_cast<const char4*>(vh + static_cast<size_t>(kt + j) * D + d4);
-      }
-      float* kr = Kf + j * DP + d4;
-      float* vr = Vf + j * DP + d4;
-      kr[0] = kv.x, kr[1] = kv.y, kr[2] = kv.z, kr[3] = kv.w;
-      vr[0] = vv.x, vr[1] = vv.y, vr[2] = vv.z, vr[3] = vv.w;
-    }
+    commit();
     __syncthreads();
-    // Scores: lane = key, warp w -> queries w + 8 i.
-    {
-      const int j = lane;
-      const bool kvalid = j < nk;
-      const float ks = kvalid ? __fmul_rn(ksh[kt + j], a.scale) : 0.0f;
-      const float vs = kvalid ? vsh[kt + j] : 0.0f;
-      float s[SI];
+    if (kt + kKT < k1) fetch(kt + kKT);
+    if (active) {
+      // S = Q K^T for this warp's 16 query vectors x 64 keys
+      float sacc[kKT / 8][4];
 #pragma unroll
-      for (int i = 0; i < SI; ++i) s[i] = 0.0f;
-      const float* kr = Kf + j * DP;
-#pragma unroll 4
-      for (int d = 0; d < D; d += 4) {
-        const float4 k4 = *reinterpret_cast<const float4*>(kr + d);
+      for (int j = 0; j < kKT / 8; ++j) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.0f;
 #pragma unroll
-        for (int i = 0; i < SI; ++i) {
-          const float4 q4 = *reinterpret_cast<const float4*>(Qs + (warp + 8 * i) * DP + d);
-          s[i] = __fmaf_rn(q4.x, k4.x, s[i]);
-          s[i] = __fmaf_rn(q4.y, k4.y, s[i]);
-          s[i] = __fmaf_rn(q4.z, k4.z, s[i]);
-          s[i] = __fmaf_rn(q4.w, k4.w, s[i]);
+      for (int kk = 0; kk < D / 16; ++kk) {
+        uint32_t ah[4], al[4];
+        const int qr = r0 + (lane & 15), qc = kk * 16 + (lane >> 4) * 8;
+        ldsm_x4(ah, Qh + qr * DP + qc);
+        ldsm_x4(al, Ql + qr * DP + qc);
+#pragma unroll
+        for (int nj = 0; nj < kKT / 16; ++nj) {  // two n8 tiles per ldmatrix.x4
+          uint32_t b[4];
+          const int kr = nj * 16 + (lane >> 4) * 8 + (lane & 7), kc = kk * 16 + ((lane >> 3) & 1) * 8;
+          ldsm_x4(b, Kh + kr * DP + kc);
+          mma_f16(sacc[2 * nj], ah, b[0], b[1]);
+          mma_f16(sacc[2 * nj], al, b[0], b[1]);
+          mma_f16(sacc[2 * nj + 1], ah, b[2], b[3]);
+          mma_f16(sacc[2 * nj + 1], al, b[2], b[3]);
         }
       }
+      // scale, mask, online softmax
+      float tmA = -INFINITY, tmB = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < SI; ++i) {
-        const int qi = warp + 8 * i;
-        const bool valid = kvalid && qi < nq && (kt + j) < Nk[qi];
-        const float sc = valid ? __fmul_rn(s[i], ks) : -INFINITY;
-        const float mt = warp_max(sc);
-        const float mo = Ms[qi];
-        const float mn = fmaxf(mo, mt);
-        float p = 0.0f, alpha = 1.0f;
-        if (mn != -INFINITY) {
-          p = valid ? exp_malkin(__fsub_rn(sc, mn)) : 0.0f;
-          alpha = mo == -INFINITY ? 0.0f : exp_malkin(__fsub_rn(mo, mn));
-        }
-        const float ps = warp_sum(p);
-        Ps[qi * (kKT + 4) + j] = __fmul_rn(p, vs);
-        __syncwarp();
-        if (lane == 0) {
-          Ms[qi] = mn;
-          Ls[qi] = __fmaf_rn(Ls[qi], alpha, ps);
-          Al[qi] = alpha;
+      for (int j = 0; j < kKT / 8; ++j) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int col = 8 * j + 2 * c + e, key = kt + col;
+          const float ks = ksc[col];
+          const bool okA = key < k1 && key < nkA, okB = key < k1 && key < nkB;
+          sacc[j][e] = okA ? __fmul_rn(sacc[j][e], ks) : -INFINITY;
+          sacc[j][2 + e] = okB ? __fmul_rn(sacc[j][2 + e], ks) : -INFINITY;
+          tmA = fmaxf(tmA, sacc[j][e]);
+          tmB = fmaxf(tmB, sacc[j][2 + e]);
         }
       }
-    }
-    __syncthreads();
-    // o = o * alpha + sum_j (p_j * vs_j) * v_j
-    {
-      const int dq = tid % DV, qg = tid / DV;
+      tmA = fmaxf(tmA, __shfl_xor_sync(0xffffffffu, tmA, 1));
+      tmA = fmaxf(tmA, __shfl_xor_sync(0xffffffffu, tmA, 2));
+      tmB = fmaxf(tmB, __shfl_xor_sync(0xffffffffu, tmB, 1));
+      tmB = fmaxf(tmB, __shfl_xor_sync(0xffffffffu, tmB, 2));
+      const float nmA = fmaxf(mA, tmA), nmB = fmaxf(mB, tmB);
+      const float alA = (mA == -INFINITY || nmA == -INFINITY) ? (nmA == -INFINITY ? 1.0f : 0.0f)
+                                                              : exp_malkin(__fsub_rn(mA, nmA));
+      const float alB = (mB == -INFINITY || nmB == -INFINITY) ? (nmB == -INFINITY ? 1.0f : 0.0f)
+                                                              : exp_malkin(__fsub_rn(mB, nmB));
+      mA = nmA;
+      mB = nmB;
+      float sA = 0.0f, sB = 0.0f;
+      uint32_t ph[kKT / 16][4], pl[kKT / 16][4];
 #pragma unroll
-      for (int i = 0; i < QI; ++i) {
-        const int qi = qg + QG * i;
-        if (qi < kQMax) {
-          const float al = Al[qi];
-          o[i][0] *= al, o[i][1] *= al, o[i][2] *= al, o[i][3] *= al;
+      for (int j = 0; j < kKT / 8; ++j) {
+        float pv[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const bool rowA = e < 2;
+          const float x = sacc[j][e], m = rowA ? mA : mB;
+          const float p = x == -INFINITY ? 0.0f : exp_malkin(__fsub_rn(x, m));
+          if (rowA)
+            sA += p;
+          else
+            sB += p;
+          pv[e] = __fmul_rn(p, vsc[8 * j + 2 * c + (e & 1)]);
         }
+        __half h0, l0, h1, l1, h2, l2, h3, l3;
+        split_h(pv[0], h0, l0);
+        split_h(pv[1], h1, l1);
+        split_h(pv[2], h2, l2);
+        split_h(pv[3], h3, l3);
+        // C layout of n-tile j -> A fragment of k16 step j / 2 (regs 0/1 from the even tile, 2/3 from the odd)
+        const int kq = j >> 1, hi = (j & 1) * 2;
+        ph[kq][hi] = pack_h2(h0, h1);
+        ph[kq][hi + 1] = pack_h2(h2, h3);
+        pl[kq][hi] = pack_h2(l0, l1);
+        pl[kq][hi + 1] = pack_h2(l2, l3);
       }
-      for (int j = 0; j < nk; j += 4) {
-        float4 v4[4];
+      sA += __shfl_xor_sync(0xffffffffu, sA, 1);
+      sA += __shfl_xor_sync(0xffffffffu, sA, 2);
+      sB += __shfl_xor_sync(0xffffffffu, sB, 1);
+      sB += __shfl_xor_sync(0xffffffffu, sB, 2);
+      lA = __fmaf_rn(lA, alA, sA);
+      lB = __fmaf_rn(lB, alB, sB);
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) v4[jj] = *reinterpret_cast<const float4*>(Vf + (j + jj) * DP + 4 * dq);
+      for (int j = 0; j < NDT; ++j) {
+        o[j][0] *= alA, o[j][1] *= alA, o[j][2] *= alB, o[j][3] *= alB;
+      }
+      // O += P' V
 #pragma unroll
-        for (int i = 0; i < QI; ++i) {
-          const int qi = qg + QG * i;
-          if (qi < kQMax) {
-            const float4 p4 = *reinterpret_cast<const float4*>(Ps + qi * (kKT + 4) + j);
-            const float pp[4] = {p4.x, p4.y, p4.z, p4.w};
+      for (int kq = 0; kq < kKT / 16; ++kq) {
 #pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-              o[i][0] = __fmaf_rn(pp[jj], v4[jj].x, o[i][0]);
-              o[i][1] = __fmaf_rn(pp[jj], v4[jj].y, o[i][1]);
-              o[i][2] = __fmaf_rn(pp[jj], v4[jj].z, o[i][2]);
-              o[i][3] = __fmaf_rn(pp[jj], v4[jj].w, o[i][3]);
-            }
-          }
+        for (int dj = 0; dj < NDT / 2; ++dj) {  // two d tiles per ldmatrix.x4.trans
+          uint32_t b[4];
+          const int vr = kq * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, vc = dj * 16 + (lane >> 4) * 8;
+          ldsm_x4_t(b, Vh + vr * DP + vc);
+          mma_f16(o[2 * dj], ph[kq], b[0], b[1]);
+          mma_f16(o[2 * dj], pl[kq], b[0], b[1]);
+          mma_f16(o[2 * dj + 1], ph[kq], b[2], b[3]);
+          mma_f16(o[2 * dj + 1], pl[kq], b[2], b[3]);
         }
       }
     }
     __syncthreads();
   }
-  // Partials: [((sg * n_chunks + chunk) * KV + kvh) * qmax + qi][D + 2] = o[D], m, l.
-  {
-    const int dq = tid % DV, qg = tid / DV;
+  // Partials: [((sg * n_chunks + chunk) * KV + kvh) * kQMax + qi][D + 2] = o[D], m, l.
+  if (active) {
     float* part = a.p.part + ((static_cast<size_t>(sg) * a.p.n_chunks + chunk) * a.KV + kvh) * kQMax * (D + 2);
+    const int qa = r0 + g, qb = r0 + g + 8;
+    constexpr float inv = 1.0f / kPScale;
 #pragma unroll
-    for (int i = 0; i < QI; ++i) {
-      const int qi = qg + QG * i;
-      if (qi < nq) {
-        float* pr = part + static_cast<size_t>(qi) * (D + 2);
-        pr[4 * dq + 0] = o[i][0];
-        pr[4 * dq + 1] = o[i][1];
-        pr[4 * dq + 2] = o[i][2];
-        pr[4 * dq + 3] = o[i][3];
-        if (dq == 0) {
-          pr[D] = Ms[qi];
-          pr[D + 1] = Ls[qi];
-        }
+    for (int j = 0; j < NDT; ++j) {
+      if (qa < nq) {
+        part[static_cast<size_t>(qa) * (D + 2) + 8 * j + 2 * c] = o[j][0] * inv;
+        part[static_cast<size_t>(qa) * (D + 2) + 8 * j + 2 * c + 1] = o[j][1] * inv;
       }
+      if (qb < nq) {
+        part[static_cast<size_t>(qb) * (D + 2) + 8 * j + 2 * c] = o[j][2] * inv;
+        part[static_cast<size_t>(qb) * (D + 2) + 8 * j + 2 * c + 1] = o[j][3] * inv;
+      }
+    }
+    if (c == 0) {
+      if (qa < nq) part[static_cast<size_t>(qa) * (D + 2) + D] = mA, part[static_cast<size_t>(qa) * (D + 2) + D + 1] = lA;
+      if (qb < nq) part[static_cast<size_t>(qb) * (D + 2) + D] = mB, part[static_cast<size_t>(qb) * (D + 2) + D + 1] = lB;
     }
   }
 }
@@ -265,28 +388,30 @@ __global__ void k_attn_combine(PartArgs a, const int32_t* __restrict__ tok_sg, f
   if (h >= a.H) return;
   const int kvh = h / a.G;
   const int sg = tok_sg[t];
-  const int t0 = a.p.sg_first[sg], t1 = a.p.sg_first[sg + 1];
-  int maxk = 0;
-  for (int u = t0; u < t1; ++u) maxk = max(maxk, a.p.n_keys[u]);
-  const int nck = (maxk + a.p.chunk - 1) / a.p.chunk;
+  const int t0 = a.p.sg_first[sg];
+  const int nck = (a.p.sg_maxk[sg] + a.p.chunk - 1) / a.p.chunk;
   const int qi = (t - t0) * a.G + (h - kvh * a.G);
   const float* part = a.p.part + (static_cast<size_t>(sg) * a.p.n_chunks * a.KV + kvh) * kQMax * (D + 2) +
                       static_cast<size_t>(qi) * (D + 2);
   const size_t cstride = static_cast<size_t>(a.KV) * kQMax * (D + 2);
   const int base = a.p.kv_base[t];
   const int e0 = a.p.anc_off[t], e1 = a.p.anc_off[t + 1];
-  // extra-key scores
   const float* qv = a.q + (static_cast<size_t>(t) * a.H + h) * D;
   float q[PER];
 #pragma unroll
   for (int m = 0; m < PER; ++m) q[m] = qv[lane + 32 * m];
-  float M = -INFINITY;
-  for (int c = 0; c < nck; ++c) M = fmaxf(M, part[c * cstride + D]);
   const int8_t* kh = a.L.k + static_cast<size_t>(kvh) * a.L.n_rows * D;
   const int8_t* vh = a.L.v + static_cast<size_t>(kvh) * a.L.n_rows * D;
   const float* ksh = a.L.ks + static_cast<size_t>(kvh) * a.L.n_rows;
   const float* vsh = a.L.vs + static_cast<size_t>(kvh) * a.L.n_rows;
-  float se_reg = -INFINITY;  // score of extra e0 + lane (<= 32 extras per token handled per pass)
+  // chunk maxima: lane c holds chunk c (up to 32 chunks per pass)
+  float M = -INFINITY;
+  for (int cb = 0; cb < nck; cb += 32) {
+    const float mc = cb + lane < nck ? part[(cb + lane) * cstride + D] : -INFINITY;
+    M = fmaxf(M, warp_max(mc));
+  }
+  // extra-key scores: lane e holds extra e (up to 32 extras per pass), independent dots
+  float se_reg = -INFINITY;
   for (int e = e0; e < e1; ++e) {
     const size_t row = static_cast<size_t>(base) + a.p.anc[e];
     float s = 0.0f;
@@ -301,14 +426,25 @@ __global__ void k_attn_combine(PartArgs a, const int32_t* __restrict__ tok_sg, f
 #pragma unroll
   for (int m = 0; m < PER; ++m) o[m] = 0.0f;
   float L = 0.0f;
-  for (int c = 0; c < nck; ++c) {
-    const float* pr = part + c * cstride;
-    const float mc = pr[D];
-    if (mc == -INFINITY) continue;
-    const float f = exp_malkin(__fsub_rn(mc, M));
-    L = __fmaf_rn(pr[D + 1], f, L);
+  for (int cb = 0; cb < nck; cb += 4) {
+    float mc[4], lc[4], oc[4][PER];
 #pragma unroll
-    for (int m = 0; m < PER; ++m) o[m] = __fmaf_rn(pr[lane + 32 * m], f, o[m]);
+    for (int u = 0; u < 4; ++u) {
+      const bool ok = cb + u < nck;
+      const float* pr = part + (cb + u) * cstride;
+      mc[u] = ok ? pr[D] : -INFINITY;
+      lc[u] = ok ? pr[D + 1] : 0.0f;
+#pragma unroll
+      for (int m = 0; m < PER; ++m) oc[u][m] = ok ? pr[lane + 32 * m] : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (mc[u] == -INFINITY) continue;
+      const float f = exp_malkin(__fsub_rn(mc[u], M));
+      L = __fmaf_rn(lc[u], f, L);
+#pragma unroll
+      for (int m = 0; m < PER; ++m) o[m] = __fmaf_rn(oc[u][m], f, o[m]);
+    }
   }
   for (int e = e0; e < e1; ++e) {
     const size_t row = static_cast<size_t>(base) + a.p.anc[e];
@@ -336,8 +472,7 @@ __global__ void k_attn_combine(PartArgs a, const int32_t* __restrict__ tok_sg, f
 
 template <int D>
 size_t part_smem() {
-  constexpr int DP = D + 4;
-  return sizeof(float) * (kQMax * DP + 2 * kKT * DP + kQMax * (kKT + 4) + 3 * kQMax) + sizeof(int) * kQMax;
+  return AttSmem<D>::BYTES;
 }
 
 template <int D>
@@ -345,10 +480,12 @@ void run_attention(const float* q, int H, int KV, float scale, const AttnLayer& 
                    cudaStream_t s) {
   PartArgs a{q, H, KV, H / KV, scale, L, p};
   const size_t smem = part_smem<D>();
-  static bool attr = false;
-  if (!attr) {
+  static bool attr[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr[dev]) {
     cudaFuncSetAttribute(k_attn_part<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    attr = true;
+    attr[dev] = true;
   }
   if (p.n_sg > 0 && p.n_chunks > 0) {
     const dim3 g1(p.n_chunks, p.n_sg, KV);
@@ -366,19 +503,22 @@ size_t attn_part_floats(int n_sg, int n_chunks, int KV, int D) {
   return static_cast<size_t>(n_sg) * n_chunks * KV * kQMax * (D + 2);
 }
 
-void launch_qkv_post(const float* y, int64_t ldy, int n, int H, int KV, int D, const float* q_norm, const float* k_norm,
-                     float eps, const float* rope_cs, const int32_t* rpos, const int32_t* kv_at, float* q_out,
-                     const AttnLayer& L, cudaStream_t s) {
+void launch_qkv_post(Slices qk, int v_n, int64_t v_col0, int64_t ldy, int n, int H, int KV, int D, const float* q_norm,
+                     const float* k_norm, float eps, const float* rope_cs, const int32_t* rpos, const int32_t* kv_at,
+                     float* q_out, const AttnLayer& L, cudaStream_t s) {
   const dim3 grid(n, (H + 2 * KV + 3) / 4);
   switch (D) {
     case 64:
-      k_qkv_post<64><<<grid, 128, 0, s>>>(y, ldy, n, H, KV, q_norm, k_norm, eps, rope_cs, rpos, kv_at, q_out, L);
+      k_qkv_post<64><<<grid, 128, 0, s>>>(qk, v_n, v_col0, ldy, n, H, KV, q_norm, k_norm, eps, rope_cs, rpos, kv_at,
+                                          q_out, L);
       break;
     case 128:
-      k_qkv_post<128><<<grid, 128, 0, s>>>(y, ldy, n, H, KV, q_norm, k_norm, eps, rope_cs, rpos, kv_at, q_out, L);
+      k_qkv_post<128><<<grid, 128, 0, s>>>(qk, v_n, v_col0, ldy, n, H, KV, q_norm, k_norm, eps, rope_cs, rpos, kv_at,
+                                           q_out, L);
       break;
     case 256:
-      k_qkv_post<256><<<grid, 128, 0, s>>>(y, ldy, n, H, KV, q_norm, k_norm, eps, rope_cs, rpos, kv_at, q_out, L);
+      k_qkv_post<256><<<grid, 128, 0, s>>>(qk, v_n, v_col0, ldy, n, H, KV, q_norm, k_norm, eps, rope_cs, rpos, kv_at,
+                                           q_out, L);
       break;
     default:
       break;

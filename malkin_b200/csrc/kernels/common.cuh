@@ -109,6 +109,19 @@ __device__ __forceinline__ int warp_isum(int v) {
   return v;
 }
 
+// Sum of n <= 16 values p[0], p[stride], ... in index order. All loads are issued before the first add, so the
+// latency of the n loads overlaps (a plain runtime-bounded loop would wait for each in turn).
+__device__ __forceinline__ float sum_strided16(const float* p, int n, int64_t stride) {
+  float v[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = i < n ? p[i * stride] : 0.0f;
+  float r = v[0];
+#pragma unroll
+  for (int i = 1; i < 16; ++i)
+    if (i < n) r = __fadd_rn(r, v[i]);
+  return r;
+}
+
 // e^x as malkin computes it for softmax and SiLU (kernels_avx512.cpp:186-202): clamp below at -87, Cody-Waite
 // reduction with ln 2 split in two, degree-6 Taylor polynomial in Horner form with fused multiply-adds, then
 // scaling by 2^n. (malkin's own algorithm, restated, so both sides exponentiate identically.)

@@ -9,6 +9,13 @@
 
 namespace mkb {
 
+// Token tiles (8 tokens each) of the activation layout for a batch of n tokens: whole GEMM passes of 18 tiles
+// once n exceeds one pass, so every pass reads initialised (zero) tiles.
+inline int act_tiles(int n) {
+  const int t = (n + 7) / 8;
+  return t <= 18 ? t : (t + 17) / 18 * 18;
+}
+
 // Quantized activations in the GEMM layout (layout.hpp). nt8 = token tiles of the current batch (layout stride).
 struct ActQ {
   uint8_t* qx = nullptr;
@@ -31,12 +38,20 @@ struct DevWeight {
 // ---- quantization (quant.cu) ----
 // x rows [n][ldx] -> act (blocks of K values); rows n..npad-1 zero-filled. K % 32 == 0.
 void launch_quant_rows(const float* x, int64_t ldx, int n, int K, const ActQ& act, cudaStream_t s);
-// rmsnorm (model.cpp:145-148) then quantize. rows: row indices into x (nullptr = 0..n-1). add (nullable): residual
-// partial added into x first (x[r] += add[r], written back; tensor-parallel allreduce result).
-void launch_rmsnorm_quant(float* x, int64_t ldx, const float* add, const int32_t* rows, const float* w, float eps, int n,
+// Split-K output slices: n_slices buffers, `stride` floats apart, summed in slice order by the consumer.
+struct Slices {
+  const float* p = nullptr;
+  int n = 0;
+  int64_t stride = 0;
+};
+// rmsnorm (model.cpp:145-148) then quantize. rows: row indices into x (nullptr = 0..n-1). add: residual
+// contributions added into x first, in slice order (x[r] += add[0][r] + add[1][r] + ..., written back).
+void launch_rmsnorm_quant(float* x, int64_t ldx, Slices add, const int32_t* rows, const float* w, float eps, int n,
                           int K, const ActQ& act, cudaStream_t s);
-// gu rows [n][ld]: gate at [0, F), up at [F, 2F): SiLU(gate) * up (kernels_avx512.cpp:271-280), quantized.
-void launch_silu_quant(const float* gu, int64_t ld, int F, int n, const ActQ& act, cudaStream_t s);
+// gu rows [n][ld] (slices): gate at [0, F), up at [F, 2F): SiLU(gate) * up (kernels_avx512.cpp:271-280), quantized.
+void launch_silu_quant(Slices gu, int64_t ld, int F, int n, const ActQ& act, cudaStream_t s);
+// dst[t * ld + i] = sum of slices (tensor parallel: the local partial before the allreduce).
+void launch_sum_slices(Slices src, int64_t ld, int n, int cols, float* dst, cudaStream_t s);
 // malkin BlockQ8 output (40-byte blocks) for tests.
 void launch_quant_blockq8(const float* x, int n, int64_t K, void* blocks, cudaStream_t s);
 // quantize_i8 rows (quant.cpp:216-222).
@@ -44,12 +59,13 @@ void launch_quant_i8(const float* x, int n, int len, int8_t* q, float* scale, cu
 void launch_silu_mul(float* g, const float* u, int64_t n, cudaStream_t s);
 
 // ---- GEMM (gemm.cu) ----
-// y[t * ldy + r] (+)= W[r] . x[t] for t < n, r < rows. split: k-unit ranges per CTA column (1 = whole K, malkin's
-// block order); atomic: accumulate with red.add (required when split > 1; y must hold the addend).
-void launch_gemm(const DevWeight& w, const ActQ& act, int n, float* y, int64_t ldy, int split, bool atomic,
-                 cudaStream_t s);
-// Split that fills the GPU for this weight (>= 1).
-int gemm_auto_split(const DevWeight& w, int n, int num_sms);
+// Slice s (of split) gets y[s * slice + t * ldy + r] = sum over slice s's k-range of W[r] . x[t], t < n, r < rows
+// (plain stores). split 1 keeps malkin's block order. status: device word for bounded-wait failures (nullable).
+void launch_gemm(const DevWeight& w, const ActQ& act, int n, float* y, int64_t ldy, int64_t slice, int split,
+                 int* status, cudaStream_t s);
+// Split that fills the GPU for this weight (>= 1), and the slices a split request produces.
+int gemm_split_for(const DevWeight& w, int num_sms);
+int gemm_slices(const DevWeight& w, int split);
 // out[(r * n + t) * nblk + b]: exact int dot of block b (Q6_K: 16-value halves).
 void launch_block_dots(const DevWeight& w, const ActQ& act, int n, int32_t* out, cudaStream_t s);
 
@@ -61,10 +77,11 @@ struct AttnLayer {
   float* vs;
   int64_t n_rows;  // rows per head (n_seq * n_ctx)
 };
-// Per token: RoPE table row rpos, KV row kv_at (absolute). y: [n][ldy] = q heads | k heads | v heads.
-void launch_qkv_post(const float* y, int64_t ldy, int n, int H, int KV, int D, const float* q_norm, const float* k_norm,
-                     float eps, const float* rope_cs, const int32_t* rpos, const int32_t* kv_at, float* q_out,
-                     const AttnLayer& L, cudaStream_t s);
+// Per token: RoPE table row rpos, KV row kv_at (absolute). y: [n][ldy] = q heads | k heads | v heads, as GEMM
+// slices: columns before v_col0 have qk.n slices, the v columns v_n slices (same stride).
+void launch_qkv_post(Slices qk, int v_n, int64_t v_col0, int64_t ldy, int n, int H, int KV, int D, const float* q_norm,
+                     const float* k_norm, float eps, const float* rope_cs, const int32_t* rpos, const int32_t* kv_at,
+                     float* q_out, const AttnLayer& L, cudaStream_t s);
 
 // Attention work description (host-built, device tables).
 struct AttnPlan {
@@ -78,6 +95,7 @@ struct AttnPlan {
   const int32_t* anc_off = nullptr;   // [n + 1]
   const int32_t* anc = nullptr;       // extra key rows (relative to kv_base)
   const int32_t* tok_sg = nullptr;    // [n] sub-group of each token
+  const int32_t* sg_maxk = nullptr;   // [n_sg] longest key prefix (n_keys) among the sub-group's tokens
   float* part = nullptr;              // partials workspace (attn_part_floats)
 };
 // Query vectors (rows x G) one sub-group may hold.

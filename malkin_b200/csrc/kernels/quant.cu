@@ -7,6 +7,8 @@
 // halves of the unsaturated ints.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.hpp"
 
@@ -78,9 +80,8 @@ __global__ void k_quant_rows(const float* __restrict__ x, int64_t ldx, int n, in
 }
 
 // grid (npad), block 256: one token row. y = x * s * w, s = 1 / sqrt(dot(x, x) / K + eps).
-__global__ void k_rmsnorm_quant(float* __restrict__ x, int64_t ldx, const float* __restrict__ add,
-                                const int32_t* __restrict__ rows, const float* __restrict__ w, float eps, int n, int K,
-                                ActQ a) {
+__global__ void k_rmsnorm_quant(float* __restrict__ x, int64_t ldx, Slices add, const int32_t* __restrict__ rows,
+                                const float* __restrict__ w, float eps, int n, int K, ActQ a) {
   const int t = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nb = K / 32;
   if (t >= n) {
@@ -91,10 +92,11 @@ __global__ void k_rmsnorm_quant(float* __restrict__ x, int64_t ldx, const float*
   float* xr = x + static_cast<size_t>(r) * ldx;
   __shared__ float red[8];
   float ss = 0.0f;
+#pragma unroll 4
   for (int i = threadIdx.x; i < K; i += blockDim.x) {
     float v = xr[i];
-    if (add) {
-      v = __fadd_rn(v, add[static_cast<size_t>(r) * ldx + i]);
+    if (add.n > 0) {
+      v = __fadd_rn(v, sum_strided16(add.p + static_cast<size_t>(r) * ldx + i, add.n, add.stride));
       xr[i] = v;
     }
     ss = __fmaf_rn(v, v, ss);
@@ -113,8 +115,10 @@ __global__ void k_rmsnorm_quant(float* __restrict__ x, int64_t ldx, const float*
   }
 }
 
+__device__ __forceinline__ float sum_slices(const Slices& s, size_t off) { return sum_strided16(s.p + off, s.n, s.stride); }
+
 // grid (ceil(nb / 8), npad), block 256.
-__global__ void k_silu_quant(const float* __restrict__ gu, int64_t ld, int F, int n, ActQ a) {
+__global__ void k_silu_quant(Slices gu, int64_t ld, int F, int n, ActQ a) {
   const int lane = threadIdx.x & 31, b = blockIdx.x * 8 + (threadIdx.x >> 5), t = blockIdx.y;
   const int nb = F / 32;
   if (b >= nb) return;
@@ -122,8 +126,8 @@ __global__ void k_silu_quant(const float* __restrict__ gu, int64_t ld, int F, in
     store_zero(a, b, t, lane);
     return;
   }
-  const float* row = gu + static_cast<size_t>(t) * ld;
-  const float g = row[b * 32 + lane], u = row[F + b * 32 + lane];
+  const size_t row = static_cast<size_t>(t) * ld;
+  const float g = sum_slices(gu, row + b * 32 + lane), u = sum_slices(gu, row + F + b * 32 + lane);
   const float e = exp_malkin(__fsub_rn(0.0f, g));
   const float h = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, e)), u);
   store_act(a, b, t, quant_block32(h, lane), lane);
@@ -158,6 +162,15 @@ __global__ void k_quant_i8(const float* __restrict__ x, int n, int len, int8_t* 
   if (lane == 0) sc[r] = d;
 }
 
+__global__ void k_sum_slices(Slices src, int64_t ld, int n, int cols, float* __restrict__ dst) {
+  const int64_t total = static_cast<int64_t>(n) * cols;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const size_t off = static_cast<size_t>(i / cols) * ld + i % cols;
+    dst[off] = sum_slices(src, off);
+  }
+}
+
 __global__ void k_silu_mul(float* __restrict__ g, const float* __restrict__ u, int64_t n) {
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -175,12 +188,18 @@ void launch_quant_rows(const float* x, int64_t ldx, int n, int K, const ActQ& ac
   k_quant_rows<<<grid, 256, 0, s>>>(x, ldx, n, nb, act);
 }
 
-void launch_rmsnorm_quant(float* x, int64_t ldx, const float* add, const int32_t* rows, const float* w, float eps, int n,
+void launch_rmsnorm_quant(float* x, int64_t ldx, Slices add, const int32_t* rows, const float* w, float eps, int n,
                           int K, const ActQ& act, cudaStream_t s) {
   k_rmsnorm_quant<<<act.nt8 * 8, 256, 0, s>>>(x, ldx, add, rows, w, eps, n, K, act);
 }
 
-void launch_silu_quant(const float* gu, int64_t ld, int F, int n, const ActQ& act, cudaStream_t s) {
+void launch_sum_slices(Slices src, int64_t ld, int n, int cols, float* dst, cudaStream_t s) {
+  const int64_t total = static_cast<int64_t>(n) * cols;
+  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 2048));
+  if (total > 0) k_sum_slices<<<blocks, 256, 0, s>>>(src, ld, n, cols, dst);
+}
+
+void launch_silu_quant(Slices gu, int64_t ld, int F, int n, const ActQ& act, cudaStream_t s) {
   const int nb = F / 32;
   dim3 grid((nb + 7) / 8, act.nt8 * 8);
   k_silu_quant<<<grid, 256, 0, s>>>(gu, ld, F, n, act);

@@ -159,7 +159,8 @@ def test_continuous_batch_equals_separate(mk, model_paths, torch_cuda):
     m2 = load(mk, path)
     a = m2.forward(batch_of(mk, ta))
     b = m2.forward(batch_of(mk, tb))
-    assert np.abs(both - np.concatenate([a, b])).max() < 2e-3
+    # int8 activation rounding can flip on float-summation-order noise, so the bound is the logits tolerance
+    assert np.abs(both - np.concatenate([a, b])).max() < TOL
 
 
 def test_profile_and_launch_count(mk, model_paths, torch_cuda):
