@@ -80,17 +80,23 @@ int current_device() {
 }
 
 // Temporary quantized-activation buffers for the kernel-level entry points.
+// exact_q8: the Q8_0 GEMM keeps the exact int8 block dots (mode kQ8Exact, or a block-dot request), which reads
+// the int8 tensor-core copy; otherwise the fp16 copy is written for the fp16 kernel.
 struct TmpAct {
   mkb::DevBuf buf;
   mkb::ActQ act;
-  TmpAct(int n, int64_t K) {
+  TmpAct(int n, int64_t K, bool exact_q8) {
     const int nt8 = mkb::act_tiles(n), npad = nt8 * 8;
     const int64_t blocks = K / 32;
     const size_t qx = static_cast<size_t>(blocks) * npad * 32, f = static_cast<size_t>(blocks) * npad * 4;
-    buf = mkb::DevBuf(qx + 3 * f + 256);
+    buf = mkb::DevBuf(4 * qx + 3 * f + 256);
     auto* p = buf.get<uint8_t>();
     act.qx = p;
-    act.dx = reinterpret_cast<float*>(p + qx);
+    if (exact_q8)
+      act.qc = p + qx;
+    else
+      act.xh = reinterpret_cast<uint16_t*>(p + qx);  // 2 bytes per value
+    act.dx = reinterpret_cast<float*>(p + 3 * qx);
     act.dsx = act.dx + blocks * npad;
     act.sh = reinterpret_cast<uint32_t*>(act.dsx + blocks * npad);
     act.nt8 = nt8;
@@ -243,10 +249,11 @@ int mk_weight_upload(int type, const void* host_rows, int64_t rows, int64_t cols
     auto w = std::make_unique<mk_weight>();
     w->device = current_device();
     const size_t rb = mkb::row_bytes(static_cast<uint32_t>(type), cols);
-    const size_t bytes = mkb::repack_bytes(static_cast<uint32_t>(type), rows, cols / u);
+    const int layout = mkb::weight_layout(static_cast<uint32_t>(type));
+    const size_t bytes = mkb::repack_layout_bytes(static_cast<uint32_t>(type), layout, rows, cols / u);
     std::vector<uint8_t> staging(bytes);
-    mkb::repack(static_cast<uint32_t>(type), static_cast<const uint8_t*>(host_rows), rb, rows, 0, cols / u,
-                staging.data(), 0);
+    mkb::repack_layout(static_cast<uint32_t>(type), layout, static_cast<const uint8_t*>(host_rows), rb, rows, 0,
+                       cols / u, staging.data(), 0);
     w->buf = mkb::DevBuf(bytes);
     mkb::cuda_check(cudaMemcpy(w->buf.get(), staging.data(), bytes, cudaMemcpyHostToDevice), "upload");
     w->w.type = static_cast<uint32_t>(type);
@@ -255,6 +262,7 @@ int mk_weight_upload(int type, const void* host_rows, int64_t rows, int64_t cols
     w->w.cols = cols;
     w->w.panels = (rows + mkb::kPanelRows - 1) / mkb::kPanelRows;
     w->w.kunits = static_cast<int>(cols / u);
+    w->w.layout = layout;
     *out = w.release();
   });
 }
@@ -277,7 +285,7 @@ int mk_matmul(const mk_weight* w, const float* dev_x, int n, float* dev_y, int s
   return guard(MK_ERR_ARG, [&] {
     if (!w || n <= 0) throw mkb::ArgError("matmul: bad argument");
     cudaStream_t s = as_stream(stream);
-    TmpAct t(n, w->w.cols);
+    TmpAct t(n, w->w.cols, mkb::q8_mode() == mkb::kQ8Exact);
     mkb::launch_quant_rows(dev_x, w->w.cols, n, static_cast<int>(w->w.cols), t.act, s);
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
@@ -302,11 +310,16 @@ int mk_block_dots(const mk_weight* w, const float* dev_x, int n, int32_t* dev_ou
   return guard(MK_ERR_ARG, [&] {
     if (!w || n <= 0) throw mkb::ArgError("block_dots: bad argument");
     cudaStream_t s = as_stream(stream);
-    TmpAct t(n, w->w.cols);
+    TmpAct t(n, w->w.cols, true);
     mkb::launch_quant_rows(dev_x, w->w.cols, n, static_cast<int>(w->w.cols), t.act, s);
-    mkb::launch_block_dots(w->w, t.act, n, dev_out, s);
+    mkb::DevBuf status(sizeof(int));
+    mkb::cuda_check(cudaMemsetAsync(status.get(), 0, sizeof(int), s), "memset");
+    mkb::launch_block_dots(w->w, t.act, n, dev_out, status.get<int>(), s);
     mkb::cuda_check(cudaGetLastError(), "block_dots");
+    int st = 0;
+    mkb::cuda_check(cudaMemcpyAsync(&st, status.get(), sizeof st, cudaMemcpyDeviceToHost, s), "status");
     mkb::cuda_check(cudaStreamSynchronize(s), "block_dots");
+    if (st != 0) throw mkb::TimeoutError("block_dots: device pipeline wait gave up");
   });
 }
 

@@ -24,6 +24,17 @@
 //   dx  [block][npad] float  (BlockQ8::d)
 //   dsx [block][npad] float  (d * float(s[0] + s[1]), the Q4_K min term, gemm_avx512.cpp:145)
 //   sh  [block][npad] uint32 (int16 s[0] | int16 s[1] << 16, the BlockQ8 half sums)
+//
+// Tensor-core layout of Q8_0 weights (the A operand of tcgen05.mma kind::i8, K-major, no swizzle). A tile is 128
+// rows; per tile and 32-value block one 4352-byte record, records ordered [tile][block]:
+//   [0,4096)     int8 values in core matrices of 8 rows x 16 bytes: (row r, value k) at
+//                (r / 8) * 256 + (k / 16) * 128 + (r % 8) * 16 + k % 16
+//   [4096,4352)  fp16 d of rows 0..127
+// Its activations (the B operand) use the same core-matrix order with tokens as rows:
+//   qc  [block][npad / 8][2][8][16 B]: (token t, value k) at block * npad * 32 + (t / 8) * 256 + (k / 16) * 128
+//       + (t % 8) * 16 + k % 16, npad a multiple of 16.
+//   xh  [block][npad / 8][4][8][8 halves]: fp16 of q * d (the dequantized Q8 value), (token t, value k) at half
+//       block * npad * 32 + (t / 8) * 256 + (k / 8) * 64 + (t % 8) * 8 + k % 8 (the fp16 GEMM's B operand).
 #pragma once
 #include <cstddef>
 #include <cstdint>
@@ -31,6 +42,8 @@
 namespace mkb {
 
 constexpr int kPanelRows = 16;
+constexpr int kTcRows = 128;
+constexpr size_t kTcRecord = 4352;
 constexpr size_t kChunkQ8_0 = 544, kChunkQ4_K = 2304, kChunkQ6_K = 3360;
 
 inline constexpr int kunit_values(uint32_t type) { return type == 8 ? 32 : 256; }

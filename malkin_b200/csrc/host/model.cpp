@@ -154,6 +154,7 @@ void Model::load(const std::string& path) {
     const Tensor* t;
     int64_t r0, nr, c0, nc;
     size_t off;  // in wbuf
+    int layout;
   };
   std::vector<Piece> pieces;
   size_t total = 0;
@@ -162,8 +163,9 @@ void Model::load(const std::string& path) {
     const int u = kunit_values(t->type);
     if (c0 % u || nc % u) throw ArgError("tensor parallel: shard of " + t->name + " not block aligned");
     total = align_up(total, 256);
-    pieces.push_back({t, r0, nr, c0, nc, total});
-    total += repack_bytes(t->type, nr, nc / u);
+    const int layout = weight_layout(t->type);
+    pieces.push_back({t, r0, nr, c0, nc, total, layout});
+    total += repack_layout_bytes(t->type, layout, nr, nc / u);
     weight_bytes_ += static_cast<int64_t>(nr) * static_cast<int64_t>(row_bytes(t->type, nc));
     return pieces.size() - 1;
   };
@@ -224,9 +226,10 @@ void Model::load(const std::string& path) {
   for (const Piece& pc : pieces) {
     const int u = kunit_values(pc.t->type);
     const size_t rb = row_bytes(pc.t->type, pc.t->cols());
-    const size_t nbytes = repack_bytes(pc.t->type, pc.nr, pc.nc / u);
+    const size_t nbytes = repack_layout_bytes(pc.t->type, pc.layout, pc.nr, pc.nc / u);
     staging.resize(nbytes);
-    repack(pc.t->type, pc.t->data + static_cast<size_t>(pc.r0) * rb, rb, pc.nr, pc.c0 / u, pc.nc / u, staging.data(), 0);
+    repack_layout(pc.t->type, pc.layout, pc.t->data + static_cast<size_t>(pc.r0) * rb, rb, pc.nr, pc.c0 / u,
+                  pc.nc / u, staging.data(), 0);
     cuda_check(cudaMemcpy(base + pc.off, staging.data(), nbytes, cudaMemcpyHostToDevice), "upload weights");
   }
   cuda_check(cudaMemcpy(base + embd_off, tok->data, tok->nbytes, cudaMemcpyHostToDevice), "upload embeddings");
@@ -247,17 +250,19 @@ void Model::load(const std::string& path) {
     w.cols = pc.nc;
     w.panels = (pc.nr + kPanelRows - 1) / kPanelRows;
     w.kunits = static_cast<int>(pc.nc / kunit_values(pc.t->type));
+    w.layout = pc.layout;
     return w;
   };
-  // Fuse consecutive same-type pieces (q|k|v, gate|up) into one weight: their panels are adjacent in wbuf.
+  // Fuse consecutive same-type pieces (q|k|v, gate|up) into one weight: their panels (tiles) are adjacent in wbuf.
   auto fuse = [&](const int* idx, int cnt, DevWeight* outw, int64_t* cols, int& nout) {
     nout = 0;
     int64_t col = 0;
     for (int i = 0; i < cnt; ++i) {
       DevWeight w = dev(idx[i]);
-      const bool adjacent = nout > 0 && outw[nout - 1].type == w.type &&
-                            outw[nout - 1].data + repack_bytes(w.type, outw[nout - 1].rows, w.kunits) == w.data &&
-                            outw[nout - 1].rows % kPanelRows == 0;
+      const bool adjacent =
+          nout > 0 && outw[nout - 1].type == w.type && outw[nout - 1].layout == w.layout &&
+          outw[nout - 1].data + repack_layout_bytes(w.type, w.layout, outw[nout - 1].rows, w.kunits) == w.data &&
+          outw[nout - 1].rows % layout_row_quantum(w.layout) == 0;
       if (adjacent) {
         outw[nout - 1].rows += w.rows;
         outw[nout - 1].panels = (outw[nout - 1].rows + kPanelRows - 1) / kPanelRows;
@@ -361,6 +366,7 @@ void Model::alloc_kv(int n_ctx, int n_seq, int max_batch) {
                o_gu = take(static_cast<size_t>(s_gu) * gu_slice_ * 4), o_p = take(static_cast<size_t>(NB) * E * 4),
                o_part = take(static_cast<size_t>(s_part) * part_slice_ * 4),
                o_lg = take(static_cast<size_t>(NB) * Vl_ * 4), o_qx = take(static_cast<size_t>(blocks) * NB * 32),
+               o_qc = take(static_cast<size_t>(blocks) * NB * 64),
                o_dx = take(static_cast<size_t>(blocks) * NB * 4), o_dsx = take(static_cast<size_t>(blocks) * NB * 4),
                o_sh = take(static_cast<size_t>(blocks) * NB * 4),
                o_cv = take(static_cast<size_t>(NB) * MK_TOPK_CAP * 4), o_ci = take(static_cast<size_t>(NB) * MK_TOPK_CAP * 4),
@@ -378,6 +384,11 @@ void Model::alloc_kv(int n_ctx, int n_seq, int max_batch) {
   part_ = reinterpret_cast<float*>(sb + o_part);
   logits_ = reinterpret_cast<float*>(sb + o_lg);
   act_.qx = sb + o_qx;
+  // the Q8_0 tensor-core GEMMs read the int8 copy (exact mode) or the fp16 copy (default) of the activations
+  if (q8_mode() == kQ8Exact)
+    act_.qc = sb + o_qc;
+  else
+    act_.xh = reinterpret_cast<uint16_t*>(sb + o_qc);
   act_.dx = reinterpret_cast<float*>(sb + o_dx);
   act_.dsx = reinterpret_cast<float*>(sb + o_dsx);
   act_.sh = reinterpret_cast<uint32_t*>(sb + o_sh);

@@ -10,6 +10,10 @@
 #include <thread>
 #include <vector>
 
+#include <cstdlib>
+#include <string>
+
+#include "../kernels/kernels.hpp"
 #include "gguf.hpp"
 #include "layout.hpp"
 
@@ -107,30 +111,86 @@ size_t repack_bytes(uint32_t type, int64_t rows, int64_t units) {
   return static_cast<size_t>(panels) * static_cast<size_t>(units) * chunk_bytes(type);
 }
 
+namespace {
+
+// Runs body(i) for i in [0, count) on n_threads threads (0 = all hardware threads).
+template <class F>
+void parallel_for(int64_t count, int n_threads, F body) {
+  std::atomic<int64_t> next{0};
+  auto worker = [&] {
+    for (int64_t i; (i = next.fetch_add(1)) < count;) body(i);
+  };
+  int nt = n_threads > 0 ? n_threads : static_cast<int>(std::thread::hardware_concurrency());
+  nt = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(nt, count)));
+  std::vector<std::thread> pool;
+  for (int i = 1; i < nt; ++i) pool.emplace_back(worker);
+  worker();
+  for (auto& t : pool) t.join();
+}
+
+}  // namespace
+
 void repack(uint32_t type, const uint8_t* src, size_t src_stride, int64_t rows, int64_t unit0, int64_t units,
             uint8_t* dst, int n_threads) {
   if (!repack_supported(type)) throw std::runtime_error(std::string("repack: unsupported type ") + type_name(type));
   const size_t cb = chunk_bytes(type);
   const size_t unit_src = type_size(type).bytes;  // GGUF bytes of one k-unit of one row
   const int64_t panels = (rows + kPanelRows - 1) / kPanelRows;
-  std::atomic<int64_t> next{0};
-  auto worker = [&] {
-    for (int64_t p; (p = next.fetch_add(1)) < panels;) {
-      const uint8_t* rp[16];
-      for (int r = 0; r < 16; ++r) {
-        const int64_t row = p * kPanelRows + r;
-        rp[r] = row < rows ? src + static_cast<size_t>(row) * src_stride : nullptr;
-      }
-      for (int64_t u = 0; u < units; ++u)
-        pack_chunk(type, rp, static_cast<size_t>(unit0 + u) * unit_src, dst + (static_cast<size_t>(p) * units + u) * cb);
+  parallel_for(panels, n_threads, [&](int64_t p) {
+    const uint8_t* rp[16];
+    for (int r = 0; r < 16; ++r) {
+      const int64_t row = p * kPanelRows + r;
+      rp[r] = row < rows ? src + static_cast<size_t>(row) * src_stride : nullptr;
     }
-  };
-  int nt = n_threads > 0 ? n_threads : static_cast<int>(std::thread::hardware_concurrency());
-  nt = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(nt, panels)));
-  std::vector<std::thread> pool;
-  for (int i = 1; i < nt; ++i) pool.emplace_back(worker);
-  worker();
-  for (auto& t : pool) t.join();
+    for (int64_t u = 0; u < units; ++u)
+      pack_chunk(type, rp, static_cast<size_t>(unit0 + u) * unit_src, dst + (static_cast<size_t>(p) * units + u) * cb);
+  });
+}
+
+size_t repack_tc_bytes(int64_t rows, int64_t blocks) {
+  const int64_t tiles = (rows + kTcRows - 1) / kTcRows;
+  return static_cast<size_t>(tiles) * static_cast<size_t>(blocks) * kTcRecord;
+}
+
+void repack_tc(const uint8_t* src, size_t src_stride, int64_t rows, int64_t block0, int64_t blocks, uint8_t* dst,
+               int n_threads) {
+  const size_t bsrc = type_size(kQ8_0).bytes;  // 34: fp16 d, 32 int8
+  const int64_t tiles = (rows + kTcRows - 1) / kTcRows;
+  parallel_for(tiles, n_threads, [&](int64_t tile) {
+    for (int64_t u = 0; u < blocks; ++u) {
+      uint8_t* rec = dst + (static_cast<size_t>(tile) * blocks + u) * kTcRecord;
+      std::memset(rec, 0, kTcRecord);
+      for (int r = 0; r < kTcRows; ++r) {
+        const int64_t row = tile * kTcRows + r;
+        if (row >= rows) break;
+        const uint8_t* s = src + static_cast<size_t>(row) * src_stride + static_cast<size_t>(block0 + u) * bsrc;
+        std::memcpy(rec + 4096 + 2 * r, s, 2);
+        for (int h = 0; h < 2; ++h) std::memcpy(rec + (r / 8) * 256 + h * 128 + (r % 8) * 16, s + 2 + 16 * h, 16);
+      }
+    }
+  });
+}
+
+int weight_layout(uint32_t type) {
+  if (type != kQ8_0) return kLayoutPanels;
+  const char* e = std::getenv("MALKIN_B200_Q8_LAYOUT");
+  return e && std::string(e) == "panels" ? kLayoutPanels : kLayoutTc;
+}
+
+int layout_row_quantum(int layout) { return layout == kLayoutTc ? kTcRows : kPanelRows; }
+
+size_t repack_layout_bytes(uint32_t type, int layout, int64_t rows, int64_t units) {
+  return layout == kLayoutTc ? repack_tc_bytes(rows, units) : repack_bytes(type, rows, units);
+}
+
+void repack_layout(uint32_t type, int layout, const uint8_t* src, size_t src_stride, int64_t rows, int64_t unit0,
+                   int64_t units, uint8_t* dst, int n_threads) {
+  if (layout == kLayoutTc) {
+    if (type != kQ8_0) throw std::runtime_error("repack: the tensor-core layout holds Q8_0 only");
+    repack_tc(src, src_stride, rows, unit0, units, dst, n_threads);
+  } else {
+    repack(type, src, src_stride, rows, unit0, units, dst, n_threads);
+  }
 }
 
 }  // namespace mkb

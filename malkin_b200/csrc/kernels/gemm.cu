@@ -18,6 +18,8 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
+#include <string>
 #include <array>
 #include <utility>
 
@@ -425,7 +427,13 @@ void launch_t(const GemmArgs& a, dim3 grid, int nt, cudaStream_t s) {
 
 }  // namespace
 
+int q8_mode() {
+  const char* e = std::getenv("MALKIN_B200_Q8_GEMM");
+  return e && std::string(e) == "fp16" ? kQ8Fp16 : kQ8Exact;
+}
+
 int gemm_split_for(const DevWeight& w, int num_sms) {
+  if (w.layout == kLayoutTc) return gemm_tc_split_for(w, num_sms);
   const int64_t tiles = (w.panels + kTilePanels - 1) / kTilePanels;
   const int max_split = std::max(1, w.kunits / (w.type == 8 ? 8 : 1));
   int best = 1;
@@ -442,6 +450,7 @@ int gemm_split_for(const DevWeight& w, int num_sms) {
 }
 
 int gemm_slices(const DevWeight& w, int split) {
+  if (w.layout == kLayoutTc) return gemm_tc_slices(w, split);
   split = std::max(1, std::min(split, w.kunits));
   const int per = (w.kunits + split - 1) / split;
   return (w.kunits + per - 1) / per;
@@ -450,6 +459,13 @@ int gemm_slices(const DevWeight& w, int split) {
 void launch_gemm(const DevWeight& w, const ActQ& act, int n, float* y, int64_t ldy, int64_t slice, int split,
                  int* status, cudaStream_t s) {
   if (n <= 0) return;
+  if (w.layout == kLayoutTc) {
+    if (act.xh)
+      launch_gemm_f16(w, act, n, y, ldy, slice, split, status, s);
+    else
+      launch_gemm_tc(w, act, n, y, ldy, slice, split, nullptr, status, s);
+    return;
+  }
   split = std::max(1, std::min(split, w.kunits));
   const int per = (w.kunits + split - 1) / split;
   const int gy = (w.kunits + per - 1) / per;
@@ -489,7 +505,11 @@ void launch_gemm(const DevWeight& w, const ActQ& act, int n, float* y, int64_t l
   }
 }
 
-void launch_block_dots(const DevWeight& w, const ActQ& act, int n, int32_t* out, cudaStream_t s) {
+void launch_block_dots(const DevWeight& w, const ActQ& act, int n, int32_t* out, int* status, cudaStream_t s) {
+  if (w.layout == kLayoutTc) {
+    launch_gemm_tc(w, act, n, nullptr, 0, 0, 1, out, status, s);
+    return;
+  }
   k_block_dots<<<static_cast<unsigned>(w.panels), 32, 0, s>>>(w.type, w.data, w.panels, w.kunits, w.rows, act, n, out);
 }
 

@@ -9,23 +9,29 @@
 
 namespace mkb {
 
-// Token tiles (8 tokens each) of the activation layout for a batch of n tokens: whole GEMM passes of 18 tiles
-// once n exceeds one pass, so every pass reads initialised (zero) tiles.
+constexpr int kMaxDevices = 64;  // per-device tables (kernel attributes, scratch addresses)
+
+// Token tiles (8 tokens each) of the activation layout for a batch of n tokens: an even count (the tensor-core
+// GEMM reads tokens in groups of 16), and whole GEMM passes of 18 tiles once n exceeds one pass, so every pass
+// reads initialised (zero) tiles.
 inline int act_tiles(int n) {
   const int t = (n + 7) / 8;
-  return t <= 18 ? t : (t + 17) / 18 * 18;
+  return t <= 18 ? (t + 1) / 2 * 2 : (t + 17) / 18 * 18;
 }
 
 // Quantized activations in the GEMM layout (layout.hpp). nt8 = token tiles of the current batch (layout stride).
 struct ActQ {
   uint8_t* qx = nullptr;
+  uint8_t* qc = nullptr;  // tensor-core order of the same int8 values (nullable)
+  uint16_t* xh = nullptr;  // fp16 of q * d in tensor-core order (nullable), layout.hpp
   float* dx = nullptr;
   float* dsx = nullptr;
   uint32_t* sh = nullptr;
   int nt8 = 0;
 };
 
-// Device weight in the panel layout.
+// Device weight in the panel layout, or (Q8_0) in the tensor-core tile layout.
+constexpr int kLayoutPanels = 0, kLayoutTc = 1;
 struct DevWeight {
   uint32_t type = 0;
   const uint8_t* data = nullptr;
@@ -33,7 +39,9 @@ struct DevWeight {
   int64_t cols = 0;    // values per row (this shard)
   int64_t panels = 0;  // ceil(rows / 16)
   int kunits = 0;      // cols / 32 (Q8_0) or cols / 256 (K-quants)
+  int layout = kLayoutPanels;
 };
+
 
 // ---- quantization (quant.cu) ----
 // x rows [n][ldx] -> act (blocks of K values); rows n..npad-1 zero-filled. K % 32 == 0.
@@ -67,7 +75,23 @@ void launch_gemm(const DevWeight& w, const ActQ& act, int n, float* y, int64_t l
 int gemm_split_for(const DevWeight& w, int num_sms);
 int gemm_slices(const DevWeight& w, int split);
 // out[(r * n + t) * nblk + b]: exact int dot of block b (Q6_K: 16-value halves).
-void launch_block_dots(const DevWeight& w, const ActQ& act, int n, int32_t* out, cudaStream_t s);
+void launch_block_dots(const DevWeight& w, const ActQ& act, int n, int32_t* out, int* status, cudaStream_t s);
+
+// ---- tensor-core Q8_0 GEMMs, reached through launch_gemm / launch_block_dots ----
+// Arithmetic of the Q8_0 GEMM: kQ8Exact (default) keeps malkin's exact int8 block dots and per-block float
+// epilogue (tcgen05 kind::i8, gemm_tc.cu; bit-identical to malkin at split 1); kQ8Fp16 multiplies the dequantized
+// operands fp16(q * d) on tcgen05 kind::f16 with fp32 accumulation across blocks (gemm_f16.cu): faster, but each
+// product carries two fp16 roundings, which move logits of the synthetic test models by up to about 2e-2. The
+// environment variable MALKIN_B200_Q8_GEMM=fp16 selects it; q8_mode() reads it on every call. launch_gemm runs the
+// fp16 kernel when act.xh is set and the int8 kernel otherwise (act.qc), so the owner of the activation buffers picks.
+enum Q8Mode { kQ8Fp16 = 0, kQ8Exact = 1 };
+int q8_mode();
+void launch_gemm_f16(const DevWeight& w, const ActQ& act, int n, float* y, int64_t ldy, int64_t slice, int split,
+                     int* status, cudaStream_t s);
+void launch_gemm_tc(const DevWeight& w, const ActQ& act, int n, float* y, int64_t ldy, int64_t slice, int split,
+                    int32_t* dots, int* status, cudaStream_t s);
+int gemm_tc_split_for(const DevWeight& w, int num_sms);
+int gemm_tc_slices(const DevWeight& w, int split);
 
 // ---- attention (attention.cu) ----
 struct AttnLayer {

@@ -54,6 +54,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   return false;
 }
 
+// mbar_wait by a whole warp with one outcome for every lane (true only if every lane saw the phase complete), so
+// the warp stays converged for the .sync.aligned instructions that follow.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* status, int code) {
+  const bool ok = mbar_wait(bar, parity, status, code);
+  return __all_sync(0xffffffffu, ok) != 0;
+}
+
 // 1-D bulk copy global -> shared, completion counted in bytes on bar. dst, src 16-byte aligned; bytes % 16 == 0.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(

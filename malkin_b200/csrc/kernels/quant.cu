@@ -53,6 +53,18 @@ __device__ __forceinline__ void store_act(const ActQ& a, int b, int t, const QBl
     const int j = t >> 3, g = t & 7;
     uint8_t* dst = a.qx + (static_cast<size_t>(b) * a.nt8 + j) * 256 + (g * 4 + c) * 8 + hi * 4;
     *reinterpret_cast<uint32_t*>(dst) = word;
+    if (a.qc) {
+      // tensor-core order: values 16 h .. 16 h + 15 of token t at (t / 8) * 256 + h * 128 + (t % 8) * 16
+      uint8_t* dq = a.qc + static_cast<size_t>(b) * npad * 32 + j * 256 + (m >> 2) * 128 + g * 16 + (m & 3) * 4;
+      *reinterpret_cast<uint32_t*>(dq) = word;
+    }
+  }
+  if (a.xh) {
+    // fp16 of the dequantized value q * d, value k of token t at (t / 8) * 256 + (k / 8) * 64 + (t % 8) * 8 + k % 8
+    // halves from the block's base
+    const __half h = __float2half_rn(__fmul_rn(static_cast<float>(qb.q), qb.d));
+    a.xh[static_cast<size_t>(b) * npad * 32 + (t >> 3) * 256 + (lane >> 3) * 64 + (t & 7) * 8 + (lane & 7)] =
+        __half_as_ushort(h);
   }
   if (lane == 0) {
     const size_t o = static_cast<size_t>(b) * npad + t;
@@ -112,6 +124,59 @@ __global__ void k_rmsnorm_quant(float* __restrict__ x, int64_t ldx, Slices add, 
     const int i = b * 32 + lane;
     const float v = __fmul_rn(__fmul_rn(xr[i], s), w[i]);
     store_act(a, b, t, quant_block32(v, lane), lane);
+  }
+}
+
+// The same with one 1024-thread block per token row and the row held in registers (K <= 8192): thread i holds
+// values i, i + 1024, ..., so warp w's lanes already hold block w + 32 j for the quantization pass, and every load
+// of the row (and of its residual slices) is in flight at once.
+constexpr int kNormThreads = 1024, kNormMaxJ = 8;
+__global__ void __launch_bounds__(kNormThreads) k_rmsnorm_quant_wide(float* __restrict__ x, int64_t ldx, Slices add,
+                                                                     const int32_t* __restrict__ rows,
+                                                                     const float* __restrict__ w, float eps, int n,
+                                                                     int K, ActQ a) {
+  const int t = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nb = K / 32;
+  if (t >= n) {
+    for (int b = warp; b < nb; b += 32) store_zero(a, b, t, lane);
+    return;
+  }
+  const int r = rows ? rows[t] : t;
+  float* xr = x + static_cast<size_t>(r) * ldx;
+  float v[kNormMaxJ], wv[kNormMaxJ];
+#pragma unroll
+  for (int j = 0; j < kNormMaxJ; ++j) {
+    const int i = threadIdx.x + kNormThreads * j;
+    v[j] = i < K ? xr[i] : 0.0f;
+    wv[j] = i < K ? w[i] : 0.0f;
+  }
+  if (add.n > 0) {
+#pragma unroll
+    for (int j = 0; j < kNormMaxJ; ++j) {
+      const int i = threadIdx.x + kNormThreads * j;
+      if (i < K) v[j] = __fadd_rn(v[j], sum_strided16(add.p + static_cast<size_t>(r) * ldx + i, add.n, add.stride));
+    }
+#pragma unroll
+    for (int j = 0; j < kNormMaxJ; ++j) {
+      const int i = threadIdx.x + kNormThreads * j;
+      if (i < K) xr[i] = v[j];
+    }
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kNormMaxJ; ++j) ss = __fmaf_rn(v[j], v[j], ss);
+  ss = warp_sum(ss);
+  __shared__ float red[kNormThreads / 32];
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  float tot = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kNormThreads / 32; ++i) tot += red[i];
+  const float sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(K)), eps)));
+#pragma unroll
+  for (int j = 0; j < kNormMaxJ; ++j) {
+    const int b = warp + 32 * j;
+    if (b < nb) store_act(a, b, t, quant_block32(__fmul_rn(__fmul_rn(v[j], sc), wv[j]), lane), lane);
   }
 }
 
@@ -190,7 +255,10 @@ void launch_quant_rows(const float* x, int64_t ldx, int n, int K, const ActQ& ac
 
 void launch_rmsnorm_quant(float* x, int64_t ldx, Slices add, const int32_t* rows, const float* w, float eps, int n,
                           int K, const ActQ& act, cudaStream_t s) {
-  k_rmsnorm_quant<<<act.nt8 * 8, 256, 0, s>>>(x, ldx, add, rows, w, eps, n, K, act);
+  if (K <= kNormThreads * kNormMaxJ)
+    k_rmsnorm_quant_wide<<<act.nt8 * 8, kNormThreads, 0, s>>>(x, ldx, add, rows, w, eps, n, K, act);
+  else
+    k_rmsnorm_quant<<<act.nt8 * 8, 256, 0, s>>>(x, ldx, add, rows, w, eps, n, K, act);
 }
 
 void launch_sum_slices(Slices src, int64_t ld, int n, int cols, float* dst, cudaStream_t s) {

@@ -11,6 +11,22 @@ def dev(torch, a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
 
+def exact_q8(monkeypatch, t=8):
+    """Q8_0 GEMMs keep malkin's exact int8 block dots and per-block float order (tcgen05 kind::i8, the default)."""
+    if t == 8:
+        monkeypatch.delenv("MALKIN_B200_Q8_GEMM", raising=False)
+
+
+def fp16_gemm_bound(oracle, t, w, rows, cols, x):
+    """Error bound of the fp16 Q8_0 GEMM, which multiplies fp16(q_w d_w) by fp16(q_x d_x) and accumulates in fp32:
+    each product carries two fp16 roundings (2^-11 relative each) and the sums fp32 rounding, so
+    |y - malkin| <= (2^-10 (1 + 2^-10) + 2 K 2^-24) * sum_k |a_k b_k| with a, b the dequantized operands."""
+    wd = np.stack([oracle.dequantize_row(t, w[r], cols) for r in range(rows)]).astype(np.float64)
+    xd = np.stack([(b["qs"].astype(np.float64) * b["d"].astype(np.float64)[:, None]).reshape(-1)
+                   for b in (oracle.quantize_row_q8(r) for r in x)])
+    return (np.abs(xd) @ np.abs(wd).T) * (2.0**-10 * (1 + 2.0**-10) + 2 * cols * 2.0**-24)
+
+
 def test_quantize_q8_bit_exact(mk, golden, torch_cuda):
     """BlockQ8 bit-identical to kern::quantize_row_q8 given the same floats (kernels_avx512.cpp:66-80)."""
     torch = torch_cuda
@@ -45,20 +61,23 @@ def test_block_dots_bit_exact(mk, oracle, golden, torch_cuda, t):
 
 
 @pytest.mark.parametrize("t", TYPES)
-def test_matmul_bit_exact_split1(mk, golden, torch_cuda, t):
+def test_matmul_bit_exact_split1(mk, golden, torch_cuda, monkeypatch, t):
     """split_k = 1 keeps malkin's block order per (row, token): y bit-identical to its compact panel kernels."""
+    exact_q8(monkeypatch, t)
     torch = torch_cuda
     w, x = golden[f"mm{t}_w"], golden[f"mm{t}_x"]
     W = mk.Weight(t, w, 35, 512)
-    assert W.device_bytes == ((35 + 15) // 16) * 16 * mk.row_bytes(t, 512)
+    quantum = 128 if t == 8 else 16  # Q8_0 streams in 128-row tensor-core tiles, K-quants in 16-row panels
+    assert W.device_bytes == ((35 + quantum - 1) // quantum) * quantum * mk.row_bytes(t, 512)
     y = torch.full((x.shape[0], 35), np.nan, dtype=torch.float32, device="cuda")
     W.matmul(dev(torch, x).data_ptr(), x.shape[0], y.data_ptr(), split_k=1)
     assert np.array_equal(y.cpu().numpy(), golden[f"mm{t}_y"])
 
 
 @pytest.mark.parametrize("t", TYPES)
-def test_matmul_split_k(mk, golden, torch_cuda, t):
+def test_matmul_split_k(mk, golden, torch_cuda, monkeypatch, t):
     """Split-K reassociates the block sum: same values within float rounding."""
+    exact_q8(monkeypatch, t)
     torch = torch_cuda
     w, x = golden[f"mm{t}_w"], golden[f"mm{t}_x"]
     W = mk.Weight(t, w, 35, 512)
@@ -71,8 +90,9 @@ def test_matmul_split_k(mk, golden, torch_cuda, t):
 
 @pytest.mark.parametrize("t", TYPES)
 @pytest.mark.parametrize("n", [1, 7, 8, 136, 150, 300])
-def test_matmul_shapes_vs_oracle(mk, oracle, torch_cuda, t, n):
+def test_matmul_shapes_vs_oracle(mk, oracle, torch_cuda, monkeypatch, t, n):
     """Ragged rows (not a multiple of 16), token counts across the 8-token tiles and the 144-token passes."""
+    exact_q8(monkeypatch, t)
     torch = torch_cuda
     from make_golden import random_rows
     rng = np.random.default_rng(n * 31 + t)
@@ -154,3 +174,68 @@ def test_attention_tree_batch_vs_oracle(mk, oracle, torch_cuda):
             want = oracle.attend(q[t, g * G * D:(g + 1) * G * D], G, D, k[g, base:], v[g, base:], ks[g, base:],
                                  vs[g, base:], nk, anc, scale)
             np.testing.assert_allclose(out[t, g * G * D:(g + 1) * G * D], want, rtol=3e-4, atol=3e-5)
+
+
+@pytest.mark.parametrize("rows,cols,n", [(128, 256, 16), (300, 512, 136), (257, 2048, 144), (130, 96, 256),
+                                         (64, 512, 257), (200, 1024, 433)])
+def test_q8_tensor_core_shapes_vs_oracle(mk, oracle, torch_cuda, monkeypatch, rows, cols, n):
+    """Q8_0 on tcgen05 kind::i8: partial 128-row tiles, K not a multiple of the 4-block stage, N = 16 .. 256 and
+    256-token passes; split 1 bit-identical to malkin's block order, and the exact block dots of the same MMAs."""
+    exact_q8(monkeypatch)
+    torch = torch_cuda
+    from make_golden import random_rows
+    rng = np.random.default_rng(rows * 7 + cols + n)
+    w = random_rows(rng, 8, rows, cols)
+    x = rng.uniform(-3, 3, (n, cols)).astype(np.float32)
+    W = mk.Weight(8, w, rows, cols)
+    y = torch.full((n, rows), np.nan, dtype=torch.float32, device="cuda")
+    W.matmul(dev(torch, x).data_ptr(), n, y.data_ptr(), split_k=1)
+    assert np.array_equal(y.cpu().numpy(), oracle.matmul(8, w, rows, cols, x))
+    dots = torch.zeros((rows, n, cols // 32), dtype=torch.int32, device="cuda")
+    W.block_dots(dev(torch, x).data_ptr(), n, dots.data_ptr())
+    assert np.array_equal(dots.cpu().numpy(), oracle.block_dots(8, w, rows, cols, x))
+    for split in (2, 5, 0):
+        y.fill_(np.nan)
+        W.matmul(dev(torch, x).data_ptr(), n, y.data_ptr(), split_k=split)
+        ref = oracle.matmul(8, w, rows, cols, x)
+        assert np.abs(y.cpu().numpy() - ref).max() <= 1e-5 * np.abs(ref).max()
+
+
+def test_q8_layouts_agree(mk, golden, torch_cuda, monkeypatch):
+    """The mma.sync panel kernel (MALKIN_B200_Q8_LAYOUT=panels) and the tcgen05 kernel give identical bits."""
+    torch = torch_cuda
+    w, x = golden["mm8_w"], golden["mm8_x"]
+    ys = []
+    exact_q8(monkeypatch)
+    for layout in ("panels", "tc"):
+        monkeypatch.setenv("MALKIN_B200_Q8_LAYOUT", layout)
+        W = mk.Weight(8, w, 35, 512)
+        y = torch.zeros((x.shape[0], 35), dtype=torch.float32, device="cuda")
+        W.matmul(dev(torch, x).data_ptr(), x.shape[0], y.data_ptr(), split_k=1)
+        ys.append(y.cpu().numpy())
+    assert np.array_equal(ys[0], ys[1]) and np.array_equal(ys[0], golden["mm8_y"])
+
+
+@pytest.mark.parametrize("rows,cols,n", [(128, 256, 16), (300, 512, 136), (257, 2048, 144), (130, 96, 256),
+                                         (64, 512, 257), (200, 1024, 433), (4096, 4096, 136)])
+def test_q8_fp16_gemm_within_bound(mk, oracle, torch_cuda, monkeypatch, rows, cols, n):
+    """The optional fp16 Q8_0 GEMM (MALKIN_B200_Q8_GEMM=fp16: tcgen05 kind::f16 on fp16(q d) operands, A from
+    TMEM) against malkin's exact result: every output within the fp16-operand error bound, at split 1, a forced
+    split and the automatic split."""
+    monkeypatch.setenv("MALKIN_B200_Q8_GEMM", "fp16")
+    torch = torch_cuda
+    from make_golden import random_rows
+    rng = np.random.default_rng(rows + 3 * cols + 5 * n)
+    w = random_rows(rng, 8, rows, cols)
+    x = rng.uniform(-3, 3, (n, cols)).astype(np.float32)
+    W = mk.Weight(8, w, rows, cols)
+    ref = oracle.matmul(8, w, rows, cols, x).astype(np.float64)
+    bound = fp16_gemm_bound(oracle, 8, w, rows, cols, x)
+    y = torch.full((n, rows), np.nan, dtype=torch.float32, device="cuda")
+    for split in (1, 5, 0):
+        y.fill_(np.nan)
+        W.matmul(dev(torch, x).data_ptr(), n, y.data_ptr(), split_k=split)
+        err = np.abs(y.cpu().numpy().astype(np.float64) - ref)
+        assert np.isfinite(err).all() and (err <= bound).all(), (split, float(np.nanmax(err)))
+        # typical error: a few fp16 roundings' worth relative to the typical output
+        assert np.sqrt((err**2).mean()) <= 1e-3 * np.sqrt((ref**2).mean()), split
