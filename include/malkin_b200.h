@@ -206,6 +206,18 @@ int mk_quantize_q8(const float* dev_x, int n, int64_t k, void* dev_blocks, void*
  * 0 = choose for speed. */
 int mk_matmul(const mk_weight* w, const float* dev_x, int n, float* dev_y, int split_k, void* stream);
 
+/* mk_matmul without any device allocation (no counterpart in the reference, which multiplies on the host): the
+ * quantized activations, split-K partial sums and status word live in a fixed 16 MiB scratch array of this library
+ * (a __device__ variable, one per device), so the call makes no cudaMalloc / cudaFree and never waits on the whole
+ * device the way cudaFree does. For callers that must not allocate per call: engines that reserve all HBM for the
+ * KV cache at start-up, and latency-bound loops that must not stall other streams. Same arguments and results as
+ * mk_matmul. Limits: about 108 bytes per token per 32 values of activations must fit (for example 256 tokens x
+ * 16384 values); split_k = 0 lowers the split until the partial sums fit, an explicit split_k whose partial sums do
+ * not fit is rejected with MK_ERR_ARG. Calls on one device share the scratch: calls that overlap in time (other
+ * streams, other threads) race, so serialise them. The first call on each device looks up the scratch address;
+ * make it before any stream capture. */
+int mk_matmul_noalloc(const mk_weight* w, const float* dev_x, int n, float* dev_y, int split_k, void* stream);
+
 /* Exact integer block dot products of the GEMM (gemm_avx512.cpp:83-98, 130-141, 179-199): dev_out[(r * n + t) *
  * nblk + b] = sum of w * x over block b (Q8_0, Q4_K: 32 values; Q6_K: 16 values, nblk = cols/16). */
 int mk_block_dots(const mk_weight* w, const float* dev_x, int n, int32_t* dev_out, void* stream);

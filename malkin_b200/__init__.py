@@ -173,6 +173,7 @@ lib.mk_weight_device_bytes.argtypes = [_vp]
 lib.mk_weight_device_bytes.restype = ctypes.c_int64
 lib.mk_quantize_q8.argtypes = [_vp, ctypes.c_int, ctypes.c_int64, _vp, _vp]
 lib.mk_matmul.argtypes = [_vp, _vp, ctypes.c_int, _vp, ctypes.c_int, _vp]
+lib.mk_matmul_noalloc.argtypes = [_vp, _vp, ctypes.c_int, _vp, ctypes.c_int, _vp]
 lib.mk_block_dots.argtypes = [_vp, _vp, ctypes.c_int, _vp, _vp]
 lib.mk_quantize_i8.argtypes = [_vp, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp]
 lib.mk_silu_mul.argtypes = [_vp, _vp, ctypes.c_int64, _vp]
@@ -184,7 +185,7 @@ EXPORTS = ("mk_last_error", "mk_version", "mk_synth_gguf", "mk_init", "mk_nccl_u
            "mk_load_gguf", "mk_alloc_kv", "mk_model_config_get", "mk_forward", "mk_move_kv", "mk_accept",
            "mk_rng_uniforms", "mk_verify_step", "mk_set_profile", "mk_stage_times", "mk_last_launch_count",
            "mk_stream", "mk_last_io_bytes", "mk_weight_upload", "mk_weight_free", "mk_weight_device_bytes", "mk_quantize_q8",
-           "mk_matmul", "mk_block_dots", "mk_quantize_i8", "mk_silu_mul", "mk_attention")
+           "mk_matmul", "mk_matmul_noalloc", "mk_block_dots", "mk_quantize_i8", "mk_silu_mul", "mk_attention")
 
 
 def version() -> str:
@@ -330,6 +331,10 @@ class Weight:
 
     def matmul(self, dev_x: int, n: int, dev_y: int, split_k: int = 0, stream: int = 0) -> None:
         _check(lib.mk_matmul(self._h, dev_x, n, dev_y, split_k, stream or None))
+
+    def matmul_noalloc(self, dev_x: int, n: int, dev_y: int, split_k: int = 0, stream: int = 0) -> None:
+        """matmul through the fixed per-device scratch (mk_matmul_noalloc): no device allocation per call."""
+        _check(lib.mk_matmul_noalloc(self._h, dev_x, n, dev_y, split_k, stream or None))
 
     def block_dots(self, dev_x: int, n: int, dev_out: int, stream: int = 0) -> None:
         _check(lib.mk_block_dots(self._h, dev_x, n, dev_out, stream or None))

@@ -306,6 +306,68 @@ int mk_matmul(const mk_weight* w, const float* dev_x, int n, float* dev_y, int s
   });
 }
 
+int mk_matmul_noalloc(const mk_weight* w, const float* dev_x, int n, float* dev_y, int split_k, void* stream) {
+  return guard(MK_ERR_ARG, [&] {
+    if (!w || !dev_x || !dev_y || n <= 0 || split_k < 0) throw mkb::ArgError("matmul_noalloc: bad argument");
+    if (current_device() != w->device)
+      throw mkb::ArgError("matmul_noalloc: the weight lives on device " + std::to_string(w->device) +
+                          ", the current device is " + std::to_string(current_device()));
+    cudaError_t e = cudaSuccess;
+    uint8_t* base = mkb::noalloc_scratch(&e);
+    mkb::cuda_check(e, "matmul_noalloc: scratch address");
+    const size_t cap = mkb::noalloc_scratch_bytes();
+    auto up = [](size_t b) { return (b + 255) / 256 * 256; };
+    // [status | qx | qc | dx | dsx | sh | split-K slices]
+    const int nt8 = mkb::act_tiles(n), npad = nt8 * 8;
+    const int64_t blocks = w->w.cols / 32;
+    const size_t qx = up(static_cast<size_t>(blocks) * npad * 32), f = up(static_cast<size_t>(blocks) * npad * 4);
+    const size_t act_end = 256 + 3 * qx + 3 * f;
+    if (act_end > cap)
+      throw mkb::ArgError("matmul_noalloc: " + std::to_string(n) + " tokens x " + std::to_string(w->w.cols) +
+                          " values need " + std::to_string(act_end) + " bytes of activations; the fixed scratch holds " +
+                          std::to_string(cap) + " (about 108 bytes per token per 32 values)");
+    const int64_t slice = static_cast<int64_t>(n) * w->w.rows;
+    const size_t room = cap - act_end;
+    auto fits = [&](int split) { return split <= 1 || static_cast<size_t>(split) * slice * 4 <= room; };
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    int split = mkb::gemm_slices(w->w, split_k > 0 ? split_k : mkb::gemm_split_for(w->w, sms));
+    if (!fits(split)) {
+      if (split_k > 0)
+        throw mkb::ArgError("matmul_noalloc: split_k " + std::to_string(split_k) + " needs " +
+                            std::to_string(static_cast<size_t>(split) * slice * 4) +
+                            " bytes of partial sums; the fixed scratch has " + std::to_string(room) + " left");
+      while (split > 1 && !fits(split)) split = mkb::gemm_slices(w->w, split - 1);
+      if (!fits(split)) split = 1;
+    }
+    cudaStream_t s = as_stream(stream);
+    int* status = reinterpret_cast<int*>(base);
+    mkb::ActQ act;
+    act.qx = base + 256;
+    if (mkb::q8_mode() == mkb::kQ8Exact)
+      act.qc = act.qx + qx;
+    else
+      act.xh = reinterpret_cast<uint16_t*>(act.qx + qx);  // 2 bytes per value
+    act.dx = reinterpret_cast<float*>(act.qx + 3 * qx);
+    act.dsx = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(act.dx) + f);
+    act.sh = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(act.dsx) + f);
+    act.nt8 = nt8;
+    float* slices = reinterpret_cast<float*>(base + act_end);
+    // the status word must start at zero; activations and slices are fully written before they are read
+    mkb::cuda_check(cudaMemsetAsync(status, 0, sizeof(int), s), "matmul_noalloc: clear status");
+    mkb::launch_quant_rows(dev_x, w->w.cols, n, static_cast<int>(w->w.cols), act, s);
+    float* out = split > 1 ? slices : dev_y;
+    mkb::launch_gemm(w->w, act, n, out, w->w.rows, slice, split, status, s);
+    if (split > 1) mkb::launch_sum_slices(mkb::Slices{out, split, slice}, w->w.rows, n, static_cast<int>(w->w.rows), dev_y, s);
+    mkb::cuda_check(cudaGetLastError(), "matmul_noalloc");
+    int st = 0;
+    mkb::cuda_check(cudaMemcpyAsync(&st, status, sizeof st, cudaMemcpyDeviceToHost, s), "matmul_noalloc: status");
+    mkb::cuda_check(cudaStreamSynchronize(s), "matmul_noalloc");
+    if (st != 0) throw mkb::TimeoutError("matmul_noalloc: device pipeline wait gave up");
+  });
+}
+
 int mk_block_dots(const mk_weight* w, const float* dev_x, int n, int32_t* dev_out, void* stream) {
   return guard(MK_ERR_ARG, [&] {
     if (!w || n <= 0) throw mkb::ArgError("block_dots: bad argument");

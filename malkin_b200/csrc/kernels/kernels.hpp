@@ -93,6 +93,11 @@ void launch_gemm_tc(const DevWeight& w, const ActQ& act, int n, float* y, int64_
 int gemm_tc_split_for(const DevWeight& w, int num_sms);
 int gemm_tc_slices(const DevWeight& w, int split);
 
+// ---- fixed scratch of the allocation-free entry point (noalloc.cu) ----
+// Bytes of the per-device scratch, and its address on the current device (nullptr and *err set on failure).
+size_t noalloc_scratch_bytes();
+uint8_t* noalloc_scratch(cudaError_t* err);
+
 // ---- attention (attention.cu) ----
 struct AttnLayer {
   int8_t* k;   // [kvh][n_rows][D]
