@@ -429,7 +429,10 @@ int mk_attention(const float* dev_q, int n, int H, int KV, int D, const int8_t* 
     mkb::AttnPlan p;
     p.n = n;
     p.n_sg = n_sg;
-    p.chunk = 256;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    p.chunk = mkb::attn_chunk_for(maxk, n_sg, KV, sms);
     p.n_chunks = (maxk + p.chunk - 1) / p.chunk;
     mkb::DevBuf tabs((sgf.size() + tsg.size() + sgm.size()) * 4);
     mkb::cuda_check(cudaMemcpy(tabs.get(), sgf.data(), sgf.size() * 4, cudaMemcpyHostToDevice), "attention");

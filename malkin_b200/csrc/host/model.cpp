@@ -400,9 +400,7 @@ void Model::alloc_kv(int n_ctx, int n_seq, int max_batch) {
   // attention plan geometry
   const int G = c.n_head / c.n_head_kv;
   sg_rows_ = std::max(1, attn_qmax() / G);
-  chunk_ = 256;
-  n_chunks_ = (n_ctx + chunk_ - 1) / chunk_;
-  max_sg_ = 0;
+  part_cap_ = 0;
   attn_part_ = DevBuf();
   meta_cap_ = 0;
   ensure_meta(static_cast<size_t>(max_batch) * 16);
@@ -567,13 +565,16 @@ void Model::forward(const mk_batch_token* batch, int n, float* host_logits) {
   sgfirst.push_back(n);
   const int m = static_cast<int>(outrows.size());
   ensure_meta(anc.size());
-  if (n_sg > max_sg_) {
+  // key chunks of the split attention: a function of n_sg (part of the graph key), about two CTAs per SM
+  const int chunk = attn_chunk_for(n_ctx_, n_sg, KVl_, num_sms_);
+  const int n_chunks = (n_ctx_ + chunk - 1) / chunk;
+  const size_t part_need = attn_part_floats(n_sg, n_chunks, KVl_, c.head_dim);
+  if (part_need > part_cap_) {
     for (auto& [k, g] : graphs_) cudaGraphExecDestroy(g);
     graphs_.clear();
-    max_sg_ = std::max(n_sg, max_sg_ * 2);
-    max_sg_ = std::min(max_sg_, max_batch_);
-    max_sg_ = std::max(max_sg_, n_sg);
-    attn_part_ = DevBuf(attn_part_floats(max_sg_, n_chunks_, KVl_, c.head_dim) * 4);
+    graph_nodes_.clear();
+    part_cap_ = std::max(part_need, part_cap_ * 2);
+    attn_part_ = DevBuf(part_cap_ * 4);
   }
   // pinned staging -> one copy
   const size_t MB = static_cast<size_t>(max_batch_);
@@ -594,8 +595,8 @@ void Model::forward(const mk_batch_token* batch, int n, float* host_logits) {
   h2d_bytes_ += static_cast<int64_t>((10 * MB + 2 + anc.size()) * 4);
   plan_.n = n;
   plan_.n_sg = n_sg;
-  plan_.chunk = chunk_;
-  plan_.n_chunks = n_chunks_;
+  plan_.chunk = chunk;
+  plan_.n_chunks = n_chunks;
   plan_.sg_first = d_sgfirst_;
   plan_.kv_base = d_kvbase_;
   plan_.n_keys = d_nkeys_;

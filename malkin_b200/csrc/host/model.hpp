@@ -163,7 +163,8 @@ class Model {
           *d_ancoff_ = nullptr, *d_sgfirst_ = nullptr, *d_toksg_ = nullptr, *d_outrows_ = nullptr, *d_sgmaxk_ = nullptr, *d_anc_ = nullptr;
   DevBuf attn_part_;
   AttnPlan plan_;
-  int n_chunks_ = 0, chunk_ = 256, sg_rows_ = 0, max_sg_ = 0;
+  int sg_rows_ = 0;
+  size_t part_cap_ = 0;  // floats of attn_part_
 
   // last forward: logits row of each batch index (-1: none), tokens
   std::vector<int> lrow_;

@@ -12,6 +12,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include <cfloat>
 
 #include "common.cuh"
@@ -101,6 +103,22 @@ struct PartArgs {
   AttnPlan p;
 };
 
+// e^x for the attention softmax through the hardware base-2 exponential (exp2f); its relative error (a few ulp)
+// is far inside the attention tolerance, and it costs a few instructions instead of a polynomial.
+__device__ __forceinline__ float exp_fast(float x) { return exp2f(__fmul_rn(x, 1.4426950408889634f)); }
+
+// Four int8 values (one word) -> two fp16x2, exactly: the bytes become fp16 1152 + q (0x6400 | (q + 128)), one
+// subtraction recovers q.
+__device__ __forceinline__ void i8x4_to_h2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t u = w ^ 0x80808080u;
+  const uint32_t a = __byte_perm(u, 0x64646464u, 0x4140), b = __byte_perm(u, 0x64646464u, 0x4342);
+  const __half2 bias = __float2half2_rn(1152.0f);
+  const __half2 ha = __hsub2(*reinterpret_cast<const __half2*>(&a), bias);
+  const __half2 hb = __hsub2(*reinterpret_cast<const __half2*>(&b), bias);
+  lo = *reinterpret_cast<const uint32_t*>(&ha);
+  hi = *reinterpret_cast<const uint32_t*>(&hb);
+}
+
 __device__ __forceinline__ uint32_t pack_h2(__half a, __half b) {
   return static_cast<uint32_t>(__half_as_ushort(a)) | (static_cast<uint32_t>(__half_as_ushort(b)) << 16);
 }
@@ -138,7 +156,7 @@ struct AttSmem {
 };
 
 template <int D>
-__global__ void __launch_bounds__(kThreads) k_attn_part(PartArgs a) {
+__global__ void __launch_bounds__(kThreads, 2) k_attn_part(PartArgs a) {  // two CTAs per SM
   using SM = AttSmem<D>;
   constexpr int DP = SM::DP;
   constexpr int NDT = D / 8;          // d tiles (n8) of O
@@ -224,12 +242,14 @@ __global__ void __launch_bounds__(kThreads) k_attn_part(PartArgs a) {
         const bool isv = i >= kKT * CH;
         const int ii = isv ? i - kKT * CH : i;
         const int j = ii / CH, ch = ii % CH;
-        const int8_t* b = reinterpret_cast<const int8_t*>(&pre[u]);
         __half* dst = (isv ? Vh : Kh) + j * DP + ch * 16;
-#pragma unroll
-        for (int e = 0; e < 16; e += 2)
-          *reinterpret_cast<uint32_t*>(dst + e) =
-              pack_h2(__int2half_rn(static_cast<int>(b[e])), __int2half_rn(static_cast<int>(b[e + 1])));
+        uint4 h0, h1;
+        i8x4_to_h2(static_cast<uint32_t>(pre[u].x), h0.x, h0.y);
+        i8x4_to_h2(static_cast<uint32_t>(pre[u].y), h0.z, h0.w);
+        i8x4_to_h2(static_cast<uint32_t>(pre[u].z), h1.x, h1.y);
+        i8x4_to_h2(static_cast<uint32_t>(pre[u].w), h1.z, h1.w);
+        reinterpret_cast<uint4*>(dst)[0] = h0;
+        reinterpret_cast<uint4*>(dst)[1] = h1;
       }
     }
     if (tid < kKT) {
@@ -263,15 +283,22 @@ __global__ void __launch_bounds__(kThreads) k_attn_part(PartArgs a) {
         const int qr = r0 + (lane & 15), qc = kk * 16 + (lane >> 4) * 8;
         ldsm_x4(ah, Qh + qr * DP + qc);
         ldsm_x4(al, Ql + qr * DP + qc);
+        uint32_t b[kKT / 16][4];
 #pragma unroll
         for (int nj = 0; nj < kKT / 16; ++nj) {  // two n8 tiles per ldmatrix.x4
-          uint32_t b[4];
           const int kr = nj * 16 + (lane >> 4) * 8 + (lane & 7), kc = kk * 16 + ((lane >> 3) & 1) * 8;
-          ldsm_x4(b, Kh + kr * DP + kc);
-          mma_f16(sacc[2 * nj], ah, b[0], b[1]);
-          mma_f16(sacc[2 * nj], al, b[0], b[1]);
-          mma_f16(sacc[2 * nj + 1], ah, b[2], b[3]);
-          mma_f16(sacc[2 * nj + 1], al, b[2], b[3]);
+          ldsm_x4(b[nj], Kh + kr * DP + kc);
+        }
+        // the hi pass over every n tile, then the lo pass: dependent MMAs on one accumulator are 8 apart
+#pragma unroll
+        for (int nj = 0; nj < kKT / 16; ++nj) {
+          mma_f16(sacc[2 * nj], ah, b[nj][0], b[nj][1]);
+          mma_f16(sacc[2 * nj + 1], ah, b[nj][2], b[nj][3]);
+        }
+#pragma unroll
+        for (int nj = 0; nj < kKT / 16; ++nj) {
+          mma_f16(sacc[2 * nj], al, b[nj][0], b[nj][1]);
+          mma_f16(sacc[2 * nj + 1], al, b[nj][2], b[nj][3]);
         }
       }
       // scale, mask, online softmax
@@ -295,9 +322,9 @@ __global__ void __launch_bounds__(kThreads) k_attn_part(PartArgs a) {
       tmB = fmaxf(tmB, __shfl_xor_sync(0xffffffffu, tmB, 2));
       const float nmA = fmaxf(mA, tmA), nmB = fmaxf(mB, tmB);
       const float alA = (mA == -INFINITY || nmA == -INFINITY) ? (nmA == -INFINITY ? 1.0f : 0.0f)
-                                                              : exp_malkin(__fsub_rn(mA, nmA));
+                                                              : exp_fast(__fsub_rn(mA, nmA));
       const float alB = (mB == -INFINITY || nmB == -INFINITY) ? (nmB == -INFINITY ? 1.0f : 0.0f)
-                                                              : exp_malkin(__fsub_rn(mB, nmB));
+                                                              : exp_fast(__fsub_rn(mB, nmB));
       mA = nmA;
       mB = nmB;
       float sA = 0.0f, sB = 0.0f;
@@ -309,7 +336,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_part(PartArgs a) {
         for (int e = 0; e < 4; ++e) {
           const bool rowA = e < 2;
           const float x = sacc[j][e], m = rowA ? mA : mB;
-          const float p = x == -INFINITY ? 0.0f : exp_malkin(__fsub_rn(x, m));
+          const float p = x == -INFINITY ? 0.0f : exp_fast(__fsub_rn(x, m));
           if (rowA)
             sA += p;
           else
@@ -341,15 +368,17 @@ __global__ void __launch_bounds__(kThreads) k_attn_part(PartArgs a) {
       // O += P' V
 #pragma unroll
       for (int kq = 0; kq < kKT / 16; ++kq) {
+        // hi pass over every d tile, then the lo pass (V fragments loaded again): dependent MMAs 16 apart
 #pragma unroll
-        for (int dj = 0; dj < NDT / 2; ++dj) {  // two d tiles per ldmatrix.x4.trans
-          uint32_t b[4];
-          const int vr = kq * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, vc = dj * 16 + (lane >> 4) * 8;
-          ldsm_x4_t(b, Vh + vr * DP + vc);
-          mma_f16(o[2 * dj], ph[kq], b[0], b[1]);
-          mma_f16(o[2 * dj], pl[kq], b[0], b[1]);
-          mma_f16(o[2 * dj + 1], ph[kq], b[2], b[3]);
-          mma_f16(o[2 * dj + 1], pl[kq], b[2], b[3]);
+        for (int pass = 0; pass < 2; ++pass) {
+#pragma unroll
+          for (int dj = 0; dj < NDT / 2; ++dj) {  // two d tiles per ldmatrix.x4.trans
+            uint32_t b[4];
+            const int vr = kq * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, vc = dj * 16 + (lane >> 4) * 8;
+            ldsm_x4_t(b, Vh + vr * DP + vc);
+            mma_f16(o[2 * dj], pass ? pl[kq] : ph[kq], b[0], b[1]);
+            mma_f16(o[2 * dj + 1], pass ? pl[kq] : ph[kq], b[2], b[3]);
+          }
         }
       }
     }
@@ -485,6 +514,7 @@ void run_attention(const float* q, int H, int KV, float scale, const AttnLayer& 
   cudaGetDevice(&dev);
   if (dev < 64 && !attr[dev]) {
     cudaFuncSetAttribute(k_attn_part<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    cudaFuncSetAttribute(k_attn_part<D>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     attr[dev] = true;
   }
   if (p.n_sg > 0 && p.n_chunks > 0) {
@@ -498,6 +528,13 @@ void run_attention(const float* q, int H, int KV, float scale, const AttnLayer& 
 }  // namespace
 
 int attn_qmax() { return kQMax; }
+
+int attn_chunk_for(int max_keys, int n_sg, int KV, int num_sms) {
+  const int pairs = std::max(1, n_sg * KV);
+  const int target = std::max(1, 2 * num_sms / pairs);  // chunks per (sub-group, kv head)
+  const int per = (std::max(1, max_keys) + target - 1) / target;
+  return std::max(kKT, (per + kKT - 1) / kKT * kKT);
+}
 
 size_t attn_part_floats(int n_sg, int n_chunks, int KV, int D) {
   return static_cast<size_t>(n_sg) * n_chunks * KV * kQMax * (D + 2);

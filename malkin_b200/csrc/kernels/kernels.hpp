@@ -129,6 +129,9 @@ struct AttnPlan {
 };
 // Query vectors (rows x G) one sub-group may hold.
 int attn_qmax();
+// Keys per attention chunk (a multiple of 64) for sequences of up to max_keys keys, n_sg sub-groups and KV heads: about
+// two CTAs per SM in total, at least 64 keys per chunk.
+int attn_chunk_for(int max_keys, int n_sg, int KV, int num_sms);
 size_t attn_part_floats(int n_sg, int n_chunks, int KV, int D);
 void launch_attention(const float* q, int H, int KV, int D, float scale, const AttnLayer& L, const AttnPlan& p,
                       float* out, cudaStream_t s);
