@@ -249,7 +249,7 @@ int mk_weight_upload(int type, const void* host_rows, int64_t rows, int64_t cols
     auto w = std::make_unique<mk_weight>();
     w->device = current_device();
     const size_t rb = mkb::row_bytes(static_cast<uint32_t>(type), cols);
-    const int layout = mkb::weight_layout(static_cast<uint32_t>(type));
+    const int layout = mkb::weight_layout(static_cast<uint32_t>(type), rows, cols);
     const size_t bytes = mkb::repack_layout_bytes(static_cast<uint32_t>(type), layout, rows, cols / u);
     std::vector<uint8_t> staging(bytes);
     mkb::repack_layout(static_cast<uint32_t>(type), layout, static_cast<const uint8_t*>(host_rows), rb, rows, 0,

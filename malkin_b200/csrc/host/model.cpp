@@ -163,7 +163,7 @@ void Model::load(const std::string& path) {
     const int u = kunit_values(t->type);
     if (c0 % u || nc % u) throw ArgError("tensor parallel: shard of " + t->name + " not block aligned");
     total = align_up(total, 256);
-    const int layout = weight_layout(t->type);
+    const int layout = weight_layout(t->type, nr, nc);
     pieces.push_back({t, r0, nr, c0, nc, total, layout});
     total += repack_layout_bytes(t->type, layout, nr, nc / u);
     weight_bytes_ += static_cast<int64_t>(nr) * static_cast<int64_t>(row_bytes(t->type, nc));

@@ -171,10 +171,15 @@ void repack_tc(const uint8_t* src, size_t src_stride, int64_t rows, int64_t bloc
   });
 }
 
-int weight_layout(uint32_t type) {
+int weight_layout(uint32_t type, int64_t rows, int64_t cols) {
   if (type != kQ8_0) return kLayoutPanels;
   const char* e = std::getenv("MALKIN_B200_Q8_LAYOUT");
-  return e && std::string(e) == "panels" ? kLayoutPanels : kLayoutTc;
+  if (e && std::string(e) == "panels") return kLayoutPanels;
+  if (e && std::string(e) == "tc") return kLayoutTc;
+  // Measured on B200 at 136 tokens (8B shapes): the tcgen05 kernel wins on q|k|v and the attention output
+  // (<= 8192 rows, K <= 8192), the mma.sync panel kernel on the wide ffn gate / up, the deep ffn down and the
+  // vocabulary head. Both give identical results.
+  return rows <= 8192 && cols <= 8192 ? kLayoutTc : kLayoutPanels;
 }
 
 int layout_row_quantum(int layout) { return layout == kLayoutTc ? kTcRows : kPanelRows; }

@@ -15,9 +15,10 @@ void repack(uint32_t type, const uint8_t* src, size_t src_stride, int64_t rows, 
 size_t repack_tc_bytes(int64_t rows, int64_t blocks);
 void repack_tc(const uint8_t* src, size_t src_stride, int64_t rows, int64_t block0, int64_t blocks, uint8_t* dst,
                int n_threads);
-// The layout the GEMMs stream `type` in (kLayoutTc / kLayoutPanels of kernels.hpp): the tensor-core tile layout for
-// Q8_0, unless the environment sets MALKIN_B200_Q8_LAYOUT=panels (the mma.sync panel kernel); panels otherwise.
-int weight_layout(uint32_t type);
+// The layout the GEMMs stream a rows x cols weight of `type` in (kLayoutTc / kLayoutPanels of kernels.hpp): for
+// Q8_0 the tensor-core tile layout or the mma.sync panels by shape (MALKIN_B200_Q8_LAYOUT=tc|panels forces one);
+// panels for the K-quants.
+int weight_layout(uint32_t type, int64_t rows, int64_t cols);
 // Rows a piece must hold for the next piece to continue the same weight (fused q|k|v, gate|up) in `layout`.
 int layout_row_quantum(int layout);
 size_t repack_layout_bytes(uint32_t type, int layout, int64_t rows, int64_t units);
