@@ -122,6 +122,18 @@ __device__ __forceinline__ float sum_strided16(const float* p, int n, int64_t st
   return r;
 }
 
+// The same for a slice count fixed at compile time (no predicates): loads first, then the sum in index order.
+template <int NS>
+__device__ __forceinline__ float sum_strided(const float* p, int64_t stride) {
+  float v[NS > 0 ? NS : 1];
+#pragma unroll
+  for (int i = 0; i < NS; ++i) v[i] = p[i * stride];
+  float r = NS > 0 ? v[0] : 0.0f;
+#pragma unroll
+  for (int i = 1; i < NS; ++i) r = __fadd_rn(r, v[i]);
+  return r;
+}
+
 // e^x as malkin computes it for softmax and SiLU (kernels_avx512.cpp:186-202): clamp below at -87, Cody-Waite
 // reduction with ln 2 split in two, degree-6 Taylor polynomial in Horner form with fused multiply-adds, then
 // scaling by 2^n. (malkin's own algorithm, restated, so both sides exponentiate identically.)

@@ -8,6 +8,8 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <array>
+#include <utility>
 
 #include "common.cuh"
 #include "kernels.hpp"
@@ -131,6 +133,7 @@ __global__ void k_rmsnorm_quant(float* __restrict__ x, int64_t ldx, Slices add, 
 // values i, i + 1024, ..., so warp w's lanes already hold block w + 32 j for the quantization pass, and every load
 // of the row (and of its residual slices) is in flight at once.
 constexpr int kNormThreads = 1024, kNormMaxJ = 8;
+template <int NS>  // residual slices added first (add.n == NS)
 __global__ void __launch_bounds__(kNormThreads) k_rmsnorm_quant_wide(float* __restrict__ x, int64_t ldx, Slices add,
                                                                      const int32_t* __restrict__ rows,
                                                                      const float* __restrict__ w, float eps, int n,
@@ -150,11 +153,11 @@ __global__ void __launch_bounds__(kNormThreads) k_rmsnorm_quant_wide(float* __re
     v[j] = i < K ? xr[i] : 0.0f;
     wv[j] = i < K ? w[i] : 0.0f;
   }
-  if (add.n > 0) {
+  if constexpr (NS > 0) {
 #pragma unroll
     for (int j = 0; j < kNormMaxJ; ++j) {
       const int i = threadIdx.x + kNormThreads * j;
-      if (i < K) v[j] = __fadd_rn(v[j], sum_strided16(add.p + static_cast<size_t>(r) * ldx + i, add.n, add.stride));
+      if (i < K) v[j] = __fadd_rn(v[j], sum_strided<NS>(add.p + static_cast<size_t>(r) * ldx + i, add.stride));
     }
 #pragma unroll
     for (int j = 0; j < kNormMaxJ; ++j) {
@@ -182,7 +185,8 @@ __global__ void __launch_bounds__(kNormThreads) k_rmsnorm_quant_wide(float* __re
 
 __device__ __forceinline__ float sum_slices(const Slices& s, size_t off) { return sum_strided16(s.p + off, s.n, s.stride); }
 
-// grid (ceil(nb / 8), npad), block 256.
+// grid (ceil(nb / 8), npad), block 256; NS = gu.n slices.
+template <int NS>
 __global__ void k_silu_quant(Slices gu, int64_t ld, int F, int n, ActQ a) {
   const int lane = threadIdx.x & 31, b = blockIdx.x * 8 + (threadIdx.x >> 5), t = blockIdx.y;
   const int nb = F / 32;
@@ -192,7 +196,8 @@ __global__ void k_silu_quant(Slices gu, int64_t ld, int F, int n, ActQ a) {
     return;
   }
   const size_t row = static_cast<size_t>(t) * ld;
-  const float g = sum_slices(gu, row + b * 32 + lane), u = sum_slices(gu, row + F + b * 32 + lane);
+  const float g = sum_strided<NS>(gu.p + row + b * 32 + lane, gu.stride);
+  const float u = sum_strided<NS>(gu.p + row + F + b * 32 + lane, gu.stride);
   const float e = exp_malkin(__fsub_rn(0.0f, g));
   const float h = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, e)), u);
   store_act(a, b, t, quant_block32(h, lane), lane);
@@ -245,6 +250,16 @@ __global__ void k_silu_mul(float* __restrict__ g, const float* __restrict__ u, i
   }
 }
 
+template <int... I>
+constexpr auto norm_table(std::integer_sequence<int, I...>) {
+  return std::array<void (*)(float*, int64_t, Slices, const int32_t*, const float*, float, int, int, ActQ),
+                    sizeof...(I)>{&k_rmsnorm_quant_wide<I>...};
+}
+template <int... I>
+constexpr auto silu_table(std::integer_sequence<int, I...>) {
+  return std::array<void (*)(Slices, int64_t, int, int, ActQ), sizeof...(I)>{&k_silu_quant<I + 1>...};
+}
+
 }  // namespace
 
 void launch_quant_rows(const float* x, int64_t ldx, int n, int K, const ActQ& act, cudaStream_t s) {
@@ -255,8 +270,9 @@ void launch_quant_rows(const float* x, int64_t ldx, int n, int K, const ActQ& ac
 
 void launch_rmsnorm_quant(float* x, int64_t ldx, Slices add, const int32_t* rows, const float* w, float eps, int n,
                           int K, const ActQ& act, cudaStream_t s) {
-  if (K <= kNormThreads * kNormMaxJ)
-    k_rmsnorm_quant_wide<<<act.nt8 * 8, kNormThreads, 0, s>>>(x, ldx, add, rows, w, eps, n, K, act);
+  static constexpr auto fns = norm_table(std::make_integer_sequence<int, 17>{});
+  if (K <= kNormThreads * kNormMaxJ && add.n >= 0 && add.n <= 16)
+    fns[add.n]<<<act.nt8 * 8, kNormThreads, 0, s>>>(x, ldx, add, rows, w, eps, n, K, act);
   else
     k_rmsnorm_quant<<<act.nt8 * 8, 256, 0, s>>>(x, ldx, add, rows, w, eps, n, K, act);
 }
@@ -270,7 +286,8 @@ void launch_sum_slices(Slices src, int64_t ld, int n, int cols, float* dst, cuda
 void launch_silu_quant(Slices gu, int64_t ld, int F, int n, const ActQ& act, cudaStream_t s) {
   const int nb = F / 32;
   dim3 grid((nb + 7) / 8, act.nt8 * 8);
-  k_silu_quant<<<grid, 256, 0, s>>>(gu, ld, F, n, act);
+  static constexpr auto fns = silu_table(std::make_integer_sequence<int, 16>{});
+  if (gu.n >= 1 && gu.n <= 16) fns[gu.n - 1]<<<grid, 256, 0, s>>>(gu, ld, F, n, act);
 }
 
 void launch_quant_blockq8(const float* x, int n, int64_t K, void* blocks, cudaStream_t s) {
