@@ -108,6 +108,16 @@ int mk_load_gguf(mk_ctx* ctx, const char* path);
 int mk_alloc_kv(mk_ctx* ctx, int n_ctx, int n_seq, int max_batch);
 int mk_model_config_get(const mk_ctx* ctx, mk_model_config* out);
 
+/* The slice of a qwen3 GGUF that tensor-parallel rank tp_rank of tp_size holds (host only, no device; no counterpart
+ * in malkin, which runs on one host): q heads [head0, head0 + heads) and kv heads [kv_head0, ...) of the column-split
+ * q / k / v, ffn rows [ffn0, ffn0 + ffn) of gate / up (and the matching ffn_down columns) in whole ffn_down blocks,
+ * vocabulary rows [vocab0, vocab0 + vocab) of the LM head. */
+typedef struct mk_tp_shard {
+  int32_t head0, heads, kv_head0, kv_heads, ffn0, ffn;
+  int64_t vocab0, vocab;
+} mk_tp_shard;
+int mk_tp_shard_of(const char* gguf_path, int tp_size, int tp_rank, mk_tp_shard* out);
+
 /* Model::forward(const BatchToken*, n, float* logits) (model.cpp:379-422): same validation, same key sets
  * (prefix + tree ancestors), same KV writes. Logits of the rows with .logits set stay on the device for
  * mk_accept; host_logits (nullable) also receives them, n_vocab floats per row in batch order. */

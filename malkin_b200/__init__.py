@@ -173,6 +173,23 @@ lib.mk_weight_device_bytes.argtypes = [_vp]
 lib.mk_weight_device_bytes.restype = ctypes.c_int64
 lib.mk_quantize_q8.argtypes = [_vp, ctypes.c_int, ctypes.c_int64, _vp, _vp]
 lib.mk_matmul.argtypes = [_vp, _vp, ctypes.c_int, _vp, ctypes.c_int, _vp]
+
+
+class TpShard(ctypes.Structure):
+    """mk_tp_shard: the slice of the model one tensor-parallel rank holds."""
+    _fields_ = [("head0", ctypes.c_int32), ("heads", ctypes.c_int32), ("kv_head0", ctypes.c_int32),
+                ("kv_heads", ctypes.c_int32), ("ffn0", ctypes.c_int32), ("ffn", ctypes.c_int32),
+                ("vocab0", ctypes.c_int64), ("vocab", ctypes.c_int64)]
+
+
+lib.mk_tp_shard_of.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.POINTER(TpShard)]
+
+
+def tp_shard_of(path: str, tp_size: int, tp_rank: int) -> TpShard:
+    """Shard geometry of rank tp_rank of tp_size for the GGUF at path (host only)."""
+    out = TpShard()
+    _check(lib.mk_tp_shard_of(path.encode(), tp_size, tp_rank, ctypes.byref(out)))
+    return out
 lib.mk_matmul_noalloc.argtypes = [_vp, _vp, ctypes.c_int, _vp, ctypes.c_int, _vp]
 lib.mk_block_dots.argtypes = [_vp, _vp, ctypes.c_int, _vp, _vp]
 lib.mk_quantize_i8.argtypes = [_vp, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp]
@@ -184,7 +201,7 @@ lib.mk_attention.argtypes = [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctyp
 EXPORTS = ("mk_last_error", "mk_version", "mk_synth_gguf", "mk_init", "mk_nccl_unique_id", "mk_shutdown",
            "mk_load_gguf", "mk_alloc_kv", "mk_model_config_get", "mk_forward", "mk_move_kv", "mk_accept",
            "mk_rng_uniforms", "mk_verify_step", "mk_set_profile", "mk_stage_times", "mk_last_launch_count",
-           "mk_stream", "mk_last_io_bytes", "mk_weight_upload", "mk_weight_free", "mk_weight_device_bytes", "mk_quantize_q8",
+           "mk_stream", "mk_last_io_bytes", "mk_tp_shard_of", "mk_weight_upload", "mk_weight_free", "mk_weight_device_bytes", "mk_quantize_q8",
            "mk_matmul", "mk_matmul_noalloc", "mk_block_dots", "mk_quantize_i8", "mk_silu_mul", "mk_attention")
 
 

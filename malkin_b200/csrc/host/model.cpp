@@ -80,9 +80,7 @@ Model::~Model() {
 // ---------------------------------------------------------------------------------------------------------------
 // load: read_config (model.cpp:177-200) + Model::Model (model.cpp:211-251) + pack (model.cpp:262-277), per shard.
 // ---------------------------------------------------------------------------------------------------------------
-void Model::load(const std::string& path) {
-  cuda_check(cudaSetDevice(device_), "cudaSetDevice");
-  Gguf f(path);
+ModelCfg read_config(const Gguf& f) {
   const std::string arch = f.get_str("general.architecture").value_or("");
   if (arch != "qwen3") throw ArgError("architecture '" + arch + "' unsupported (supported: qwen3)");
   auto need = [&](const std::string& k) {
@@ -103,7 +101,39 @@ void Model::load(const std::string& path) {
   if (c.head_dim % 32 || c.n_head % c.n_head_kv) throw ArgError("model: unsupported head layout");
   if (c.head_dim != 64 && c.head_dim != 128 && c.head_dim != 256)
     throw UnsupportedError("unsupported: head_dim " + std::to_string(c.head_dim) + " (64, 128, 256)");
+  const Tensor* out = f.tensor("output.weight");
+  if (!out) out = f.tensor("token_embd.weight");  // tied embeddings
+  if (!out) throw ArgError("model: tensor token_embd.weight missing");
+  c.n_vocab = static_cast<int>(out->rows());
+  return c;
+}
 
+TpShard tp_shard(const ModelCfg& c, int ffn_unit, int tp, int rank) {
+  if (tp < 1 || rank < 0 || rank >= tp) throw ArgError("tensor parallel: bad rank " + std::to_string(rank) + " of " +
+                                                       std::to_string(tp));
+  if (c.n_head % tp || c.n_head_kv % tp)
+    throw ArgError("tensor parallel: " + std::to_string(tp) + " ranks do not divide the heads");
+  if (ffn_unit <= 0 || c.n_ff % ffn_unit) throw ArgError("model: n_ff not a multiple of the ffn_down block");
+  TpShard s;
+  s.heads = c.n_head / tp;
+  s.head0 = rank * s.heads;
+  s.kv_heads = c.n_head_kv / tp;
+  s.kv_head0 = rank * s.kv_heads;
+  // ffn rows in whole k-units of ffn_down (32 or 256 values), as even as the units allow
+  const int nfu = c.n_ff / ffn_unit;
+  const int fu0 = static_cast<int>(static_cast<int64_t>(rank) * nfu / tp);
+  const int fu1 = static_cast<int>(static_cast<int64_t>(rank + 1) * nfu / tp);
+  s.ffn0 = fu0 * ffn_unit;
+  s.ffn = (fu1 - fu0) * ffn_unit;
+  s.vocab0 = static_cast<int64_t>(rank) * c.n_vocab / tp;
+  s.vocab = static_cast<int64_t>(rank + 1) * c.n_vocab / tp - s.vocab0;
+  return s;
+}
+
+void Model::load(const std::string& path) {
+  cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+  Gguf f(path);
+  ModelCfg c = read_config(f);
   auto weight = [&](const std::string& name, bool required) -> const Tensor* {
     const Tensor* t = f.tensor(name);
     if (!t) {
@@ -122,31 +152,25 @@ void Model::load(const std::string& path) {
   const Tensor* tok = weight("token_embd.weight", true);
   const Tensor* out = weight("output.weight", false);
   if (!out) out = tok;  // tied embeddings
-  c.n_vocab = static_cast<int>(out->rows());
   cfg_ = c;
   const int tp = tp_size_, r = tp_rank_;
   const int D = c.head_dim, E = c.n_embd;
-  if (c.n_head % tp || c.n_head_kv % tp)
-    throw ArgError("tensor parallel: " + std::to_string(tp) + " ranks do not divide the heads");
-  Hl_ = c.n_head / tp;
-  KVl_ = c.n_head_kv / tp;
 
   auto check_mat = [&](const Tensor* t) {
     if (!repack_supported(t->type))
       throw UnsupportedError(std::string("unsupported: tensor ") + t->name + " has type " + type_name(t->type) +
                                " (this path streams Q8_0 Q4_K Q6_K)");
   };
-  // ffn split in whole k-units of ffn_down (32 or 256 values)
+  // shard geometry (tensor parallel): heads, ffn rows in whole k-units of ffn_down, vocabulary rows
   const Tensor* down0 = weight("blk.0.ffn_down.weight", true);
   check_mat(down0);
-  const int fu = kunit_values(down0->type);
-  if (c.n_ff % fu) throw ArgError("model: n_ff not a multiple of the ffn_down block");
-  const int nfu = c.n_ff / fu;
-  const int fu0 = static_cast<int>(static_cast<int64_t>(r) * nfu / tp), fu1 = static_cast<int>(static_cast<int64_t>(r + 1) * nfu / tp);
-  F0_ = fu0 * fu;
-  Fl_ = (fu1 - fu0) * fu;
-  V0_ = static_cast<int64_t>(r) * c.n_vocab / tp;
-  Vl_ = static_cast<int64_t>(r + 1) * c.n_vocab / tp - V0_;
+  const TpShard sh = tp_shard(c, kunit_values(down0->type), tp, r);
+  Hl_ = sh.heads;
+  KVl_ = sh.kv_heads;
+  F0_ = sh.ffn0;
+  Fl_ = sh.ffn;
+  V0_ = sh.vocab0;
+  Vl_ = sh.vocab;
   const int64_t HDl = static_cast<int64_t>(Hl_) * D, KDl = static_cast<int64_t>(KVl_) * D;
 
   // Device byte plan.

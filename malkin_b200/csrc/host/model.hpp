@@ -14,6 +14,7 @@
 
 #include "../../../include/malkin_b200.h"
 #include "../kernels/kernels.hpp"
+#include "gguf.hpp"
 
 namespace mkb {
 
@@ -65,6 +66,15 @@ struct TimeoutError : std::runtime_error {      // MK_ERR_TIMEOUT: a device-side
 
 // Throws CudaError with the CUDA error string.
 void cuda_check(cudaError_t e, const char* what);
+
+// The config of a qwen3 GGUF (read_config, model.cpp:78-101), and the slice of it one tensor-parallel rank holds:
+// q / kv heads (column split), ffn rows in whole k-units of ffn_down, vocabulary rows (split of the LM head).
+ModelCfg read_config(const Gguf& f);
+struct TpShard {
+  int head0 = 0, heads = 0, kv_head0 = 0, kv_heads = 0, ffn0 = 0, ffn = 0;
+  int64_t vocab0 = 0, vocab = 0;
+};
+TpShard tp_shard(const ModelCfg& c, int ffn_unit, int tp, int rank);
 
 class Model {
  public:
