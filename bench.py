@@ -180,6 +180,18 @@ def peaks():
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "of fallback"
 
 
+def profiled_traffic(name: str):
+    """DRAM bytes per launch of a kernel from its committed ncu summary (profiles/<name>.md, a line
+    'dram_bytes_per_launch: <int>'), or None."""
+    try:
+        for line in open(os.path.join(ROOT, "profiles", name + ".md")):
+            if line.strip().startswith("dram_bytes_per_launch:"):
+                return int(line.split(":", 1)[1].strip().split()[0])
+    except (OSError, ValueError):
+        pass
+    return None
+
+
 def cpu_baseline_sample(path: str, cfg: dict, accepted_per_step: int, steps: int = 1):
     """malkin's own CPU path (oracle/_ref) on the same weights and tree shape, all physical cores; KV prefix rows
     exist but are not prefilled (attention reads the same number of keys)."""
@@ -254,6 +266,67 @@ def config_json(args, cfg):
             "parallelism": f"tp{args.gpus}", "l2": "inputs larger than L2 (weights stream from HBM every step)"}
 
 
+# ---------------------------------------------------------------------------------------------------------------
+# Kernel probes (for ncu captures of one kernel at the 8B verify shapes; not part of the timed benchmark)
+# ---------------------------------------------------------------------------------------------------------------
+PROBE_GEMM_SHAPES = {"gate+up": (24576, 4096), "down": (4096, 12288), "qkv": (6144, 4096), "wo": (4096, 4096),
+                     "lm_head": (151936, 4096)}
+
+
+def probe_gemm(shapes, layouts, n: int, reps: int) -> None:
+    """Q8_0 matmul (mk_matmul, automatic split) on seeded random weights of the 8B shapes, n tokens."""
+    import torch
+    import malkin_b200 as mk
+    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+    from make_golden import random_rows
+    rng = np.random.default_rng(0)
+    for name in shapes:
+        rows, cols = PROBE_GEMM_SHAPES[name]
+        w = random_rows(rng, Q8_0, rows, cols)
+        x = torch.from_numpy(rng.uniform(-3, 3, (n, cols)).astype(np.float32)).cuda()
+        y = torch.zeros((n, rows), device="cuda")
+        for layout in layouts:
+            os.environ.pop("MALKIN_B200_Q8_LAYOUT", None)
+            if layout != "auto":
+                os.environ["MALKIN_B200_Q8_LAYOUT"] = layout
+            W = mk.Weight(Q8_0, w, rows, cols)
+            for _ in range(reps):
+                W.matmul(x.data_ptr(), n, y.data_ptr(), split_k=0)
+            torch.cuda.synchronize()
+            print(json.dumps({"probe": "gemm", "shape": name, "layout": layout, "rows": rows, "cols": cols, "n": n}))
+            del W
+
+
+def probe_attention(reps: int) -> None:
+    """Tree attention (mk_attention) at the 8B verify shape: 8 requests x 17 tree rows, 2049 contiguous keys plus
+    the node's ancestors, 32 q heads / 8 kv heads, D = 128, seeded int8 KV."""
+    import torch
+    import malkin_b200 as mk
+    reqs, tok, P, H, KV, D, n_ctx = 8, 17, 2048, 32, 8, 128, 2304
+    n_rows, n = reqs * n_ctx, reqs * tok
+    rng = np.random.default_rng(0)
+    q = torch.from_numpy(rng.standard_normal((n, H, D)).astype(np.float32)).cuda()
+    k = torch.from_numpy(rng.integers(-127, 128, (KV, n_rows, D)).astype(np.int8)).cuda()
+    v = torch.from_numpy(rng.integers(-127, 128, (KV, n_rows, D)).astype(np.int8)).cuda()
+    ks = torch.from_numpy(rng.uniform(0.001, 0.02, (KV, n_rows)).astype(np.float32)).cuda()
+    vs = torch.from_numpy(rng.uniform(0.001, 0.02, (KV, n_rows)).astype(np.float32)).cuda()
+    kv_base, n_keys, anc_off, anc = [], [], [0], []
+    for r in range(reqs):
+        for t in range(tok):
+            kv_base.append(r * n_ctx)
+            n_keys.append(P + 1)
+            anc += [P + 1 + 2 * i for i in range((t + 1) // 2)]
+            anc_off.append(len(anc))
+    ti = lambda a: torch.tensor(a, dtype=torch.int32).cuda()  # noqa: E731
+    kvb, nk, ao, an = ti(kv_base), ti(n_keys), ti(anc_off), ti(anc)
+    out = torch.zeros((n, H, D), device="cuda")
+    for _ in range(reps):
+        mk.attention(q.data_ptr(), n, H, KV, D, k.data_ptr(), v.data_ptr(), ks.data_ptr(), vs.data_ptr(), n_rows,
+                     kvb.data_ptr(), nk.data_ptr(), ao.data_ptr(), an.data_ptr(), out.data_ptr())
+    torch.cuda.synchronize()
+    print(json.dumps({"probe": "attention", "n": n, "heads": H, "kv_heads": KV, "keys": P + 1}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -262,7 +335,16 @@ def main():
     ap.add_argument("--config", default="8b", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="malkin_b200", choices=["malkin_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--probe", choices=["gemm", "attention"], help="run one kernel probe instead of the benchmark")
+    ap.add_argument("--probe-shapes", default="gate+up,qkv", help="gemm probe: " + ",".join(PROBE_GEMM_SHAPES))
+    ap.add_argument("--probe-layouts", default="auto", help="gemm probe: auto,tc,panels")
+    ap.add_argument("--probe-n", type=int, default=136)
+    ap.add_argument("--probe-reps", type=int, default=3)
     args = ap.parse_args()
+    if args.probe == "gemm":
+        return probe_gemm(args.probe_shapes.split(","), args.probe_layouts.split(","), args.probe_n, args.probe_reps)
+    if args.probe == "attention":
+        return probe_attention(args.probe_reps)
     args.warmup = max(3, args.warmup)
     cfg = CONFIGS[args.config]
     if args.impl == "reference":
@@ -402,9 +484,11 @@ def main():
         "e2e": {"value": A_step * args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": h2d // args.steps,
                 "d2h_bytes_per_step": d2h // args.steps},
         "gpu_launches": launches,
-        "roofline": {"kernel": "gate+up weight-streaming GEMM (k_gemm_q8_0)", "bound": "hbm", "achieved": gu_gbs,
-                     "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": (gu_gbs / pk["hbm_gbs"]) if gu_gbs else None,
-                     "peak_source": pk_src, "traffic": None,
+        "roofline": {"kernel": "gate+up weight-streaming GEMM (k_gemm<Q8_0>, mma.sync panels)", "bound": "hbm",
+                     "achieved": gu_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": (gu_gbs / pk["hbm_gbs"]) if gu_gbs else None, "peak_source": pk_src,
+                     "traffic": profiled_traffic("gemm_q8_gate_up_8b") if args.config == "8b" else None,
+                     "traffic_source": "profiles/gemm_q8_gate_up_8b.md (ncu, one launch at the 8B gate+up shape)",
                      "algorithmic_bytes_per_launch": gu_bytes / spec_of(cfg)["n_layer"],
                      "stage_ms": {k: float(v) for k, v in zip(
                          ["norm+qkv", "qk-norm/rope/kv", "attention", "wo+res+norm", "gate+up", "silu+quant", "down",

@@ -465,7 +465,7 @@ int mk_attention(const float* dev_q, int n, int H, int KV, int D, const int8_t* 
     p.part = part.get<float>();
     mkb::AttnLayer L{const_cast<int8_t*>(dev_k), const_cast<int8_t*>(dev_v), const_cast<float*>(dev_ks),
                      const_cast<float*>(dev_vs), n_rows};
-    mkb::launch_attention(dev_q, H, KV, D, 1.0f / std::sqrt(static_cast<float>(D)), L, p, dev_out, s);
+    mkb::launch_attention(dev_q, H, KV, D, 1.0f / std::sqrt(static_cast<float>(D)), L, p, dev_out, mkb::ActQ{}, s);
     mkb::cuda_check(cudaGetLastError(), "attention");
     mkb::cuda_check(cudaStreamSynchronize(s), "attention");
   });

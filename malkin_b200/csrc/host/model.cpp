@@ -480,7 +480,6 @@ void Model::gemm(const DevWeight& w, int split, int n, float* y, int64_t ldy, in
 void Model::run_forward(int n, int m) {
   const ModelCfg& c = cfg_;
   const int D = c.head_dim, E = c.n_embd;
-  const int64_t HD = static_cast<int64_t>(Hl_) * D;
   const float scale = 1.0f / std::sqrt(static_cast<float>(D));
   const int nt8 = act_tiles(n);
   if (profile_) {
@@ -503,9 +502,9 @@ void Model::run_forward(int n, int m) {
                     L.k_norm, c.rms_eps, rope_.get<float>(), d_rpos_, d_kvat_, q_, kv_layers_[static_cast<size_t>(il)],
                     stream_);
     stage(1);
-    launch_attention(q_, Hl_, KVl_, D, scale, kv_layers_[static_cast<size_t>(il)], plan_, att_, stream_);
+    act_.nt8 = nt8;
+    launch_attention(q_, Hl_, KVl_, D, scale, kv_layers_[static_cast<size_t>(il)], plan_, nullptr, act_, stream_);
     stage(2);
-    launch_quant_rows(att_, HD, n, static_cast<int>(HD), act_, stream_);
     gemm(L.wo, L.wo_split, n, part_, E, part_slice_);
     Slices wo_add{part_, L.wo_split, part_slice_};
     if (tp) {

@@ -18,6 +18,7 @@
 
 #include "common.cuh"
 #include "kernels.hpp"
+#include "quant.cuh"
 #include "pipeline.cuh"
 
 namespace mkb {
@@ -409,12 +410,19 @@ __global__ void __launch_bounds__(kThreads, 2) k_attn_part(PartArgs a) {  // two
 
 // ---------------- combine chunks + extra (ancestor) keys ----------------
 // grid (n, ceil(H / 4)), block 128: one warp per (token, head).
+// out (nullable): [n][H][D] floats. act (act.qx nullable): the same rows quantized to Q8 blocks straight into the
+// GEMM activation layouts (head h = blocks h * D / 32 ..), rows n .. npad - 1 zero-filled (blockIdx.x >= n).
 template <int D>
-__global__ void k_attn_combine(PartArgs a, const int32_t* __restrict__ tok_sg, float* __restrict__ out) {
+__global__ void k_attn_combine(PartArgs a, const int32_t* __restrict__ tok_sg, float* __restrict__ out, ActQ act) {
   constexpr int PER = D / 32;
   const int t = blockIdx.x, lane = threadIdx.x & 31;
   const int h = blockIdx.y * 4 + (threadIdx.x >> 5);
   if (h >= a.H) return;
+  if (t >= a.p.n) {
+#pragma unroll
+    for (int m = 0; m < PER; ++m) store_act(act, h * PER + m, t, QBlock{0, 0.0f, 0, 0}, lane);
+    return;
+  }
   const int kvh = h / a.G;
   const int sg = tok_sg[t];
   const int t0 = a.p.sg_first[sg];
@@ -439,17 +447,33 @@ __global__ void k_attn_combine(PartArgs a, const int32_t* __restrict__ tok_sg, f
     const float mc = cb + lane < nck ? part[(cb + lane) * cstride + D] : -INFINITY;
     M = fmaxf(M, warp_max(mc));
   }
-  // extra-key scores: lane e holds extra e (up to 32 extras per pass), independent dots
+  // extra-key scores: lane e holds extra e (up to 32 extras per pass); dots in batches of 8 whose loads and
+  // butterfly reductions run side by side (the same xor order as warp_sum)
   float se_reg = -INFINITY;
-  for (int e = e0; e < e1; ++e) {
-    const size_t row = static_cast<size_t>(base) + a.p.anc[e];
-    float s = 0.0f;
+  for (int eb = e0; eb < e1; eb += 8) {
+    float s8[8];
 #pragma unroll
-    for (int m = 0; m < PER; ++m) s = __fmaf_rn(q[m], static_cast<float>(kh[row * D + lane + 32 * m]), s);
-    s = warp_sum(s);
-    s = __fmul_rn(s, __fmul_rn(ksh[row], a.scale));
-    if (((e - e0) & 31) == lane) se_reg = s;
-    M = fmaxf(M, s);
+    for (int u = 0; u < 8; ++u) {
+      s8[u] = 0.0f;
+      if (eb + u < e1) {
+        const size_t row = static_cast<size_t>(base) + a.p.anc[eb + u];
+#pragma unroll
+        for (int m = 0; m < PER; ++m) s8[u] = __fmaf_rn(q[m], static_cast<float>(kh[row * D + lane + 32 * m]), s8[u]);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int u = 0; u < 8; ++u) s8[u] += __shfl_xor_sync(0xffffffffu, s8[u], o);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      if (eb + u < e1) {
+        const size_t row = static_cast<size_t>(base) + a.p.anc[eb + u];
+        const float sc = __fmul_rn(s8[u], __fmul_rn(ksh[row], a.scale));
+        if (((eb + u - e0) & 31) == lane) se_reg = sc;
+        M = fmaxf(M, sc);
+      }
+    }
   }
   float o[PER];
 #pragma unroll
@@ -494,9 +518,15 @@ __global__ void k_attn_combine(PartArgs a, const int32_t* __restrict__ tok_sg, f
     for (int m = 0; m < PER; ++m) o[m] = __fmaf_rn(pv, static_cast<float>(vh[row * D + lane + 32 * m]), o[m]);
   }
   const float inv = __fdiv_rn(1.0f, L);
-  float* dst = out + (static_cast<size_t>(t) * a.H + h) * D;
+  if (out) {
+    float* dst = out + (static_cast<size_t>(t) * a.H + h) * D;
 #pragma unroll
-  for (int m = 0; m < PER; ++m) dst[lane + 32 * m] = __fmul_rn(o[m], inv);
+    for (int m = 0; m < PER; ++m) dst[lane + 32 * m] = __fmul_rn(o[m], inv);
+  }
+  if (act.qx) {
+#pragma unroll
+    for (int m = 0; m < PER; ++m) store_act(act, h * PER + m, t, quant_block32(__fmul_rn(o[m], inv), lane), lane);
+  }
 }
 
 template <int D>
@@ -506,7 +536,7 @@ size_t part_smem() {
 
 template <int D>
 void run_attention(const float* q, int H, int KV, float scale, const AttnLayer& L, const AttnPlan& p, float* out,
-                   cudaStream_t s) {
+                   const ActQ& act, cudaStream_t s) {
   PartArgs a{q, H, KV, H / KV, scale, L, p};
   const size_t smem = part_smem<D>();
   static bool attr[64] = {};
@@ -521,8 +551,8 @@ void run_attention(const float* q, int H, int KV, float scale, const AttnLayer& 
     const dim3 g1(p.n_chunks, p.n_sg, KV);
     k_attn_part<D><<<g1, kThreads, smem, s>>>(a);
   }
-  const dim3 g2(p.n, (H + 3) / 4);
-  k_attn_combine<D><<<g2, 128, 0, s>>>(a, p.tok_sg, out);
+  const dim3 g2(act.qx ? act.nt8 * 8 : p.n, (H + 3) / 4);
+  k_attn_combine<D><<<g2, 128, 0, s>>>(a, p.tok_sg, out, act);
 }
 
 }  // namespace
@@ -563,16 +593,16 @@ void launch_qkv_post(Slices qk, int v_n, int64_t v_col0, int64_t ldy, int n, int
 }
 
 void launch_attention(const float* q, int H, int KV, int D, float scale, const AttnLayer& L, const AttnPlan& p,
-                      float* out, cudaStream_t s) {
+                      float* out, const ActQ& act, cudaStream_t s) {
   switch (D) {
     case 64:
-      run_attention<64>(q, H, KV, scale, L, p, out, s);
+      run_attention<64>(q, H, KV, scale, L, p, out, act, s);
       break;
     case 128:
-      run_attention<128>(q, H, KV, scale, L, p, out, s);
+      run_attention<128>(q, H, KV, scale, L, p, out, act, s);
       break;
     case 256:
-      run_attention<256>(q, H, KV, scale, L, p, out, s);
+      run_attention<256>(q, H, KV, scale, L, p, out, act, s);
       break;
     default:
       break;

@@ -133,8 +133,9 @@ int attn_qmax();
 // two CTAs per SM in total, at least 64 keys per chunk.
 int attn_chunk_for(int max_keys, int n_sg, int KV, int num_sms);
 size_t attn_part_floats(int n_sg, int n_chunks, int KV, int D);
+// out: [n][H][D] floats (nullable); act: the same rows quantized into the GEMM activation layouts (act.qx nullable).
 void launch_attention(const float* q, int H, int KV, int D, float scale, const AttnLayer& L, const AttnPlan& p,
-                      float* out, cudaStream_t s);
+                      float* out, const ActQ& act, cudaStream_t s);
 
 // ---- misc (misc.cu) ----
 // Token embedding rows (GGUF Q8_0 / Q4_K / Q6_K / F32 / F16 rows) -> x [n][E].
