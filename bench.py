@@ -487,7 +487,7 @@ def main():
         "roofline": {"kernel": "gate+up weight-streaming GEMM (k_gemm<Q8_0>, mma.sync panels)", "bound": "hbm",
                      "achieved": gu_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": (gu_gbs / pk["hbm_gbs"]) if gu_gbs else None, "peak_source": pk_src,
-                     "traffic": profiled_traffic("gemm_q8_gate_up_8b") if args.config == "8b" else None,
+                     "traffic": profiled_traffic("gemm_q8_gate_up_8b") if args.config == "8b" and world == 1 else None,
                      "traffic_source": "profiles/gemm_q8_gate_up_8b.md (ncu, one launch at the 8B gate+up shape)",
                      "algorithmic_bytes_per_launch": gu_bytes / spec_of(cfg)["n_layer"],
                      "stage_ms": {k: float(v) for k, v in zip(
