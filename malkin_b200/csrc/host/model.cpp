@@ -628,6 +628,7 @@ void Model::forward(const mk_batch_token* batch, int n, float* host_logits) {
   plan_.tok_sg = d_toksg_;
   plan_.sg_maxk = d_sgmaxk_;
   plan_.part = attn_part_.get<float>();
+  plan_.status = status_;
 
   if (profile_) {
     run_forward(n, m);

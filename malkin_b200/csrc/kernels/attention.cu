@@ -13,6 +13,8 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
+#include <string>
 
 #include <cfloat>
 
@@ -20,6 +22,7 @@
 #include "kernels.hpp"
 #include "quant.cuh"
 #include "pipeline.cuh"
+#include "tcgen05.cuh"
 
 namespace mkb {
 
@@ -529,6 +532,354 @@ __global__ void k_attn_combine(PartArgs a, const int32_t* __restrict__ tok_sg, f
   }
 }
 
+// ---------------- partial attention over a key chunk on tcgen05 (D = 128) ----------------
+// One CTA = (sub-group, KV head, key chunk), like k_attn_part, with the products on the 5th-generation tensor core:
+// S = Q Kᵀ (M = 128 query rows, the sub-group's G x rows zero-padded; N = 64 keys; K = 128) accumulates into one of
+// two TMEM buffers from Q hi and Q lo (fp16, ~22 bits together) against the int8 K tile converted exactly to fp16;
+// O += P' V (M = 128, N = 128 = D, K = 64 keys) accumulates into a TMEM O from P' = p · v_scale · 2^12 split into fp16
+// hi + lo, against the int8 V tile in fp16 (read MN-major). Warp roles (320 threads, one CTA per SM):
+//   0      TMEM owner; lane 0 issues the MMAs (S of tile j, then P'V of tile j - 1) and the commits
+//   1      TMA producer: the raw int8 K / V rows of each tile and their scales into a 2-stage staging ring
+//   2..5   converters: Q (once) and each staged tile into fp16 UMMA core-matrix layouts (2 buffers)
+//   6..9   softmax: one query row per thread (TMEM lane quarter warp % 4): scale, mask, online max / sum, P' hi/lo
+//          into shared memory, rescale O in TMEM when the row maximum grows; at the end O, m, l -> partials
+// Every wait is bounded; TMEM is released on every path. Partials use k_attn_part's format (combined unchanged).
+namespace tc_attn {
+constexpr int kM = 128, kN = 64, kDh = 128;
+constexpr int kThreads = 320;
+constexpr uint32_t kCols = 256;  // S0 [0, 64), S1 [64, 128), O [128, 256)
+constexpr int kErrBase = 16;     // status codes 16.. (bounded waits)
+// shared-memory map (bytes)
+constexpr uint32_t QH = 0, QL = QH + kM * kDh * 2, KF = QL + kM * kDh * 2, VF = KF + 2 * kN * kDh * 2,
+                   PH = VF + 2 * kN * kDh * 2, PL = PH + kM * kN * 2, RAW = PL + kM * kN * 2,
+                   RAWB = 2 * kN * kDh,  // one staged tile: K rows then V rows (int8)
+                   SCF = RAW + 2 * RAWB,  // scales: [2][ks * scale 64 | vs * 2^12 64]
+                   NKR = SCF + 2 * 2 * kN * 4,  // n_keys per query row [128]
+                   BAR = NKR + kM * 4, BYTES = BAR + 32 * 8 + 16;
+// K-major core-matrix offsets (bytes) of an fp16 tile whose rows are `r` and K index `k`, 16 K-chunks per row group
+__device__ __forceinline__ uint32_t kmaj(int r, int k, int kchunks) {
+  return static_cast<uint32_t>((r >> 3) * (kchunks * 128) + (k >> 3) * 128 + (r & 7) * 16 + (k & 7) * 2);
+}
+}  // namespace tc_attn
+
+__global__ void __launch_bounds__(tc_attn::kThreads, 1) k_attn_part_tc(PartArgs a) {
+  using namespace tc_attn;
+  constexpr int D = kDh;
+  extern __shared__ __align__(1024) uint8_t sm[];
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + BAR);
+  uint64_t *raw_full = bar, *raw_free = bar + 2, *kv_full = bar + 4, *kv_free = bar + 6, *s_full = bar + 8,
+           *s_free = bar + 10, *p_ready = bar + 12, *o_done = bar + 13, *mma_done = bar + 14;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sm + BAR + 32 * 8);
+  int* nkr = reinterpret_cast<int*>(sm + NKR);
+
+  const int chunk = blockIdx.x, sg = blockIdx.y, kvh = blockIdx.z;
+  const int t0 = a.p.sg_first[sg], t1 = a.p.sg_first[sg + 1];
+  const int nq = (t1 - t0) * a.G;
+  const int maxk = a.p.sg_maxk[sg];
+  const int k0 = chunk * a.p.chunk;
+  if (k0 >= maxk) return;  // whole CTA, before any barrier or TMEM
+  const int k1 = min(maxk, k0 + a.p.chunk);
+  const int T = (k1 - k0 + kN - 1) / kN;  // key tiles
+  const int base = a.p.kv_base[t0];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int* status = a.p.status;  // bounded waits record the first timeout here (nullable)
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&raw_full[i], 1);
+      mbar_init(&raw_free[i], 4);
+      mbar_init(&kv_full[i], 4);
+      mbar_init(&kv_free[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
+    }
+    mbar_init(p_ready, 4);
+    mbar_init(o_done, 1);
+    mbar_init(mma_done, 1);
+    mbar_fence_init();
+  }
+  for (int r = threadIdx.x; r < kM; r += blockDim.x) nkr[r] = r < nq ? a.p.n_keys[t0 + r / a.G] : 0;
+  if (warp == 0) tmem_alloc(tmem_holder, kCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const int8_t* kh = a.L.k + (static_cast<size_t>(kvh) * a.L.n_rows + base) * D;
+  const int8_t* vh = a.L.v + (static_cast<size_t>(kvh) * a.L.n_rows + base) * D;
+  const float* ksh = a.L.ks + static_cast<size_t>(kvh) * a.L.n_rows + base;
+  const float* vsh = a.L.vs + static_cast<size_t>(kvh) * a.L.n_rows + base;
+
+  if (warp == 0) {
+    // ---------------- MMA issuer ----------------
+    const uint32_t idesc_s = umma_idesc_f16_f32(kM, kN);
+    const uint32_t idesc_pv = umma_idesc_f16_f32(kM, D) | (1u << 16);  // B (V) MN-major
+    const uint32_t qh = smem_addr(sm + QH), ql = smem_addr(sm + QL);
+    bool ok = true;
+    auto pv = [&](int i) {  // O += P'(tile i) V(tile i)
+      if (!mbar_wait_warp(p_ready, i & 1, status, kErrBase + 6)) return false;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t vb = smem_addr(sm + VF + (i & 1) * kN * D * 2);
+        for (int pass = 0; pass < 2; ++pass) {
+          const uint32_t pb = smem_addr(sm + (pass ? PL : PH));
+          for (int ks = 0; ks < kN / 16; ++ks)
+            tc_mma_f16_ss(tmem + 128, umma_desc_kmajor(pb + ks * 256, 128, 1024),
+                          umma_desc_kmajor(vb + ks * 256, 128, 1024), idesc_pv, (i > 0 || pass > 0 || ks > 0) ? 1u : 0u);
+        }
+        tc_commit(o_done);
+        tc_commit(&kv_free[i & 1]);
+      }
+      __syncwarp();
+      return true;
+    };
+    for (int j = 0; j < T && ok; ++j) {
+      const int b = j & 1;
+      if (!mbar_wait_warp(&kv_full[b], (j >> 1) & 1, status, kErrBase + 0)) break;
+      if (j >= 2 && !mbar_wait_warp(&s_free[b], ((j >> 1) - 1) & 1, status, kErrBase + 1)) break;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t kb = smem_addr(sm + KF + b * kN * D * 2);
+        for (int pass = 0; pass < 2; ++pass)
+          for (int kk = 0; kk < D / 16; ++kk)
+            tc_mma_f16_ss(tmem + b * kN, umma_desc_kmajor((pass ? ql : qh) + kk * 256, 128, 2048),
+                          umma_desc_kmajor(kb + kk * 256, 128, 2048), idesc_s, (pass > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&s_full[b]);
+      }
+      __syncwarp();
+      if (j >= 1) ok = pv(j - 1);
+    }
+    if (ok) pv(T - 1);
+    if (lane == 0) tc_commit(mma_done);
+    __syncwarp();
+    mbar_wait_warp(mma_done, 0, status, kErrBase + 7);
+  } else if (warp == 1) {
+    // ---------------- TMA producer: raw int8 rows + scales of each tile ----------------
+    int issued = 0;
+    for (int j = 0; j < T; ++j, ++issued) {
+      const int b = j & 1, kt = k0 + j * kN, nk = min(kN, k1 - kt);
+      if (j >= 2 && !mbar_wait_warp(&raw_free[b], ((j >> 1) - 1) & 1, status, kErrBase + 2)) break;
+      uint8_t* raw = sm + RAW + b * RAWB;
+      if (lane == 0) {
+        // the tile's nk valid rows of K and of V (128 bytes each; row addresses are 128-byte aligned)
+        mbar_arrive_expect_tx(&raw_full[b], static_cast<uint32_t>(2 * nk * D));
+        bulk_g2s(raw, kh + static_cast<size_t>(kt) * D, nk * D, &raw_full[b]);
+        bulk_g2s(raw + kN * D, vh + static_cast<size_t>(kt) * D, nk * D, &raw_full[b]);
+      }
+      __syncwarp();
+    }
+    for (int j = issued > 2 ? issued - 2 : 0; j < issued; ++j)
+      if (!mbar_wait_warp(&raw_full[j & 1], (j >> 1) & 1, status, kErrBase + 3)) break;
+  } else if (warp < 6) {
+    // ---------------- converters ----------------
+    const int ct = threadIdx.x - 64;  // 0..127
+    // Q rows (query r = token (r / G), head kvh * G + r % G) as fp16 hi + lo, zero past nq; each warp takes rows
+    // warp - 2 + 4 i, eight rows' loads in flight at a time
+    for (int r0 = warp - 2; r0 < kM; r0 += 32) {
+      float4 v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int r = r0 + 4 * i;
+        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (r < nq) {
+          const int t = t0 + r / a.G, h = kvh * a.G + r % a.G;
+          v[i] = reinterpret_cast<const float4*>(a.q + (static_cast<size_t>(t) * a.H + h) * D)[lane];
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int r = r0 + 4 * i;
+        const float x[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+        __half hi[4], lo[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) split_h(x[e], hi[e], lo[e]);
+        const uint32_t off = kmaj(r, 4 * lane, D / 8);
+        *reinterpret_cast<uint2*>(sm + QH + off) = make_uint2(pack_h2(hi[0], hi[1]), pack_h2(hi[2], hi[3]));
+        *reinterpret_cast<uint2*>(sm + QL + off) = make_uint2(pack_h2(lo[0], lo[1]), pack_h2(lo[2], lo[3]));
+      }
+    }
+    bool ok = true;
+    // scales of the next tile prefetched into registers (threads ct < 64: key ct)
+    float ks_next = 0.0f, vs_next = 0.0f;
+    if (ct < kN && ct < min(kN, k1 - k0)) ks_next = ksh[k0 + ct], vs_next = vsh[k0 + ct];
+    for (int j = 0; j < T && ok; ++j) {
+      const int b = j & 1, kt = k0 + j * kN, nk = min(kN, k1 - kt);
+      const float ks_cur = ks_next, vs_cur = vs_next;
+      if (ct < kN && j + 1 < T && ct < min(kN, k1 - kt - kN)) ks_next = ksh[kt + kN + ct], vs_next = vsh[kt + kN + ct];
+      if (!mbar_wait_warp(&raw_full[b], (j >> 1) & 1, status, kErrBase + 4)) break;
+      if (j >= 2 && !mbar_wait_warp(&kv_free[b], ((j >> 1) - 1) & 1, status, kErrBase + 5)) break;
+      const uint8_t* raw = sm + RAW + b * RAWB;
+      uint8_t* kf = sm + KF + b * kN * D * 2;
+      uint8_t* vf = sm + VF + b * kN * D * 2;
+      // 64 keys x 8 chunks of 16 values, K and V: 4 chunks of each per thread, rows past nk zero. Thread ct takes
+      // key ct % 64 and chunks (j + key) % 8: eight consecutive threads then read and write eight different bank
+      // groups (staged rows are 128 bytes apart; the core-matrix rows 16 bytes apart).
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int key = ct & (kN - 1), d16 = (((ct >> 6) * 4 + u) + key) & 7;
+        uint4 wk = make_uint4(0, 0, 0, 0), wv = make_uint4(0, 0, 0, 0);
+        if (key < nk) {
+          wk = *reinterpret_cast<const uint4*>(raw + key * D + d16 * 16);
+          wv = *reinterpret_cast<const uint4*>(raw + kN * D + key * D + d16 * 16);
+        }
+        uint4 k0h, k1h, v0h, v1h;
+        i8x4_to_h2(wk.x, k0h.x, k0h.y);
+        i8x4_to_h2(wk.y, k0h.z, k0h.w);
+        i8x4_to_h2(wk.z, k1h.x, k1h.y);
+        i8x4_to_h2(wk.w, k1h.z, k1h.w);
+        i8x4_to_h2(wv.x, v0h.x, v0h.y);
+        i8x4_to_h2(wv.y, v0h.z, v0h.w);
+        i8x4_to_h2(wv.z, v1h.x, v1h.y);
+        i8x4_to_h2(wv.w, v1h.z, v1h.w);
+        // K: K-major (rows = keys, 16 chunks of 8 dims); V: MN-major (8 dims contiguous, 8 keys per core matrix)
+        *reinterpret_cast<uint4*>(kf + kmaj(key, d16 * 16, D / 8)) = k0h;
+        *reinterpret_cast<uint4*>(kf + kmaj(key, d16 * 16 + 8, D / 8)) = k1h;
+        *reinterpret_cast<uint4*>(vf + (2 * d16) * 1024 + (key >> 3) * 128 + (key & 7) * 16) = v0h;
+        *reinterpret_cast<uint4*>(vf + (2 * d16 + 1) * 1024 + (key >> 3) * 128 + (key & 7) * 16) = v1h;
+      }
+      if (ct < kN) {  // scales: k * softmax scale, v * 2^12; zero past nk
+        float* scf = reinterpret_cast<float*>(sm + SCF + b * 2 * kN * 4);
+        scf[ct] = ct < nk ? __fmul_rn(ks_cur, a.scale) : 0.0f;
+        scf[kN + ct] = ct < nk ? __fmul_rn(vs_cur, kPScale) : 0.0f;
+      }
+      // generic-proxy writes -> visible to the tensor core (async proxy); staging free for the producer
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&kv_full[b]);
+        mbar_arrive(&raw_free[b]);
+      }
+      ok = true;
+    }
+  } else {
+    // ---------------- softmax: query row r of this thread ----------------
+    const int quarter = warp & 3, r = 32 * quarter + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(32 * quarter) << 16;
+    const int nk_r = nkr[r];
+    float m = -INFINITY, l = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < T && ok; ++j) {
+      const int b = j & 1, kt = k0 + j * kN;
+      // the tile's scales (written by the converters) and its scores
+      if (!mbar_wait_warp(&kv_full[b], (j >> 1) & 1, status, kErrBase + 11) ||
+          !mbar_wait_warp(&s_full[b], (j >> 1) & 1, status, kErrBase + 8)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float sc[kN];  // this row's scores of the tile (bits from TMEM, then scaled and masked in place)
+      tmem_ld32(tmem + lane_base + b * kN, *reinterpret_cast<uint32_t(*)[32]>(&sc[0]));
+      tmem_ld32(tmem + lane_base + b * kN + 32, *reinterpret_cast<uint32_t(*)[32]>(&sc[32]));
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[b]);
+      const float* scf = reinterpret_cast<const float*>(sm + SCF + b * 2 * kN * 4);
+      float mt = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kN; ++c) {
+        const int key = kt + c;
+        const bool valid = key < k1 && key < nk_r;
+        sc[c] = valid ? __fmul_rn(sc[c], scf[c]) : -INFINITY;
+        mt = fmaxf(mt, sc[c]);
+      }
+      // Lazy rescaling: the reference maximum m moves (and O, l are rescaled) only when a score exceeds it by more than
+      // kLazy nats, so p = e^(s - m) <= e^kLazy and P' = p * v_scale * 2^12 stays inside fp16 for |v| < 254; O and l
+      // are always relative to the same m, which the partial stores. The decision is per warp (TMEM access is
+      // warp-wide); rows with no new maximum get a factor 1.
+      constexpr float kLazy = 2.0f;
+      const bool grow = mt > m + kLazy || (m == -INFINITY && mt != -INFINITY);
+      const bool resc = __any_sync(0xffffffffu, grow);
+      float mn = m, alpha = 1.0f;
+      if (resc && mt > m) {
+        mn = mt;
+        alpha = m == -INFINITY ? 0.0f : exp_fast(__fsub_rn(m, mn));
+      }
+      m = mn;
+      float sum = 0.0f;
+      uint32_t ph[kN / 2], pl[kN / 2];
+#pragma unroll
+      for (int c = 0; c < kN; c += 2) {
+        float pv[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const float x = sc[c + u];
+          const float p = x == -INFINITY ? 0.0f : exp_fast(__fsub_rn(x, mn));
+          sum += p;
+          pv[u] = __fmul_rn(p, scf[kN + c + u]);
+        }
+        __half h0, l0, h1, l1;
+        split_h(pv[0], h0, l0);
+        split_h(pv[1], h1, l1);
+        ph[c / 2] = pack_h2(h0, h1);
+        pl[c / 2] = pack_h2(l0, l1);
+      }
+      l = __fmaf_rn(l, alpha, sum);
+      // P'V of the previous tile must be done before O is rescaled and P is overwritten
+      if (j >= 1 && !mbar_wait_warp(o_done, (j - 1) & 1, status, kErrBase + 9)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (j >= 1 && resc) {
+#pragma unroll
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t ov[32];
+          tmem_ld32(tmem + lane_base + 128 + c0, ov);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__fmul_rn(__uint_as_float(ov[e]), alpha));
+          tmem_st32(tmem + lane_base + 128 + c0, ov);
+        }
+        tmem_wait_st();
+      }
+#pragma unroll
+      for (int c8 = 0; c8 < kN / 8; ++c8) {
+        const uint32_t off = kmaj(r, c8 * 8, kN / 8);
+        *reinterpret_cast<uint4*>(sm + PH + off) = make_uint4(ph[4 * c8], ph[4 * c8 + 1], ph[4 * c8 + 2], ph[4 * c8 + 3]);
+        *reinterpret_cast<uint4*>(sm + PL + off) = make_uint4(pl[4 * c8], pl[4 * c8 + 1], pl[4 * c8 + 2], pl[4 * c8 + 3]);
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_ready);
+    }
+    // final O (after the last P'V) -> partials, like k_attn_part: o / 2^12, m, l
+    if (ok && mbar_wait_warp(o_done, (T - 1) & 1, status, kErrBase + 10)) {
+      tc_fence_after();
+      float* part = a.p.part + ((static_cast<size_t>(sg) * a.p.n_chunks + chunk) * a.KV + kvh) * kQMax * (D + 2);
+      constexpr float inv = 1.0f / kPScale;
+#pragma unroll
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        uint32_t ov[32];
+        tmem_ld32(tmem + lane_base + 128 + c0, ov);
+        tmem_wait_ld();
+        if (r < nq)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) part[static_cast<size_t>(r) * (D + 2) + c0 + e] = __uint_as_float(ov[e]) * inv;
+      }
+      if (r < nq) {
+        part[static_cast<size_t>(r) * (D + 2) + D] = m;
+        part[static_cast<size_t>(r) * (D + 2) + D + 1] = l;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kCols);
+  }
+}
+
+// Tree attention partials: the mma.sync kernel by default; MALKIN_B200_ATTN=tc selects the tcgen05 one (D = 128).
+// Both pass the same oracle tests; on the 8B verify shape the tcgen05 kernel is slower today (95 us vs 67 us per
+// layer): one query tile per CTA leaves S -> softmax -> P'V a serial chain per key tile at one CTA per SM, where the
+// mma.sync kernel runs two CTAs per SM.
+bool attn_use_tc() {
+  const char* e = std::getenv("MALKIN_B200_ATTN");
+  return e && std::string(e) == "tc";
+}
+
 template <int D>
 size_t part_smem() {
   return AttSmem<D>::BYTES;
@@ -549,7 +900,21 @@ void run_attention(const float* q, int H, int KV, float scale, const AttnLayer& 
   }
   if (p.n_sg > 0 && p.n_chunks > 0) {
     const dim3 g1(p.n_chunks, p.n_sg, KV);
-    k_attn_part<D><<<g1, kThreads, smem, s>>>(a);
+    if constexpr (D == tc_attn::kDh) {
+      if (attn_use_tc()) {
+        static bool tc_attr[kMaxDevices] = {};
+        if (dev < kMaxDevices && !tc_attr[dev]) {
+          cudaFuncSetAttribute(k_attn_part_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(tc_attn::BYTES));
+          tc_attr[dev] = true;
+        }
+        k_attn_part_tc<<<g1, tc_attn::kThreads, tc_attn::BYTES, s>>>(a);
+      } else {
+        k_attn_part<D><<<g1, kThreads, smem, s>>>(a);
+      }
+    } else {
+      k_attn_part<D><<<g1, kThreads, smem, s>>>(a);
+    }
   }
   const dim3 g2(act.qx ? act.nt8 * 8 : p.n, (H + 3) / 4);
   k_attn_combine<D><<<g2, 128, 0, s>>>(a, p.tok_sg, out, act);

@@ -126,6 +126,7 @@ struct AttnPlan {
   const int32_t* tok_sg = nullptr;    // [n] sub-group of each token
   const int32_t* sg_maxk = nullptr;   // [n_sg] longest key prefix (n_keys) among the sub-group's tokens
   float* part = nullptr;              // partials workspace (attn_part_floats)
+  int* status = nullptr;              // device word for bounded-wait failures (nullable)
 };
 // Query vectors (rows x G) one sub-group may hold.
 int attn_qmax();

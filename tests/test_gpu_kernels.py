@@ -141,8 +141,14 @@ def test_attention_golden(mk, golden, torch_cuda):
         np.testing.assert_allclose(out.reshape(-1), golden[f"att{i}_out"], rtol=2e-4, atol=2e-5)
 
 
-def test_attention_tree_batch_vs_oracle(mk, oracle, torch_cuda):
-    """Two sequences, a 9-node tree on one and a 5-token prompt chunk on the other, long prefix (several chunks)."""
+@pytest.mark.parametrize("kernel", ["tc", "mma"])
+def test_attention_tree_batch_vs_oracle(mk, oracle, torch_cuda, monkeypatch, kernel):
+    """Two sequences, a 9-node tree on one and a 5-token prompt chunk on the other, long prefix (several chunks),
+    through the mma.sync partial kernel (default) and the tcgen05 one (MALKIN_B200_ATTN=tc, D = 128)."""
+    if kernel == "tc":
+        monkeypatch.setenv("MALKIN_B200_ATTN", "tc")
+    else:
+        monkeypatch.delenv("MALKIN_B200_ATTN", raising=False)
     torch = torch_cuda
     rng = np.random.default_rng(5)
     H, KV, D, n_ctx = 8, 2, 128, 700
