@@ -79,24 +79,25 @@ int current_device() {
   return d;
 }
 
-// Temporary quantized-activation buffers for the kernel-level entry points.
-// exact_q8: the Q8_0 GEMM keeps the exact int8 block dots (mode kQ8Exact, or a block-dot request), which reads
-// the int8 tensor-core copy; otherwise the fp16 copy is written for the fp16 kernel.
+// Temporary quantized-activation buffers for the kernel-level entry points: int8 qx | the tensor-core copy the Q8_0
+// mode reads (int8 qc for kQ8Exact / kQ8Split and block-dot requests, fp16 xh for kQ8Fp16) | dx | dsx | sh.
 struct TmpAct {
   mkb::DevBuf buf;
   mkb::ActQ act;
-  TmpAct(int n, int64_t K, bool exact_q8) {
+  TmpAct(int n, int64_t K, int mode) {
     const int nt8 = mkb::act_tiles(n), npad = nt8 * 8;
     const int64_t blocks = K / 32;
     const size_t qx = static_cast<size_t>(blocks) * npad * 32, f = static_cast<size_t>(blocks) * npad * 4;
-    buf = mkb::DevBuf(4 * qx + 3 * f + 256);
+    const size_t tc = qx / 32 * mkb::q8_act_bytes(mode);
+    buf = mkb::DevBuf(qx + tc + 3 * f + 256);
     auto* p = buf.get<uint8_t>();
     act.qx = p;
-    if (exact_q8)
-      act.qc = p + qx;
-    else
+    act.q8 = mode;
+    if (mode == mkb::kQ8Fp16)
       act.xh = reinterpret_cast<uint16_t*>(p + qx);  // 2 bytes per value
-    act.dx = reinterpret_cast<float*>(p + 3 * qx);
+    else
+      act.qc = p + qx;
+    act.dx = reinterpret_cast<float*>(p + qx + tc);
     act.dsx = act.dx + blocks * npad;
     act.sh = reinterpret_cast<uint32_t*>(act.dsx + blocks * npad);
     act.nt8 = nt8;
@@ -298,15 +299,15 @@ int mk_matmul(const mk_weight* w, const float* dev_x, int n, float* dev_y, int s
   return guard(MK_ERR_ARG, [&] {
     if (!w || n <= 0) throw mkb::ArgError("matmul: bad argument");
     cudaStream_t s = as_stream(stream);
-    TmpAct t(n, w->w.cols, mkb::q8_mode() == mkb::kQ8Exact);
+    mkb::DevBuf status(sizeof(int));
+    mkb::cuda_check(cudaMemsetAsync(status.get(), 0, sizeof(int), s), "memset");
+    TmpAct t(n, w->w.cols, mkb::q8_mode());
     mkb::launch_quant_rows(dev_x, w->w.cols, n, static_cast<int>(w->w.cols), t.act, s);
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int split = mkb::gemm_slices(w->w, split_k > 0 ? split_k : mkb::gemm_split_for(w->w, sms));
     const int64_t slice = static_cast<int64_t>(n) * w->w.rows;
-    mkb::DevBuf status(sizeof(int));
-    mkb::cuda_check(cudaMemsetAsync(status.get(), 0, sizeof(int), s), "memset");
     mkb::DevBuf slices(split > 1 ? static_cast<size_t>(split) * slice * 4 : 0);
     float* out = split > 1 ? slices.get<float>() : dev_y;
     mkb::launch_gemm(w->w, t.act, n, out, w->w.rows, slice, split, status.get<int>(), s);
@@ -315,7 +316,7 @@ int mk_matmul(const mk_weight* w, const float* dev_x, int n, float* dev_y, int s
     int st = 0;
     mkb::cuda_check(cudaMemcpyAsync(&st, status.get(), sizeof st, cudaMemcpyDeviceToHost, s), "status");
     mkb::cuda_check(cudaStreamSynchronize(s), "matmul");
-    if (st != 0) throw mkb::TimeoutError("matmul: device pipeline wait gave up");
+    if (st != 0) mkb::throw_device_status(st, "matmul");
   });
 }
 
@@ -330,15 +331,18 @@ int mk_matmul_noalloc(const mk_weight* w, const float* dev_x, int n, float* dev_
     mkb::cuda_check(e, "matmul_noalloc: scratch address");
     const size_t cap = mkb::noalloc_scratch_bytes();
     auto up = [](size_t b) { return (b + 255) / 256 * 256; };
-    // [status | qx | qc | dx | dsx | sh | split-K slices]
+    // [status | qx | tensor-core copy (qc or xh) | dx | dsx | sh | split-K slices]
+    const int mode = mkb::q8_mode();
     const int nt8 = mkb::act_tiles(n), npad = nt8 * 8;
     const int64_t blocks = w->w.cols / 32;
     const size_t qx = up(static_cast<size_t>(blocks) * npad * 32), f = up(static_cast<size_t>(blocks) * npad * 4);
-    const size_t act_end = 256 + 3 * qx + 3 * f;
+    const size_t tc = qx / 32 * mkb::q8_act_bytes(mode);
+    const size_t act_end = 256 + qx + tc + 3 * f;
     if (act_end > cap)
       throw mkb::ArgError("matmul_noalloc: " + std::to_string(n) + " tokens x " + std::to_string(w->w.cols) +
                           " values need " + std::to_string(act_end) + " bytes of activations; the fixed scratch holds " +
-                          std::to_string(cap) + " (about 108 bytes per token per 32 values)");
+                          std::to_string(cap) + " (about " + std::to_string(44 + mkb::q8_act_bytes(mode)) +
+                          " bytes per token per 32 values)");
     const int64_t slice = static_cast<int64_t>(n) * w->w.rows;
     const size_t room = cap - act_end;
     auto fits = [&](int split) { return split <= 1 || static_cast<size_t>(split) * slice * 4 <= room; };
@@ -358,11 +362,12 @@ int mk_matmul_noalloc(const mk_weight* w, const float* dev_x, int n, float* dev_
     int* status = reinterpret_cast<int*>(base);
     mkb::ActQ act;
     act.qx = base + 256;
-    if (mkb::q8_mode() == mkb::kQ8Exact)
-      act.qc = act.qx + qx;
-    else
+    act.q8 = mode;
+    if (mode == mkb::kQ8Fp16)
       act.xh = reinterpret_cast<uint16_t*>(act.qx + qx);  // 2 bytes per value
-    act.dx = reinterpret_cast<float*>(act.qx + 3 * qx);
+    else
+      act.qc = act.qx + qx;
+    act.dx = reinterpret_cast<float*>(act.qx + qx + tc);
     act.dsx = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(act.dx) + f);
     act.sh = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(act.dsx) + f);
     act.nt8 = nt8;
@@ -377,7 +382,7 @@ int mk_matmul_noalloc(const mk_weight* w, const float* dev_x, int n, float* dev_
     int st = 0;
     mkb::cuda_check(cudaMemcpyAsync(&st, status, sizeof st, cudaMemcpyDeviceToHost, s), "matmul_noalloc: status");
     mkb::cuda_check(cudaStreamSynchronize(s), "matmul_noalloc");
-    if (st != 0) throw mkb::TimeoutError("matmul_noalloc: device pipeline wait gave up");
+    if (st != 0) mkb::throw_device_status(st, "matmul_noalloc");
   });
 }
 
@@ -385,16 +390,16 @@ int mk_block_dots(const mk_weight* w, const float* dev_x, int n, int32_t* dev_ou
   return guard(MK_ERR_ARG, [&] {
     if (!w || n <= 0) throw mkb::ArgError("block_dots: bad argument");
     cudaStream_t s = as_stream(stream);
-    TmpAct t(n, w->w.cols, true);
-    mkb::launch_quant_rows(dev_x, w->w.cols, n, static_cast<int>(w->w.cols), t.act, s);
     mkb::DevBuf status(sizeof(int));
     mkb::cuda_check(cudaMemsetAsync(status.get(), 0, sizeof(int), s), "memset");
+    TmpAct t(n, w->w.cols, mkb::kQ8Exact);
+    mkb::launch_quant_rows(dev_x, w->w.cols, n, static_cast<int>(w->w.cols), t.act, s);
     mkb::launch_block_dots(w->w, t.act, n, dev_out, status.get<int>(), s);
     mkb::cuda_check(cudaGetLastError(), "block_dots");
     int st = 0;
     mkb::cuda_check(cudaMemcpyAsync(&st, status.get(), sizeof st, cudaMemcpyDeviceToHost, s), "status");
     mkb::cuda_check(cudaStreamSynchronize(s), "block_dots");
-    if (st != 0) throw mkb::TimeoutError("block_dots: device pipeline wait gave up");
+    if (st != 0) mkb::throw_device_status(st, "block_dots");
   });
 }
 

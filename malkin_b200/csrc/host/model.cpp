@@ -390,7 +390,7 @@ void Model::alloc_kv(int n_ctx, int n_seq, int max_batch) {
                o_gu = take(static_cast<size_t>(s_gu) * gu_slice_ * 4), o_p = take(static_cast<size_t>(NB) * E * 4),
                o_part = take(static_cast<size_t>(s_part) * part_slice_ * 4),
                o_lg = take(static_cast<size_t>(NB) * Vl_ * 4), o_qx = take(static_cast<size_t>(blocks) * NB * 32),
-               o_qc = take(static_cast<size_t>(blocks) * NB * 64),
+               o_qc = take(static_cast<size_t>(blocks) * NB * q8_act_bytes(q8_mode())),
                o_dx = take(static_cast<size_t>(blocks) * NB * 4), o_dsx = take(static_cast<size_t>(blocks) * NB * 4),
                o_sh = take(static_cast<size_t>(blocks) * NB * 4),
                o_cv = take(static_cast<size_t>(NB) * MK_TOPK_CAP * 4), o_ci = take(static_cast<size_t>(NB) * MK_TOPK_CAP * 4),
@@ -408,11 +408,12 @@ void Model::alloc_kv(int n_ctx, int n_seq, int max_batch) {
   part_ = reinterpret_cast<float*>(sb + o_part);
   logits_ = reinterpret_cast<float*>(sb + o_lg);
   act_.qx = sb + o_qx;
-  // the Q8_0 tensor-core GEMMs read the int8 copy (exact mode) or the fp16 copy (default) of the activations
-  if (q8_mode() == kQ8Exact)
-    act_.qc = sb + o_qc;
-  else
+  // the Q8_0 tensor-core GEMMs read the int8 copy (exact and split modes) or the fp16 copy of the activations
+  act_.q8 = q8_mode();
+  if (act_.q8 == kQ8Fp16)
     act_.xh = reinterpret_cast<uint16_t*>(sb + o_qc);
+  else
+    act_.qc = sb + o_qc;
   act_.dx = reinterpret_cast<float*>(sb + o_dx);
   act_.dsx = reinterpret_cast<float*>(sb + o_dsx);
   act_.sh = reinterpret_cast<uint32_t*>(sb + o_sh);
@@ -711,12 +712,19 @@ void Model::forward(const mk_batch_token* batch, int n, float* host_logits) {
   }
 }
 
+void throw_device_status(int code, const std::string& what) {
+  if (code == kErrFp16Range)
+    throw UnsupportedError(what + ": an activation exceeds the fp16 range (65504) of the split-fp16 Q8_0 GEMM; "
+                           "MALKIN_B200_Q8_GEMM=exact computes it in f32");
+  throw TimeoutError(what + ": device pipeline wait gave up (code " + std::to_string(code) + ")");
+}
+
 void Model::check_status() {
   int st = 0;
   cuda_check(cudaMemcpy(&st, status_, sizeof st, cudaMemcpyDeviceToHost), "status");
   if (st != 0) {
     cuda_check(cudaMemset(status_, 0, sizeof st), "status reset");
-    throw TimeoutError("device pipeline wait gave up (code " + std::to_string(st) + "): results of this step are invalid");
+    throw_device_status(st, "forward (results of this step are invalid)");
   }
 }
 
@@ -869,7 +877,7 @@ void Model::accept(const mk_proposal* props, int np, mk_accept_result* res) {
   if (*h_status != 0) {
     const int code = *h_status;
     cuda_check(cudaMemset(status_, 0, sizeof(int)), "status reset");
-    throw TimeoutError("device pipeline wait gave up (code " + std::to_string(code) + "): results of this step are invalid");
+    throw_device_status(code, "verify step (results of this step are invalid)");
   }
   for (int i = 0; i < np; ++i) {
     const AcceptOut& o = h_out[i];

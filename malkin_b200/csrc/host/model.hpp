@@ -66,6 +66,9 @@ struct TimeoutError : std::runtime_error {      // MK_ERR_TIMEOUT: a device-side
 
 // Throws CudaError with the CUDA error string.
 void cuda_check(cudaError_t e, const char* what);
+// Throws for a nonzero device status word: UnsupportedError for an activation outside the fp16 range of the
+// split-fp16 GEMM (malkin's f32 path has no such limit), TimeoutError for a bounded wait that gave up.
+void throw_device_status(int code, const std::string& what);
 
 // The config of a qwen3 GGUF (read_config, model.cpp:78-101), and the slice of it one tensor-parallel rank holds:
 // q / kv heads (column split), ffn rows in whole k-units of ffn_down, vocabulary rows (split of the LM head).

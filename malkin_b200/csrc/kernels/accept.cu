@@ -26,7 +26,31 @@ __global__ void k_argmax(const float* __restrict__ logits, int64_t ld, int V, in
   const float* l = logits + static_cast<size_t>(row) * ld;
   float bv = -INFINITY;
   int bi = INT32_MAX;
-  for (int i = tid; i < V; i += blockDim.x) {
+  // (value, lowest index) is order independent, so the row may be read in any order: 16-byte loads, four in flight
+  // per thread, when the row is 16-byte aligned; the scalar tail (and unaligned rows) after.
+  int done = 0;
+  if ((reinterpret_cast<uintptr_t>(l) & 15) == 0) {
+    const float4* l4 = reinterpret_cast<const float4*>(l);
+    const int n4 = V / 4;
+    const int step = static_cast<int>(blockDim.x);
+    for (int b = tid; b < n4; b += 4 * step) {
+      float4 q[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        q[u] = b + u * step < n4 ? l4[b + u * step] : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (b + u * step >= n4) break;
+        const int i = 4 * (b + u * step);
+        if (better(q[u].x, i, bv, bi)) bv = q[u].x, bi = i;
+        if (better(q[u].y, i + 1, bv, bi)) bv = q[u].y, bi = i + 1;
+        if (better(q[u].z, i + 2, bv, bi)) bv = q[u].z, bi = i + 2;
+        if (better(q[u].w, i + 3, bv, bi)) bv = q[u].w, bi = i + 3;
+      }
+    }
+    done = n4 * 4;
+  }
+  for (int i = done + tid; i < V; i += blockDim.x) {
     const float v = l[i];
     if (better(v, i, bv, bi)) bv = v, bi = i;
   }
@@ -340,7 +364,7 @@ void launch_argmax(const float* logits, int64_t ld, int m, int V, int vbase, flo
 
 void launch_argmax_kc(const float* logits, int64_t ld, int m, int V, int vbase, int kc, float* best_v, int32_t* best_i,
                       cudaStream_t s) {
-  if (m > 0) k_argmax<<<m, 512, 0, s>>>(logits, ld, V, vbase, kc, best_v, best_i);
+  if (m > 0) k_argmax<<<m, 1024, 0, s>>>(logits, ld, V, vbase, kc, best_v, best_i);
 }
 
 void launch_topk(const float* logits, int64_t ld, int m, int V, int vbase, int k, int kc, float* cand_v,

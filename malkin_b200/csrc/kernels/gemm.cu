@@ -429,11 +429,13 @@ void launch_t(const GemmArgs& a, dim3 grid, int nt, cudaStream_t s) {
 
 int q8_mode() {
   const char* e = std::getenv("MALKIN_B200_Q8_GEMM");
-  return e && std::string(e) == "fp16" ? kQ8Fp16 : kQ8Exact;
+  if (e && std::string(e) == "fp16") return kQ8Fp16;
+  if (e && std::string(e) == "split") return kQ8Split;
+  return kQ8Exact;
 }
 
 int gemm_split_for(const DevWeight& w, int num_sms) {
-  if (w.layout == kLayoutTc) return gemm_tc_split_for(w, num_sms);
+  if (w.layout == kLayoutTc) return q8_mode() == kQ8Split ? gemm_x3_split_for(w, num_sms) : gemm_tc_split_for(w, num_sms);
   const int64_t tiles = (w.panels + kTilePanels - 1) / kTilePanels;
   const int max_split = std::max(1, w.kunits / (w.type == 8 ? 8 : 1));
   int best = 1;
@@ -460,7 +462,9 @@ void launch_gemm(const DevWeight& w, const ActQ& act, int n, float* y, int64_t l
                  int* status, cudaStream_t s) {
   if (n <= 0) return;
   if (w.layout == kLayoutTc) {
-    if (act.xh)
+    if (act.q8 == kQ8Split)
+      launch_gemm_x3(w, act, n, y, ldy, slice, split, status, s);
+    else if (act.q8 == kQ8Fp16)
       launch_gemm_f16(w, act, n, y, ldy, slice, split, status, s);
     else
       launch_gemm_tc(w, act, n, y, ldy, slice, split, nullptr, status, s);

@@ -19,11 +19,19 @@ inline int act_tiles(int n) {
   return t <= 18 ? (t + 1) / 2 * 2 : (t + 17) / 18 * 18;
 }
 
+// Status-word code of an activation outside the fp16 range of the split-fp16 GEMM operand (bounded-wait timeouts use
+// codes 1-10 and 16 up).
+constexpr int kErrFp16Range = 11;
+
+// Arithmetic of the Q8_0 tensor-core GEMM (see launch_gemm below).
+enum Q8Mode { kQ8Fp16 = 0, kQ8Exact = 1, kQ8Split = 2 };
+
 // Quantized activations in the GEMM layout (layout.hpp). nt8 = token tiles of the current batch (layout stride).
 struct ActQ {
   uint8_t* qx = nullptr;
   uint8_t* qc = nullptr;  // tensor-core order of the same int8 values (nullable)
   uint16_t* xh = nullptr;  // fp16 of q * d in tensor-core order (nullable), layout.hpp
+  int q8 = kQ8Exact;       // Q8Mode the tensor-core Q8_0 GEMM runs in (qc for exact / split, xh for fp16)
   float* dx = nullptr;
   float* dsx = nullptr;
   uint32_t* sh = nullptr;
@@ -78,14 +86,24 @@ int gemm_slices(const DevWeight& w, int split);
 void launch_block_dots(const DevWeight& w, const ActQ& act, int n, int32_t* out, int* status, cudaStream_t s);
 
 // ---- tensor-core Q8_0 GEMMs, reached through launch_gemm / launch_block_dots ----
-// Arithmetic of the Q8_0 GEMM: kQ8Exact (default) keeps malkin's exact int8 block dots and per-block float
-// epilogue (tcgen05 kind::i8, gemm_tc.cu; bit-identical to malkin at split 1); kQ8Fp16 multiplies the dequantized
-// operands fp16(q * d) on tcgen05 kind::f16 with fp32 accumulation across blocks (gemm_f16.cu): faster, but each
-// product carries two fp16 roundings, which move logits of the synthetic test models by up to about 2e-2. The
-// environment variable MALKIN_B200_Q8_GEMM=fp16 selects it; q8_mode() reads it on every call. launch_gemm runs the
-// fp16 kernel when act.xh is set and the int8 kernel otherwise (act.qc), so the owner of the activation buffers picks.
-enum Q8Mode { kQ8Fp16 = 0, kQ8Exact = 1 };
+// Arithmetic of the Q8_0 GEMM:
+//   kQ8Exact  malkin's exact int8 block dots and per-block float epilogue (tcgen05 kind::i8, gemm_tc.cu, plus the
+//             mma.sync panel kernel for the shapes it wins); bit-identical to malkin at split 1.
+//   kQ8Split  the dequantized operands q * d split into fp16 hi + lo terms, three kind::f16 MMAs per 16 values
+//             accumulated in fp32 across blocks (gemm_x3.cu): about 2^-21 relative error per product, no per-block
+//             epilogue. Reads the int8 qc copy and dx like the exact kernel. Needs |q_x * d_x| < 65520 (fp16
+//             range); a value outside it sets kErrFp16Range.
+//   kQ8Fp16   one fp16 term per operand (gemm_f16.cu): two fp16 roundings per product, which move logits of the
+//             synthetic test models by up to about 2e-2.
+// The environment variable MALKIN_B200_Q8_GEMM (exact | split | fp16) selects it; q8_mode() reads it on every call.
+// launch_gemm runs the kernel of act.q8, which the owner of the activation buffers sets with the buffers.
 int q8_mode();
+// Bytes per (32-value block, padded token) of the tensor-core activation copy the mode reads: int8 qc (32) or
+// fp16 xh (64).
+inline int q8_act_bytes(int mode) { return mode == kQ8Fp16 ? 64 : 32; }
+void launch_gemm_x3(const DevWeight& w, const ActQ& act, int n, float* y, int64_t ldy, int64_t slice, int split,
+                    int* status, cudaStream_t s);
+int gemm_x3_split_for(const DevWeight& w, int num_sms);
 void launch_gemm_f16(const DevWeight& w, const ActQ& act, int n, float* y, int64_t ldy, int64_t slice, int split,
                      int* status, cudaStream_t s);
 void launch_gemm_tc(const DevWeight& w, const ActQ& act, int n, float* y, int64_t ldy, int64_t slice, int split,

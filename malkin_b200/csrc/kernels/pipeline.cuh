@@ -61,6 +61,31 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, i
   return __all_sync(0xffffffffu, ok) != 0;
 }
 
+// mbar_wait_warp for a warp in which only lane 0 acts on the guarded data (an MMA issuer): lane 0 alone polls, so
+// the wait costs one shared-memory access per poll instead of 32, and the outcome is broadcast to the warp.
+__device__ __forceinline__ bool mbar_wait_lane0(uint64_t* bar, uint32_t parity, int* status, int code) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, status, code) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+// mbar_wait_warp for waits that are long or off the critical path: the warp sleeps about sleep_ns between polls,
+// leaving its issue slots and the shared-memory pipe to the warps doing the work (the bound grows to
+// kWaitLimit * sleep_ns).
+__device__ __forceinline__ bool mbar_wait_warp_sleep(uint64_t* bar, uint32_t parity, int* status, int code,
+                                                     uint32_t sleep_ns) {
+  bool ok = false;
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) {
+      ok = true;
+      break;
+    }
+    __nanosleep(sleep_ns);
+  }
+  if (!ok && status) atomicCAS(status, 0, code);
+  return __all_sync(0xffffffffu, ok) != 0;
+}
+
 // 1-D bulk copy global -> shared, completion counted in bytes on bar. dst, src 16-byte aligned; bytes % 16 == 0.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(

@@ -245,3 +245,56 @@ def test_q8_fp16_gemm_within_bound(mk, oracle, torch_cuda, monkeypatch, rows, co
         assert np.isfinite(err).all() and (err <= bound).all(), (split, float(np.nanmax(err)))
         # typical error: a few fp16 roundings' worth relative to the typical output
         assert np.sqrt((err**2).mean()) <= 1e-3 * np.sqrt((ref**2).mean()), split
+
+
+@pytest.mark.parametrize("rows,cols,n", [(128, 256, 16), (300, 512, 136), (257, 2048, 144), (130, 96, 256),
+                                         (64, 512, 257), (200, 1024, 433), (4096, 4096, 136)])
+def test_q8_split_gemm_within_bound(mk, oracle, torch_cuda, monkeypatch, rows, cols, n):
+    """The split-fp16 Q8_0 GEMM (MALKIN_B200_Q8_GEMM=split: q d as fp16 hi + lo on both operands, three tcgen05
+    kind::f16 MMAs per 16 values, one fp32 accumulator) against malkin's exact result. Per product the split loses
+    at most 2^-21 relative (A = hi + lo exact, B keeps 22 bits, the A_lo B_lo term dropped); the rest is fp32
+    accumulation on both sides, so |y - malkin| <= (2^-20 + 2 K 2^-24) * sum_k |a_k b_k|. The typical error is set by
+    the tensor core's fp32 accumulation (about one 2^-24 step per MMA, six MMAs per block: 1.4e-5 of the output RMS at
+    K = 4096), far below the one-term fp16 kernel's 1e-3."""
+    monkeypatch.setenv("MALKIN_B200_Q8_GEMM", "split")
+    torch = torch_cuda
+    from make_golden import random_rows
+    rng = np.random.default_rng(rows + 3 * cols + 5 * n + 1)
+    w = random_rows(rng, 8, rows, cols)
+    x = rng.uniform(-3, 3, (n, cols)).astype(np.float32)
+    W = mk.Weight(8, w, rows, cols)
+    ref = oracle.matmul(8, w, rows, cols, x).astype(np.float64)
+    wd = np.stack([oracle.dequantize_row(8, w[r], cols) for r in range(rows)]).astype(np.float64)
+    xd = np.stack([(b["qs"].astype(np.float64) * b["d"].astype(np.float64)[:, None]).reshape(-1)
+                   for b in (oracle.quantize_row_q8(r) for r in x)])
+    bound = (np.abs(xd) @ np.abs(wd).T) * (2.0**-20 + 2 * cols * 2.0**-24)
+    y = torch.full((n, rows), np.nan, dtype=torch.float32, device="cuda")
+    for split in (1, 5, 0):
+        y.fill_(np.nan)
+        W.matmul(dev(torch, x).data_ptr(), n, y.data_ptr(), split_k=split)
+        err = np.abs(y.cpu().numpy().astype(np.float64) - ref)
+        assert np.isfinite(err).all() and (err <= bound).all(), (split, float(np.nanmax(err)))
+        typical = max(1e-5, 6 * (cols // 32) * 2.0**-24)
+        assert np.sqrt((err**2).mean()) <= typical * np.sqrt((ref**2).mean()), (split, float(np.sqrt((err**2).mean())))
+    # the exact int8 block dots stay available in this mode
+    dots = torch.zeros((rows, n, cols // 32), dtype=torch.int32, device="cuda")
+    W.block_dots(dev(torch, x).data_ptr(), n, dots.data_ptr())
+    assert np.array_equal(dots.cpu().numpy(), oracle.block_dots(8, w, rows, cols, x))
+
+
+def test_q8_split_gemm_rejects_fp16_overflow(mk, torch_cuda, monkeypatch):
+    """An activation beyond the fp16 range of the split operand is reported (MK_ERR_UNSUPPORTED), not rounded to inf."""
+    monkeypatch.setenv("MALKIN_B200_Q8_GEMM", "split")
+    torch = torch_cuda
+    from make_golden import random_rows
+    rng = np.random.default_rng(5)
+    w = random_rows(rng, 8, 128, 256)
+    x = rng.uniform(-3, 3, (16, 256)).astype(np.float32)
+    x[3, 17] = 1.0e5
+    W = mk.Weight(8, w, 128, 256)
+    y = torch.zeros((16, 128), dtype=torch.float32, device="cuda")
+    with pytest.raises(mk.MalkinError, match="fp16 range"):
+        W.matmul(dev(torch, x).data_ptr(), 16, y.data_ptr(), split_k=1)
+    x[3, 17] = 6.0e4  # inside the range: accepted
+    W.matmul(dev(torch, x).data_ptr(), 16, y.data_ptr(), split_k=1)
+    assert np.isfinite(y.cpu().numpy()).all()

@@ -32,7 +32,7 @@ def test_noalloc_matches_matmul_on_consecutive_calls(mk, torch_cuda, t):
 
 def test_noalloc_rejects_activations_beyond_scratch(mk, torch_cuda):
     torch = torch_cuda
-    rows, cols, n = 64, 4096, 2048  # 128 blocks x 2048 tokens x 108 B > 16 MiB
+    rows, cols, n = 64, 4096, 2048  # 128 blocks x 2048 tokens x 76 B > 16 MiB
     W, _ = _weight(mk, 8, rows, cols, 7)
     x = torch.zeros((n, cols), device="cuda")
     y = torch.zeros((n, rows), device="cuda")
