@@ -4,6 +4,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <stdexcept>
 #include <string>
@@ -69,6 +70,7 @@ Model::~Model() {
   cudaSetDevice(device_);
   for (auto& [k, g] : graphs_) cudaGraphExecDestroy(g);
   graphs_.clear();
+  close_tp_exchange();
   if (nccl_) dl_comm_destroy(static_cast<ncclComm_t>(nccl_));
   if (meta_host_) cudaFreeHost(meta_host_);
   if (acc_host_) cudaFreeHost(acc_host_);
@@ -422,6 +424,7 @@ void Model::alloc_kv(int n_ctx, int n_seq, int max_batch) {
   gath_v_ = reinterpret_cast<float*>(sb + o_gv);
   gath_i_ = reinterpret_cast<int32_t*>(sb + o_gi);
   status_ = reinterpret_cast<int*>(sb + o_st);
+  setup_tp_exchange(static_cast<size_t>(NB) * E);
   // attention plan geometry
   const int G = c.n_head / c.n_head_kv;
   sg_rows_ = std::max(1, attn_qmax() / G);
@@ -469,6 +472,92 @@ void Model::stage(int i) {
   pstage_[pk_++] = i;
 }
 
+// Exchange buffers for the peer-memory rank sum: allocated and zeroed here, their CUDA IPC handles allgathered over
+// NCCL (which also orders every rank's zeroing before any rank's first publish), the peers' handles opened. Every
+// rank must be able to map every peer; the ranks agree on that with a min-allreduce and fall back to NCCL together
+// otherwise (also when MALKIN_B200_TP_REDUCE=nccl).
+void Model::setup_tp_exchange(size_t floats) {
+  close_tp_exchange();
+  if (tp_size_ <= 1) return;
+  auto comm = static_cast<ncclComm_t>(nccl_);
+  const size_t cap = (floats + 63) / 64 * 64;
+  const size_t bytes = 2 * cap * sizeof(float) + kMaxTp * sizeof(int) + 64;
+  tpx_ = DevBuf(bytes);
+  cuda_check(cudaMemsetAsync(tpx_.get(), 0, bytes, stream_), "tp exchange memset");
+  cudaIpcMemHandle_t mine{};
+  int ok = 1;
+  const char* e = std::getenv("MALKIN_B200_TP_REDUCE");
+  if (e && std::string(e) == "nccl") ok = 0;
+  if (ok && cudaIpcGetMemHandle(&mine, tpx_.get()) != cudaSuccess) {
+    cudaGetLastError();
+    ok = 0;
+  }
+  DevBuf hbuf(static_cast<size_t>(tp_size_) * sizeof mine + sizeof(int));
+  auto* hb = hbuf.get<uint8_t>();
+  cuda_check(cudaMemcpyAsync(hb + tp_rank_ * sizeof mine, &mine, sizeof mine, cudaMemcpyHostToDevice, stream_),
+             "ipc handle upload");
+  nccl_check(dl_all_gather(hb + tp_rank_ * sizeof mine, hb, sizeof mine, ncclUint8, comm, stream_), "ipc allgather");
+  std::vector<cudaIpcMemHandle_t> all(static_cast<size_t>(tp_size_));
+  cuda_check(cudaMemcpyAsync(all.data(), hb, all.size() * sizeof mine, cudaMemcpyDeviceToHost, stream_),
+             "ipc handle download");
+  cuda_check(cudaStreamSynchronize(stream_), "ipc exchange");
+  for (int r = 0; r < tp_size_ && ok; ++r) {
+    if (r == tp_rank_) continue;
+    void* p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, all[static_cast<size_t>(r)], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      ok = 0;
+    } else {
+      tpx_peer_[r] = p;
+    }
+  }
+  // every rank takes the same path
+  int* d_ok = reinterpret_cast<int*>(hb + tp_size_ * sizeof mine);
+  cuda_check(cudaMemcpyAsync(d_ok, &ok, sizeof ok, cudaMemcpyHostToDevice, stream_), "tp ok upload");
+  nccl_check(dl_all_reduce(d_ok, d_ok, 1, ncclInt32, ncclMin, comm, stream_), "tp ok allreduce");
+  int all_ok = 0;
+  cuda_check(cudaMemcpyAsync(&all_ok, d_ok, sizeof all_ok, cudaMemcpyDeviceToHost, stream_), "tp ok download");
+  cuda_check(cudaStreamSynchronize(stream_), "tp ok");
+  if (!all_ok) {
+    close_tp_exchange();
+    return;
+  }
+  TpExchange& x = tpx_args_;
+  x = TpExchange{};
+  for (int r = 0; r < tp_size_; ++r) {
+    auto* base = static_cast<uint8_t*>(r == tp_rank_ ? tpx_.get() : tpx_peer_[r]);
+    x.data[r] = reinterpret_cast<float*>(base);
+    x.flags[r] = reinterpret_cast<int*>(base + 2 * cap * sizeof(float));
+  }
+  auto* own = tpx_.get<uint8_t>() + 2 * cap * sizeof(float) + kMaxTp * sizeof(int);
+  x.epoch = reinterpret_cast<int*>(own);
+  x.counter = reinterpret_cast<unsigned*>(own + 32);
+  x.rank = tp_rank_;
+  x.size = tp_size_;
+  x.cap = static_cast<int64_t>(cap);
+  tpx_on_ = true;
+}
+
+void Model::close_tp_exchange() {
+  for (auto& p : tpx_peer_) {
+    if (p) cudaIpcCloseMemHandle(p);
+    p = nullptr;
+  }
+  tpx_ = DevBuf();
+  tpx_on_ = false;
+}
+
+void Model::tp_sum(Slices parts, int n) {
+  const int E = cfg_.n_embd;
+  if (tpx_on_) {
+    launch_tp_publish(tpx_args_, parts, E, n, E, stream_);
+    launch_tp_gather(tpx_args_, n, E, p_, status_, stream_);
+  } else {
+    launch_sum_slices(parts, E, n, E, p_, stream_);
+    allreduce(p_, static_cast<size_t>(n) * E);
+  }
+}
+
 void Model::allreduce(float* buf, size_t count) {
   nccl_check(dl_all_reduce(buf, buf, count, ncclFloat, ncclSum, static_cast<ncclComm_t>(nccl_), stream_),
              "allreduce");
@@ -509,8 +598,7 @@ void Model::run_forward(int n, int m) {
     gemm(L.wo, L.wo_split, n, part_, E, part_slice_);
     Slices wo_add{part_, L.wo_split, part_slice_};
     if (tp) {
-      launch_sum_slices(wo_add, E, n, E, p_, stream_);
-      allreduce(p_, static_cast<size_t>(n) * E);
+      tp_sum(wo_add, n);
       wo_add = Slices{p_, 1, 0};
     }
     launch_rmsnorm_quant(x_, E, wo_add, nullptr, L.ffn_norm, c.rms_eps, n, E, act_, stream_);
@@ -522,8 +610,7 @@ void Model::run_forward(int n, int m) {
     gemm(L.down, L.down_split, n, part_, E, part_slice_);
     pending = Slices{part_, L.down_split, part_slice_};
     if (tp) {
-      launch_sum_slices(pending, E, n, E, p_, stream_);
-      allreduce(p_, static_cast<size_t>(n) * E);
+      tp_sum(pending, n);
       pending = Slices{p_, 1, 0};
     }
     stage(6);

@@ -128,6 +128,11 @@ class Model {
   // y slices = W x: slice s at y + s * slice (split-K partial sums, summed in order by the consumer)
   void gemm(const DevWeight& w, int split, int n, float* y, int64_t ldy, int64_t slice);
   void allreduce(float* buf, size_t count);
+  // The rank sum of row-split partials (split-K slices) into p_: peer-memory kernels when the exchange is set up,
+  // else slice sum + ncclAllReduce.
+  void tp_sum(Slices parts, int n);
+  void setup_tp_exchange(size_t floats);
+  void close_tp_exchange();
   void stage(int i);                             // profile lap
   void ensure_meta(size_t anc_cap);
   void check_status();  // throws TimeoutError if a kernel recorded a failed bounded wait
@@ -135,6 +140,11 @@ class Model {
   ModelCfg cfg_;
   int device_ = 0, tp_rank_ = 0, tp_size_ = 1, num_sms_ = 148;
   void* nccl_ = nullptr;  // ncclComm_t
+  // tensor-parallel exchange over peer memory (tp_reduce.cu): own buffer, peers' IPC mappings, kernel arguments
+  DevBuf tpx_;
+  void* tpx_peer_[kMaxTp] = {};
+  TpExchange tpx_args_;
+  bool tpx_on_ = false;
   cudaStream_t stream_ = nullptr;
   bool loaded_ = false;
 

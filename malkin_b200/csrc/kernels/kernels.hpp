@@ -111,6 +111,24 @@ void launch_gemm_tc(const DevWeight& w, const ActQ& act, int n, float* y, int64_
 int gemm_tc_split_for(const DevWeight& w, int num_sms);
 int gemm_tc_slices(const DevWeight& w, int split);
 
+// ---- tensor-parallel sum over NVLink peer memory (tp_reduce.cu) ----
+// Rank r's exchange buffer: data[r] = two halves of `cap` floats, flags[r] = one int per rank (the last epoch that
+// rank published into r); the pointers of the other ranks are their CUDA IPC mappings in this process.
+constexpr int kMaxTp = 8;
+constexpr int kErrTpWait = 12;  // status code: a rank's partial never arrived
+struct TpExchange {
+  float* data[kMaxTp] = {};
+  int* flags[kMaxTp] = {};
+  int* epoch = nullptr;         // this rank's call counter (device)
+  unsigned* counter = nullptr;  // this rank's CTA arrival counter (device)
+  int rank = 0, size = 1;
+  int64_t cap = 0;
+};
+// publish: this rank's split-K slices, summed in slice order, into its half of the exchange; gather: the sum over
+// ranks in rank order into dst (n x cols, cols % 4 == 0). Run both, in this order, on every rank.
+void launch_tp_publish(const TpExchange& x, Slices src, int64_t ld, int n, int cols, cudaStream_t s);
+void launch_tp_gather(const TpExchange& x, int n, int cols, float* dst, int* status, cudaStream_t s);
+
 // ---- fixed scratch of the allocation-free entry point (noalloc.cu) ----
 // Bytes of the per-device scratch, and its address on the current device (nullptr and *err set on failure).
 size_t noalloc_scratch_bytes();

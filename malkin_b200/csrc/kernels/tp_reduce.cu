@@ -1,0 +1,128 @@
+// Tensor-parallel sum of the row-split GEMM partials (attention output and ffn down) over NVLink peer memory:
+// the B200-native replacement of "sum the split-K slices, then ncclAllReduce" (malkin has no tensor parallelism; the
+// sum is the allreduce of the Megatron split of wo / down).
+//
+// Every rank owns an exchange buffer (two halves of `cap` floats, a flag word per rank, an epoch counter and a CTA
+// arrival counter), mapped into every other rank with CUDA IPC. One call is two kernels on the rank's stream:
+//   publish: sums this rank's split-K slices (slice order) into half (epoch & 1) of its own buffer; each CTA
+//            fences system-wide and counts its arrival, and the last one advances the epoch and stores it with
+//            release semantics into flag[rank] of every rank's buffer;
+//   gather:  waits (bounded) until every rank's flag in this rank's buffer has reached the epoch, then sums the
+//            ranks' halves in rank order 0..size-1, so every rank gets bit-identical results.
+// A half is rewritten two calls later; by then every rank has published the call in between, which it does only
+// after its gather of the earlier call finished, so no rank still reads it. A wait that runs out records
+// kErrTpWait in the status word and the kernel returns (a rank that died or never launched).
+#include <cuda_runtime.h>
+
+#include "kernels.hpp"
+
+namespace mkb {
+
+namespace {
+
+constexpr uint32_t kTpWaitLimit = 1u << 24;  // polls of about 64 ns: about a second at most
+
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void k_tp_publish(TpExchange x, Slices src, int64_t ld, int n, int cols) {
+  const int e = *x.epoch + 1;  // the previous call's kernels have finished (stream order)
+  float* dst = x.data[x.rank] + static_cast<int64_t>(e & 1) * x.cap;
+  const int c4 = cols / 4;
+  const int64_t total4 = static_cast<int64_t>(n) * c4;  // cols % 4 == 0
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total4;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = i / c4, c = (i % c4) * 4;
+    const float4* p = reinterpret_cast<const float4*>(src.p + t * ld + c);
+    float4 v = p[0];
+    for (int s = 1; s < src.n; ++s) {
+      const float4 u = *reinterpret_cast<const float4*>(src.p + s * src.stride + t * ld + c);
+      v.x = __fadd_rn(v.x, u.x);
+      v.y = __fadd_rn(v.y, u.y);
+      v.z = __fadd_rn(v.z, u.z);
+      v.w = __fadd_rn(v.w, u.w);
+    }
+    reinterpret_cast<float4*>(dst)[i] = v;
+  }
+  // the CTA's stores, made visible to the CTA by the barrier, are ordered before the arrival by thread 0's fence
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const unsigned prev = atomicAdd(x.counter, 1u);
+    if (prev == gridDim.x - 1) {  // every CTA's part of the half is written and fenced
+      __threadfence_system();
+      *x.counter = 0;
+      *x.epoch = e;
+      for (int r = 0; r < x.size; ++r) st_release_sys(x.flags[r] + x.rank, e);
+    }
+  }
+}
+
+__global__ void k_tp_gather(TpExchange x, int n, int cols, float* __restrict__ dst, int* status) {
+  const int e = *x.epoch;  // set by this rank's publish (stream order)
+  __shared__ int ready;
+  if (threadIdx.x == 0) {
+    bool ok = true;
+    for (int r = 0; r < x.size && ok; ++r) {
+      uint32_t it = 0;
+      while (ld_acquire_sys(x.flags[x.rank] + r) < e) {
+        if (++it >= kTpWaitLimit) {
+          ok = false;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    if (!ok && status) atomicCAS(status, 0, kErrTpWait);
+    ready = ok;
+  }
+  __syncthreads();
+  if (!ready) return;
+  const int64_t off = static_cast<int64_t>(e & 1) * x.cap;
+  const int64_t total4 = static_cast<int64_t>(n) * cols / 4;  // cols % 4 == 0
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total4;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float4 v[kMaxTp];
+#pragma unroll
+    for (int r = 0; r < kMaxTp; ++r)  // every rank's load in flight at once
+      if (r < x.size) v[r] = __ldcv(reinterpret_cast<const float4*>(x.data[r] + off) + i);
+    float4 acc = v[0];
+#pragma unroll
+    for (int r = 1; r < kMaxTp; ++r)
+      if (r < x.size) {
+        acc.x = __fadd_rn(acc.x, v[r].x);
+        acc.y = __fadd_rn(acc.y, v[r].y);
+        acc.z = __fadd_rn(acc.z, v[r].z);
+        acc.w = __fadd_rn(acc.w, v[r].w);
+      }
+    reinterpret_cast<float4*>(dst)[i] = acc;
+  }
+}
+
+int tp_grid(int64_t items, int per_cta) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t g = (items + per_cta - 1) / per_cta;
+  return static_cast<int>(g < 1 ? 1 : (g > 4 * sms ? 4 * sms : g));
+}
+
+}  // namespace
+
+void launch_tp_publish(const TpExchange& x, Slices src, int64_t ld, int n, int cols, cudaStream_t s) {
+  if (n <= 0) return;
+  k_tp_publish<<<tp_grid(static_cast<int64_t>(n) * cols / 4, 256), 256, 0, s>>>(x, src, ld, n, cols);
+}
+
+void launch_tp_gather(const TpExchange& x, int n, int cols, float* dst, int* status, cudaStream_t s) {
+  if (n <= 0) return;
+  k_tp_gather<<<tp_grid(static_cast<int64_t>(n) * cols / 4, 256), 256, 0, s>>>(x, n, cols, dst, status);
+}
+
+}  // namespace mkb
