@@ -475,19 +475,22 @@ void Model::stage(int i) {
 // Exchange buffers for the peer-memory rank sum: allocated and zeroed here, their CUDA IPC handles allgathered over
 // NCCL (which also orders every rank's zeroing before any rank's first publish), the peers' handles opened. Every
 // rank must be able to map every peer; the ranks agree on that with a min-allreduce and fall back to NCCL together
-// otherwise (also when MALKIN_B200_TP_REDUCE=nccl).
+// otherwise (also when MALKIN_B200_TP_REDUCE=nccl). MALKIN_B200_TP_REDUCE=twoshot selects reduce + allgather
+// instead of the one-shot gather (every rank must set the same).
 void Model::setup_tp_exchange(size_t floats) {
   close_tp_exchange();
   if (tp_size_ <= 1) return;
   auto comm = static_cast<ncclComm_t>(nccl_);
   const size_t cap = (floats + 63) / 64 * 64;
-  const size_t bytes = 2 * cap * sizeof(float) + kMaxTp * sizeof(int) + 64;
+  // [data: 2 halves | red: 2 halves | flags[kMaxTp] | flags2[kMaxTp] | epoch, counter, counter2 (32 B apart)]
+  const size_t bytes = 4 * cap * sizeof(float) + 2 * kMaxTp * sizeof(int) + 128;
   tpx_ = DevBuf(bytes);
   cuda_check(cudaMemsetAsync(tpx_.get(), 0, bytes, stream_), "tp exchange memset");
   cudaIpcMemHandle_t mine{};
   int ok = 1;
   const char* e = std::getenv("MALKIN_B200_TP_REDUCE");
   if (e && std::string(e) == "nccl") ok = 0;
+  tpx_twoshot_ = e && std::string(e) == "twoshot";
   if (ok && cudaIpcGetMemHandle(&mine, tpx_.get()) != cudaSuccess) {
     cudaGetLastError();
     ok = 0;
@@ -527,11 +530,14 @@ void Model::setup_tp_exchange(size_t floats) {
   for (int r = 0; r < tp_size_; ++r) {
     auto* base = static_cast<uint8_t*>(r == tp_rank_ ? tpx_.get() : tpx_peer_[r]);
     x.data[r] = reinterpret_cast<float*>(base);
-    x.flags[r] = reinterpret_cast<int*>(base + 2 * cap * sizeof(float));
+    x.red[r] = reinterpret_cast<float*>(base + 2 * cap * sizeof(float));
+    x.flags[r] = reinterpret_cast<int*>(base + 4 * cap * sizeof(float));
+    x.flags2[r] = x.flags[r] + kMaxTp;
   }
-  auto* own = tpx_.get<uint8_t>() + 2 * cap * sizeof(float) + kMaxTp * sizeof(int);
+  auto* own = tpx_.get<uint8_t>() + 4 * cap * sizeof(float) + 2 * kMaxTp * sizeof(int);
   x.epoch = reinterpret_cast<int*>(own);
   x.counter = reinterpret_cast<unsigned*>(own + 32);
+  x.counter2 = reinterpret_cast<unsigned*>(own + 64);
   x.rank = tp_rank_;
   x.size = tp_size_;
   x.cap = static_cast<int64_t>(cap);
@@ -551,7 +557,12 @@ void Model::tp_sum(Slices parts, int n) {
   const int E = cfg_.n_embd;
   if (tpx_on_) {
     launch_tp_publish(tpx_args_, parts, E, n, E, stream_);
-    launch_tp_gather(tpx_args_, n, E, p_, status_, stream_);
+    if (tpx_twoshot_) {
+      launch_tp_reduce(tpx_args_, n, E, status_, stream_);
+      launch_tp_allgather(tpx_args_, n, E, p_, status_, stream_);
+    } else {
+      launch_tp_gather(tpx_args_, n, E, p_, status_, stream_);
+    }
   } else {
     launch_sum_slices(parts, E, n, E, p_, stream_);
     allreduce(p_, static_cast<size_t>(n) * E);

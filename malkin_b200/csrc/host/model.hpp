@@ -145,6 +145,7 @@ class Model {
   void* tpx_peer_[kMaxTp] = {};
   TpExchange tpx_args_;
   bool tpx_on_ = false;
+  bool tpx_twoshot_ = false;
   cudaStream_t stream_ = nullptr;
   bool loaded_ = false;
 

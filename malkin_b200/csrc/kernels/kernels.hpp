@@ -119,8 +119,11 @@ constexpr int kErrTpWait = 12;  // status code: a rank's partial never arrived
 struct TpExchange {
   float* data[kMaxTp] = {};
   int* flags[kMaxTp] = {};
-  int* epoch = nullptr;         // this rank's call counter (device)
-  unsigned* counter = nullptr;  // this rank's CTA arrival counter (device)
+  float* red[kMaxTp] = {};   // two-shot: rank r's reduced rows (two halves of `cap` floats)
+  int* flags2[kMaxTp] = {};  // two-shot: the last epoch rank q reduced its rows for, in rank r's buffer
+  int* epoch = nullptr;          // this rank's call counter (device)
+  unsigned* counter = nullptr;   // this rank's CTA arrival counters (device): publish, reduce
+  unsigned* counter2 = nullptr;
   int rank = 0, size = 1;
   int64_t cap = 0;
 };
@@ -128,6 +131,11 @@ struct TpExchange {
 // ranks in rank order into dst (n x cols, cols % 4 == 0). Run both, in this order, on every rank.
 void launch_tp_publish(const TpExchange& x, Slices src, int64_t ld, int n, int cols, cudaStream_t s);
 void launch_tp_gather(const TpExchange& x, int n, int cols, float* dst, int* status, cudaStream_t s);
+// Two-shot alternative to gather (after publish): reduce sums this rank's 1/size of the rows over the ranks (rank
+// order) into its red half; allgather copies every rank's reduced rows into dst. Same sums, bit for bit; each rank
+// reads 2 (size - 1) / size of the data from peers instead of (size - 1) times it.
+void launch_tp_reduce(const TpExchange& x, int n, int cols, int* status, cudaStream_t s);
+void launch_tp_allgather(const TpExchange& x, int n, int cols, float* dst, int* status, cudaStream_t s);
 
 // ---- fixed scratch of the allocation-free entry point (noalloc.cu) ----
 // Bytes of the per-device scratch, and its address on the current device (nullptr and *err set on failure).

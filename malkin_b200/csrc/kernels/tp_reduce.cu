@@ -12,6 +12,10 @@
 // A half is rewritten two calls later; by then every rank has published the call in between, which it does only
 // after its gather of the earlier call finished, so no rank still reads it. A wait that runs out records
 // kErrTpWait in the status word and the kernel returns (a rank that died or never launched).
+// Two-shot (opt-in): after publish, reduce sums this rank's 1/size of the rows over all ranks into its red half and
+// releases flags2; allgather waits for every rank's flags2 and copies each rank's reduced rows. Each rank reads
+// 2 (size - 1) / size of the data from peers (one-shot: size - 1 times it); the sums are the same, bit for bit. The
+// red half of a call is rewritten two calls later, after every rank published the next call (after its allgather).
 #include <cuda_runtime.h>
 
 #include "kernels.hpp"
@@ -105,6 +109,80 @@ __global__ void k_tp_gather(TpExchange x, int n, int cols, float* __restrict__ d
   }
 }
 
+// Bounded wait (thread 0 of the CTA) until flags[0..size) all reach e; false (and status) if one never does.
+__device__ bool wait_flags(const int* flags, int size, int e, int* status) {
+  __shared__ int ready;
+  if (threadIdx.x == 0) {
+    bool ok = true;
+    for (int r = 0; r < size && ok; ++r) {
+      uint32_t it = 0;
+      while (ld_acquire_sys(flags + r) < e) {
+        if (++it >= kTpWaitLimit) {
+          ok = false;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    if (!ok && status) atomicCAS(status, 0, kErrTpWait);
+    ready = ok;
+  }
+  __syncthreads();
+  return ready != 0;
+}
+
+// Rows of rank q's share of the reduction, in float4 units: [q * total4 / size, (q + 1) * total4 / size).
+__device__ __forceinline__ int64_t share_begin(int64_t total4, int q, int size) { return total4 * q / size; }
+
+__global__ void k_tp_reduce(TpExchange x, int n, int cols, int* status) {
+  const int e = *x.epoch;  // set by this rank's publish (stream order)
+  if (!wait_flags(x.flags[x.rank], x.size, e, status)) return;
+  const int64_t off = static_cast<int64_t>(e & 1) * x.cap;
+  const int64_t total4 = static_cast<int64_t>(n) * cols / 4;
+  const int64_t b = share_begin(total4, x.rank, x.size), end = share_begin(total4, x.rank + 1, x.size);
+  for (int64_t i = b + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < end;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float4 v[kMaxTp];
+#pragma unroll
+    for (int r = 0; r < kMaxTp; ++r)
+      if (r < x.size) v[r] = __ldcv(reinterpret_cast<const float4*>(x.data[r] + off) + i);
+    float4 acc = v[0];
+#pragma unroll
+    for (int r = 1; r < kMaxTp; ++r)
+      if (r < x.size) {
+        acc.x = __fadd_rn(acc.x, v[r].x);
+        acc.y = __fadd_rn(acc.y, v[r].y);
+        acc.z = __fadd_rn(acc.z, v[r].z);
+        acc.w = __fadd_rn(acc.w, v[r].w);
+      }
+    reinterpret_cast<float4*>(x.red[x.rank] + off)[i] = acc;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const unsigned prev = atomicAdd(x.counter2, 1u);
+    if (prev == gridDim.x - 1) {  // the whole share is reduced and fenced
+      __threadfence_system();
+      *x.counter2 = 0;
+      for (int r = 0; r < x.size; ++r) st_release_sys(x.flags2[r] + x.rank, e);
+    }
+  }
+}
+
+__global__ void k_tp_allgather(TpExchange x, int n, int cols, float* __restrict__ dst, int* status) {
+  const int e = *x.epoch;
+  if (!wait_flags(x.flags2[x.rank], x.size, e, status)) return;
+  const int64_t off = static_cast<int64_t>(e & 1) * x.cap;
+  const int64_t total4 = static_cast<int64_t>(n) * cols / 4;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total4;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int q = static_cast<int>(i * x.size / total4);  // owner of row i: the share with begin <= i < end
+    while (q > 0 && i < share_begin(total4, q, x.size)) --q;
+    while (q + 1 < x.size && i >= share_begin(total4, q + 1, x.size)) ++q;
+    reinterpret_cast<float4*>(dst)[i] = __ldcv(reinterpret_cast<const float4*>(x.red[q] + off) + i);
+  }
+}
+
 int tp_grid(int64_t items, int per_cta) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -123,6 +201,16 @@ void launch_tp_publish(const TpExchange& x, Slices src, int64_t ld, int n, int c
 void launch_tp_gather(const TpExchange& x, int n, int cols, float* dst, int* status, cudaStream_t s) {
   if (n <= 0) return;
   k_tp_gather<<<tp_grid(static_cast<int64_t>(n) * cols / 4, 256), 256, 0, s>>>(x, n, cols, dst, status);
+}
+
+void launch_tp_reduce(const TpExchange& x, int n, int cols, int* status, cudaStream_t s) {
+  if (n <= 0) return;
+  k_tp_reduce<<<tp_grid(static_cast<int64_t>(n) * cols / 4 / x.size + 1, 256), 256, 0, s>>>(x, n, cols, status);
+}
+
+void launch_tp_allgather(const TpExchange& x, int n, int cols, float* dst, int* status, cudaStream_t s) {
+  if (n <= 0) return;
+  k_tp_allgather<<<tp_grid(static_cast<int64_t>(n) * cols / 4, 256), 256, 0, s>>>(x, n, cols, dst, status);
 }
 
 }  // namespace mkb
