@@ -104,7 +104,9 @@ int mk_shutdown(mk_ctx* ctx);
  * uploads it. The file can be unmapped once this returns. */
 int mk_load_gguf(mk_ctx* ctx, const char* path);
 /* Model::alloc_kv (model.cpp:296-301): int8 KV cache for n_seq sequences of n_ctx positions, in HBM.
- * max_batch: largest forward batch (malkin: kMaxBatch = 256, model.h:35); 0 = 256. */
+ * max_batch: largest forward batch (malkin: kMaxBatch = 256, model.h:35); 0 = 256. Under tensor parallelism it is
+ * collective (every rank calls it with the same arguments): it maps the ranks' exchange buffers into each other
+ * with CUDA IPC for the rank sum, so the ranks must be separate processes. */
 int mk_alloc_kv(mk_ctx* ctx, int n_ctx, int n_seq, int max_batch);
 int mk_model_config_get(const mk_ctx* ctx, mk_model_config* out);
 
