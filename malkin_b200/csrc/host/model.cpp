@@ -476,7 +476,7 @@ void Model::stage(int i) {
 // NCCL (which also orders every rank's zeroing before any rank's first publish), the peers' handles opened. Every
 // rank must be able to map every peer; the ranks agree on that with a min-allreduce and fall back to NCCL together
 // otherwise (also when MALKIN_B200_TP_REDUCE=nccl). MALKIN_B200_TP_REDUCE=twoshot selects reduce + allgather
-// instead of the one-shot gather (every rank must set the same).
+// instead of the one-shot gather when every rank sets it.
 void Model::setup_tp_exchange(size_t floats) {
   close_tp_exchange();
   if (tp_size_ <= 1) return;
@@ -495,7 +495,7 @@ void Model::setup_tp_exchange(size_t floats) {
     cudaGetLastError();
     ok = 0;
   }
-  DevBuf hbuf(static_cast<size_t>(tp_size_) * sizeof mine + sizeof(int));
+  DevBuf hbuf(static_cast<size_t>(tp_size_) * sizeof mine + 2 * sizeof(int));
   auto* hb = hbuf.get<uint8_t>();
   cuda_check(cudaMemcpyAsync(hb + tp_rank_ * sizeof mine, &mine, sizeof mine, cudaMemcpyHostToDevice, stream_),
              "ipc handle upload");
@@ -514,13 +514,16 @@ void Model::setup_tp_exchange(size_t floats) {
       tpx_peer_[r] = p;
     }
   }
-  // every rank takes the same path
+  // every rank takes the same path: peer exchange only if every rank mapped every peer, two-shot only if every
+  // rank asked for it
+  int agree[2] = {ok, tpx_twoshot_ ? 1 : 0};
   int* d_ok = reinterpret_cast<int*>(hb + tp_size_ * sizeof mine);
-  cuda_check(cudaMemcpyAsync(d_ok, &ok, sizeof ok, cudaMemcpyHostToDevice, stream_), "tp ok upload");
-  nccl_check(dl_all_reduce(d_ok, d_ok, 1, ncclInt32, ncclMin, comm, stream_), "tp ok allreduce");
-  int all_ok = 0;
-  cuda_check(cudaMemcpyAsync(&all_ok, d_ok, sizeof all_ok, cudaMemcpyDeviceToHost, stream_), "tp ok download");
+  cuda_check(cudaMemcpyAsync(d_ok, agree, sizeof agree, cudaMemcpyHostToDevice, stream_), "tp ok upload");
+  nccl_check(dl_all_reduce(d_ok, d_ok, 2, ncclInt32, ncclMin, comm, stream_), "tp ok allreduce");
+  cuda_check(cudaMemcpyAsync(agree, d_ok, sizeof agree, cudaMemcpyDeviceToHost, stream_), "tp ok download");
   cuda_check(cudaStreamSynchronize(stream_), "tp ok");
+  const int all_ok = agree[0];
+  tpx_twoshot_ = agree[1] != 0;
   if (!all_ok) {
     close_tp_exchange();
     return;
