@@ -18,8 +18,8 @@
 // runs on across items without a per-CTA ramp, and the accumulator is double-buffered (N <= 192) so an item's
 // epilogue overlaps the next item's MMAs. Warps (608 threads):
 //   0      weight producer: TMA bulk copies of 4 records (layout.hpp, tile-major) per stage into a deep ring
-//   1      activation producer: the int8 block (N x 32) and its N scales per stage, by cp.async (bulk copies would
-//          queue behind the weight ring's in the TMA unit)
+//   1      activation producer: the int8 block (N x 32) and its N scales per stage, by cp.async (the TMA unit is
+//          left to the weight stream; measured no slower than bulk copies)
 //   2      TMEM owner; lane 0 issues the six MMAs (K = 16 each) of every block and the commits
 //   3..10  dequant: warp w serves TMEM lane quarter w % 4 (its 32 weight rows) and every other block of a stage;
 //          each thread forms hi / lo of q * d_w for its row's 32 values and stores them into an A slot in TMEM
@@ -236,9 +236,9 @@ __global__ void __launch_bounds__(kX3Threads, 1) k_gemm_x3(X3Args a) {
       if (!mbar_wait_warp(&wfull[i % kX3WStages], (i / kX3WStages) & 1, a.status, kErrWaitFull)) break;
   } else if (warp == kX3WarpB) {
     // ---------------- activation producer ----------------
-    // cp.async (16 bytes per lane and copy, through L1, not the TMA unit: behind the deep weight ring a bulk copy
-    // would wait for every weight stage queued before it). Each lane's copies of a stage arrive on rfull when they
-    // land (cp.async.mbarrier.arrive.noinc, 32 arrivals per stage).
+    // cp.async (16 bytes per lane and copy, through L1 rather than the TMA unit, which streams the weights). Each
+    // lane's copies of a stage arrive on rfull when they land (cp.async.mbarrier.arrive.noinc, 32 arrivals per
+    // stage).
     constexpr int CH = N * 36 / 16;  // 16-byte chunks per stage: N * 2 of int8 values, N / 4 of scales
     int n = 0;
     bool ok = true;
