@@ -203,8 +203,9 @@ __global__ void __launch_bounds__(kX3Threads, 1) k_gemm_x3(X3Args a) {
     b1 = min(a.kblocks, b0 + a.per_split);
   };
   // An item's blocks run in groups of kX3WRec (one weight stage each), the groups rotated by the tile index: CTAs
-  // that share a K range start at different groups, so they do not all read the same activation block from the
-  // same L2 lines at the same time. Group g of [b0, b1) starts at block group_start(g) and holds group_len(g).
+  // that share a K range start at different groups instead of reading the same activation block at the same time
+  // (measured neutral on B200; the fp32 accumulation order per item follows the rotation). Group g of [b0, b1)
+  // starts at block group_start(g).
   auto groups = [&](int b0, int b1) { return (b1 - b0 + kX3WRec - 1) / kX3WRec; };
   auto group_start = [&](int tile, int b0, int b1, int g) { return b0 + ((g + tile) % groups(b0, b1)) * kX3WRec; };
 
