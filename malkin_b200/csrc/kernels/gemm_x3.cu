@@ -57,8 +57,9 @@ constexpr uint32_t kX3Cols = 512;
 constexpr int kX3MaxSlots = 8;  // A slots of 32 columns: hi K 0-15 | hi K 16-31 | lo K 0-15 | lo K 16-31
 constexpr int kErrX3AFull = 8, kErrX3AEmpty = 9, kErrX3Acc = 10;
 constexpr uint32_t kX3WStageBytes = kX3WRec * static_cast<uint32_t>(kTcRecord);
-// Sleep between polls of a wait (ns): waiting warps would otherwise take issue slots and shared-memory pipe cycles
-// from the dequant and converter warps. The MMA issuer polls without sleeping (its waits are on the critical path).
+// Sleep between polls of a wait (ns) for warps off the MMA's critical path, so their polling does not compete for
+// issue slots with the dequant and converter warps (measured within noise of polling without sleeping). The MMA
+// issuer polls without sleeping.
 constexpr uint32_t kX3SleepProducer = 128, kX3SleepWorker = 32, kX3SleepEpilogue = 256;
 
 struct X3Args {
