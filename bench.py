@@ -258,12 +258,17 @@ def run_reference(args, cfg):
 
 def config_json(args, cfg):
     m = spec_of(cfg)
-    return {"workload": f"qwen3-{args.config} synthetic, {cfg['requests']} req x {2 * cfg['kk']}-node trees "
-                        f"(chain {cfg['kk']} + siblings), {cfg['prompt']}-token KV prefix, greedy accept",
-            "model": f"Qwen3-{args.config} architecture", "weights": "Q8_0" if m["type_default"] == Q8_0 else
-            ("Q4_K" if m["type_default"] == Q4_K else "Q6_K"), "requests": cfg["requests"],
-            "rows_per_step": cfg["requests"] * (2 * cfg["kk"] + 1), "prompt": cfg["prompt"],
-            "parallelism": f"tp{args.gpus}", "l2": "inputs larger than L2 (weights stream from HBM every step)"}
+    out = {"workload": f"qwen3-{args.config} architecture synthetic, {cfg['requests']} req x {2 * cfg['kk']}-node "
+                       f"trees (chain {cfg['kk']} + siblings), {cfg['prompt']}-token KV prefix, greedy accept",
+           "weights": "Q8_0" if m["type_default"] == Q8_0 else ("Q4_K" if m["type_default"] == Q4_K else "Q6_K"),
+           "requests": cfg["requests"], "rows_per_step": cfg["requests"] * (2 * cfg["kk"] + 1),
+           "prompt": cfg["prompt"], "parallelism": f"tp{args.gpus}",
+           "q8_gemm": os.environ.get("MALKIN_B200_Q8_GEMM", "exact"),
+           "l2": "inputs larger than L2 (weights stream from HBM every step)"}
+    if args.gpus > 1:
+        out["tp_reduce"] = {"nccl": "ncclAllReduce", "twoshot": "peer memory, two-shot"}.get(
+            os.environ.get("MALKIN_B200_TP_REDUCE", ""), "peer memory, one-shot")
+    return out
 
 
 # ---------------------------------------------------------------------------------------------------------------
