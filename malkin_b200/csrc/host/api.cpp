@@ -163,9 +163,9 @@ int mk_alloc_kv(mk_ctx* ctx, int n_ctx, int n_seq, int max_batch) {
 int mk_tp_shard_of(const char* gguf_path, int tp_size, int tp_rank, mk_tp_shard* out) {
   return guard(MK_ERR_ARG, [&] {
     if (!gguf_path || !out) throw mkb::ArgError("tp_shard: null argument");
-    mkb::Gguf f(gguf_path);
+    mkb::GgufReader f(gguf_path);
     const mkb::ModelCfg c = mkb::read_config(f);
-    const mkb::Tensor* down0 = f.tensor("blk.0.ffn_down.weight");
+    const mkb::TensorView* down0 = f.find("blk.0.ffn_down.weight");
     if (!down0) throw mkb::ArgError("model: tensor blk.0.ffn_down.weight missing");
     if (!mkb::repack_supported(down0->type)) throw mkb::UnsupportedError("tp_shard: unsupported ffn_down type");
     const mkb::TpShard sh = mkb::tp_shard(c, mkb::kunit_values(down0->type), tp_size, tp_rank);

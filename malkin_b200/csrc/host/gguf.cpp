@@ -6,6 +6,7 @@
 #include <unistd.h>
 
 #include <cerrno>
+#include <cstdio>
 #include <cstring>
 #include <stdexcept>
 
@@ -77,12 +78,6 @@ size_t row_bytes(uint32_t t, int64_t n) {
   return static_cast<size_t>(n / s.block) * s.bytes;
 }
 
-int64_t Tensor::nelements() const {
-  int64_t n = 1;
-  for (int64_t d : ne) n *= d;
-  return n;
-}
-
 float fp16_to_fp32(uint16_t h) {
   _Float16 f;
   std::memcpy(&f, &h, 2);
@@ -98,88 +93,260 @@ uint16_t fp32_to_fp16(float f) {
 
 namespace {
 
-// GGUF value type ids.
-enum : uint32_t { kU8, kI8, kU16, kI16, kU32, kI32, kVF32, kBool, kStr, kArr, kU64, kI64, kF64 };
-
-class Cursor {
- public:
-  Cursor(const uint8_t* p, size_t n) : p_(p), end_(p + n), base_(p) {}
-  template <typename T>
-  T get() {
-    need(sizeof(T));
-    T v;
-    std::memcpy(&v, p_, sizeof(T));
-    p_ += sizeof(T);
-    return v;
-  }
-  std::string str() {
-    const auto n = get<uint64_t>();
-    need(n);
-    std::string s(reinterpret_cast<const char*>(p_), n);
-    p_ += n;
-    return s;
-  }
-  void skip(size_t n) {
-    need(n);
-    p_ += n;
-  }
-  size_t offset() const { return static_cast<size_t>(p_ - base_); }
-
- private:
-  void need(size_t n) const {
-    if (static_cast<size_t>(end_ - p_) < n) throw std::runtime_error("gguf: truncated header");
-  }
-  const uint8_t* p_;
-  const uint8_t* end_;
-  const uint8_t* base_;
+// GGUF metadata value types (format constants).
+enum MetaType : uint32_t {
+  kMetaU8 = 0,
+  kMetaI8,
+  kMetaU16,
+  kMetaI16,
+  kMetaU32,
+  kMetaI32,
+  kMetaF32,
+  kMetaBool,
+  kMetaString,
+  kMetaArray,
+  kMetaU64,
+  kMetaI64,
+  kMetaF64,
+  kMetaTypeCount
 };
 
-bool is_int_type(uint32_t t) { return t <= kI32 || t == kU64 || t == kI64; }
+// Per metadata type: fixed byte width (0: variable length), and whether it is an integer / a signed one.
+struct MetaTypeInfo {
+  uint8_t width;
+  bool integer;
+  bool is_signed;
+};
+constexpr MetaTypeInfo kMetaTypes[kMetaTypeCount] = {
+    {1, true, false}, {1, true, true},   {2, true, false},  {2, true, true}, {4, true, false},
+    {4, true, true},  {4, false, false}, {1, false, false}, {0, false, false}, {0, false, false},
+    {8, true, false}, {8, true, true},   {8, false, false},
+};
 
-int64_t read_int(Cursor& c, uint32_t t) {
-  switch (t) {
-    case kU8:
-      return c.get<uint8_t>();
-    case kI8:
-      return c.get<int8_t>();
-    case kU16:
-      return c.get<uint16_t>();
-    case kI16:
-      return c.get<int16_t>();
-    case kU32:
-      return c.get<uint32_t>();
-    case kI32:
-      return c.get<int32_t>();
-    case kU64:
-      return static_cast<int64_t>(c.get<uint64_t>());
-    case kI64:
-      return c.get<int64_t>();
-    default:
-      throw std::runtime_error("gguf: not an integer type");
+constexpr uint32_t kGgufMagic = 0x46554747u;  // "GGUF" read as a little-endian u32
+constexpr uint32_t kMaxDims = 4;
+
+// Bounds-checked little-endian decoding of the header bytes. Each read names the field it reads, so a truncated
+// or corrupt file reports that field and the byte offset where decoding stopped.
+class HeaderDecoder {
+ public:
+  HeaderDecoder(const uint8_t* bytes, size_t len, const std::string& path) : bytes_(bytes), len_(len), path_(path) {}
+
+  [[noreturn]] void fail(const std::string& msg) const {
+    throw std::runtime_error("gguf: " + path_ + ": " + msg + " (header byte " + std::to_string(pos_) + ")");
+  }
+  size_t pos() const { return pos_; }
+  size_t left() const { return len_ - pos_; }
+
+  const uint8_t* take(uint64_t n, const char* what) {
+    if (n > left()) fail(std::string(what) + " runs past the end of the file");
+    const uint8_t* p = bytes_ + pos_;
+    pos_ += static_cast<size_t>(n);
+    return p;
+  }
+  uint32_t u32(const char* what) { return static_cast<uint32_t>(unsigned_of(4, what)); }
+  uint64_t u64(const char* what) { return unsigned_of(8, what); }
+  std::string_view text(const char* what) {
+    const uint64_t n = u64(what);
+    return {reinterpret_cast<const char*>(take(n, what)), static_cast<size_t>(n)};
+  }
+  // An integer metadata value of type t, widened to int64 (u64 values above INT64_MAX are rejected).
+  int64_t integer(uint32_t t, const char* what) {
+    const MetaTypeInfo& info = kMetaTypes[t];
+    const uint64_t raw = unsigned_of(info.width, what);
+    if (info.is_signed && info.width < 8) {
+      const int shift = 64 - 8 * info.width;
+      return static_cast<int64_t>(raw << shift) >> shift;
+    }
+    if (!info.is_signed && raw > static_cast<uint64_t>(INT64_MAX)) fail(std::string(what) + " exceeds int64");
+    return static_cast<int64_t>(raw);
+  }
+
+ private:
+  uint64_t unsigned_of(int width, const char* what) {
+    uint64_t v = 0;
+    std::memcpy(&v, take(static_cast<uint64_t>(width), what), static_cast<size_t>(width));  // little-endian host
+    return v;
+  }
+  const uint8_t* bytes_;
+  size_t len_;
+  size_t pos_ = 0;
+  const std::string& path_;
+};
+
+struct CloseOnExit {
+  int fd;
+  ~CloseOnExit() {
+    if (fd >= 0) ::close(fd);
+  }
+};
+
+}  // namespace
+
+int64_t TensorView::nelements() const {
+  int64_t n = 1;
+  for (int64_t d : ne) n *= d;
+  return n;
+}
+
+GgufReader::GgufReader(const std::string& path) {
+  CloseOnExit file{::open(path.c_str(), O_RDONLY | O_CLOEXEC)};
+  if (file.fd < 0) throw std::runtime_error("gguf: " + path + ": open: " + std::strerror(errno));
+  struct stat st {};
+  if (fstat(file.fd, &st) != 0) throw std::runtime_error("gguf: " + path + ": stat: " + std::strerror(errno));
+  if (!S_ISREG(st.st_mode)) throw std::runtime_error("gguf: " + path + ": not a regular file");
+  map_len_ = static_cast<size_t>(st.st_size);
+  if (map_len_ < 24) throw std::runtime_error("gguf: " + path + ": " + std::to_string(map_len_) +
+                                              " bytes, shorter than a GGUF header");
+  void* m = mmap(nullptr, map_len_, PROT_READ, MAP_PRIVATE, file.fd, 0);
+  if (m == MAP_FAILED) throw std::runtime_error("gguf: " + path + ": mmap: " + std::strerror(errno));
+  map_ = static_cast<const uint8_t*>(m);  // the mapping outlives the descriptor
+  try {
+    decode(path);
+  } catch (...) {
+    munmap(const_cast<uint8_t*>(map_), map_len_);
+    map_ = nullptr;
+    throw;
   }
 }
 
-size_t scalar_bytes(uint32_t t) {
-  switch (t) {
-    case kU8:
-    case kI8:
-    case kBool:
-      return 1;
-    case kU16:
-    case kI16:
-      return 2;
-    case kU32:
-    case kI32:
-    case kVF32:
-      return 4;
-    case kU64:
-    case kI64:
-    case kF64:
-      return 8;
-    default:
-      return 0;
-  }
+GgufReader::~GgufReader() {
+  if (map_) munmap(const_cast<uint8_t*>(map_), map_len_);
 }
+
+void GgufReader::decode(const std::string& path) {
+  HeaderDecoder d(map_, map_len_, path);
+  const uint32_t magic = d.u32("magic");
+  if (magic != kGgufMagic) {
+    char hex[16];
+    std::snprintf(hex, sizeof hex, "0x%08x", magic);
+    d.fail(std::string("not a GGUF file (magic ") + hex + ")");
+  }
+  version_ = d.u32("version");
+  if (version_ != 3) d.fail("GGUF version " + std::to_string(version_) + "; this reader handles version 3");
+  const uint64_t n_tensors = d.u64("tensor count");
+  const uint64_t n_meta = d.u64("metadata count");
+  // every metadata entry takes at least 13 bytes (key length, type, 1-byte value), every tensor info 28
+  if (n_meta > d.left() / 13 || n_tensors > d.left() / 28) d.fail("entry counts exceed the file size");
+
+  meta_.reserve(static_cast<size_t>(n_meta));
+  for (uint64_t i = 0; i < n_meta; ++i) {
+    const std::string key(d.text("metadata key"));
+    const uint32_t t = d.u32("metadata value type");
+    if (t >= kMetaTypeCount) d.fail("metadata " + key + ": unknown value type " + std::to_string(t));
+    MetaValue v;
+    if (kMetaTypes[t].integer) {
+      v = d.integer(t, "metadata integer");
+    } else if (t == kMetaF32) {
+      float f;
+      std::memcpy(&f, d.take(4, "metadata f32"), 4);
+      v = static_cast<double>(f);
+    } else if (t == kMetaF64) {
+      double f;
+      std::memcpy(&f, d.take(8, "metadata f64"), 8);
+      v = f;
+    } else if (t == kMetaBool) {
+      v = *d.take(1, "metadata bool") != 0;
+    } else if (t == kMetaString) {
+      v = std::string(d.text("metadata string"));
+    } else {  // array: element type, count, elements (skipped; only the count is kept)
+      const uint32_t et = d.u32("array element type");
+      const uint64_t count = d.u64("array length");
+      if (et >= kMetaTypeCount || et == kMetaArray) d.fail("metadata " + key + ": unsupported array element type");
+      if (et == kMetaString) {
+        for (uint64_t j = 0; j < count; ++j) d.text("array string");
+      } else {
+        const uint64_t w = kMetaTypes[et].width;
+        if (count > d.left() / w) d.fail("metadata " + key + ": array runs past the end of the file");
+        d.take(count * w, "array data");
+      }
+      v = ArrayInfo{et, static_cast<int64_t>(count)};
+    }
+    meta_.insert_or_assign(key, std::move(v));
+  }
+
+  if (const auto a = meta_int("general.alignment")) {
+    if (*a <= 0 || (*a & (*a - 1)) || *a > (1 << 20)) d.fail("general.alignment " + std::to_string(*a) + " is not a power of two");
+    alignment_ = static_cast<size_t>(*a);
+  }
+
+  std::vector<uint64_t> rel_off(static_cast<size_t>(n_tensors));
+  dir_.resize(static_cast<size_t>(n_tensors));
+  for (uint64_t i = 0; i < n_tensors; ++i) {
+    TensorView& t = dir_[static_cast<size_t>(i)];
+    t.name = std::string(d.text("tensor name"));
+    const uint32_t nd = d.u32("tensor rank");
+    if (nd == 0 || nd > kMaxDims) d.fail("tensor " + t.name + ": rank " + std::to_string(nd) + " outside 1..4");
+    int64_t elems = 1;
+    for (uint32_t k = 0; k < nd; ++k) {
+      const uint64_t e = d.u64("tensor dimension");
+      if (e == 0 || e > (uint64_t{1} << 40) || static_cast<uint64_t>(elems) > (uint64_t{1} << 50) / e)
+        d.fail("tensor " + t.name + ": dimension " + std::to_string(e) + " out of range");
+      elems *= static_cast<int64_t>(e);
+      t.ne.push_back(static_cast<int64_t>(e));
+    }
+    t.type = d.u32("tensor type");
+    const TypeSize ts = type_size(t.type);
+    if (ts.block == 0) d.fail("tensor " + t.name + ": unknown ggml type " + std::to_string(t.type));
+    if (t.ne[0] % ts.block)
+      d.fail("tensor " + t.name + ": row of " + std::to_string(t.ne[0]) + " values is not whole " + type_name(t.type) +
+             " blocks");
+    t.nbytes = static_cast<size_t>(elems / ts.block) * ts.bytes;
+    rel_off[static_cast<size_t>(i)] = d.u64("tensor data offset");
+  }
+
+  const size_t data_begin = (d.pos() + alignment_ - 1) / alignment_ * alignment_;
+  for (size_t i = 0; i < dir_.size(); ++i) {
+    TensorView& t = dir_[i];
+    const uint64_t off = rel_off[i];
+    if (off % alignment_) d.fail("tensor " + t.name + ": data offset " + std::to_string(off) + " not aligned");
+    if (data_begin > map_len_ || off > map_len_ - data_begin || t.nbytes > map_len_ - data_begin - off)
+      d.fail("tensor " + t.name + ": data lies outside the file");
+    t.data = map_ + data_begin + off;
+  }
+  index_.reserve(dir_.size());
+  for (size_t i = 0; i < dir_.size(); ++i)
+    if (!index_.emplace(std::string_view(dir_[i].name), i).second) d.fail("tensor " + dir_[i].name + " appears twice");
+}
+
+std::optional<int64_t> GgufReader::meta_int(std::string_view key) const {
+  const auto it = meta_.find(std::string(key));
+  if (it == meta_.end()) return std::nullopt;
+  if (const auto* i = std::get_if<int64_t>(&it->second)) return *i;
+  if (const auto* b = std::get_if<bool>(&it->second)) return *b ? 1 : 0;
+  return std::nullopt;
+}
+
+std::optional<double> GgufReader::meta_real(std::string_view key) const {
+  const auto it = meta_.find(std::string(key));
+  if (it == meta_.end()) return std::nullopt;
+  if (const auto* f = std::get_if<double>(&it->second)) return *f;
+  if (const auto* i = std::get_if<int64_t>(&it->second)) return static_cast<double>(*i);
+  return std::nullopt;
+}
+
+std::optional<std::string> GgufReader::meta_text(std::string_view key) const {
+  const auto it = meta_.find(std::string(key));
+  if (it == meta_.end()) return std::nullopt;
+  if (const auto* s = std::get_if<std::string>(&it->second)) return *s;
+  return std::nullopt;
+}
+
+int64_t GgufReader::meta_count(std::string_view key) const {
+  const auto it = meta_.find(std::string(key));
+  if (it == meta_.end()) return -1;
+  if (const auto* a = std::get_if<ArrayInfo>(&it->second)) return a->count;
+  return -1;
+}
+
+const TensorView* GgufReader::find(std::string_view name) const {
+  const auto it = index_.find(name);
+  return it == index_.end() ? nullptr : &dir_[it->second];
+}
+
+// ---- writer ----
+
+namespace {
 
 template <typename T>
 void put(std::vector<uint8_t>& b, T v) {
@@ -194,158 +361,31 @@ void put_str(std::vector<uint8_t>& b, const std::string& s) {
 
 }  // namespace
 
-Gguf::Gguf(const std::string& path) {
-  fd_ = ::open(path.c_str(), O_RDONLY);
-  if (fd_ < 0) throw std::runtime_error("cannot open " + path + ": " + std::strerror(errno));
-  struct stat st {};
-  if (fstat(fd_, &st) != 0) throw std::runtime_error("cannot stat " + path);
-  size_ = static_cast<size_t>(st.st_size);
-  void* m = mmap(nullptr, size_, PROT_READ, MAP_SHARED, fd_, 0);
-  if (m == MAP_FAILED) {
-    ::close(fd_);
-    fd_ = -1;
-    throw std::runtime_error("mmap failed: " + std::string(std::strerror(errno)));
-  }
-  base_ = static_cast<uint8_t*>(m);
-  try {
-    Cursor c(base_, size_);
-    if (c.get<uint32_t>() != 0x46554747u) throw std::runtime_error(path + " is not a GGUF file");
-    const auto version = c.get<uint32_t>();
-    if (version < 3) throw std::runtime_error("GGUF v" + std::to_string(version) + " unsupported, need v3");
-    const auto n_tensors = c.get<uint64_t>();
-    const auto n_kv = c.get<uint64_t>();
-    for (uint64_t i = 0; i < n_kv; ++i) {
-      const std::string key = c.str();
-      const auto t = c.get<uint32_t>();
-      Value v;
-      if (is_int_type(t)) {
-        v.kind = Value::kInt;
-        v.i = read_int(c, t);
-      } else if (t == kVF32) {
-        v.kind = Value::kFloat;
-        v.f = c.get<float>();
-      } else if (t == kF64) {
-        v.kind = Value::kFloat;
-        v.f = c.get<double>();
-      } else if (t == kBool) {
-        v.kind = Value::kBool;
-        v.i = c.get<uint8_t>() != 0;
-      } else if (t == kStr) {
-        v.kind = Value::kStr;
-        v.s = c.str();
-      } else if (t == kArr) {
-        v.kind = Value::kArr;
-        const auto et = c.get<uint32_t>();
-        const auto n = c.get<uint64_t>();
-        v.arr_len = static_cast<int64_t>(n);
-        if (et == kStr) {
-          for (uint64_t j = 0; j < n; ++j) c.skip(c.get<uint64_t>());
-        } else if (scalar_bytes(et)) {
-          c.skip(scalar_bytes(et) * n);
-        } else {
-          throw std::runtime_error("gguf: nested arrays unsupported");
-        }
-      } else {
-        throw std::runtime_error("gguf: bad value type " + std::to_string(t));
-      }
-      kv_[key] = std::move(v);
-    }
-    struct Info {
-      Tensor t;
-      uint64_t off;
-    };
-    std::vector<Info> infos;
-    for (uint64_t i = 0; i < n_tensors; ++i) {
-      Info in;
-      in.t.name = c.str();
-      const auto nd = c.get<uint32_t>();
-      for (uint32_t d = 0; d < nd; ++d) in.t.ne.push_back(static_cast<int64_t>(c.get<uint64_t>()));
-      in.t.type = c.get<uint32_t>();
-      in.off = c.get<uint64_t>();
-      infos.push_back(std::move(in));
-    }
-    const auto align = static_cast<size_t>(get_int("general.alignment").value_or(32));
-    const size_t data_start = (c.offset() + align - 1) / align * align;
-    for (auto& in : infos) {
-      Tensor& t = in.t;
-      t.nbytes = row_bytes(t.type, t.ne[0]) * static_cast<size_t>(t.nelements() / t.ne[0]);
-      if (data_start + in.off + t.nbytes > size_) throw std::runtime_error("gguf: tensor " + t.name + " out of bounds");
-      t.data = base_ + data_start + in.off;
-      tensors_[t.name] = std::move(t);
-    }
-  } catch (...) {
-    munmap(base_, size_);
-    ::close(fd_);
-    base_ = nullptr;
-    fd_ = -1;
-    throw;
-  }
-}
-
-Gguf::~Gguf() {
-  if (base_) munmap(base_, size_);
-  if (fd_ >= 0) ::close(fd_);
-}
-
-std::optional<int64_t> Gguf::get_int(const std::string& key) const {
-  auto it = kv_.find(key);
-  if (it == kv_.end()) return std::nullopt;
-  if (it->second.kind == Value::kInt || it->second.kind == Value::kBool) return it->second.i;
-  return std::nullopt;
-}
-
-std::optional<double> Gguf::get_float(const std::string& key) const {
-  auto it = kv_.find(key);
-  if (it == kv_.end()) return std::nullopt;
-  if (it->second.kind == Value::kFloat) return it->second.f;
-  if (it->second.kind == Value::kInt) return static_cast<double>(it->second.i);
-  return std::nullopt;
-}
-
-std::optional<std::string> Gguf::get_str(const std::string& key) const {
-  auto it = kv_.find(key);
-  if (it == kv_.end() || it->second.kind != Value::kStr) return std::nullopt;
-  return it->second.s;
-}
-
-int64_t Gguf::array_len(const std::string& key) const {
-  auto it = kv_.find(key);
-  if (it == kv_.end() || it->second.kind != Value::kArr) return -1;
-  return it->second.arr_len;
-}
-
-const Tensor* Gguf::tensor(const std::string& name) const {
-  auto it = tensors_.find(name);
-  return it == tensors_.end() ? nullptr : &it->second;
-}
-
-// ---- writer ----
-
 void GgufWriter::add_str(const std::string& key, const std::string& v) {
   put_str(head_, key);
-  put<uint32_t>(head_, kStr);
+  put<uint32_t>(head_, kMetaString);
   put_str(head_, v);
   ++n_kv_;
 }
 
 void GgufWriter::add_u32(const std::string& key, uint32_t v) {
   put_str(head_, key);
-  put<uint32_t>(head_, kU32);
+  put<uint32_t>(head_, kMetaU32);
   put<uint32_t>(head_, v);
   ++n_kv_;
 }
 
 void GgufWriter::add_f32(const std::string& key, float v) {
   put_str(head_, key);
-  put<uint32_t>(head_, kVF32);
+  put<uint32_t>(head_, kMetaF32);
   put<float>(head_, v);
   ++n_kv_;
 }
 
 void GgufWriter::add_str_array(const std::string& key, const std::vector<std::string>& v) {
   put_str(head_, key);
-  put<uint32_t>(head_, kArr);
-  put<uint32_t>(head_, kStr);
+  put<uint32_t>(head_, kMetaArray);
+  put<uint32_t>(head_, kMetaString);
   put<uint64_t>(head_, v.size());
   for (const auto& s : v) put_str(head_, s);
   ++n_kv_;
@@ -373,7 +413,7 @@ void GgufWriter::open(const std::string& path) {
   put<uint64_t>(hdr, n_kv_ + 1);
   hdr.insert(hdr.end(), head_.begin(), head_.end());
   put_str(hdr, "general.alignment");
-  put<uint32_t>(hdr, kU32);
+  put<uint32_t>(hdr, kMetaU32);
   put<uint32_t>(hdr, static_cast<uint32_t>(kAlign));
   size_t off = 0;
   for (auto& in : infos_) {

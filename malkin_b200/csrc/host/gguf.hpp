@@ -1,16 +1,27 @@
-// GGUF v3 reader and writer (host). The reader covers what malkin's GgufFile reads (gguf.cpp:205-249):
-// magic, version >= 3, key/value metadata of every GGUF value type, tensor infos, data aligned to
-// general.alignment (default 32). The writer emits files that reader (and malkin's) accept.
+// GGUF v3 container, host side: a read-only mapped view (GgufReader) and a streaming writer (GgufWriter).
+//
+// Format (GGUF v3, little-endian; the ggml project's gguf.md):
+//   u32 magic "GGUF" | u32 version | u64 tensor_count | u64 metadata_kv_count
+//   metadata_kv_count x { string key | u32 value_type | value }
+//   tensor_count x { string name | u32 n_dims | n_dims x u64 ne | u32 ggml_type | u64 offset }
+//   padding to general.alignment (default 32) | tensor data (offsets relative to here, each aligned)
+// where string = u64 length + bytes, and an array value = u32 element type + u64 count + elements.
+// The reader keeps what the verify path needs: every metadata scalar and string, array element counts, and a
+// directory of tensor views into the mapping. malkin reads the same files (gguf.cpp:205-249); both sides must
+// agree on the bytes, not on the parser.
 #pragma once
 #include <cstddef>
 #include <cstdint>
-#include <map>
 #include <optional>
 #include <string>
+#include <string_view>
+#include <unordered_map>
+#include <variant>
 #include <vector>
 
 namespace mkb {
 
+// ggml tensor type ids (format constants, gguf.h:12-29).
 enum GgmlType : uint32_t {
   kF32 = 0,
   kF16 = 1,
@@ -21,20 +32,21 @@ enum GgmlType : uint32_t {
   kBF16 = 30,
 };
 
-// Elements per block and bytes per block of a ggml type (gguf.cpp:60-95); block 0 = unknown type.
+// Elements per block and bytes per block of a ggml type; block 0 = unknown type.
 struct TypeSize {
   int64_t block;
   size_t bytes;
 };
 TypeSize type_size(uint32_t t);
 const char* type_name(uint32_t t);
-// Bytes of n elements of type t; throws if n is not a multiple of the block.
+// Bytes of n elements of type t; throws if the type is unknown or n is not a multiple of its block.
 size_t row_bytes(uint32_t t, int64_t n);
 
-struct Tensor {
+// One tensor of a mapped file: shape (ne[0] contiguous), type and its bytes inside the mapping.
+struct TensorView {
   std::string name;
   uint32_t type = 0;
-  std::vector<int64_t> ne;  // ne[0] contiguous
+  std::vector<int64_t> ne;
   const uint8_t* data = nullptr;
   size_t nbytes = 0;
   int64_t nelements() const;
@@ -42,34 +54,44 @@ struct Tensor {
   int64_t rows() const { return ne.empty() ? 0 : nelements() / ne[0]; }
 };
 
-class Gguf {
+class GgufReader {
  public:
-  explicit Gguf(const std::string& path);
-  ~Gguf();
-  Gguf(const Gguf&) = delete;
-  Gguf& operator=(const Gguf&) = delete;
+  // Maps `path` read-only and decodes its header; throws std::runtime_error("gguf: <path>: ...") on any
+  // malformed or truncated header, unknown tensor type or tensor outside the file.
+  explicit GgufReader(const std::string& path);
+  ~GgufReader();
+  GgufReader(const GgufReader&) = delete;
+  GgufReader& operator=(const GgufReader&) = delete;
 
-  std::optional<int64_t> get_int(const std::string& key) const;
-  std::optional<double> get_float(const std::string& key) const;
-  std::optional<std::string> get_str(const std::string& key) const;
-  // Entries of an array-valued key (any element type), or -1 if absent.
-  int64_t array_len(const std::string& key) const;
-  const Tensor* tensor(const std::string& name) const;
-  const std::map<std::string, Tensor>& tensors() const { return tensors_; }
+  // Metadata lookups; std::nullopt when the key is absent or holds another kind of value (booleans read as 0/1
+  // integers, integers also read as reals).
+  std::optional<int64_t> meta_int(std::string_view key) const;
+  std::optional<double> meta_real(std::string_view key) const;
+  std::optional<std::string> meta_text(std::string_view key) const;
+  // Element count of an array-valued key, or -1.
+  int64_t meta_count(std::string_view key) const;
+
+  const TensorView* find(std::string_view name) const;
+  const std::vector<TensorView>& directory() const { return dir_; }
+  uint32_t version() const { return version_; }
+  size_t alignment() const { return alignment_; }
 
  private:
-  struct Value {
-    enum Kind { kInt, kFloat, kBool, kStr, kArr } kind = kInt;
-    int64_t i = 0;
-    double f = 0;
-    std::string s;
-    int64_t arr_len = 0;
+  struct ArrayInfo {
+    uint32_t elem_type;
+    int64_t count;
   };
-  int fd_ = -1;
-  uint8_t* base_ = nullptr;
-  size_t size_ = 0;
-  std::map<std::string, Value> kv_;
-  std::map<std::string, Tensor> tensors_;
+  using MetaValue = std::variant<int64_t, double, bool, std::string, ArrayInfo>;
+
+  void decode(const std::string& path);
+
+  const uint8_t* map_ = nullptr;
+  size_t map_len_ = 0;
+  uint32_t version_ = 0;
+  size_t alignment_ = 32;
+  std::unordered_map<std::string, MetaValue> meta_;
+  std::vector<TensorView> dir_;
+  std::unordered_map<std::string_view, size_t> index_;  // views into dir_[i].name
 };
 
 // Streaming GGUF writer: metadata and tensor infos first, then the data region, which callers fill in place

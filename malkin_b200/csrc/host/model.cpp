@@ -82,11 +82,11 @@ Model::~Model() {
 // ---------------------------------------------------------------------------------------------------------------
 // load: read_config (model.cpp:177-200) + Model::Model (model.cpp:211-251) + pack (model.cpp:262-277), per shard.
 // ---------------------------------------------------------------------------------------------------------------
-ModelCfg read_config(const Gguf& f) {
-  const std::string arch = f.get_str("general.architecture").value_or("");
+ModelCfg read_config(const GgufReader& f) {
+  const std::string arch = f.meta_text("general.architecture").value_or("");
   if (arch != "qwen3") throw ArgError("architecture '" + arch + "' unsupported (supported: qwen3)");
   auto need = [&](const std::string& k) {
-    auto v = f.get_int("qwen3." + k);
+    auto v = f.meta_int("qwen3." + k);
     if (!v) throw ArgError("model: metadata qwen3." + k + " missing");
     return static_cast<int>(*v);
   };
@@ -95,16 +95,16 @@ ModelCfg read_config(const Gguf& f) {
   c.n_embd = need("embedding_length");
   c.n_ff = need("feed_forward_length");
   c.n_head = need("attention.head_count");
-  c.n_head_kv = static_cast<int>(f.get_int("qwen3.attention.head_count_kv").value_or(c.n_head));
-  c.head_dim = static_cast<int>(f.get_int("qwen3.attention.key_length").value_or(c.n_embd / c.n_head));
-  c.n_ctx_train = static_cast<int>(f.get_int("qwen3.context_length").value_or(4096));
-  c.rope_base = static_cast<float>(f.get_float("qwen3.rope.freq_base").value_or(10000.0));
-  c.rms_eps = static_cast<float>(f.get_float("qwen3.attention.layer_norm_rms_epsilon").value_or(1e-6));
+  c.n_head_kv = static_cast<int>(f.meta_int("qwen3.attention.head_count_kv").value_or(c.n_head));
+  c.head_dim = static_cast<int>(f.meta_int("qwen3.attention.key_length").value_or(c.n_embd / c.n_head));
+  c.n_ctx_train = static_cast<int>(f.meta_int("qwen3.context_length").value_or(4096));
+  c.rope_base = static_cast<float>(f.meta_real("qwen3.rope.freq_base").value_or(10000.0));
+  c.rms_eps = static_cast<float>(f.meta_real("qwen3.attention.layer_norm_rms_epsilon").value_or(1e-6));
   if (c.head_dim % 32 || c.n_head % c.n_head_kv) throw ArgError("model: unsupported head layout");
   if (c.head_dim != 64 && c.head_dim != 128 && c.head_dim != 256)
     throw UnsupportedError("unsupported: head_dim " + std::to_string(c.head_dim) + " (64, 128, 256)");
-  const Tensor* out = f.tensor("output.weight");
-  if (!out) out = f.tensor("token_embd.weight");  // tied embeddings
+  const TensorView* out = f.find("output.weight");
+  if (!out) out = f.find("token_embd.weight");  // tied embeddings
   if (!out) throw ArgError("model: tensor token_embd.weight missing");
   c.n_vocab = static_cast<int>(out->rows());
   return c;
@@ -134,10 +134,10 @@ TpShard tp_shard(const ModelCfg& c, int ffn_unit, int tp, int rank) {
 
 void Model::load(const std::string& path) {
   cuda_check(cudaSetDevice(device_), "cudaSetDevice");
-  Gguf f(path);
+  GgufReader f(path);
   ModelCfg c = read_config(f);
-  auto weight = [&](const std::string& name, bool required) -> const Tensor* {
-    const Tensor* t = f.tensor(name);
+  auto weight = [&](const std::string& name, bool required) -> const TensorView* {
+    const TensorView* t = f.find(name);
     if (!t) {
       if (required) throw ArgError("model: tensor " + name + " missing");
       return nullptr;
@@ -145,26 +145,26 @@ void Model::load(const std::string& path) {
     return t;
   };
   auto norm = [&](const std::string& name, int64_t n) {
-    const Tensor* t = f.tensor(name);
+    const TensorView* t = f.find(name);
     if (!t) throw ArgError("model: tensor " + name + " missing");
     if (t->type != kF32 || t->nelements() != n)
       throw ArgError("model: norm " + name + " not F32[" + std::to_string(n) + "]");
     return t;
   };
-  const Tensor* tok = weight("token_embd.weight", true);
-  const Tensor* out = weight("output.weight", false);
+  const TensorView* tok = weight("token_embd.weight", true);
+  const TensorView* out = weight("output.weight", false);
   if (!out) out = tok;  // tied embeddings
   cfg_ = c;
   const int tp = tp_size_, r = tp_rank_;
   const int D = c.head_dim, E = c.n_embd;
 
-  auto check_mat = [&](const Tensor* t) {
+  auto check_mat = [&](const TensorView* t) {
     if (!repack_supported(t->type))
       throw UnsupportedError(std::string("unsupported: tensor ") + t->name + " has type " + type_name(t->type) +
                                " (this path streams Q8_0 Q4_K Q6_K)");
   };
   // shard geometry (tensor parallel): heads, ffn rows in whole k-units of ffn_down, vocabulary rows
-  const Tensor* down0 = weight("blk.0.ffn_down.weight", true);
+  const TensorView* down0 = weight("blk.0.ffn_down.weight", true);
   check_mat(down0);
   const TpShard sh = tp_shard(c, kunit_values(down0->type), tp, r);
   Hl_ = sh.heads;
@@ -177,14 +177,14 @@ void Model::load(const std::string& path) {
 
   // Device byte plan.
   struct Piece {
-    const Tensor* t;
+    const TensorView* t;
     int64_t r0, nr, c0, nc;
     size_t off;  // in wbuf
     int layout;
   };
   std::vector<Piece> pieces;
   size_t total = 0;
-  auto add_piece = [&](const Tensor* t, int64_t r0, int64_t nr, int64_t c0, int64_t nc) -> size_t {
+  auto add_piece = [&](const TensorView* t, int64_t r0, int64_t nr, int64_t c0, int64_t nc) -> size_t {
     check_mat(t);
     const int u = kunit_values(t->type);
     if (c0 % u || nc % u) throw ArgError("tensor parallel: shard of " + t->name + " not block aligned");
@@ -198,7 +198,7 @@ void Model::load(const std::string& path) {
   weight_bytes_ = 0;
   struct LayerPlan {
     int qkv[3], nqkv, wo, gu[2], ngu, down;
-    const Tensor *an, *fn, *qn, *kn;
+    const TensorView *an, *fn, *qn, *kn;
   };
   std::vector<LayerPlan> lp(static_cast<size_t>(c.n_layer));
   for (int i = 0; i < c.n_layer; ++i) {
@@ -208,13 +208,13 @@ void Model::load(const std::string& path) {
     L.fn = norm(p + "ffn_norm.weight", E);
     L.qn = norm(p + "attn_q_norm.weight", D);
     L.kn = norm(p + "attn_k_norm.weight", D);
-    const Tensor* wq = weight(p + "attn_q.weight", true);
-    const Tensor* wk = weight(p + "attn_k.weight", true);
-    const Tensor* wv = weight(p + "attn_v.weight", true);
-    const Tensor* wo = weight(p + "attn_output.weight", true);
-    const Tensor* wg = weight(p + "ffn_gate.weight", true);
-    const Tensor* wu = weight(p + "ffn_up.weight", true);
-    const Tensor* wd = weight(p + "ffn_down.weight", true);
+    const TensorView* wq = weight(p + "attn_q.weight", true);
+    const TensorView* wk = weight(p + "attn_k.weight", true);
+    const TensorView* wv = weight(p + "attn_v.weight", true);
+    const TensorView* wo = weight(p + "attn_output.weight", true);
+    const TensorView* wg = weight(p + "ffn_gate.weight", true);
+    const TensorView* wu = weight(p + "ffn_up.weight", true);
+    const TensorView* wd = weight(p + "ffn_down.weight", true);
     if (wq->cols() != E || wk->cols() != E || wv->cols() != E || wg->cols() != E || wu->cols() != E ||
         wo->cols() != static_cast<int64_t>(c.n_head) * D || wd->cols() != c.n_ff || wq->rows() != static_cast<int64_t>(c.n_head) * D ||
         wk->rows() != static_cast<int64_t>(c.n_head_kv) * D || wv->rows() != static_cast<int64_t>(c.n_head_kv) * D ||
@@ -241,7 +241,7 @@ void Model::load(const std::string& path) {
   embd_row_bytes_ = row_bytes(tok->type, tok->cols());
   if (tok->cols() != E) throw ArgError("model: token_embd width != n_embd");
   total += tok->nbytes;
-  const Tensor* onorm = norm("output_norm.weight", E);
+  const TensorView* onorm = norm("output_norm.weight", E);
   total = align_up(total, 256);
   const size_t norm_off = total;
   total += static_cast<size_t>(c.n_layer) * (2 * E + 2 * D) * 4 + static_cast<size_t>(E) * 4;
@@ -261,7 +261,7 @@ void Model::load(const std::string& path) {
   cuda_check(cudaMemcpy(base + embd_off, tok->data, tok->nbytes, cudaMemcpyHostToDevice), "upload embeddings");
   embd_ = base + embd_off;
   float* nb = reinterpret_cast<float*>(base + norm_off);
-  auto put_norm = [&](const Tensor* t, int64_t n) {
+  auto put_norm = [&](const TensorView* t, int64_t n) {
     cuda_check(cudaMemcpy(nb, t->data, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice), "upload norms");
     const float* p = nb;
     nb += n;

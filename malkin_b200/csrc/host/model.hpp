@@ -72,7 +72,7 @@ void throw_device_status(int code, const std::string& what);
 
 // The config of a qwen3 GGUF (read_config, model.cpp:78-101), and the slice of it one tensor-parallel rank holds:
 // q / kv heads (column split), ffn rows in whole k-units of ffn_down, vocabulary rows (split of the LM head).
-ModelCfg read_config(const Gguf& f);
+ModelCfg read_config(const GgufReader& f);
 struct TpShard {
   int head0 = 0, heads = 0, kv_head0 = 0, kv_heads = 0, ffn0 = 0, ffn = 0;
   int64_t vocab0 = 0, vocab = 0;
