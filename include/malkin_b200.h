@@ -47,12 +47,12 @@ const char* mk_version(void);
 /* ---------------------------------------------------------------------------------------------------------
  * Synthetic model writer. malkin has no weight quantizer or GGUF writer; this is the stand-in the benchmark
  * configurations name ("N(0, sigma) seeded weights, norms 1.0, quantized, written as GGUF"). The file is a
- * GGUF v3 that malkin's own GgufFile + read_config (gguf.cpp:205-249, model.cpp:177-200) load unchanged.
+ * GGUF v3 that malkin's own GgufFile + read_config (gguf.cpp:205-249, model.cpp:78-101) load unchanged.
  * ------------------------------------------------------------------------------------------------------- */
 typedef struct mk_synth_spec {
   int32_t n_layer, n_embd, n_ff, n_head, n_head_kv, head_dim, n_vocab, n_ctx_train;
   float rope_base, rms_eps;
-  int32_t tied;           /* 1: no output.weight (LM head = token_embd, model.cpp:215-216) */
+  int32_t tied;           /* 1: no output.weight (LM head = token_embd, model.cpp:116-117) */
   int32_t type_default;   /* weight type of every matrix not named below */
   int32_t type_attn_v;    /* attn_v.weight */
   int32_t type_ffn_down;  /* ffn_down.weight */
@@ -99,11 +99,11 @@ int mk_nccl_unique_id(void* out128);
 /* Releases every device resource of the context (NCCL communicator included). */
 int mk_shutdown(mk_ctx* ctx);
 
-/* GgufFile + Model(const GgufFile&, n_ctx = 0, n_seq) (gguf.cpp:205, model.cpp:211-251): parses the GGUF,
- * repacks this rank's shard of every matrix into the device panel layout (Model::pack, model.cpp:262-277) and
+/* GgufFile + Model(const GgufFile&, n_ctx = 0, n_seq) (gguf.cpp:205, model.cpp:112-152): parses the GGUF,
+ * repacks this rank's shard of every matrix into the device panel layout (Model::pack, model.cpp:163-178) and
  * uploads it. The file can be unmapped once this returns. */
 int mk_load_gguf(mk_ctx* ctx, const char* path);
-/* Model::alloc_kv (model.cpp:296-301): int8 KV cache for n_seq sequences of n_ctx positions, in HBM.
+/* Model::alloc_kv (model.cpp:197-202): int8 KV cache for n_seq sequences of n_ctx positions, in HBM.
  * max_batch: largest forward batch (malkin: kMaxBatch = 256, model.h:35); 0 = 256. Under tensor parallelism it is
  * collective (every rank calls it with the same arguments): it maps the ranks' exchange buffers into each other
  * with CUDA IPC for the rank sum, so the ranks must be separate processes. */
@@ -120,12 +120,23 @@ typedef struct mk_tp_shard {
 } mk_tp_shard;
 int mk_tp_shard_of(const char* gguf_path, int tp_size, int tp_rank, mk_tp_shard* out);
 
-/* Model::forward(const BatchToken*, n, float* logits) (model.cpp:379-422): same validation, same key sets
+/* Self-check of the tensor-parallel rank sum (no counterpart in malkin, which has no tensor parallelism). Runs rank 0's
+ * own exchange kernels (publish + gather; twoshot != 0: publish + reduce + allgather) on the current device for
+ * n_calls consecutive calls, against size - 1 (1..7) peers emulated by the host: before each call the host writes
+ * every present peer's partial and the flags it would release. absent[k] (NULL: none) names a peer (1..size-1) that
+ * does not take part in call k, or -1; rank 0's waits then give up after wait_polls polls of about 64 ns each.
+ * host_parts: n_calls x size x n x cols floats (cols % 4 == 0), rank r's partial of call k; host_out: n_calls x n x
+ * cols, the sum over ranks in rank order that rank 0 received; call_status[k]: MK_OK, or MK_ERR_TIMEOUT when a wait of
+ * call k gave up. Shows that a wait that runs out reaches the caller and that the calls after it are still right. */
+int mk_tp_exchange_check(int size, int twoshot, int n, int cols, int n_calls, const int* absent, int wait_polls,
+                         const float* host_parts, float* host_out, int* call_status);
+
+/* Model::forward(const BatchToken*, n, float* logits) (model.cpp:280-323): same validation, same key sets
  * (prefix + tree ancestors), same KV writes. Logits of the rows with .logits set stay on the device for
  * mk_accept; host_logits (nullable) also receives them, n_vocab floats per row in batch order. */
 int mk_forward(mk_ctx* ctx, const mk_batch_token* batch, int n, float* host_logits);
 
-/* Model::move_kv (model.cpp:531-539): copies KV row `from` to row `to` of sequence seq, all layers. */
+/* Model::move_kv (model.cpp:432-440): copies KV row `from` to row `to` of sequence seq, all layers. */
 int mk_move_kv(mk_ctx* ctx, int from, int to, int seq);
 
 /* Sampling parameters (sampler.h:10-18). Penalties must be 0 on this path (MK_ERR_UNSUPPORTED otherwise). */
@@ -140,7 +151,7 @@ typedef struct mk_sampling {
 
 #define MK_MAX_TOPK 64
 
-/* One decoding slot's proposal (engine.h:269-274). Greedy: the tree [next, c0, a0, c1, a1, ...] laid out by
+/* One decoding slot's proposal (engine.h:126-131). Greedy: the tree [next, c0, a0, c1, a1, ...] laid out by
  * Engine::build_batch (engine.cpp:362-379) starting at batch index root; sampled: the chain [next, d0, ...]. */
 typedef struct mk_proposal {
   int32_t seq;        /* slot = KV sequence */
@@ -176,7 +187,7 @@ typedef struct mk_accept_result {
 int mk_accept(mk_ctx* ctx, const mk_proposal* props, int n_props, mk_accept_result* out);
 
 /* The uniform stream a malkin Sampler draws from (sampler.h:39 std::mt19937_64 seeded with `seed`,
- * sampler.cpp:110 / 126 std::uniform_real_distribution<double>(0, 1)): values skip .. skip + n - 1. The host keeps
+ * sampler.cpp:66 / 82 std::uniform_real_distribution<double>(0, 1)): values skip .. skip + n - 1. The host keeps
  * one stream per request and passes the unconsumed tail to mk_accept. */
 int mk_rng_uniforms(uint64_t seed, int64_t skip, int n, double* out);
 
@@ -185,7 +196,7 @@ int mk_rng_uniforms(uint64_t seed, int64_t skip, int n, double* out);
 int mk_verify_step(mk_ctx* ctx, const mk_batch_token* batch, int n, const mk_proposal* props, int n_props,
                    mk_accept_result* out);
 
-/* Per-stage device time of the last forward, ms, in the 8 MALKIN_PROFILE stages (model.cpp:150-173):
+/* Per-stage device time of the last forward, ms, in the 8 MALKIN_PROFILE stages (model.cpp:52-76):
  * norm+qkv, qk-norm/rope/kv, attention, wo+res+norm, gate+up, silu+quant, down, output. Enabled by
  * mk_set_profile(ctx, 1) (forward then runs without its CUDA graph). */
 int mk_set_profile(mk_ctx* ctx, int on);
@@ -203,17 +214,17 @@ void* mk_stream(const mk_ctx* ctx);
  * ------------------------------------------------------------------------------------------------------- */
 typedef struct mk_weight mk_weight;
 
-/* pack_weight_into (quant.cpp:300-311): repacks rows x cols GGUF rows of `type` (host, row-major) into the
+/* pack_weight_into (quant.cpp:218-229): repacks rows x cols GGUF rows of `type` (host, row-major) into the
  * device panel layout on the current device. */
 int mk_weight_upload(int type, const void* host_rows, int64_t rows, int64_t cols, mk_weight** out);
 int mk_weight_free(mk_weight* w);
 int64_t mk_weight_device_bytes(const mk_weight* w);
 
-/* quantize_row_q8 over n rows (quant.cpp:275-281, kernels_avx512.cpp:66-80): dev_x n x k floats (row stride
+/* quantize_row_q8 over n rows (quant.cpp:132, 193-199, kernels_avx512.cpp:66-80): dev_x n x k floats (row stride
  * k), dev_blocks n * k/32 malkin BlockQ8 {float d; int16 s[2]; int8 qs[32]} (40 bytes each). */
 int mk_quantize_q8(const float* dev_x, int n, int64_t k, void* dev_blocks, void* stream);
 
-/* matmul (quant.cpp:412): dev_y[t * rows + r] = W[r] . x[t], activations quantized to Q8 blocks on device.
+/* matmul (quant.cpp:330-351): dev_y[t * rows + r] = W[r] . x[t], activations quantized to Q8 blocks on device.
  * split_k = 1 keeps malkin's per-row block order (results bit-identical to its compact panel kernels);
  * 0 = choose for speed. */
 int mk_matmul(const mk_weight* w, const float* dev_x, int n, float* dev_y, int split_k, void* stream);
@@ -225,22 +236,25 @@ int mk_matmul(const mk_weight* w, const float* dev_x, int n, float* dev_y, int s
  * KV cache at start-up, and latency-bound loops that must not stall other streams. Same arguments and results as
  * mk_matmul. Limits: about 76 bytes per token per 32 values of activations must fit (108 with the optional fp16
  * Q8_0 GEMM; for example 256 tokens x 16384 values); split_k = 0 lowers the split until the partial sums fit, an
- * explicit split_k whose partial sums do not fit is rejected with MK_ERR_ARG. Calls on one device share the scratch: calls that overlap in time (other
- * streams, other threads) race, so serialise them. The first call on each device looks up the scratch address;
- * make it before any stream capture. */
+ * explicit split_k whose partial sums do not fit is rejected with MK_ERR_ARG. Calls on one device share the scratch:
+ * calls that overlap in time (other streams, other threads) race, so serialise them. Each call synchronizes `stream`
+ * before it returns (it reads the kernels' status word back). The first call on each device looks up the scratch
+ * address and keeps it; make that first call before any stream capture. The kept address belongs to the device's
+ * primary context and does not survive cudaDeviceReset: a process that resets a device must not call this entry
+ * point on that device afterwards. */
 int mk_matmul_noalloc(const mk_weight* w, const float* dev_x, int n, float* dev_y, int split_k, void* stream);
 
 /* Exact integer block dot products of the GEMM (gemm_avx512.cpp:83-98, 130-141, 179-199): dev_out[(r * n + t) *
  * nblk + b] = sum of w * x over block b (Q8_0, Q4_K: 32 values; Q6_K: 16 values, nblk = cols/16). */
 int mk_block_dots(const mk_weight* w, const float* dev_x, int n, int32_t* dev_out, void* stream);
 
-/* quantize_i8 (quant.cpp:216-222) of n rows of len values: dev_q int8, dev_scale one float per row. */
+/* quantize_i8 (quant.cpp:134-140) of n rows of len values: dev_q int8, dev_scale one float per row. */
 int mk_quantize_i8(const float* dev_x, int n, int len, int8_t* dev_q, float* dev_scale, void* stream);
 
 /* kern::silu_mul (kernels_avx512.cpp:271-280) in place on dev_g (n values). */
 int mk_silu_mul(float* dev_g, const float* dev_u, int64_t n, void* stream);
 
-/* Tree-masked GQA attention (Model::attention + kern::attend_gqa, model.cpp:303-346, kernels_avx512.cpp:228-306)
+/* Tree-masked GQA attention (Model::attention + kern::attend_gqa, model.cpp:204-247, kernels_avx512.cpp:229-307)
  * on caller buffers: n query tokens x H heads x D (dev_q, float); KV cache of one layer in this library's
  * head-major layout: dev_k / dev_v int8 [KV][n_rows][D], dev_ks / dev_vs float [KV][n_rows];
  * per token: dev_kv_base (first row of its sequence), dev_n_keys (contiguous keys from kv_base), extra key rows

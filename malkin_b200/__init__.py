@@ -118,7 +118,7 @@ class AcceptResult(ctypes.Structure):
 
 
 class Proposal:
-    """One decoding slot's proposal (engine.h:269-274). Greedy: tree [next, c0, a0, c1, a1, ...] from batch index
+    """One decoding slot's proposal (engine.h:126-131). Greedy: tree [next, c0, a0, c1, a1, ...] from batch index
     root; sampled (temperature > 0): chain [next, d0, ...] with draft distributions q and the slot's uniforms."""
 
     def __init__(self, seq: int, root: int, cache_len: int, chain: Sequence[int] = (),
@@ -201,7 +201,7 @@ lib.mk_attention.argtypes = [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctyp
 EXPORTS = ("mk_last_error", "mk_version", "mk_synth_gguf", "mk_init", "mk_nccl_unique_id", "mk_shutdown",
            "mk_load_gguf", "mk_alloc_kv", "mk_model_config_get", "mk_forward", "mk_move_kv", "mk_accept",
            "mk_rng_uniforms", "mk_verify_step", "mk_set_profile", "mk_stage_times", "mk_last_launch_count",
-           "mk_stream", "mk_last_io_bytes", "mk_tp_shard_of", "mk_weight_upload", "mk_weight_free", "mk_weight_device_bytes", "mk_quantize_q8",
+           "mk_stream", "mk_last_io_bytes", "mk_tp_shard_of", "mk_tp_exchange_check", "mk_weight_upload", "mk_weight_free", "mk_weight_device_bytes", "mk_quantize_q8",
            "mk_matmul", "mk_matmul_noalloc", "mk_block_dots", "mk_quantize_i8", "mk_silu_mul", "mk_attention")
 
 
@@ -229,6 +229,23 @@ def rng_uniforms(seed: int, n: int, skip: int = 0) -> np.ndarray:
     out = np.empty(n, dtype=np.float64)
     _check(lib.mk_rng_uniforms(seed, skip, n, out.ctypes.data_as(_P_F64)))
     return out
+
+
+lib.mk_tp_exchange_check.argtypes = [ctypes.c_int] * 5 + [ctypes.c_void_p, ctypes.c_int] + [ctypes.c_void_p] * 3
+
+
+def tp_exchange_check(parts: np.ndarray, twoshot: bool = False, absent: Optional[Sequence[int]] = None,
+                      wait_polls: int = 1 << 24):
+    """Rank 0's tensor-parallel exchange kernels against host-emulated peers (mk_tp_exchange_check).
+    parts: [calls, size, n, cols] float32. Returns (sums [calls, n, cols], status per call)."""
+    parts = np.ascontiguousarray(parts, dtype=np.float32)
+    calls, size, n, cols = parts.shape
+    out = np.zeros((calls, n, cols), dtype=np.float32)
+    st = np.zeros(calls, dtype=np.int32)
+    ab = None if absent is None else np.ascontiguousarray(absent, dtype=np.int32)
+    _check(lib.mk_tp_exchange_check(size, int(twoshot), n, cols, calls, None if ab is None else ab.ctypes.data,
+                                    wait_polls, parts.ctypes.data, out.ctypes.data, st.ctypes.data))
+    return out, st
 
 
 def nccl_unique_id() -> bytes:

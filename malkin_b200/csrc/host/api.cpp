@@ -173,6 +173,15 @@ int mk_tp_shard_of(const char* gguf_path, int tp_size, int tp_rank, mk_tp_shard*
   });
 }
 
+int mk_tp_exchange_check(int size, int twoshot, int n, int cols, int n_calls, const int* absent, int wait_polls,
+                         const float* host_parts, float* host_out, int* call_status) {
+  return guard(MK_ERR_ARG, [&] {
+    if (wait_polls <= 0) throw mkb::ArgError("tp_exchange_check: wait_polls must be positive");
+    mkb::tp_exchange_check(size, twoshot != 0, n, cols, n_calls, absent, static_cast<uint32_t>(wait_polls), host_parts,
+                           host_out, call_status);
+  });
+}
+
 int mk_model_config_get(const mk_ctx* ctx, mk_model_config* out) {
   return guard(MK_ERR_ARG, [&] {
     if (!out) throw mkb::ArgError("null output");

@@ -80,7 +80,7 @@ Model::~Model() {
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// load: read_config (model.cpp:177-200) + Model::Model (model.cpp:211-251) + pack (model.cpp:262-277), per shard.
+// load: read_config (model.cpp:78-101) + Model::Model (model.cpp:112-152) + pack (model.cpp:163-178), per shard.
 // ---------------------------------------------------------------------------------------------------------------
 ModelCfg read_config(const GgufReader& f) {
   const std::string arch = f.meta_text("general.architecture").value_or("");
@@ -327,7 +327,7 @@ void Model::load(const std::string& path) {
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// alloc_kv (model.cpp:296-301) + scratch for max_batch tokens (model.cpp:239-250).
+// alloc_kv (model.cpp:197-202) + scratch for max_batch tokens (model.cpp:139-151).
 // ---------------------------------------------------------------------------------------------------------------
 void Model::alloc_kv(int n_ctx, int n_seq, int max_batch) {
   if (!loaded_) throw StateError("alloc_kv before load");
@@ -354,7 +354,7 @@ void Model::alloc_kv(int n_ctx, int n_seq, int max_batch) {
     const size_t lo = static_cast<size_t>(il) * KVl_ * R;
     kv_layers_[static_cast<size_t>(il)] = {kbase + lo * D, vbase + lo * D, ksb + lo, vsb + lo, R};
   }
-  // RoPE table [pos][cos D/2 | sin D/2], the reference's float angles and libm cos / sin (model.cpp:434-440).
+  // RoPE table [pos][cos D/2 | sin D/2], the reference's float angles and libm cos / sin (model.cpp:336-340).
   {
     std::vector<float> tab(static_cast<size_t>(n_ctx) * D);
     for (int p = 0; p < n_ctx; ++p) {
@@ -638,7 +638,7 @@ void Model::run_forward(int n, int m) {
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// forward (model.cpp:379-422)
+// forward (model.cpp:280-323)
 // ---------------------------------------------------------------------------------------------------------------
 void Model::forward(const mk_batch_token* batch, int n, float* host_logits) {
   if (!loaded_ || n_ctx_ == 0) throw StateError("forward before load / alloc_kv");

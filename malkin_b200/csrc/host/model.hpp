@@ -73,6 +73,9 @@ void throw_device_status(int code, const std::string& what);
 // The config of a qwen3 GGUF (read_config, model.cpp:78-101), and the slice of it one tensor-parallel rank holds:
 // q / kv heads (column split), ffn rows in whole k-units of ffn_down, vocabulary rows (split of the LM head).
 ModelCfg read_config(const GgufReader& f);
+// mk_tp_exchange_check (tp_check.cpp): rank 0's rank-sum kernels against host-emulated peers on one device.
+void tp_exchange_check(int size, bool twoshot, int n, int cols, int n_calls, const int* absent, uint32_t wait_polls,
+                       const float* parts, float* out, int* call_status);
 struct TpShard {
   int head0 = 0, heads = 0, kv_head0 = 0, kv_heads = 0, ffn0 = 0, ffn = 0;
   int64_t vocab0 = 0, vocab = 0;

@@ -1,5 +1,5 @@
 // Host repack of GGUF rows into the device panel layout (layout.hpp); the B200 counterpart of malkin's
-// pack_weight_into / kern::pack_panel (quant.cpp:300-311, gemm_avx512.cpp:376-544). Rows beyond the source are
+// pack_weight_into / kern::pack_panel (quant.cpp:218-229, gemm_avx512.cpp:376-544). Rows beyond the source are
 // zero-filled (they contribute exactly 0: zero scales), so matrices of any row count pad to whole panels.
 #include "repack.hpp"
 
@@ -21,7 +21,7 @@ namespace mkb {
 
 namespace {
 
-// 6-bit value k (0..255) of a Q6_K super-block, stored +32 (quant.cpp:190-210 layout).
+// 6-bit value k (0..255) of a Q6_K super-block, stored +32 (quant.cpp:108-128 layout).
 inline int q6_at(const uint8_t* s, int k) {
   const int n = k / 128, rem = k % 128, c = rem / 32, l = rem % 32;
   const uint8_t lo = s[64 * n + l + (c & 1) * 32];

@@ -1,6 +1,6 @@
 // Synthetic Qwen3 GGUF writer: the stand-in for "seeded N(0, sigma) weights, norms 1.0, quantized, written as GGUF"
 // (malkin ships no weight quantizer and no GGUF writer). Tensor names, shapes and metadata keys are the ones
-// malkin's read_config / Model constructor bind (model.cpp:177-234). Quantizers: Q8_0 (per-32 absmax), Q4_K and
+// malkin's read_config / Model constructor bind (model.cpp:78-135). Quantizers: Q8_0 (per-32 absmax), Q4_K and
 // Q6_K (simple min/max and absmax fits; the format, not the fit, is what both sides must agree on: they read the
 // same bytes). Every row's values depend only on (seed, tensor index, row), so the file is identical for any
 // thread count.
@@ -59,7 +59,7 @@ void quant_q8_0(const float* x, uint8_t* y, int64_t k) {
 }
 
 // Q4_K super-block (144 bytes): fp16 d, fp16 dmin, 12 bytes of 6-bit (scale, min) per 32-value sub-block packed as
-// scale_min_k4 unpacks them (kernels.h:18-26), then 128 bytes of nibbles (quant.cpp:159-172 layout).
+// scale_min_k4 unpacks them (kernels.h:18-26), then 128 bytes of nibbles (quant.cpp:77-90 layout).
 void quant_q4_k(const float* x, uint8_t* y, int64_t k) {
   for (int64_t sb = 0; sb < k / 256; ++sb, x += 256, y += 144) {
     float scale[8], mn[8];
@@ -101,7 +101,7 @@ void quant_q4_k(const float* x, uint8_t* y, int64_t k) {
 }
 
 // Q6_K super-block (210 bytes): ql[128] low nibbles, qh[64] 2-bit highs, int8 scale per 16 values, fp16 d
-// (quant.cpp:190-210 layout): value p has scale sc[p / 16] and 6-bit q stored +32.
+// (quant.cpp:108-128 layout): value p has scale sc[p / 16] and 6-bit q stored +32.
 void quant_q6_k(const float* x, uint8_t* y, int64_t k) {
   for (int64_t sb = 0; sb < k / 256; ++sb, x += 256, y += 210) {
     float scale[16];

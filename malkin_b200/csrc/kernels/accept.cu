@@ -206,7 +206,7 @@ struct Dist {
   int id[MK_TOPK_CAP];
 };
 
-// Sampler::distribution (sampler.cpp:66-106) from the row's top-k candidates (sorted value desc).
+// Sampler::distribution (sampler.cpp:22-62) from the row's top-k candidates (sorted value desc).
 __device__ void distribution(const float* cv, const int32_t* ci, int k, float temp, float top_p, float min_p, Dist& out) {
   float e[MK_TOPK_CAP];
   const float mx = cv[0];
@@ -243,7 +243,7 @@ __device__ float prob_of(const float* p, const int* id, int n, int d) {
   return 0.0f;
 }
 
-// Sampler::draw (sampler.cpp:108-116): no uniform consumed for a one-entry distribution.
+// Sampler::draw (sampler.cpp:64-72): no uniform consumed for a one-entry distribution.
 __device__ int draw(const float* p, const int* id, int n, const double* U, int nu, int& u, int& status) {
   if (n == 1) return id[0];
   if (u >= nu) {

@@ -1,8 +1,8 @@
-// Attention side of a decoder layer (model.cpp:468-496): q/k head RMSNorm + NeoX RoPE + int8 KV write, then
+// Attention side of a decoder layer (model.cpp:369-392): q/k head RMSNorm + NeoX RoPE + int8 KV write, then
 // tree-masked GQA attention over the HBM-resident int8 KV cache (Model::attention + kern::attend_gqa,
-// model.cpp:303-346, kernels_avx512.cpp:228-306).
+// model.cpp:204-247, kernels_avx512.cpp:229-307).
 //
-// Key sets (model.cpp:405-420): token t attends keys [0, n_keys[t]) of its sequence, then its extra rows anc[...]
+// Key sets (model.cpp:306-321): token t attends keys [0, n_keys[t]) of its sequence, then its extra rows anc[...]
 // (tree ancestors, root first, itself last). Rows of one sequence that share the prefix form a sub-group; one
 // CTA takes a (sub-group, KV head, key chunk) and scores every (row, query head) of the sub-group against the
 // chunk, so each prefix key is read once per sub-group and KV head (GQA: the G query heads share it).
@@ -72,7 +72,7 @@ __global__ void k_qkv_post(Slices qk, int v_n, int64_t v_col0, int64_t ldy, int 
     for (int m = 0; m < PER; ++m) dst[lane + 32 * m] = v[m];
     return;
   }
-  // quantize_i8 (quant.cpp:216-222) into the cache row kv_at[t] of this KV head.
+  // quantize_i8 (quant.cpp:134-140) into the cache row kv_at[t] of this KV head.
   float amax = 0.0f;
 #pragma unroll
   for (int m = 0; m < PER; ++m) amax = fmaxf(amax, fabsf(v[m]));

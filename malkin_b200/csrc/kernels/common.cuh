@@ -134,7 +134,7 @@ __device__ __forceinline__ float sum_strided(const float* p, int64_t stride) {
   return r;
 }
 
-// e^x as malkin computes it for softmax and SiLU (kernels_avx512.cpp:186-202): clamp below at -87, Cody-Waite
+// e^x as malkin computes it for softmax and SiLU (kernels_avx512.cpp:186-203): clamp below at -87, Cody-Waite
 // reduction with ln 2 split in two, degree-6 Taylor polynomial in Horner form with fused multiply-adds, then
 // scaling by 2^n. (malkin's own algorithm, restated, so both sides exponentiate identically.)
 __device__ __forceinline__ float exp_malkin(float x) {

@@ -60,7 +60,7 @@ struct Slices {
   int n = 0;
   int64_t stride = 0;
 };
-// rmsnorm (model.cpp:145-148) then quantize. rows: row indices into x (nullptr = 0..n-1). add: residual
+// rmsnorm (model.cpp:46-49) then quantize. rows: row indices into x (nullptr = 0..n-1). add: residual
 // contributions added into x first, in slice order (x[r] += add[0][r] + add[1][r] + ..., written back).
 void launch_rmsnorm_quant(float* x, int64_t ldx, Slices add, const int32_t* rows, const float* w, float eps, int n,
                           int K, const ActQ& act, cudaStream_t s);
@@ -70,7 +70,7 @@ void launch_silu_quant(Slices gu, int64_t ld, int F, int n, const ActQ& act, cud
 void launch_sum_slices(Slices src, int64_t ld, int n, int cols, float* dst, cudaStream_t s);
 // malkin BlockQ8 output (40-byte blocks) for tests.
 void launch_quant_blockq8(const float* x, int n, int64_t K, void* blocks, cudaStream_t s);
-// quantize_i8 rows (quant.cpp:216-222).
+// quantize_i8 rows (quant.cpp:134-140).
 void launch_quant_i8(const float* x, int n, int len, int8_t* q, float* scale, cudaStream_t s);
 void launch_silu_mul(float* g, const float* u, int64_t n, cudaStream_t s);
 
@@ -116,6 +116,7 @@ int gemm_tc_slices(const DevWeight& w, int split);
 // rank published into r); the pointers of the other ranks are their CUDA IPC mappings in this process.
 constexpr int kMaxTp = 8;
 constexpr int kErrTpWait = 12;  // status code: a rank's partial never arrived
+constexpr uint32_t kTpWaitPolls = 1u << 24;  // polls of about 64 ns: about a second at most
 struct TpExchange {
   float* data[kMaxTp] = {};
   int* flags[kMaxTp] = {};
@@ -126,6 +127,7 @@ struct TpExchange {
   unsigned* counter2 = nullptr;
   int rank = 0, size = 1;
   int64_t cap = 0;
+  uint32_t wait_polls = kTpWaitPolls;  // a flag wait gives up after this many polls (status kErrTpWait)
 };
 // publish: this rank's split-K slices, summed in slice order, into its half of the exchange; gather: the sum over
 // ranks in rank order into dst (n x cols, cols % 4 == 0). Run both, in this order, on every rank.

@@ -1,5 +1,5 @@
-// Token embedding gather + dequantize (Model::run, model.cpp:430-433 -> dequantize_row, quant.cpp:152-251) and
-// KV row moves (Model::move_kv, model.cpp:531-539).
+// Token embedding gather + dequantize (Model::run, model.cpp:331-334 -> dequantize_row, quant.cpp:70-169) and
+// KV row moves (Model::move_kv, model.cpp:432-440).
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 

@@ -1,6 +1,6 @@
 // Fixed device scratch for the allocation-free matmul entry point (mk_matmul_noalloc): a file-scope __device__
 // array in this library's own module, so a call makes no cudaMalloc / cudaFree. Its address is looked up once per
-// device with that device current.
+// device with that device current and kept for the life of the process (it does not survive cudaDeviceReset).
 #include <cuda_runtime.h>
 
 #include <mutex>

@@ -1,5 +1,5 @@
 // Activation quantization to Q8 blocks (kern::quantize_row_q8, kernels_avx512.cpp:66-80), fused with the ops that
-// produce the activations: RMSNorm (model.cpp:145-148) and SiLU(gate) * up (kernels_avx512.cpp:271-280).
+// produce the activations: RMSNorm (model.cpp:46-49) and SiLU(gate) * up (kernels_avx512.cpp:271-280).
 // One warp quantizes one 32-value block: lane i holds value i.
 //
 // Bit-exactness with malkin's BlockQ8 given the same float input: d = amax / 127 (IEEE division), id = 1 / d
@@ -162,7 +162,7 @@ __global__ void k_quant_blockq8(const float* __restrict__ x, int64_t K, uint8_t*
   }
 }
 
-// quantize_i8 (quant.cpp:216-222) of one row per warp: d = amax / 127, q = lrintf(x * (1 / d)).
+// quantize_i8 (quant.cpp:134-140) of one row per warp: d = amax / 127, q = lrintf(x * (1 / d)).
 __global__ void k_quant_i8(const float* __restrict__ x, int n, int len, int8_t* __restrict__ q, float* __restrict__ sc) {
   const int lane = threadIdx.x & 31, r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (r >= n) return;

@@ -11,7 +11,8 @@
 //            ranks' halves in rank order 0..size-1, so every rank gets bit-identical results.
 // A half is rewritten two calls later; by then every rank has published the call in between, which it does only
 // after its gather of the earlier call finished, so no rank still reads it. A wait that runs out records
-// kErrTpWait in the status word and the kernel returns (a rank that died or never launched).
+// kErrTpWait in the status word and the kernel returns (a rank that died or never launched); a wait gives up after
+// x.wait_polls polls.
 // Two-shot (opt-in): after publish, reduce sums this rank's 1/size of the rows over all ranks into its red half and
 // releases flags2; allgather waits for every rank's flags2 and copies each rank's reduced rows. Each rank reads
 // 2 (size - 1) / size of the data from peers (one-shot: size - 1 times it); the sums are the same, bit for bit. The
@@ -24,7 +25,7 @@ namespace mkb {
 
 namespace {
 
-constexpr uint32_t kTpWaitLimit = 1u << 24;  // polls of about 64 ns: about a second at most
+constexpr unsigned kTpCallFailed = 0x80000000u;  // counter2 bit: a CTA of this reduce gave up waiting
 
 __device__ __forceinline__ void st_release_sys(int* p, int v) {
   asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -68,15 +69,15 @@ __global__ void k_tp_publish(TpExchange x, Slices src, int64_t ld, int n, int co
   }
 }
 
-__global__ void k_tp_gather(TpExchange x, int n, int cols, float* __restrict__ dst, int* status) {
-  const int e = *x.epoch;  // set by this rank's publish (stream order)
+// Bounded wait (thread 0 of the CTA) until flags[0..size) all reach e; false (and status) if one never does.
+__device__ bool wait_flags(const int* flags, int size, int e, uint32_t polls, int* status) {
   __shared__ int ready;
   if (threadIdx.x == 0) {
     bool ok = true;
-    for (int r = 0; r < x.size && ok; ++r) {
+    for (int r = 0; r < size && ok; ++r) {
       uint32_t it = 0;
-      while (ld_acquire_sys(x.flags[x.rank] + r) < e) {
-        if (++it >= kTpWaitLimit) {
+      while (ld_acquire_sys(flags + r) < e) {
+        if (++it >= polls) {
           ok = false;
           break;
         }
@@ -87,7 +88,12 @@ __global__ void k_tp_gather(TpExchange x, int n, int cols, float* __restrict__ d
     ready = ok;
   }
   __syncthreads();
-  if (!ready) return;
+  return ready != 0;
+}
+
+__global__ void k_tp_gather(TpExchange x, int n, int cols, float* __restrict__ dst, int* status) {
+  const int e = *x.epoch;  // set by this rank's publish (stream order)
+  if (!wait_flags(x.flags[x.rank], x.size, e, x.wait_polls, status)) return;
   const int64_t off = static_cast<int64_t>(e & 1) * x.cap;
   const int64_t total4 = static_cast<int64_t>(n) * cols / 4;  // cols % 4 == 0
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total4;
@@ -109,37 +115,15 @@ __global__ void k_tp_gather(TpExchange x, int n, int cols, float* __restrict__ d
   }
 }
 
-// Bounded wait (thread 0 of the CTA) until flags[0..size) all reach e; false (and status) if one never does.
-__device__ bool wait_flags(const int* flags, int size, int e, int* status) {
-  __shared__ int ready;
-  if (threadIdx.x == 0) {
-    bool ok = true;
-    for (int r = 0; r < size && ok; ++r) {
-      uint32_t it = 0;
-      while (ld_acquire_sys(flags + r) < e) {
-        if (++it >= kTpWaitLimit) {
-          ok = false;
-          break;
-        }
-        __nanosleep(64);
-      }
-    }
-    if (!ok && status) atomicCAS(status, 0, kErrTpWait);
-    ready = ok;
-  }
-  __syncthreads();
-  return ready != 0;
-}
-
 // Rows of rank q's share of the reduction, in float4 units: [q * total4 / size, (q + 1) * total4 / size).
 __device__ __forceinline__ int64_t share_begin(int64_t total4, int q, int size) { return total4 * q / size; }
 
 __global__ void k_tp_reduce(TpExchange x, int n, int cols, int* status) {
   const int e = *x.epoch;  // set by this rank's publish (stream order)
-  if (!wait_flags(x.flags[x.rank], x.size, e, status)) return;
+  const bool ok = wait_flags(x.flags[x.rank], x.size, e, x.wait_polls, status);
   const int64_t off = static_cast<int64_t>(e & 1) * x.cap;
   const int64_t total4 = static_cast<int64_t>(n) * cols / 4;
-  const int64_t b = share_begin(total4, x.rank, x.size), end = share_begin(total4, x.rank + 1, x.size);
+  const int64_t b = share_begin(total4, x.rank, x.size), end = ok ? share_begin(total4, x.rank + 1, x.size) : b;
   for (int64_t i = b + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < end;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     float4 v[kMaxTp];
@@ -157,21 +141,25 @@ __global__ void k_tp_reduce(TpExchange x, int n, int cols, int* status) {
       }
     reinterpret_cast<float4*>(x.red[x.rank] + off)[i] = acc;
   }
+  // Every CTA arrives, also one whose wait gave up (it marks the call failed first), so the counter is back at zero
+  // for the next call; the share is released to the peers only when every CTA reduced its part.
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence_system();
+    if (!ok) atomicOr(x.counter2, kTpCallFailed);
     const unsigned prev = atomicAdd(x.counter2, 1u);
-    if (prev == gridDim.x - 1) {  // the whole share is reduced and fenced
+    if ((prev & ~kTpCallFailed) == gridDim.x - 1) {  // last arrival: the whole share is reduced and fenced
       __threadfence_system();
       *x.counter2 = 0;
-      for (int r = 0; r < x.size; ++r) st_release_sys(x.flags2[r] + x.rank, e);
+      if (!(prev & kTpCallFailed))
+        for (int r = 0; r < x.size; ++r) st_release_sys(x.flags2[r] + x.rank, e);
     }
   }
 }
 
 __global__ void k_tp_allgather(TpExchange x, int n, int cols, float* __restrict__ dst, int* status) {
   const int e = *x.epoch;
-  if (!wait_flags(x.flags2[x.rank], x.size, e, status)) return;
+  if (!wait_flags(x.flags2[x.rank], x.size, e, x.wait_polls, status)) return;
   const int64_t off = static_cast<int64_t>(e & 1) * x.cap;
   const int64_t total4 = static_cast<int64_t>(n) * cols / 4;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total4;

@@ -26,10 +26,20 @@ _P_F64 = ctypes.POINTER(ctypes.c_double)
 _vp = ctypes.c_void_p
 
 
+def reference_src() -> str:
+    """The reference's src/ directory: $MALKIN_REF_SRC, else a checkout named `reference` beside this repository
+    ("" when neither exists)."""
+    env = os.environ.get("MALKIN_REF_SRC")
+    if env:
+        return env
+    sib = os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference", "src")
+    return sib if os.path.isdir(sib) else ""
+
+
 def build(ref: bool = True) -> None:
-    """Compiles liboracle.so (always) and _ref (when the reference sources are mounted)."""
-    subprocess.run(["make", "-C", HERE, os.path.join(HERE, "liboracle.so")] + (["ref"] if ref else []), check=True,
-                   stdout=subprocess.DEVNULL)
+    """Compiles liboracle.so (always) and _ref (when the reference sources are found)."""
+    subprocess.run(["make", "-C", HERE, os.path.join(HERE, "liboracle.so")] +
+                   (["ref", f"REF={reference_src()}"] if ref else []), check=True, stdout=subprocess.DEVNULL)
 
 
 def _p(a: np.ndarray, t):

@@ -57,7 +57,7 @@ float orc_fp16_to_fp32(uint16_t h) {
 /* round half to even, as vcvtps2dq under the default MXCSR and lrintf */
 static int rne(float x) { return (int)lrintf(x); }
 
-/* e^x of malkin's softmax / SiLU (kernels_avx512.cpp:186-202): clamp at -87, Cody-Waite with ln 2 in two parts,
+/* e^x of malkin's softmax / SiLU (kernels_avx512.cpp:186-203): clamp at -87, Cody-Waite with ln 2 in two parts,
  * degree-6 Taylor in Horner form with fused multiply-adds, scale by 2^n. */
 static float exp_malkin(float x) {
   if (x < -87.0f) x = -87.0f;
@@ -74,7 +74,7 @@ static float exp_malkin(float x) {
   return ldexpf(p, (int)n);
 }
 
-/* ---------------- quantization (kernels_avx512.cpp:66-80, quant.cpp:216-222) ---------------- */
+/* ---------------- quantization (kernels_avx512.cpp:66-80, quant.cpp:134-140) ---------------- */
 
 void orc_quantize_row_q8(const float* x, orc_block_q8* y, int64_t k) {
   for (int64_t i = 0; i < k / 32; ++i, x += 32) {
@@ -105,7 +105,7 @@ float orc_quantize_i8(const float* x, int n, int8_t* q) {
   return d;
 }
 
-/* ---------------- GGUF formats (quant.cpp:152-251, kernels.h:18-26) ---------------- */
+/* ---------------- GGUF formats (quant.cpp:70-169, kernels.h:18-26) ---------------- */
 
 static void scale_min_k4(int j, const uint8_t* q, int* sc, int* m) {
   if (j < 4) {
@@ -287,7 +287,7 @@ void orc_matmul(int type, const uint8_t* w, int64_t rows, int64_t cols, const fl
 
 /* ---------------- small ops ---------------- */
 
-/* rmsnorm (model.cpp:145-148) */
+/* rmsnorm (model.cpp:46-49) */
 static void rmsnorm(float* y, const float* x, const float* w, int n, float eps) {
   float ss = 0.0f;
   for (int i = 0; i < n; ++i) ss = fmaf(x[i], x[i], ss);
@@ -300,7 +300,7 @@ void orc_silu_mul(int64_t n, float* g, const float* u) {
   for (int64_t i = 0; i < n; ++i) g[i] = g[i] / (1.0f + exp_malkin(0.0f - g[i])) * u[i];
 }
 
-/* kern::attend_gqa (kernels_avx512.cpp:228-306): one token, the G heads of one KV head. Keys 0..n-1 then extra[].
+/* kern::attend_gqa (kernels_avx512.cpp:229-307): one token, the G heads of one KV head. Keys 0..n-1 then extra[].
  * k / v: head row 0 of int8 values, rows `stride` bytes apart; scales at ks[row] / vs[row]. */
 void orc_attend(const float* q, int G, int D, const int8_t* k, const int8_t* v, const float* ks, const float* vs,
                 int64_t stride, int n, const int* extra, int ne, float scale, float* out) {
@@ -425,7 +425,7 @@ void orc_model_close(orc_model* m) {
   free(m);
 }
 
-/* GgufFile + read_config + Model::Model + alloc_kv (model.cpp:177-251, 296-301); NULL on error. */
+/* GgufFile + read_config + Model::Model + alloc_kv (model.cpp:78-152, 197-202); NULL on error. */
 orc_model* orc_model_open(const char* path, int n_ctx, int n_seq) {
   FILE* f = fopen(path, "rb");
   if (!f) return NULL;
@@ -559,7 +559,7 @@ static void matmul_w(const orc_tensor* w, const float* x, int n, float* y) {
   orc_matmul(w->type, w->data, t_rows(w), w->ne[0], x, n, y);
 }
 
-/* Model::forward(const BatchToken*, n, logits) + Model::run (model.cpp:379-525). Returns 0, or -1 on a batch
+/* Model::forward(const BatchToken*, n, logits) + Model::run (model.cpp:280-430). Returns 0, or -1 on a batch
  * malkin rejects (same checks). */
 int orc_model_forward(orc_model* m, int n, const int32_t* id, const int32_t* seq, const int32_t* pos,
                       const int32_t* want, const int32_t* kvp, const int32_t* parent, float* logits) {
@@ -665,7 +665,7 @@ int orc_model_forward(orc_model* m, int n, const int32_t* id, const int32_t* seq
   return 0;
 }
 
-/* Model::move_kv (model.cpp:531-539) */
+/* Model::move_kv (model.cpp:432-440) */
 void orc_model_move_kv(orc_model* m, int from, int to, int seq) {
   if (from == to) return;
   const int64_t b = (int64_t)seq * m->n_ctx;
@@ -749,7 +749,7 @@ static float prob_of(const float* p, const int32_t* id, int n, int d) {
   return 0.0f;
 }
 
-/* Sampler::draw (sampler.cpp:108-116) */
+/* Sampler::draw (sampler.cpp:64-72) */
 static int draw(const float* p, const int32_t* id, int n, const double* U, int* u) {
   if (n == 1) return id[0];
   double r = U[(*u)++];
@@ -795,7 +795,7 @@ int orc_accept_greedy(orc_model* m, const float* logits, int V, int kk, const in
   return n;
 }
 
-/* Engine::accept_sampled + Sampler::verify (engine.cpp:482-507, sampler.cpp:124-141) with the uniform stream U.
+/* Engine::accept_sampled + Sampler::verify (engine.cpp:482-507, sampler.cpp:80-97) with the uniform stream U.
  * Rows 0..kk of logits: [next, d0, ...]. Returns the accepted count; *next, *u_used. */
 int orc_accept_sampled(const float* logits, int V, orc_sampling s, int kk, const int32_t* chain, const float* q_p,
                        const int32_t* q_id, const int32_t* q_n, const double* U, int32_t* acc_ids, int32_t* next,

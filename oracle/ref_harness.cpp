@@ -5,14 +5,15 @@
 // as the checker or as the timed CPU baseline; the product (malkin_b200) never links or calls it.
 //
 // What is exposed (reference citations are src/<file>:<line> in kekzl/malkin v0.2.0):
-//   model      GgufFile + Model(f, n_ctx, n_seq) + Model::forward(const BatchToken*, n, logits)   model.cpp:211,379
-//              Model::move_kv                                                                     model.cpp:531
-//   quant      quantize_row_q8 (kern::quantize_row_q8), quantize_i8, dequantize_row, matmul        quant.cpp:214-412
+//   model      GgufFile + Model(f, n_ctx, n_seq) + Model::forward(const BatchToken*, n, logits)   model.cpp:112,280
+//              Model::move_kv                                                                     model.cpp:432
+//   quant      quantize_row_q8 (kern::quantize_row_q8), quantize_i8, dequantize_row, matmul        quant.cpp:132-351
 //   attention  kern::attend_gqa (tree ancestors as extra keys)                                    kernels_avx512.cpp:282
 //   sampler    Sampler::distribution / draw / verify                                              sampler.cpp:22-97
 //   accept     Engine::accept_greedy / accept_sampled restated over Model::move_kv and Sampler,   engine.cpp:441-507
 //              because they are private members of Engine (whose tokenizer needs pcre2, absent
 //              here). emit() is taken as "continue" (no end-of-generation token, no stop string).
+#include <cstddef>
 #include <cstdint>
 #include <cstring>
 #include <memory>
@@ -30,7 +31,29 @@
 #include "quant.h"
 #include "sampler.h"
 
+#include "../include/malkin_b200.h"
+
 using namespace malkin;
+
+// The C ABI's structs mirror malkin's: a BatchToken array and the sampling parameters cross the boundary as they are
+// (model.h:25-30, sampler.h:10-18; mk_sampling stops before SamplingParams::seed, the host owns the RNG).
+#define MK_SAME_FIELD(A, B, fa, fb) \
+  static_assert(offsetof(A, fa) == offsetof(B, fb) && sizeof(A::fa) == sizeof(B::fb), #A "." #fa " != " #B "." #fb)
+static_assert(sizeof(mk_batch_token) == sizeof(BatchToken) && alignof(mk_batch_token) == alignof(BatchToken));
+MK_SAME_FIELD(mk_batch_token, BatchToken, id, id);
+MK_SAME_FIELD(mk_batch_token, BatchToken, seq, seq);
+MK_SAME_FIELD(mk_batch_token, BatchToken, pos, pos);
+MK_SAME_FIELD(mk_batch_token, BatchToken, logits, logits);
+MK_SAME_FIELD(mk_batch_token, BatchToken, kv, kv);
+MK_SAME_FIELD(mk_batch_token, BatchToken, parent, parent);
+MK_SAME_FIELD(mk_sampling, SamplingParams, temperature, temperature);
+MK_SAME_FIELD(mk_sampling, SamplingParams, top_p, top_p);
+MK_SAME_FIELD(mk_sampling, SamplingParams, top_k, top_k);
+MK_SAME_FIELD(mk_sampling, SamplingParams, min_p, min_p);
+MK_SAME_FIELD(mk_sampling, SamplingParams, presence_penalty, presence_penalty);
+MK_SAME_FIELD(mk_sampling, SamplingParams, frequency_penalty, frequency_penalty);
+static_assert(sizeof(mk_sampling) == offsetof(SamplingParams, seed));
+#undef MK_SAME_FIELD
 
 namespace {
 
@@ -104,7 +127,7 @@ void ref_model_cfg(void* h, int* out, float* f) {
   f[1] = c.rms_eps;
 }
 
-// Model::forward(const BatchToken*, n, logits) (model.cpp:379-422); 0 = ok, -1 = exception (message in err).
+// Model::forward(const BatchToken*, n, logits) (model.cpp:280-323); 0 = ok, -1 = exception (message in err).
 int ref_model_forward(void* h, int n, const int32_t* id, const int32_t* seq, const int32_t* pos, const int32_t* logits,
                       const int32_t* kv, const int32_t* parent, float* out, char* err, int errlen) {
   try {
@@ -146,7 +169,7 @@ int ref_dequantize_row(int type, const void* src, float* dst, int64_t k) {
 
 float ref_fp16_to_fp32(uint16_t h) { return fp16_to_fp32(h); }
 
-// y[t * rows + r] = W[r] . x[t] through malkin's matmul (quant.cpp:412): mode 0 = row path (vec_dot),
+// y[t * rows + r] = W[r] . x[t] through malkin's matmul (quant.cpp:330-351): mode 0 = row path (vec_dot),
 // 1 = compact panels (pack_weight), 2 = compact + wide panels (wide used when n > kWideMinTokens).
 int ref_matmul(int type, const uint8_t* w, int64_t rows, int64_t cols, int mode, const float* x, int n, float* y) {
   try {
@@ -181,7 +204,7 @@ void ref_silu_mul(int64_t n, float* g, const float* u) { kern::silu_mul(n, g, u)
 
 // ---- sampler.h ----
 
-// The uniform stream Sampler draws from (sampler.h:39, sampler.cpp:110 / 126): n values of
+// The uniform stream Sampler draws from (sampler.h:39, sampler.cpp:66 / 82): n values of
 // std::uniform_real_distribution<double>(0, 1) over std::mt19937_64(seed).
 void ref_uniforms(uint64_t seed, int n, double* out) {
   std::mt19937_64 rng(seed);

@@ -125,7 +125,7 @@ def test_sampled_accept_identical_decisions(mk, oracle, model_paths, torch_cuda)
 
 
 def test_batch_validation_errors(mk, model_paths, torch_cuda):
-    """Model::forward's checks (model.cpp:379-404): errors, not crashes; the context stays usable."""
+    """Model::forward's checks (model.cpp:280-305): errors, not crashes; the context stays usable."""
     m = load(mk, model_paths["q8"], n_ctx=16, n_seq=1)
     cases = [
         [mk.BatchToken(1, 1, 0, True)],                 # bad sequence

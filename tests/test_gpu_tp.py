@@ -1,6 +1,9 @@
-"""Tensor parallel on 2 GPUs (skipped with fewer): one process per GPU over NCCL, q / k / v / gate / up column-split,
-wo / down row-split with an allreduce, vocabulary-split LM head with gathered candidates. Logits and greedy accepts
-must match the single-GPU path (2e-2 max-abs logits; identical accepted paths where the top-1 margin exceeds 1e-2)."""
+"""Tensor parallel on 2 / 4 / 8 GPUs (skipped with fewer): one process per GPU over NCCL, q / k / v / gate / up
+column-split, wo / down row-split with a rank sum (peer-memory one-shot or two-shot exchange, or NCCL allreduce),
+vocabulary-split LM head with gathered candidates. Logits and greedy accepts must match the single-GPU path (2e-2
+max-abs logits; identical accepted paths where the top-1 margin exceeds 1e-2). On one GPU: the exchange kernels
+against host-emulated peers, including a peer that never arrives (the bounded wait must reach the caller as
+MK_ERR_TIMEOUT and leave the next calls correct)."""
 import numpy as np
 import pytest
 
@@ -40,8 +43,10 @@ def _run(mk, path, device, rank, world, nccl_id, seed):
     return pl, tl, acc
 
 
-def _child(rank, world, nccl_id, path, seed, q):
+def _child(rank, world, nccl_id, path, seed, q, mode):
+    import os
     import sys
+    os.environ["MALKIN_B200_TP_REDUCE"] = mode
     sys.path[:0] = ["tests", "tests/golden"]
     import malkin_b200 as mk
     try:
@@ -50,28 +55,30 @@ def _child(rank, world, nccl_id, path, seed, q):
         q.put((rank, None, repr(e)))
 
 
-def test_tp2_matches_single_gpu(mk, model_paths, torch_cuda):
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("mode", ["oneshot", "twoshot", "nccl"])
+def test_tp_matches_single_gpu(mk, model_paths, torch_cuda, world, mode):
     torch = torch_cuda
-    if torch.cuda.device_count() < 2:
-        pytest.skip("tensor parallel needs 2 GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"tensor parallel over {world} ranks needs {world} GPUs")
     import torch.multiprocessing as mp
     path, seed = model_paths["q8"], 7
     ref_pl, ref_tl, ref_acc = _run(mk, path, 0, 0, 1, None, seed)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     nccl_id = mk.nccl_unique_id()
-    procs = [ctx.Process(target=_child, args=(r, 2, nccl_id, path, seed, q)) for r in range(2)]
+    procs = [ctx.Process(target=_child, args=(r, world, nccl_id, path, seed, q, mode)) for r in range(world)]
     for p in procs:
         p.start()
     out = {}
-    for _ in range(2):
+    for _ in range(world):
         rank, res, err = q.get(timeout=300)
         assert err is None, err
         out[rank] = res
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    for rank in range(2):  # every rank returns the full logits and the same accepts
+    for rank in range(world):  # every rank returns the full logits and the same accepts
         pl, tl, acc = out[rank]
         assert np.abs(pl - ref_pl).max() < TOL
         assert np.abs(tl - ref_tl).max() < TOL
@@ -80,3 +87,21 @@ def test_tp2_matches_single_gpu(mk, model_paths, torch_cuda):
             root = j * 7
             if np.all(s[root:root + 7, -1] - s[root:root + 7, -2] > 1e-2):
                 assert a == b
+
+
+@pytest.mark.parametrize("twoshot", [False, True])
+@pytest.mark.parametrize("size", [2, 8])
+def test_tp_exchange_timeout_then_correct(mk, torch_cuda, twoshot, size):
+    """Rank 0's exchange kernels on one GPU against host-emulated peers: call 1 complete, call 2 with peer 1 absent
+    (its flag is never set: the bounded wait gives up and the call reports MK_ERR_TIMEOUT), calls 3 and 4 complete
+    again and must give the exact rank-order sums, which shows the arrival counters and epochs were left consistent."""
+    rng = np.random.default_rng(size + 10 * twoshot)
+    calls, n, cols = 4, 17, 4096
+    parts = rng.standard_normal((calls, size, n, cols)).astype(np.float32)
+    out, st = mk.tp_exchange_check(parts, twoshot=twoshot, absent=[-1, 1, -1, -1], wait_polls=1 << 14)
+    assert list(st) == [mk.MK_OK, mk.MK_ERR_TIMEOUT, mk.MK_OK, mk.MK_OK]
+    for k in (0, 2, 3):
+        want = parts[k, 0].copy()
+        for r in range(1, size):
+            want = (want + parts[k, r]).astype(np.float32)
+        assert np.array_equal(out[k], want), k
