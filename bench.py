@@ -72,11 +72,16 @@ def spec_of(cfg: dict) -> dict:
     return dict(head_dim=128, n_vocab=151936, n_ctx_train=40960, rope_base=1e6, sigma=0.02, seed=0, **m)
 
 
-def ensure_model(name: str) -> str:
-    """Writes the synthetic GGUF once per box (rank 0); other ranks wait on the marker file."""
-    import malkin_b200 as mk
+def ensure_model(name: str, child: bool = False) -> str:
+    """Writes the synthetic GGUF once per box (rank 0); other ranks wait on the marker file. child=True writes it from
+    a separate process (`bench.py --write-model NAME`), so the calling process never maps this repository's library
+    (the reference arm measures malkin alone)."""
     path = model_path(name)
     if not os.path.exists(path + ".done"):
+        if child:
+            subprocess.run([sys.executable, os.path.abspath(__file__), "--write-model", name], check=True)
+            return path
+        import malkin_b200 as mk
         tmp = path + f".tmp{os.getpid()}"
         mk.synth_gguf(tmp, **spec_of(CONFIGS[name]))
         os.replace(tmp, path)
@@ -146,7 +151,7 @@ def clocks_start():
         return None, None
 
 
-def clocks_stop(handle, device: int):
+def clocks_stop(handle, devices):
     p, out = handle
     if p is None:
         return None
@@ -155,9 +160,10 @@ def clocks_stop(handle, device: int):
     out.close()
     sm, mx, reasons = [], 0.0, set()
     names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    want = {str(d) for d in devices}
     for line in open(out.name):
         f = [x.strip() for x in line.split(",")]
-        if len(f) < 9 or f[0] != str(device):
+        if len(f) < 9 or f[0] not in want:
             continue
         try:
             sm.append(float(f[1]))
@@ -170,7 +176,8 @@ def clocks_stop(handle, device: int):
     os.unlink(out.name)
     if not sm:
         return None
-    return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+    return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm),
+            "gpus": sorted(int(d) for d in want)}
 
 
 def peaks():
@@ -192,22 +199,30 @@ def profiled_traffic(name: str):
     return None
 
 
-def cpu_baseline_sample(path: str, cfg: dict, accepted_per_step: int, steps: int = 1):
-    """malkin's own CPU path (oracle/_ref) on the same weights and tree shape, all physical cores; KV prefix rows
-    exist but are not prefilled (attention reads the same number of keys)."""
+def reference_model(path: str, cfg: dict):
+    """malkin's CPU path (oracle/_ref) with the configuration's weights loaded and KV for its requests, all physical
+    cores; (ref, model, load seconds) or (None, reason, 0)."""
     from oracle import Ref, RefModel
     why = Ref.available()
     if why:
-        return None, why
+        return None, why, 0.0
     r = Ref()
+    r.set_threads(r.physical_cores())
+    t0 = time.perf_counter()
+    m = RefModel(r, path, cfg["prompt"] + 2 * cfg["kk"] + 8, cfg["requests"])
+    return r, m, time.perf_counter() - t0
+
+
+def cpu_baseline_sample(path: str, cfg: dict, accepted_per_step: int, steps: int = 1, loaded=None):
+    """malkin's own CPU path (oracle/_ref) on the same weights and tree shape, all physical cores. The KV prefix rows
+    exist but are not prefilled: malkin's cache is LazyBytes (gguf.cpp:281-296), anonymous pages never written, so its
+    attention reads zero pages rather than DRAM-resident keys and the time is optimistic for the CPU."""
+    r, m, load_s = loaded if loaded else reference_model(path, cfg)
+    if r is None:
+        return None, m
     cores = r.physical_cores()
-    r.set_threads(cores)
     R, P, kk = cfg["requests"], cfg["prompt"], cfg["kk"]
     V = spec_of(cfg)["n_vocab"]
-    n_ctx = P + 2 * kk + 8
-    t0 = time.perf_counter()
-    m = RefModel(r, path, n_ctx, R)
-    load_s = time.perf_counter() - t0
     _, chains, alts, _ = draft_plan(cfg, V)
     rng = np.random.default_rng(3)
     reqs = [(s, P, int(rng.integers(0, V)), chains[s], alts[s]) for s in range(R)]
@@ -231,8 +246,9 @@ def cpu_baseline_sample(path: str, cfg: dict, accepted_per_step: int, steps: int
     t = min(times)
     return dict(value=accepted_per_step / t, unit="tok/s", cores=cores, kind="reference",
                 sample=f"{steps} verify step(s) of the {R}x{2 * kk + 1}-row tree batch (ms/step {t * 1e3:.1f}, "
-                       f"model load {load_s:.1f} s), prefix KV not prefilled, accepted/step from the seeded draft "
-                       f"rule"), None
+                       f"model load {load_s:.1f} s); prefix KV rows not prefilled: malkin's lazily allocated cache "
+                       f"pages are never written, so its attention reads zero pages (optimistic for the CPU); "
+                       f"accepted/step from the seeded draft rule"), None
 
 
 def run_reference(args, cfg):
@@ -242,7 +258,7 @@ def run_reference(args, cfg):
         return
     V = spec_of(cfg)["n_vocab"]
     _, _, _, A = draft_plan(cfg, V)
-    path = ensure_model(args.config)
+    path = ensure_model(args.config, child=True)
     base, why = cpu_baseline_sample(path, cfg, A, steps=max(1, min(args.steps, 2)))
     line = {"impl": "reference", "metric": METRIC, "unit": "tok/s", "higher_is_better": True,
             "n_gpus": args.gpus, "steps": max(1, min(args.steps, 2)), "warmup": 0, "dtype": "int8 x int8 -> fp32",
@@ -332,6 +348,67 @@ def probe_attention(reps: int) -> None:
     print(json.dumps({"probe": "attention", "n": n, "heads": H, "kv_heads": KV, "keys": P + 1}))
 
 
+PARITY_PREFIX = {"0.6b": 512, "4b": 256, "8b": 128, "14b": 64, "32b": 64, "8b-l2": 128, "tiny": 64}
+
+
+def parity_leg(mk, m, cfg, loaded, rank, world, max_batch):
+    """Parity of this run's model against malkin's CPU path on a short-prefix case of the configuration's batch
+    (oracle/parity.py): every rank runs the device side (collective under tensor parallelism), rank 0 the reference
+    side. Returns the comparison (rank 0) or None."""
+    from oracle.parity import compare, device_leg, reference_leg
+    name = next(k for k, v in CONFIGS.items() if v is cfg)
+    R, kk, P = cfg["requests"], cfg["kk"], PARITY_PREFIX.get(name, 64)
+    try:
+        d = device_leg(mk, m, R, P, kk, seed=11, max_batch=max_batch, sampled=True)
+    except Exception as e:
+        return {"ok": False, "error": f"device side: {e}"}
+    if rank != 0:
+        return None
+    r, rm, _ = loaded if loaded else (None, "reference leg skipped", 0.0)
+    if r is None:
+        return {"ok": None, "unavailable": str(rm)}
+    try:
+        c = compare(d, reference_leg(r, rm, d))
+    except Exception as e:
+        return {"ok": False, "error": f"reference side: {e}"}
+    c["case"] = (f"{R} req x {P}-token prefix (the timed run's {cfg['prompt']}), {2 * kk + 1}-row trees greedy + "
+                 f"{kk + 1}-row chains sampled at temperature 0.8, tp{world}")
+    return c
+
+
+def sampled_variant(mk, m, cfg, nexts, P, timed, steps):
+    """Times the configuration's sampled mode (temperature 0.8 rejection accept over chain-only rows) on the same
+    state: drafts drawn from Dirichlet(1) weights over the target's top-8 at each chain node, seeded uniforms; every
+    step consumes the same uniforms, so every step does identical work."""
+    from oracle.parity import SAMPLING, chain_rows
+    R, kk = cfg["requests"], cfg["kk"]
+    rng = np.random.default_rng(4)
+    dchain = np.zeros((R, kk), dtype=np.int64)
+    qs = [[] for _ in range(R)]
+    for d in range(kk):
+        rows, roots = chain_rows([(s, P, nexts[s], dchain[s]) for s in range(R)], kk)
+        lg = m.forward([mk.BatchToken(*r) for r in rows])
+        for s in range(R):
+            top = np.argsort(-lg[roots[s] + d], kind="stable")[:8]
+            w = rng.dirichlet(np.ones(8)).astype(np.float32)
+            qs[s].append([(float(p), int(t)) for p, t in zip(w, top)])
+            cdf = np.cumsum(w.astype(np.float64))
+            dchain[s, d] = int(top[min(7, int(np.searchsorted(cdf, rng.random() * cdf[-1], side="right")))])
+    rows, roots = chain_rows([(s, P, nexts[s], dchain[s]) for s in range(R)], kk)
+    batch = mk.make_batch(mk.BatchToken(*r) for r in rows)
+    samp = mk.Sampling(**SAMPLING)
+    props = [mk.Proposal(seq=s, root=roots[s], cache_len=P, chain=dchain[s], sampling=samp, q=qs[s],
+                         uniforms=mk.rng_uniforms(77 + s, 2 * kk + 4)) for s in range(R)]
+    for _ in range(3):
+        m.verify_step(batch, props)
+    res, ms, launches = timed(batch, props)
+    A = sum(r.n_accepted + 1 for r in res)
+    ms_step = ms / steps
+    return {"value": A / (ms_step / 1e3), "unit": "tok/s", "ms_per_step": ms_step, "accepted_per_step": A,
+            "rows_per_step": len(rows), "gpu_launches": launches,
+            "mode": "temperature 0.8 rejection accept, top_p 0.95, top_k 40, min_p 0.05, chain-only rows"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -345,7 +422,12 @@ def main():
     ap.add_argument("--probe-layouts", default="auto", help="gemm probe: auto,tc,panels")
     ap.add_argument("--probe-n", type=int, default=136)
     ap.add_argument("--probe-reps", type=int, default=3)
+    ap.add_argument("--no-parity", action="store_true", help="skip the parity leg against malkin's CPU path")
+    ap.add_argument("--write-model", metavar="CONFIG", help="write the configuration's synthetic GGUF and exit")
     args = ap.parse_args()
+    if args.write_model:
+        print(ensure_model(args.write_model))
+        return
     if args.probe == "gemm":
         return probe_gemm(args.probe_shapes.split(","), args.probe_layouts.split(","), args.probe_n, args.probe_reps)
     if args.probe == "attention":
@@ -425,31 +507,40 @@ def main():
     for _ in range(args.warmup):
         m.verify_step(batch, props)
     stream = torch.cuda.ExternalStream(m.stream)
-    # timed: device events on the library's stream, K steps, max over ranks
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
+
+    def timed(b, ps):
+        """K steps on the library's stream between device events, after a barrier; max over ranks."""
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        n_launch = 0
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            out = m.verify_step(b, ps)
+            n_launch += m.last_launch_count() + 3  # forward graph kernels + candidates, accept, move_kv
+        e1.record(stream)
+        e1.synchronize()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        t_ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([t_ms], dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            t_ms = float(t.item())
+        return out, t_ms, n_launch
+
+    # the clock sampler starts before the first barrier (its start-up must not delay one rank's first step)
     clk = clocks_start() if rank == 0 else (None, None)
-    launches = 0
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record(stream)
-    for _ in range(args.steps):
-        res = m.verify_step(batch, props)
-        launches += m.last_launch_count() + 3  # forward graph kernels + candidates, accept, move_kv
-    ev1.record(stream)
-    ev1.synchronize()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    clocks = clocks_stop(clk, local) if rank == 0 else None
-    ms = ev0.elapsed_time(ev1)
-    if world > 1:
-        t = torch.tensor([ms], dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    res, ms, launches = timed(batch, props)
+    clocks = clocks_stop(clk, list(range(world))) if rank == 0 else None
     A_step = sum(r.n_accepted + 1 for r in res)
     ms_step = ms / args.steps
     value = A_step / (ms_step / 1e3)
+    # sampled mode of the same configuration (temperature 0.8 rejection accept): chain-only rows, kk + 1 per request
+    # (engine.cpp:366-378); drafts drawn from Dirichlet(1) weights over the target's top-8 at each chain node
+    sampled = sampled_variant(mk, m, cfg, nexts, P, timed, args.steps)
     # e2e: the same steps through the public API from host inputs, host wall clock (inputs rebuilt every step)
     m.io_bytes()
     if world > 1:
@@ -502,13 +593,27 @@ def main():
                           "frac": (step_bytes / (pk["hbm_gbs"] * 1e9)) / (ms_step / 1e3)},
         "clocks": clocks, "load_s": load_s, "prefill_s": prefill_s,
     }
+    if sampled:
+        line["sampled"] = sampled
+    # Reference leg (after every timed region): malkin's CPU path on rank 0 times the CPU baseline (N = 1) and
+    # checks parity on a short-prefix case of the same model and batch shape (every N; all ranks run the device side).
+    loaded = None
+    if rank == 0 and not (args.no_cpu_baseline and args.no_parity):
+        try:
+            loaded = reference_model(path, cfg)
+        except Exception as e:  # the reference leg is reported, never fatal
+            loaded = (None, str(e), 0.0)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            base, why = cpu_baseline_sample(path, cfg, A_step)
-        except Exception as e:  # the baseline is reported, never fatal
+            base, why = cpu_baseline_sample(path, cfg, A_step, loaded=loaded)
+        except Exception as e:
             base, why = None, str(e)
         line["cpu_baseline"] = base if base else {"value": None, "unit": "tok/s", "kind": "reference",
                                                   "sample": f"unavailable: {why}"}
+    if not args.no_parity:
+        line["parity"] = parity_leg(mk, m, cfg, loaded if rank == 0 else None, rank, world, max_batch)
+        if world > 1:
+            dist.barrier()  # the other ranks wait for rank 0's reference side before the communicator goes away
     if rank == 0:
         print(json.dumps(line), flush=True)
     m.close()
