@@ -88,11 +88,16 @@ __global__ void k_qkv_post(Slices qk, int v_n, int64_t v_col0, int64_t ldy, int 
 
 // ---------------- partial attention over a key chunk (tensor cores) ----------------
 // One CTA = (sub-group, KV head, key chunk). Query vectors (sub-group rows x G heads, at most kQMax) are split into
-// m16 tiles, one per warp. Per tile of 64 keys: S = Q K^T with mma.sync m16n8k16 (fp16 in, fp32 accumulate) where Q
-// is split into fp16 hi + lo parts (q = hi + lo to ~22 bits) and int8 K converts to fp16 exactly; then the online
-// softmax in registers (a row lives in one quad of lanes); then O += P V with P' = p * v_scale * 2^12 split into fp16
-// hi + lo (the power-of-two scale keeps P' in fp16's normal range; it is divided out exactly at the end) and int8 V
-// in fp16. K / V int8 tiles for the next 64 keys are prefetched into registers while the current tile computes.
+// m16 tiles, one per warp. Per tile of 64 keys: S = Q K^T with mma.sync m16n8k16 (fp16 in, fp32 accumulate), int8 K
+// converted to fp16 exactly; then the online softmax in registers (a row lives in one quad of lanes); then
+// O += P' V with P' = p * v_scale * 2^12 in fp16 (the power-of-two scale keeps P' in fp16's normal range; it is
+// divided out exactly at the end) and int8 V in fp16. Q and P' are fp16 (11 significant bits): their rounding
+// (relative 2^-12) stays well below the int8 quantization of K, V and of the attention output that feeds the next
+// GEMM. kSplit = true keeps the earlier two-term form (fp16 hi + lo for Q and P', ~22 bits, twice the MMAs) for
+// error measurements (MALKIN_B200_ATTN_SPLIT=1).
+// K / V int8 tiles stream global -> registers one tile ahead and are converted into one of two shared-memory buffers,
+// so each 64-key tile costs one CTA barrier: the warps that pass the barrier of tile i have all finished tile i - 1,
+// whose buffer the next conversion reuses only after the barrier of tile i + 1.
 constexpr int kQMax = 96;   // query vectors per sub-group (6 warps x 16)
 constexpr int kKT = 64;     // keys per tile
 constexpr int kAttWarps = kQMax / 16;
@@ -151,28 +156,25 @@ __device__ __forceinline__ void mma_f16(float (&d)[4], const uint32_t (&a)[4], u
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-template <int D>
+template <int D, bool kSplit>
 struct AttSmem {
   static constexpr int DP = D + 8;  // padded fp16 row (conflict-free ldmatrix)
-  static constexpr size_t QH = 0, QL = QH + sizeof(__half) * kQMax * DP, K = QL + sizeof(__half) * kQMax * DP,
-                          V = K + sizeof(__half) * kKT * DP, KS = V + sizeof(__half) * kKT * DP, VS = KS + 4 * kKT,
-                          NK = VS + 4 * kKT, BYTES = NK + 4 * kQMax;
+  static constexpr size_t QTERM = sizeof(__half) * kQMax * DP, KVTILE = sizeof(__half) * kKT * DP;
+  static constexpr size_t QH = 0, QL = QH + QTERM, K = QL + (kSplit ? QTERM : 0), V = K + 2 * KVTILE,
+                          KS = V + 2 * KVTILE, VS = KS + 2 * 4 * kKT, NK = VS + 2 * 4 * kKT, BYTES = NK + 4 * kQMax;
 };
 
-template <int D>
-__global__ void __launch_bounds__(kThreads, 2) k_attn_part(PartArgs a) {  // two CTAs per SM
-  using SM = AttSmem<D>;
+template <int D, bool kSplit>
+__global__ void __launch_bounds__(kThreads, kSplit ? 1 : 2) k_attn_part(PartArgs a) {
+  using SM = AttSmem<D, kSplit>;
   constexpr int DP = SM::DP;
   constexpr int NDT = D / 8;          // d tiles (n8) of O
   constexpr int CH = D / 16;          // 16-byte int8 chunks per key row
   constexpr int PF = (2 * kKT * CH + kThreads - 1) / kThreads;  // prefetch chunks per thread (K and V)
+  constexpr int TP = kSplit ? 2 : 1;  // fp16 terms of Q and P'
   extern __shared__ __align__(128) uint8_t sm[];
   __half* Qh = reinterpret_cast<__half*>(sm + SM::QH);
   __half* Ql = reinterpret_cast<__half*>(sm + SM::QL);
-  __half* Kh = reinterpret_cast<__half*>(sm + SM::K);
-  __half* Vh = reinterpret_cast<__half*>(sm + SM::V);
-  float* ksc = reinterpret_cast<float*>(sm + SM::KS);
-  float* vsc = reinterpret_cast<float*>(sm + SM::VS);
   int* Nk = reinterpret_cast<int*>(sm + SM::NK);
 
   const int chunk = blockIdx.x, sg = blockIdx.y, kvh = blockIdx.z;
@@ -185,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_attn_part(PartArgs a) {  // two
   const int k1 = min(maxk, k0 + a.p.chunk);
   const int base = a.p.kv_base[t0];
 
-  // Q (hi / lo fp16), zero rows past nq: warp w loads its 16 query vectors, lanes over d (independent loads first)
+  // Q in fp16 (hi / lo when split), zero rows past nq: warp w loads its 16 query vectors, lanes over d
   {
     constexpr int PL = D / 32;  // values per lane
     float qv[16][PL];
@@ -202,10 +204,14 @@ __global__ void __launch_bounds__(kThreads, 2) k_attn_part(PartArgs a) {  // two
       const int qi = warp * 16 + i;
 #pragma unroll
       for (int m = 0; m < PL; ++m) {
-        __half hi, lo;
-        split_h(qv[i][m], hi, lo);
-        Qh[qi * DP + lane + 32 * m] = hi;
-        Ql[qi * DP + lane + 32 * m] = lo;
+        if constexpr (kSplit) {
+          __half hi, lo;
+          split_h(qv[i][m], hi, lo);
+          Qh[qi * DP + lane + 32 * m] = hi;
+          Ql[qi * DP + lane + 32 * m] = lo;
+        } else {
+          Qh[qi * DP + lane + 32 * m] = __float2half_rn(qv[i][m]);
+        }
       }
     }
   }
@@ -238,7 +244,10 @@ __global__ void __launch_bounds__(kThreads, 2) k_attn_part(PartArgs a) {  // two
       pvs = tid < nk ? __fmul_rn(vsh[kt + tid], kPScale) : 0.0f;
     }
   };
-  auto commit = [&]() {
+  // registers -> shared buffer b (fp16 K / V rows, scales)
+  auto commit = [&](int b) {
+    __half* Kb = reinterpret_cast<__half*>(sm + SM::K + b * SM::KVTILE);
+    __half* Vb = reinterpret_cast<__half*>(sm + SM::V + b * SM::KVTILE);
 #pragma unroll
     for (int u = 0; u < PF; ++u) {
       const int i = tid + u * kThreads;
@@ -246,7 +255,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_attn_part(PartArgs a) {  // two
         const bool isv = i >= kKT * CH;
         const int ii = isv ? i - kKT * CH : i;
         const int j = ii / CH, ch = ii % CH;
-        __half* dst = (isv ? Vh : Kh) + j * DP + ch * 16;
+        __half* dst = (isv ? Vb : Kb) + j * DP + ch * 16;
         uint4 h0, h1;
         i8x4_to_h2(static_cast<uint32_t>(pre[u].x), h0.x, h0.y);
         i8x4_to_h2(static_cast<uint32_t>(pre[u].y), h0.z, h0.w);
@@ -257,8 +266,8 @@ __global__ void __launch_bounds__(kThreads, 2) k_attn_part(PartArgs a) {  // two
       }
     }
     if (tid < kKT) {
-      ksc[tid] = pks;
-      vsc[tid] = pvs;
+      reinterpret_cast<float*>(sm + SM::KS)[b * kKT + tid] = pks;
+      reinterpret_cast<float*>(sm + SM::VS)[b * kKT + tid] = pvs;
     }
   };
 
@@ -272,121 +281,126 @@ __global__ void __launch_bounds__(kThreads, 2) k_attn_part(PartArgs a) {  // two
   __syncthreads();
   const int nkA = Nk[min(r0 + g, kQMax - 1)], nkB = Nk[min(r0 + g + 8, kQMax - 1)];
 
-  for (int kt = k0; kt < k1; kt += kKT) {
-    commit();
+  int buf = 0;
+  for (int kt = k0; kt < k1; kt += kKT, buf ^= 1) {
+    commit(buf);
     __syncthreads();
     if (kt + kKT < k1) fetch(kt + kKT);
-    if (active) {
-      // S = Q K^T for this warp's 16 query vectors x 64 keys
-      float sacc[kKT / 8][4];
+    if (!active) continue;
+    const __half* Kh = reinterpret_cast<const __half*>(sm + SM::K + buf * SM::KVTILE);
+    const __half* Vh = reinterpret_cast<const __half*>(sm + SM::V + buf * SM::KVTILE);
+    const float* ksc = reinterpret_cast<const float*>(sm + SM::KS) + buf * kKT;
+    const float* vsc = reinterpret_cast<const float*>(sm + SM::VS) + buf * kKT;
+    // S = Q K^T for this warp's 16 query vectors x 64 keys
+    float sacc[kKT / 8][4];
 #pragma unroll
-      for (int j = 0; j < kKT / 8; ++j) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.0f;
+    for (int j = 0; j < kKT / 8; ++j) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.0f;
 #pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        uint32_t ah[4], al[4];
-        const int qr = r0 + (lane & 15), qc = kk * 16 + (lane >> 4) * 8;
-        ldsm_x4(ah, Qh + qr * DP + qc);
-        ldsm_x4(al, Ql + qr * DP + qc);
-        uint32_t b[kKT / 16][4];
+    for (int kk = 0; kk < D / 16; ++kk) {
+      uint32_t aq[TP][4];
+      const int qr = r0 + (lane & 15), qc = kk * 16 + (lane >> 4) * 8;
+      ldsm_x4(aq[0], Qh + qr * DP + qc);
+      if constexpr (kSplit) ldsm_x4(aq[TP - 1], Ql + qr * DP + qc);
+      uint32_t b[kKT / 16][4];
 #pragma unroll
-        for (int nj = 0; nj < kKT / 16; ++nj) {  // two n8 tiles per ldmatrix.x4
-          const int kr = nj * 16 + (lane >> 4) * 8 + (lane & 7), kc = kk * 16 + ((lane >> 3) & 1) * 8;
-          ldsm_x4(b[nj], Kh + kr * DP + kc);
-        }
-        // the hi pass over every n tile, then the lo pass: dependent MMAs on one accumulator are 8 apart
+      for (int nj = 0; nj < kKT / 16; ++nj) {  // two n8 tiles per ldmatrix.x4
+        const int kr = nj * 16 + (lane >> 4) * 8 + (lane & 7), kc = kk * 16 + ((lane >> 3) & 1) * 8;
+        ldsm_x4(b[nj], Kh + kr * DP + kc);
+      }
+      // one pass per term over every n tile: dependent MMAs on one accumulator are 8 apart
+#pragma unroll
+      for (int tp = 0; tp < TP; ++tp)
 #pragma unroll
         for (int nj = 0; nj < kKT / 16; ++nj) {
-          mma_f16(sacc[2 * nj], ah, b[nj][0], b[nj][1]);
-          mma_f16(sacc[2 * nj + 1], ah, b[nj][2], b[nj][3]);
+          mma_f16(sacc[2 * nj], aq[tp], b[nj][0], b[nj][1]);
+          mma_f16(sacc[2 * nj + 1], aq[tp], b[nj][2], b[nj][3]);
         }
+    }
+    // scale, mask, online softmax
+    float tmA = -INFINITY, tmB = -INFINITY;
 #pragma unroll
-        for (int nj = 0; nj < kKT / 16; ++nj) {
-          mma_f16(sacc[2 * nj], al, b[nj][0], b[nj][1]);
-          mma_f16(sacc[2 * nj + 1], al, b[nj][2], b[nj][3]);
-        }
+    for (int j = 0; j < kKT / 8; ++j) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int col = 8 * j + 2 * c + e, key = kt + col;
+        const float ks = ksc[col];
+        const bool okA = key < k1 && key < nkA, okB = key < k1 && key < nkB;
+        sacc[j][e] = okA ? __fmul_rn(sacc[j][e], ks) : -INFINITY;
+        sacc[j][2 + e] = okB ? __fmul_rn(sacc[j][2 + e], ks) : -INFINITY;
+        tmA = fmaxf(tmA, sacc[j][e]);
+        tmB = fmaxf(tmB, sacc[j][2 + e]);
       }
-      // scale, mask, online softmax
-      float tmA = -INFINITY, tmB = -INFINITY;
+    }
+    tmA = fmaxf(tmA, __shfl_xor_sync(0xffffffffu, tmA, 1));
+    tmA = fmaxf(tmA, __shfl_xor_sync(0xffffffffu, tmA, 2));
+    tmB = fmaxf(tmB, __shfl_xor_sync(0xffffffffu, tmB, 1));
+    tmB = fmaxf(tmB, __shfl_xor_sync(0xffffffffu, tmB, 2));
+    const float nmA = fmaxf(mA, tmA), nmB = fmaxf(mB, tmB);
+    const float alA = (mA == -INFINITY || nmA == -INFINITY) ? (nmA == -INFINITY ? 1.0f : 0.0f)
+                                                            : exp_fast(__fsub_rn(mA, nmA));
+    const float alB = (mB == -INFINITY || nmB == -INFINITY) ? (nmB == -INFINITY ? 1.0f : 0.0f)
+                                                            : exp_fast(__fsub_rn(mB, nmB));
+    mA = nmA;
+    mB = nmB;
+    float sA = 0.0f, sB = 0.0f;
+    uint32_t pp[TP][kKT / 16][4];
 #pragma unroll
-      for (int j = 0; j < kKT / 8; ++j) {
+    for (int j = 0; j < kKT / 8; ++j) {
+      float pv[4];
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int col = 8 * j + 2 * c + e, key = kt + col;
-          const float ks = ksc[col];
-          const bool okA = key < k1 && key < nkA, okB = key < k1 && key < nkB;
-          sacc[j][e] = okA ? __fmul_rn(sacc[j][e], ks) : -INFINITY;
-          sacc[j][2 + e] = okB ? __fmul_rn(sacc[j][2 + e], ks) : -INFINITY;
-          tmA = fmaxf(tmA, sacc[j][e]);
-          tmB = fmaxf(tmB, sacc[j][2 + e]);
-        }
+      for (int e = 0; e < 4; ++e) {
+        const bool rowA = e < 2;
+        const float x = sacc[j][e], m = rowA ? mA : mB;
+        const float p = x == -INFINITY ? 0.0f : exp_fast(__fsub_rn(x, m));
+        if (rowA)
+          sA += p;
+        else
+          sB += p;
+        pv[e] = __fmul_rn(p, vsc[8 * j + 2 * c + (e & 1)]);
       }
-      tmA = fmaxf(tmA, __shfl_xor_sync(0xffffffffu, tmA, 1));
-      tmA = fmaxf(tmA, __shfl_xor_sync(0xffffffffu, tmA, 2));
-      tmB = fmaxf(tmB, __shfl_xor_sync(0xffffffffu, tmB, 1));
-      tmB = fmaxf(tmB, __shfl_xor_sync(0xffffffffu, tmB, 2));
-      const float nmA = fmaxf(mA, tmA), nmB = fmaxf(mB, tmB);
-      const float alA = (mA == -INFINITY || nmA == -INFINITY) ? (nmA == -INFINITY ? 1.0f : 0.0f)
-                                                              : exp_fast(__fsub_rn(mA, nmA));
-      const float alB = (mB == -INFINITY || nmB == -INFINITY) ? (nmB == -INFINITY ? 1.0f : 0.0f)
-                                                              : exp_fast(__fsub_rn(mB, nmB));
-      mA = nmA;
-      mB = nmB;
-      float sA = 0.0f, sB = 0.0f;
-      uint32_t ph[kKT / 16][4], pl[kKT / 16][4];
-#pragma unroll
-      for (int j = 0; j < kKT / 8; ++j) {
-        float pv[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const bool rowA = e < 2;
-          const float x = sacc[j][e], m = rowA ? mA : mB;
-          const float p = x == -INFINITY ? 0.0f : exp_fast(__fsub_rn(x, m));
-          if (rowA)
-            sA += p;
-          else
-            sB += p;
-          pv[e] = __fmul_rn(p, vsc[8 * j + 2 * c + (e & 1)]);
-        }
+      // C layout of n-tile j -> A fragment of k16 step j / 2 (regs 0/1 from the even tile, 2/3 from the odd)
+      const int kq = j >> 1, hi = (j & 1) * 2;
+      if constexpr (kSplit) {
         __half h0, l0, h1, l1, h2, l2, h3, l3;
         split_h(pv[0], h0, l0);
         split_h(pv[1], h1, l1);
         split_h(pv[2], h2, l2);
         split_h(pv[3], h3, l3);
-        // C layout of n-tile j -> A fragment of k16 step j / 2 (regs 0/1 from the even tile, 2/3 from the odd)
-        const int kq = j >> 1, hi = (j & 1) * 2;
-        ph[kq][hi] = pack_h2(h0, h1);
-        ph[kq][hi + 1] = pack_h2(h2, h3);
-        pl[kq][hi] = pack_h2(l0, l1);
-        pl[kq][hi + 1] = pack_h2(l2, l3);
+        pp[0][kq][hi] = pack_h2(h0, h1);
+        pp[0][kq][hi + 1] = pack_h2(h2, h3);
+        pp[TP - 1][kq][hi] = pack_h2(l0, l1);
+        pp[TP - 1][kq][hi + 1] = pack_h2(l2, l3);
+      } else {
+        const __half2 p01 = __floats2half2_rn(pv[0], pv[1]), p23 = __floats2half2_rn(pv[2], pv[3]);
+        pp[0][kq][hi] = *reinterpret_cast<const uint32_t*>(&p01);
+        pp[0][kq][hi + 1] = *reinterpret_cast<const uint32_t*>(&p23);
       }
-      sA += __shfl_xor_sync(0xffffffffu, sA, 1);
-      sA += __shfl_xor_sync(0xffffffffu, sA, 2);
-      sB += __shfl_xor_sync(0xffffffffu, sB, 1);
-      sB += __shfl_xor_sync(0xffffffffu, sB, 2);
-      lA = __fmaf_rn(lA, alA, sA);
-      lB = __fmaf_rn(lB, alB, sB);
+    }
+    sA += __shfl_xor_sync(0xffffffffu, sA, 1);
+    sA += __shfl_xor_sync(0xffffffffu, sA, 2);
+    sB += __shfl_xor_sync(0xffffffffu, sB, 1);
+    sB += __shfl_xor_sync(0xffffffffu, sB, 2);
+    lA = __fmaf_rn(lA, alA, sA);
+    lB = __fmaf_rn(lB, alB, sB);
 #pragma unroll
-      for (int j = 0; j < NDT; ++j) {
-        o[j][0] *= alA, o[j][1] *= alA, o[j][2] *= alB, o[j][3] *= alB;
-      }
-      // O += P' V
+    for (int j = 0; j < NDT; ++j) {
+      o[j][0] *= alA, o[j][1] *= alA, o[j][2] *= alB, o[j][3] *= alB;
+    }
+    // O += P' V: one pass per term over every d tile (V fragments loaded again for the second term)
 #pragma unroll
-      for (int kq = 0; kq < kKT / 16; ++kq) {
-        // hi pass over every d tile, then the lo pass (V fragments loaded again): dependent MMAs 16 apart
+    for (int kq = 0; kq < kKT / 16; ++kq) {
 #pragma unroll
-        for (int pass = 0; pass < 2; ++pass) {
+      for (int tp = 0; tp < TP; ++tp) {
 #pragma unroll
-          for (int dj = 0; dj < NDT / 2; ++dj) {  // two d tiles per ldmatrix.x4.trans
-            uint32_t b[4];
-            const int vr = kq * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, vc = dj * 16 + (lane >> 4) * 8;
-            ldsm_x4_t(b, Vh + vr * DP + vc);
-            mma_f16(o[2 * dj], pass ? pl[kq] : ph[kq], b[0], b[1]);
-            mma_f16(o[2 * dj + 1], pass ? pl[kq] : ph[kq], b[2], b[3]);
-          }
+        for (int dj = 0; dj < NDT / 2; ++dj) {  // two d tiles per ldmatrix.x4.trans
+          uint32_t b[4];
+          const int vr = kq * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, vc = dj * 16 + (lane >> 4) * 8;
+          ldsm_x4_t(b, Vh + vr * DP + vc);
+          mma_f16(o[2 * dj], pp[tp][kq], b[0], b[1]);
+          mma_f16(o[2 * dj + 1], pp[tp][kq], b[2], b[3]);
         }
       }
     }
-    __syncthreads();
   }
   // Partials: [((sg * n_chunks + chunk) * KV + kvh) * kQMax + qi][D + 2] = o[D], m, l.
   if (active) {
@@ -880,23 +894,29 @@ bool attn_use_tc() {
   return e && std::string(e) == "tc";
 }
 
-template <int D>
-size_t part_smem() {
-  return AttSmem<D>::BYTES;
+// MALKIN_B200_ATTN_SPLIT=1: two-term fp16 Q and P' (error measurements); default one term.
+bool attn_split() {
+  static const bool on = [] {
+    const char* e = std::getenv("MALKIN_B200_ATTN_SPLIT");
+    return e && std::string(e) == "1";
+  }();
+  return on;
 }
 
 template <int D>
 void run_attention(const float* q, int H, int KV, float scale, const AttnLayer& L, const AttnPlan& p, float* out,
                    const ActQ& act, cudaStream_t s) {
   PartArgs a{q, H, KV, H / KV, scale, L, p};
-  const size_t smem = part_smem<D>();
-  static bool attr[64] = {};
+  const bool split = attn_split();
+  const size_t smem = split ? AttSmem<D, true>::BYTES : AttSmem<D, false>::BYTES;
+  auto part_fn = split ? k_attn_part<D, true> : k_attn_part<D, false>;
+  static bool attr[64][2] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && !attr[dev]) {
-    cudaFuncSetAttribute(k_attn_part<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    cudaFuncSetAttribute(k_attn_part<D>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    attr[dev] = true;
+  if (dev < 64 && !attr[dev][split]) {
+    cudaFuncSetAttribute(part_fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    cudaFuncSetAttribute(part_fn, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    attr[dev][split] = true;
   }
   if (p.n_sg > 0 && p.n_chunks > 0) {
     const dim3 g1(p.n_chunks, p.n_sg, KV);
@@ -910,10 +930,10 @@ void run_attention(const float* q, int H, int KV, float scale, const AttnLayer& 
         }
         k_attn_part_tc<<<g1, tc_attn::kThreads, tc_attn::BYTES, s>>>(a);
       } else {
-        k_attn_part<D><<<g1, kThreads, smem, s>>>(a);
+        part_fn<<<g1, kThreads, smem, s>>>(a);
       }
     } else {
-      k_attn_part<D><<<g1, kThreads, smem, s>>>(a);
+      part_fn<<<g1, kThreads, smem, s>>>(a);
     }
   }
   const dim3 g2(act.qx ? act.nt8 * 8 : p.n, (H + 3) / 4);

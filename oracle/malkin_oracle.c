@@ -6,8 +6,11 @@
  * Pinned by tests/test_oracle.py against oracle/_ref (malkin's own sources compiled unchanged) and against the
  * committed golden fixtures under tests/golden/ (made by tests/golden/make_golden.py from oracle/_ref):
  *   bit-exact:  quantize_row_q8 / BlockQ8, quantize_i8, dequantize_row, integer block dots, matmul through the
- *               compact panel kernels (same float operations in the same block order);
- *   tolerance:  attention, the full forward's logits, accept decisions on identical logits.
+ *               compact panel kernels, attention, and the full forward's logits: every float operation of malkin's
+ *               path is restated in malkin's order, including the 16-lane AVX-512 partial sums and their horizontal
+ *               reduction (reduce16) and the fused multiply-adds g++ forms from model.cpp / quant.cpp scalar code
+ *               (FMA contraction is on for C++ at -O2 -march=x86-64-v4), so logits are bit-identical;
+ *   decisions:  accept walks and sampler decisions on identical logits.
  * Built with -ffp-contract=off so every a*b+c below is two roundings unless written as fmaf.
  */
 #include <math.h>
@@ -163,8 +166,9 @@ int orc_dequantize_row(int type, const uint8_t* b, float* y, int64_t k) {
           int s0, m0, s1, m1;
           scale_min_k4(2 * j, b + 4, &s0, &m0);
           scale_min_k4(2 * j + 1, b + 4, &s1, &m1);
-          for (int l = 0; l < 32; ++l) *y++ = d * (float)s0 * (float)(q[l] & 0xF) - dmin * (float)m0;
-          for (int l = 0; l < 32; ++l) *y++ = d * (float)s1 * (float)(q[l] >> 4) - dmin * (float)m1;
+          /* d * s * q - dmin * m as g++ contracts it: fma(q, d * s, -(dmin * m)) */
+          for (int l = 0; l < 32; ++l) *y++ = fmaf((float)(q[l] & 0xF), d * (float)s0, -(dmin * (float)m0));
+          for (int l = 0; l < 32; ++l) *y++ = fmaf((float)(q[l] >> 4), d * (float)s1, -(dmin * (float)m1));
         }
       }
       return 0;
@@ -287,11 +291,30 @@ void orc_matmul(int type, const uint8_t* w, int64_t rows, int64_t cols, const fl
 
 /* ---------------- small ops ---------------- */
 
-/* rmsnorm (model.cpp:46-49) */
+/* The 16-lane horizontal sum of an AVX-512 register (_mm512_reduce_add_ps): lanes i and i + 8 first, then i and
+ * i + 4, then i and i + 2, then lanes 0 and 1 (IEEE addition is commutative, so operand order does not matter). */
+static float reduce16(const float* a) {
+  float b[8], c[4];
+  for (int i = 0; i < 8; ++i) b[i] = a[i + 8] + a[i];
+  for (int i = 0; i < 4; ++i) c[i] = b[i + 4] + b[i];
+  return (c[0] + c[2]) + (c[1] + c[3]);
+}
+
+/* kern::dot_f32 (kernels_avx512.cpp:82-89): 16 lanes, lane l accumulating elements l, l + 16, ... by fma in order,
+ * then reduce16; a scalar tail for n % 16. */
+static float dot_f32_16(const float* w, const float* x, int n) {
+  float acc[16] = {0};
+  int i = 0;
+  for (; i + 16 <= n; i += 16)
+    for (int l = 0; l < 16; ++l) acc[l] = fmaf(w[i + l], x[i + l], acc[l]);
+  float s = reduce16(acc);
+  for (; i < n; ++i) s += w[i] * x[i];
+  return s;
+}
+
+/* rmsnorm (model.cpp:46-49): s = 1 / sqrt(dot_f32(x, x) / n + eps), y = x * s * w */
 static void rmsnorm(float* y, const float* x, const float* w, int n, float eps) {
-  float ss = 0.0f;
-  for (int i = 0; i < n; ++i) ss = fmaf(x[i], x[i], ss);
-  const float s = 1.0f / sqrtf(ss / (float)n + eps);
+  const float s = 1.0f / sqrtf(dot_f32_16(x, x, n) / (float)n + eps);
   for (int i = 0; i < n; ++i) y[i] = x[i] * s * w[i];
 }
 
@@ -311,17 +334,21 @@ void orc_attend(const float* q, int G, int D, const int8_t* k, const int8_t* v, 
     for (int j = 0; j < nk; ++j) {
       const int64_t row = j < n ? j : extra[j - n];
       const int8_t* kr = k + row * stride;
-      float acc = 0.0f;
-      for (int d = 0; d < D; ++d) acc = fmaf(q[h * D + d], (float)kr[d], acc);
-      s[j] = acc * (ks[row] * scale);
+      /* attend_t's score: 16 lanes over d, the first product a multiply, then fma in d order; reduce16 */
+      float acc[16];
+      for (int l = 0; l < 16; ++l) acc[l] = q[h * D + l] * (float)kr[l];
+      for (int d0 = 16; d0 < D; d0 += 16)
+        for (int l = 0; l < 16; ++l) acc[l] = fmaf(q[h * D + d0 + l], (float)kr[d0 + l], acc[l]);
+      s[j] = reduce16(acc) * (ks[row] * scale);
       if (s[j] > mx) mx = s[j];
     }
-    float sum = 0.0f;
+    /* softmax_inplace (kernels_avx512.cpp:205-226): e = exp(s - max); sums in 16 lanes (key j in lane j % 16) */
+    float sum16[16] = {0};
     for (int j = 0; j < nk; ++j) {
       s[j] = exp_malkin(s[j] - mx);
-      sum += s[j];
+      sum16[j % 16] += s[j];
     }
-    const float inv = 1.0f / sum;
+    const float inv = 1.0f / reduce16(sum16);
     for (int d = 0; d < D; ++d) out[h * D + d] = 0.0f;
     for (int j = 0; j < nk; ++j) {
       const int64_t row = j < n ? j : extra[j - n];
@@ -625,10 +652,12 @@ int orc_model_forward(orc_model* m, int n, const int32_t* id, const int32_t* seq
       for (int hh = 0; hh < H + KV; ++hh) {
         float* vv = hh < H ? q + ((size_t)t * H + hh) * D : k + ((size_t)t * KV + (hh - H)) * D;
         rmsnorm(vv, vv, (const float*)(hh < H ? L[2] : L[3])->data, D, m->rms_eps);
+        /* RoPE as g++ -O2 -march=x86-64-v4 compiles model.cpp's rope (FMA contraction is on for C++):
+         * x0 * cos - x1 * sin -> fma(x0, cos, -(x1 * sin)); x0 * sin + x1 * cos -> fma(x0, sin, x1 * cos) */
         for (int i = 0; i < D / 2; ++i) {
           const float x0 = vv[i], x1 = vv[i + D / 2];
-          vv[i] = x0 * c0[i] - x1 * c0[D / 2 + i];
-          vv[i + D / 2] = x0 * c0[D / 2 + i] + x1 * c0[i];
+          vv[i] = fmaf(x0, c0[i], -(x1 * c0[D / 2 + i]));
+          vv[i + D / 2] = fmaf(x0, c0[D / 2 + i], x1 * c0[i]);
         }
       }
       for (int hh = 0; hh < KV; ++hh) {
