@@ -234,8 +234,8 @@ int mk_matmul(const mk_weight* w, const float* dev_x, int n, float* dev_y, int s
  * (a __device__ variable, one per device), so the call makes no cudaMalloc / cudaFree and never waits on the whole
  * device the way cudaFree does. For callers that must not allocate per call: engines that reserve all HBM for the
  * KV cache at start-up, and latency-bound loops that must not stall other streams. Same arguments and results as
- * mk_matmul. Limits: about 76 bytes per token per 32 values of activations must fit (108 with the optional fp16
- * Q8_0 GEMM; for example 256 tokens x 16384 values); split_k = 0 lowers the split until the partial sums fit, an
+ * mk_matmul. Limits: about 76 bytes per token per 32 values of activations must fit (for example 256 tokens x
+ * 16384 values); split_k = 0 lowers the split until the partial sums fit, an
  * explicit split_k whose partial sums do not fit is rejected with MK_ERR_ARG. Calls on one device share the scratch:
  * calls that overlap in time (other streams, other threads) race, so serialise them. Each call synchronizes `stream`
  * before it returns (it reads the kernels' status word back). The first call on each device looks up the scratch

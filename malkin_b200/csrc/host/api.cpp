@@ -79,24 +79,20 @@ int current_device() {
   return d;
 }
 
-// Temporary quantized-activation buffers for the kernel-level entry points: int8 qx | the tensor-core copy the Q8_0
-// mode reads (int8 qc for kQ8Exact / kQ8Split and block-dot requests, fp16 xh for kQ8Fp16) | dx | dsx | sh.
+// Temporary quantized-activation buffers for the kernel-level entry points: int8 qx | the same int8 values in the
+// tensor-core order (qc) | dx | dsx | sh.
 struct TmpAct {
   mkb::DevBuf buf;
   mkb::ActQ act;
-  TmpAct(int n, int64_t K, int mode) {
+  TmpAct(int n, int64_t K) {
     const int nt8 = mkb::act_tiles(n), npad = nt8 * 8;
     const int64_t blocks = K / 32;
     const size_t qx = static_cast<size_t>(blocks) * npad * 32, f = static_cast<size_t>(blocks) * npad * 4;
-    const size_t tc = qx / 32 * mkb::q8_act_bytes(mode);
+    const size_t tc = qx;
     buf = mkb::DevBuf(qx + tc + 3 * f + 256);
     auto* p = buf.get<uint8_t>();
     act.qx = p;
-    act.q8 = mode;
-    if (mode == mkb::kQ8Fp16)
-      act.xh = reinterpret_cast<uint16_t*>(p + qx);  // 2 bytes per value
-    else
-      act.qc = p + qx;
+    act.qc = p + qx;
     act.dx = reinterpret_cast<float*>(p + qx + tc);
     act.dsx = act.dx + blocks * npad;
     act.sh = reinterpret_cast<uint32_t*>(act.dsx + blocks * npad);
@@ -310,7 +306,7 @@ int mk_matmul(const mk_weight* w, const float* dev_x, int n, float* dev_y, int s
     cudaStream_t s = as_stream(stream);
     mkb::DevBuf status(sizeof(int));
     mkb::cuda_check(cudaMemsetAsync(status.get(), 0, sizeof(int), s), "memset");
-    TmpAct t(n, w->w.cols, mkb::q8_mode());
+    TmpAct t(n, w->w.cols);
     mkb::launch_quant_rows(dev_x, w->w.cols, n, static_cast<int>(w->w.cols), t.act, s);
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
@@ -340,18 +336,16 @@ int mk_matmul_noalloc(const mk_weight* w, const float* dev_x, int n, float* dev_
     mkb::cuda_check(e, "matmul_noalloc: scratch address");
     const size_t cap = mkb::noalloc_scratch_bytes();
     auto up = [](size_t b) { return (b + 255) / 256 * 256; };
-    // [status | qx | tensor-core copy (qc or xh) | dx | dsx | sh | split-K slices]
-    const int mode = mkb::q8_mode();
+    // [status | qx | tensor-core copy qc | dx | dsx | sh | split-K slices]
     const int nt8 = mkb::act_tiles(n), npad = nt8 * 8;
     const int64_t blocks = w->w.cols / 32;
     const size_t qx = up(static_cast<size_t>(blocks) * npad * 32), f = up(static_cast<size_t>(blocks) * npad * 4);
-    const size_t tc = qx / 32 * mkb::q8_act_bytes(mode);
+    const size_t tc = qx;
     const size_t act_end = 256 + qx + tc + 3 * f;
     if (act_end > cap)
       throw mkb::ArgError("matmul_noalloc: " + std::to_string(n) + " tokens x " + std::to_string(w->w.cols) +
                           " values need " + std::to_string(act_end) + " bytes of activations; the fixed scratch holds " +
-                          std::to_string(cap) + " (about " + std::to_string(44 + mkb::q8_act_bytes(mode)) +
-                          " bytes per token per 32 values)");
+                          std::to_string(cap) + " (about 76 bytes per token per 32 values)");
     const int64_t slice = static_cast<int64_t>(n) * w->w.rows;
     const size_t room = cap - act_end;
     auto fits = [&](int split) { return split <= 1 || static_cast<size_t>(split) * slice * 4 <= room; };
@@ -371,11 +365,7 @@ int mk_matmul_noalloc(const mk_weight* w, const float* dev_x, int n, float* dev_
     int* status = reinterpret_cast<int*>(base);
     mkb::ActQ act;
     act.qx = base + 256;
-    act.q8 = mode;
-    if (mode == mkb::kQ8Fp16)
-      act.xh = reinterpret_cast<uint16_t*>(act.qx + qx);  // 2 bytes per value
-    else
-      act.qc = act.qx + qx;
+    act.qc = act.qx + qx;
     act.dx = reinterpret_cast<float*>(act.qx + qx + tc);
     act.dsx = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(act.dx) + f);
     act.sh = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(act.dsx) + f);
@@ -401,7 +391,7 @@ int mk_block_dots(const mk_weight* w, const float* dev_x, int n, int32_t* dev_ou
     cudaStream_t s = as_stream(stream);
     mkb::DevBuf status(sizeof(int));
     mkb::cuda_check(cudaMemsetAsync(status.get(), 0, sizeof(int), s), "memset");
-    TmpAct t(n, w->w.cols, mkb::kQ8Exact);
+    TmpAct t(n, w->w.cols);
     mkb::launch_quant_rows(dev_x, w->w.cols, n, static_cast<int>(w->w.cols), t.act, s);
     mkb::launch_block_dots(w->w, t.act, n, dev_out, status.get<int>(), s);
     mkb::cuda_check(cudaGetLastError(), "block_dots");
@@ -433,16 +423,18 @@ int mk_attention(const float* dev_q, int n, int H, int KV, int D, const int8_t* 
                  const int32_t* dev_n_keys, const int32_t* dev_anc_off, const int32_t* dev_anc, float* dev_out,
                  void* stream) {
   return guard(MK_ERR_ARG, [&] {
-    if (n <= 0 || H <= 0 || KV <= 0 || H % KV || (D != 64 && D != 128 && D != 256))
-      throw mkb::ArgError("attention: bad shape");
+    if (n <= 0 || H <= 0 || KV <= 0 || H % KV || H / KV > 8 || (D != 64 && D != 128 && D != 256))
+      throw mkb::ArgError("attention: bad shape (H a multiple of KV, at most 8 query heads per KV head, D 64 / 128 / 256)");
     cudaStream_t s = as_stream(stream);
-    std::vector<int32_t> kvb(n), nk(n);
+    std::vector<int32_t> kvb(n), nk(n), ao(n + 1);
     mkb::cuda_check(cudaMemcpy(kvb.data(), dev_kv_base, n * 4, cudaMemcpyDeviceToHost), "attention");
     mkb::cuda_check(cudaMemcpy(nk.data(), dev_n_keys, n * 4, cudaMemcpyDeviceToHost), "attention");
+    mkb::cuda_check(cudaMemcpy(ao.data(), dev_anc_off, (n + 1) * 4, cudaMemcpyDeviceToHost), "attention");
     const int G = H / KV, rows = std::max(1, mkb::attn_qmax() / G);
     std::vector<int32_t> sgf, tsg(n), sgm;
-    int maxk = 1;
+    int maxk = 1, maxlist = 1;
     for (int t = 0; t < n; ++t) {
+      maxlist = std::max(maxlist, nk[t] + ao[t + 1] - ao[t]);
       if (t == 0 || kvb[t] != kvb[t - 1] || t - sgf.back() >= rows) {
         sgf.push_back(t);
         sgm.push_back(0);
@@ -456,11 +448,7 @@ int mk_attention(const float* dev_q, int n, int H, int KV, int D, const int8_t* 
     mkb::AttnPlan p;
     p.n = n;
     p.n_sg = n_sg;
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    p.chunk = mkb::attn_chunk_for(maxk, n_sg, KV, sms);
-    p.n_chunks = (maxk + p.chunk - 1) / p.chunk;
+    p.kchunks = mkb::attn_key_chunks(maxk);
     mkb::DevBuf tabs((sgf.size() + tsg.size() + sgm.size()) * 4);
     mkb::cuda_check(cudaMemcpy(tabs.get(), sgf.data(), sgf.size() * 4, cudaMemcpyHostToDevice), "attention");
     mkb::cuda_check(cudaMemcpy(tabs.get<int32_t>() + sgf.size(), tsg.data(), tsg.size() * 4, cudaMemcpyHostToDevice),
@@ -468,7 +456,8 @@ int mk_attention(const float* dev_q, int n, int H, int KV, int D, const int8_t* 
     mkb::cuda_check(cudaMemcpy(tabs.get<int32_t>() + sgf.size() + tsg.size(), sgm.data(), sgm.size() * 4,
                                cudaMemcpyHostToDevice),
                     "attention");
-    mkb::DevBuf part(mkb::attn_part_floats(n_sg, p.n_chunks, KV, D) * 4);
+    const int64_t sstride = (maxlist + 3) / 4 * 4;
+    mkb::DevBuf ws(mkb::attn_ws_floats(n, H, sstride, D) * 4);
     p.sg_first = tabs.get<int32_t>();
     p.tok_sg = tabs.get<int32_t>() + sgf.size();
     p.sg_maxk = tabs.get<int32_t>() + sgf.size() + tsg.size();
@@ -476,7 +465,10 @@ int mk_attention(const float* dev_q, int n, int H, int KV, int D, const int8_t* 
     p.n_keys = dev_n_keys;
     p.anc_off = dev_anc_off;
     p.anc = dev_anc;
-    p.part = part.get<float>();
+    p.sbuf = ws.get<float>();
+    p.sstride = sstride;
+    p.inv = p.sbuf + static_cast<size_t>(n) * H * sstride;
+    p.att = p.inv + static_cast<size_t>(n) * H;
     mkb::AttnLayer L{const_cast<int8_t*>(dev_k), const_cast<int8_t*>(dev_v), const_cast<float*>(dev_ks),
                      const_cast<float*>(dev_vs), n_rows};
     mkb::launch_attention(dev_q, H, KV, D, 1.0f / std::sqrt(static_cast<float>(D)), L, p, dev_out, mkb::ActQ{}, s);

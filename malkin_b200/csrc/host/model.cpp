@@ -101,6 +101,9 @@ ModelCfg read_config(const GgufReader& f) {
   c.rope_base = static_cast<float>(f.meta_real("qwen3.rope.freq_base").value_or(10000.0));
   c.rms_eps = static_cast<float>(f.meta_real("qwen3.attention.layer_norm_rms_epsilon").value_or(1e-6));
   if (c.head_dim % 32 || c.n_head % c.n_head_kv) throw ArgError("model: unsupported head layout");
+  if (c.n_head / c.n_head_kv > 8)
+    throw UnsupportedError("unsupported: more than 8 query heads per KV head (" + std::to_string(c.n_head) + " / " +
+                           std::to_string(c.n_head_kv) + ")");
   if (c.head_dim != 64 && c.head_dim != 128 && c.head_dim != 256)
     throw UnsupportedError("unsupported: head_dim " + std::to_string(c.head_dim) + " (64, 128, 256)");
   const TensorView* out = f.find("output.weight");
@@ -392,7 +395,7 @@ void Model::alloc_kv(int n_ctx, int n_seq, int max_batch) {
                o_gu = take(static_cast<size_t>(s_gu) * gu_slice_ * 4), o_p = take(static_cast<size_t>(NB) * E * 4),
                o_part = take(static_cast<size_t>(s_part) * part_slice_ * 4),
                o_lg = take(static_cast<size_t>(NB) * Vl_ * 4), o_qx = take(static_cast<size_t>(blocks) * NB * 32),
-               o_qc = take(static_cast<size_t>(blocks) * NB * q8_act_bytes(q8_mode())),
+               o_qc = take(static_cast<size_t>(blocks) * NB * 32),
                o_dx = take(static_cast<size_t>(blocks) * NB * 4), o_dsx = take(static_cast<size_t>(blocks) * NB * 4),
                o_sh = take(static_cast<size_t>(blocks) * NB * 4),
                o_cv = take(static_cast<size_t>(NB) * MK_TOPK_CAP * 4), o_ci = take(static_cast<size_t>(NB) * MK_TOPK_CAP * 4),
@@ -410,12 +413,8 @@ void Model::alloc_kv(int n_ctx, int n_seq, int max_batch) {
   part_ = reinterpret_cast<float*>(sb + o_part);
   logits_ = reinterpret_cast<float*>(sb + o_lg);
   act_.qx = sb + o_qx;
-  // the Q8_0 tensor-core GEMMs read the int8 copy (exact and split modes) or the fp16 copy of the activations
-  act_.q8 = q8_mode();
-  if (act_.q8 == kQ8Fp16)
-    act_.xh = reinterpret_cast<uint16_t*>(sb + o_qc);
-  else
-    act_.qc = sb + o_qc;
+  // the Q8_0 tensor-core GEMM reads the int8 copy in the UMMA core-matrix order
+  act_.qc = sb + o_qc;
   act_.dx = reinterpret_cast<float*>(sb + o_dx);
   act_.dsx = reinterpret_cast<float*>(sb + o_dsx);
   act_.sh = reinterpret_cast<uint32_t*>(sb + o_sh);
@@ -428,8 +427,9 @@ void Model::alloc_kv(int n_ctx, int n_seq, int max_batch) {
   // attention plan geometry
   const int G = c.n_head / c.n_head_kv;
   sg_rows_ = std::max(1, attn_qmax() / G);
-  part_cap_ = 0;
-  attn_part_ = DevBuf();
+  // attention workspace: a score row per (token, head) long enough for any key list (prefix + extra rows)
+  attn_sstride_ = static_cast<int64_t>(n_ctx) + max_batch;
+  attn_ws_ = DevBuf(attn_ws_floats(max_batch, Hl_, attn_sstride_, D) * sizeof(float));
   meta_cap_ = 0;
   ensure_meta(static_cast<size_t>(max_batch) * 16);
 }
@@ -690,17 +690,6 @@ void Model::forward(const mk_batch_token* batch, int n, float* host_logits) {
   sgfirst.push_back(n);
   const int m = static_cast<int>(outrows.size());
   ensure_meta(anc.size());
-  // key chunks of the split attention: a function of n_sg (part of the graph key), about two CTAs per SM
-  const int chunk = attn_chunk_for(n_ctx_, n_sg, KVl_, num_sms_);
-  const int n_chunks = (n_ctx_ + chunk - 1) / chunk;
-  const size_t part_need = attn_part_floats(n_sg, n_chunks, KVl_, c.head_dim);
-  if (part_need > part_cap_) {
-    for (auto& [k, g] : graphs_) cudaGraphExecDestroy(g);
-    graphs_.clear();
-    graph_nodes_.clear();
-    part_cap_ = std::max(part_need, part_cap_ * 2);
-    attn_part_ = DevBuf(part_cap_ * 4);
-  }
   // pinned staging -> one copy
   const size_t MB = static_cast<size_t>(max_batch_);
   int32_t* h = meta_host_;
@@ -720,8 +709,7 @@ void Model::forward(const mk_batch_token* batch, int n, float* host_logits) {
   h2d_bytes_ += static_cast<int64_t>((10 * MB + 2 + anc.size()) * 4);
   plan_.n = n;
   plan_.n_sg = n_sg;
-  plan_.chunk = chunk;
-  plan_.n_chunks = n_chunks;
+  plan_.kchunks = attn_key_chunks(n_ctx_);
   plan_.sg_first = d_sgfirst_;
   plan_.kv_base = d_kvbase_;
   plan_.n_keys = d_nkeys_;
@@ -729,7 +717,14 @@ void Model::forward(const mk_batch_token* batch, int n, float* host_logits) {
   plan_.anc = d_anc_;
   plan_.tok_sg = d_toksg_;
   plan_.sg_maxk = d_sgmaxk_;
-  plan_.part = attn_part_.get<float>();
+  {
+    float* ws = attn_ws_.get<float>();
+    const size_t sb = static_cast<size_t>(max_batch_) * Hl_ * static_cast<size_t>(attn_sstride_);
+    plan_.sbuf = ws;
+    plan_.sstride = attn_sstride_;
+    plan_.inv = ws + sb;
+    plan_.att = ws + sb + static_cast<size_t>(max_batch_) * Hl_;
+  }
   plan_.status = status_;
 
   if (profile_) {
@@ -814,9 +809,6 @@ void Model::forward(const mk_batch_token* batch, int n, float* host_logits) {
 }
 
 void throw_device_status(int code, const std::string& what) {
-  if (code == kErrFp16Range)
-    throw UnsupportedError(what + ": an activation exceeds the fp16 range (65504) of the split-fp16 Q8_0 GEMM; "
-                           "MALKIN_B200_Q8_GEMM=exact computes it in f32");
   throw TimeoutError(what + ": device pipeline wait gave up (code " + std::to_string(code) + ")");
 }
 

@@ -188,10 +188,11 @@ class Model {
   size_t meta_cap_ = 0;  // int32 entries
   int32_t *d_ids_ = nullptr, *d_rpos_ = nullptr, *d_kvat_ = nullptr, *d_kvbase_ = nullptr, *d_nkeys_ = nullptr,
           *d_ancoff_ = nullptr, *d_sgfirst_ = nullptr, *d_toksg_ = nullptr, *d_outrows_ = nullptr, *d_sgmaxk_ = nullptr, *d_anc_ = nullptr;
-  DevBuf attn_part_;
+  DevBuf attn_ws_;             // attention scores / probabilities, inverses, output (attn_ws_floats)
+  int64_t attn_sstride_ = 0;
   AttnPlan plan_;
   int sg_rows_ = 0;
-  size_t part_cap_ = 0;  // floats of attn_part_
+
 
   // last forward: logits row of each batch index (-1: none), tokens
   std::vector<int> lrow_;

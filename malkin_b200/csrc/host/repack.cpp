@@ -176,8 +176,6 @@ int weight_layout(uint32_t type, int64_t rows, int64_t cols) {
   const char* e = std::getenv("MALKIN_B200_Q8_LAYOUT");
   if (e && std::string(e) == "panels") return kLayoutPanels;
   if (e && std::string(e) == "tc") return kLayoutTc;
-  // the split-fp16 kernel (tensor-core layout) is the fastest for every Q8_0 shape
-  if (q8_mode() == kQ8Split) return kLayoutTc;
   // Measured on B200 at 136 tokens (8B shapes): the tcgen05 kernel wins on q|k|v and the attention output
   // (<= 8192 rows, K <= 8192), the mma.sync panel kernel on the wide ffn gate / up, the deep ffn down and the
   // vocabulary head. Both give identical results.

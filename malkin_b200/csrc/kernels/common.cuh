@@ -109,6 +109,31 @@ __device__ __forceinline__ int warp_isum(int v) {
   return v;
 }
 
+// The horizontal sum of malkin's 16-lane AVX-512 accumulators (_mm512_reduce_add_ps), over the 16 consecutive lanes
+// that hold them (lane l of each half-warp holds accumulator l): lanes l and l ^ 8 first, then l ^ 4, l ^ 2, l ^ 1 -
+// the same additions in the same pairing (IEEE addition is commutative), so every lane of the half-warp ends with the
+// bit-identical sum.
+__device__ __forceinline__ float reduce16(float v) {
+  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 8));
+  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
+  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
+  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
+  return v;
+}
+
+// kern::dot_f32(n, x, x) (kernels_avx512.cpp:82-89) of a row in shared memory, the way malkin's RMSNorm computes it
+// (model.cpp:46-49): 16 accumulators, accumulator l summing x[l + 16 k]^2 by fma in k order from zero, then reduce16.
+// Called by one whole warp (lanes 0..15 run the chains); every lane returns the sum. n % 16 == 0.
+__device__ __forceinline__ float dot16_self(const float* x, int n, int lane) {
+  float acc = 0.0f;
+  if (lane < 16) {
+#pragma unroll 8
+    for (int i = lane; i < n; i += 16) acc = __fmaf_rn(x[i], x[i], acc);
+  }
+  acc = reduce16(acc);
+  return __shfl_sync(0xffffffffu, acc, 0);
+}
+
 // Sum of n <= 16 values p[0], p[stride], ... in index order. All loads are issued before the first add, so the
 // latency of the n loads overlaps (a plain runtime-bounded loop would wait for each in turn).
 __device__ __forceinline__ float sum_strided16(const float* p, int n, int64_t stride) {

@@ -1,11 +1,13 @@
 // Quantized weight-streaming GEMM: y[t][r] = sum over blocks of float(int8 block dot) * (weight scale * act scale),
 // the arithmetic of malkin's panel kernels k_q8_0 / k_q45_k / k_q6_k (gemm_avx512.cpp:67-205), on B200.
 //
-// Pipeline: a CTA owns a tile of 16 panels (256 weight rows) and one k-range (split-K slice). Warp 0 streams the
-// tile's weight chunks and the matching activation blocks (Q8 fragments, scales) from HBM / L2 into a 2-3 stage
-// shared-memory ring with TMA bulk copies (cp.async.bulk, completion counted on mbarriers) and refills a stage as
-// soon as all eight warps have released it; every warp takes 2 panels x all tokens of the pass. Every weight byte
-// is read from HBM once and every activation byte once per CTA.
+// Pipeline: a CTA owns a tile of 2 WP panels (32 WP weight rows), one token pass of WT x NTW tiles of 8 tokens
+// (WT = 8 / WP) and one k-range (split-K slice). Warp 0 streams the tile's weight chunks and the matching activation
+// blocks (Q8 fragments, scales) from HBM / L2 into a 2-3 stage shared-memory ring with TMA bulk copies
+// (cp.async.bulk, completion counted on mbarriers) and refills a stage as soon as all eight warps have released it;
+// warp w takes panels 2 (w % WP), +1 x token tiles (w / WP) NTW .. + NTW - 1. Token passes (grid.z) and narrow
+// tiles (WP < 8) give the SMs work without splitting K, so every (row, token) sums its blocks in malkin's order;
+// the passes of one tile read its weights from L2 after the first.
 //
 // Arithmetic per 32-value block (16-value half for Q6_K) and 16 x 8 tile: one int8 mma.sync gives the exact
 // integer dots; its accumulator init carries the float-conversion bias (kMagicBits) so the dot becomes a float with
@@ -18,6 +20,8 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
+#include <cstdio>
 #include <cstdlib>
 #include <string>
 #include <array>
@@ -31,7 +35,7 @@ namespace mkb {
 
 namespace {
 
-constexpr int kTilePanels = 16;
+constexpr int kTilePanels = 16;                      // panels of the widest tile (WP = 8)
 constexpr int kConsumers = 8;                        // warps, 2 panels each; warp 0 also issues the TMA copies
 constexpr int kThreadsG = kConsumers * 32;           // 2 warps per SM sub-partition: up to 255 registers
 constexpr int kMaxNT = 18;                           // 144 tokens per pass
@@ -72,11 +76,11 @@ struct GemmArgs {
   int* status;
 };
 
-// Shared-memory layout of one stage.
-template <uint32_t T, int NT>
+// Shared-memory layout of one stage (NT token tiles, TP panels).
+template <uint32_t T, int NT, int TP = kTilePanels>
 struct Stage {
   using C = TypeCfg<T>;
-  static constexpr uint32_t A = kTilePanels * C::KS * C::UNIT;
+  static constexpr uint32_t A = TP * C::KS * C::UNIT;
   static constexpr uint32_t B = C::KS * C::BPU * NT * 256;
   static constexpr uint32_t DX = C::KS * C::BPU * NT * 8 * 4;
   static constexpr uint32_t EX = (C::kDsx || C::kSh) ? DX : 0;
@@ -96,18 +100,21 @@ __device__ __forceinline__ void q4k_scale_min(int j, uint32_t w1, uint32_t w2, u
   }
 }
 
-template <uint32_t T, int NT>
+// NTW token tiles per warp, WP panel pairs per CTA (WT = 8 / WP warps along the tokens).
+template <uint32_t T, int NTW, int WP>
 __global__ void __launch_bounds__(kThreadsG, 1) k_gemm(GemmArgs a) {
   using C = TypeCfg<T>;
-  using S = Stage<T, NT>;
+  constexpr int WT = kConsumers / WP, NT = WT * NTW, TP = 2 * WP;
+  using S = Stage<T, NT, TP>;
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::NS * S::BYTES);
   uint64_t* empty = full + C::NS;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
-  const int64_t p0 = static_cast<int64_t>(blockIdx.x) * kTilePanels;
-  const int tile_panels = static_cast<int>(a.panels - p0 < kTilePanels ? a.panels - p0 : kTilePanels);
+  const int64_t p0 = static_cast<int64_t>(blockIdx.x) * TP;
+  const int tile_panels = static_cast<int>(a.panels - p0 < TP ? a.panels - p0 : TP);
   const int u0 = blockIdx.y * a.per_split, u1 = min(a.kunits, u0 + a.per_split);
-  const int t0 = blockIdx.z * (kMaxNT * 8);  // first token of this pass
+  const int t0 = blockIdx.z * (NT * 8);  // first token of this pass
+  const int jt0 = (warp / WP) * NTW;     // this warp's first token tile within the pass
   const int npad = a.nt8 * 8;
   const int n_it = (u1 - u0 + C::KS - 1) / C::KS;
   if (threadIdx.x == 0) {
@@ -150,15 +157,15 @@ __global__ void __launch_bounds__(kThreadsG, 1) k_gemm(GemmArgs a) {
   if (warp == 0)
     for (int it = 0; it < C::NS && it < n_it; ++it) issue(it);
 
-  // ---------------- consumers: warp owns panels 2w, 2w+1 of the tile ----------------
-  const int pw = 2 * warp;
+  // ---------------- consumers: warp owns panels pw, pw + 1 of the tile x token tiles jt0 .. jt0 + NTW - 1 ----------------
+  const int pw = 2 * (warp % WP);
   const bool has0 = pw < tile_panels, has1 = pw + 1 < tile_panels;
   const f2 magic2 = f2_make(kMagicF, kMagicF);
-  f2 acc[2][NT][2];
+  f2 acc[2][NTW][2];
 #pragma unroll
   for (int q = 0; q < 2; ++q)
 #pragma unroll
-    for (int j = 0; j < NT; ++j) acc[q][j][0] = acc[q][j][1] = f2_make(0.0f, 0.0f);
+    for (int j = 0; j < NTW; ++j) acc[q][j][0] = acc[q][j][1] = f2_make(0.0f, 0.0f);
 
   for (int it = 0; it < n_it; ++it) {
     const int s = it % C::NS, r = it / C::NS;
@@ -168,9 +175,9 @@ __global__ void __launch_bounds__(kThreadsG, 1) k_gemm(GemmArgs a) {
     if (has0) {
       const uint8_t* sa0 = st + pw * (C::KS * C::UNIT);
       const uint8_t* sa1 = sa0 + C::KS * C::UNIT;
-      const uint8_t* sb = st + S::A + lane * 8;
-      const float* sdx = reinterpret_cast<const float*>(st + S::A + S::B) + 2 * c;
-      const float* sex = reinterpret_cast<const float*>(st + S::A + S::B + S::DX) + 2 * c;
+      const uint8_t* sb = st + S::A + jt0 * 256 + lane * 8;
+      const float* sdx = reinterpret_cast<const float*>(st + S::A + S::B) + 8 * jt0 + 2 * c;
+      const float* sex = reinterpret_cast<const float*>(st + S::A + S::B + S::DX) + 8 * jt0 + 2 * c;
       for (int u = 0; u < uk; ++u) {
         const uint8_t* ca[2] = {sa0 + u * C::UNIT, sa1 + u * C::UNIT};
         if constexpr (T == 8) {
@@ -187,7 +194,7 @@ __global__ void __launch_bounds__(kThreadsG, 1) k_gemm(GemmArgs a) {
           const uint8_t* sbb = sb + u * NT * 256;
           const float* dxb = sdx + u * NT * 8;
 #pragma unroll
-          for (int j = 0; j < NT; ++j) {
+          for (int j = 0; j < NTW; ++j) {
             const uint2 b = *reinterpret_cast<const uint2*>(sbb + j * 256);
             const float2 dx = *reinterpret_cast<const float2*>(dxb + 8 * j);
             const f2 DX = f2_make(dx.x, dx.y);
@@ -231,7 +238,7 @@ __global__ void __launch_bounds__(kThreadsG, 1) k_gemm(GemmArgs a) {
             const float* dxb = sdx + bl * NT * 8;
             const float* dsb = sex + bl * NT * 8;
 #pragma unroll
-            for (int j = 0; j < NT; ++j) {
+            for (int j = 0; j < NTW; ++j) {
               const uint2 b = *reinterpret_cast<const uint2*>(sbb + j * 256);
               const float2 dx = *reinterpret_cast<const float2*>(dxb + 8 * j);
               const float2 ds = *reinterpret_cast<const float2*>(dsb + 8 * j);
@@ -285,7 +292,7 @@ __global__ void __launch_bounds__(kThreadsG, 1) k_gemm(GemmArgs a) {
             const float* dxb = sdx + bl * NT * 8;
             const uint32_t* shb = reinterpret_cast<const uint32_t*>(sex) + bl * NT * 8;
 #pragma unroll
-            for (int j = 0; j < NT; ++j) {
+            for (int j = 0; j < NTW; ++j) {
               const uint2 b = *reinterpret_cast<const uint2*>(sbb + j * 256);
               const float2 dx = *reinterpret_cast<const float2*>(dxb + 8 * j);
               const uint2 sv = *reinterpret_cast<const uint2*>(shb + 8 * j);
@@ -325,8 +332,8 @@ __global__ void __launch_bounds__(kThreadsG, 1) k_gemm(GemmArgs a) {
     if (pw + q >= tile_panels) break;
     const int64_t r0 = (p0 + pw + q) * 16 + g, r1 = r0 + 8;
 #pragma unroll
-    for (int j = 0; j < NT; ++j) {
-      const int t = t0 + 8 * j + 2 * c;
+    for (int j = 0; j < NTW; ++j) {
+      const int t = t0 + 8 * (jt0 + j) + 2 * c;
       const float v[4] = {f2_lo(acc[q][j][0]), f2_hi(acc[q][j][0]), f2_lo(acc[q][j][1]), f2_hi(acc[q][j][1])};
       const int tt[4] = {t, t + 1, t, t + 1};
       const int64_t rr[4] = {r0, r0, r1, r1};
@@ -400,55 +407,142 @@ __global__ void k_block_dots(uint32_t type, const uint8_t* __restrict__ w, int64
 
 using GemmFn = void (*)(GemmArgs);
 
-template <uint32_t T, int... N>
-constexpr std::array<GemmFn, sizeof...(N)> table(std::integer_sequence<int, N...>) {
-  return {&k_gemm<T, N + 1>...};
-}
+// Kernel variants: WP = 8 (16-panel tiles) with NTW = 1..18 token tiles per warp; WP = 2 (4 panels, 4 warps along the
+// tokens) with NTW = 1..4; WP = 1 (2 panels, 8 warps along the tokens) with NTW = 1..3.
+struct Variant {
+  GemmFn fn;
+  uint32_t smem;
+  int wp, ntw;
+};
+constexpr int kVariants = kMaxNT + 4 + 3;
 
-template <uint32_t T, int... N>
-constexpr std::array<uint32_t, sizeof...(N)> smem_table(std::integer_sequence<int, N...>) {
-  return {Stage<T, N + 1>::SMEM...};
+template <uint32_t T, int WP, int... N>
+constexpr void fill(Variant* v, std::integer_sequence<int, N...>) {
+  ((v[N] = Variant{&k_gemm<T, N + 1, WP>, Stage<T, (kConsumers / WP) * (N + 1), 2 * WP>::SMEM, WP, N + 1}), ...);
 }
 
 template <uint32_t T>
-void launch_t(const GemmArgs& a, dim3 grid, int nt, cudaStream_t s) {
-  static constexpr auto fns = table<T>(std::make_integer_sequence<int, kMaxNT>{});
-  static constexpr auto sm = smem_table<T>(std::make_integer_sequence<int, kMaxNT>{});
-  // per device: the attribute is a property of the device context
-  static bool attr[64][kMaxNT] = {};
+constexpr std::array<Variant, kVariants> variants() {
+  std::array<Variant, kVariants> v{};
+  fill<T, 8>(v.data(), std::make_integer_sequence<int, kMaxNT>{});
+  fill<T, 2>(v.data() + kMaxNT, std::make_integer_sequence<int, 4>{});
+  fill<T, 1>(v.data() + kMaxNT + 4, std::make_integer_sequence<int, 3>{});
+  return v;
+}
+
+template <uint32_t T>
+const std::array<Variant, kVariants>& variant_table() {
+  static constexpr auto v = variants<T>();
+  return v;
+}
+
+const std::array<Variant, kVariants>& table_of(uint32_t type) {
+  return type == 12 ? variant_table<12>() : (type == 14 ? variant_table<14>() : variant_table<8>());
+}
+
+struct DevInfo {
+  int sms = 148;
+  int occ[3][kVariants] = {};  // resident CTAs per SM of each variant (0 = not yet queried)
+  bool attr[3][kVariants] = {};
+};
+
+DevInfo& dev_info(int dev) {
+  static DevInfo info[kMaxDevices];
+  static bool init[kMaxDevices] = {};
+  DevInfo& d = info[dev < kMaxDevices ? dev : 0];
+  if (!init[dev < kMaxDevices ? dev : 0]) {
+    cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+    init[dev < kMaxDevices ? dev : 0] = true;
+  }
+  return d;
+}
+
+int type_index(uint32_t type) { return type == 12 ? 1 : (type == 14 ? 2 : 0); }
+
+// Prepares variant i on the current device (shared-memory opt-in) and returns its residency.
+int prepare(uint32_t type, int i) {
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && !attr[dev][nt - 1]) {
-    cudaFuncSetAttribute(fns[nt - 1], cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm[nt - 1]));
-    attr[dev][nt - 1] = true;
+  DevInfo& d = dev_info(dev);
+  const int ti = type_index(type);
+  const Variant& v = table_of(type)[i];
+  if (!d.attr[ti][i]) {
+    cudaFuncSetAttribute(v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(v.smem));
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, v.fn, kThreadsG, v.smem) != cudaSuccess) {
+      cudaGetLastError();
+      occ = 1;
+    }
+    d.occ[ti][i] = occ > 0 ? occ : 1;
+    d.attr[ti][i] = true;
   }
-  fns[nt - 1]<<<grid, kThreadsG, sm[nt - 1], s>>>(a);
+  return d.occ[ti][i];
+}
+
+struct Plan {
+  int variant = 0, passes = 1;
+};
+
+// The kernel shape for a weight, n tokens (tiles of 8, at most nt8 readable) and split-K slices. With one slice the
+// SMs are filled by token passes and narrow tiles instead: the estimate is the busiest SM's share of the per-block
+// float work (the bound of these kernels) plus the L2 re-reads the passes and narrow tiles cost.
+Plan plan_for(const DevWeight& w, int n, int nt8, int split) {
+  const int tiles = (n + 7) / 8;
+  const auto& tab = table_of(w.type);
+  Plan best;
+  if (split > 1) {  // K slices fill the SMs: the widest tile, every token in as few passes as possible
+    const int passes = (tiles + kMaxNT - 1) / kMaxNT;
+    best.variant = (passes == 1 ? tiles : kMaxNT) - 1;
+    best.passes = passes;
+    return best;
+  }
+  // MALKIN_B200_GEMM_PLAN=<wp>:<ntw> forces one kernel shape (tests and measurements), when it is valid here
+  if (const char* e = std::getenv("MALKIN_B200_GEMM_PLAN")) {
+    int wp = 0, ntw = 0;
+    if (std::sscanf(e, "%d:%d", &wp, &ntw) == 2)
+      for (int i = 0; i < kVariants; ++i)
+        if (tab[i].wp == wp && tab[i].ntw == ntw) {
+          const int nt = (kConsumers / wp) * ntw, passes = (tiles + nt - 1) / nt;
+          if (passes * nt <= nt8) return Plan{i, passes};
+        }
+  }
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int sms = dev_info(dev).sms;
+  const double blocks = static_cast<double>(w.kunits) * (w.type == 8 ? 1 : 8);  // 32-value blocks per row
+  const double wbytes = static_cast<double>(w.panels) * 16 * w.kunits * (w.type == 8 ? 34 : (w.type == 12 ? 144 : 210));
+  const double abytes_tile = blocks * 8 * 36;  // one token tile's activations (int8 + scale), all blocks
+  double best_t = 1e30;
+  for (int i = 0; i < kVariants; ++i) {
+    const Variant& v = tab[i];
+    const int nt = (kConsumers / v.wp) * v.ntw;  // token tiles per CTA
+    if (nt > 2 * tiles + 1 && i != 0) continue;  // far more token columns than tokens
+    const int passes = (tiles + nt - 1) / nt;
+    if (passes * nt > nt8) continue;  // a pass may not read past the padded activation rows
+    const int64_t rtiles = (w.panels + 2 * v.wp - 1) / (2 * v.wp);
+    const int64_t ctas = rtiles * passes;
+    const int occ = prepare(w.type, i);
+    // per-SM float work: CTAs round-robin over SMs, `occ` of them share an SM at a time
+    const double per_sm_ctas = std::ceil(static_cast<double>(ctas) / sms);
+    const double work = per_sm_ctas * (2.0 * v.wp * 16) * (nt * 8.0) * blocks;  // element-blocks on the busiest SM
+    const double t_fp = work * 3.0 / (128.0 * 1.9e9);                          // 3 FP32 ops per element-block
+    const double l2 = wbytes * passes + abytes_tile * tiles * rtiles;          // bytes through L2
+    const double t_l2 = l2 / 18e12;
+    const double t = std::max(t_fp, t_l2) + (occ > 1 ? 0.0 : 0.2e-6 * per_sm_ctas);
+    if (t < best_t * 0.98) best_t = t, best.variant = i, best.passes = passes;
+  }
+  return best;
 }
 
 }  // namespace
 
-int q8_mode() {
-  const char* e = std::getenv("MALKIN_B200_Q8_GEMM");
-  if (e && std::string(e) == "fp16") return kQ8Fp16;
-  if (e && std::string(e) == "split") return kQ8Split;
-  return kQ8Exact;
-}
-
+// Split-K is never chosen automatically: token passes and narrow tiles fill the SMs (plan_for) and keep every
+// (row, token) sum in malkin's block order, so results are bit-identical to its compact panel kernels. An explicit
+// split (mk_matmul's split_k > 1) still runs, with per-slice sums added in slice order.
 int gemm_split_for(const DevWeight& w, int num_sms) {
-  if (w.layout == kLayoutTc) return q8_mode() == kQ8Split ? gemm_x3_split_for(w, num_sms) : gemm_tc_split_for(w, num_sms);
-  const int64_t tiles = (w.panels + kTilePanels - 1) / kTilePanels;
-  const int max_split = std::max(1, w.kunits / (w.type == 8 ? 8 : 1));
-  int best = 1;
-  double best_eff = 0.0;
-  for (int s = 1; s <= std::min(16, max_split); ++s) {
-    const int per = (w.kunits + s - 1) / s;
-    const int real = (w.kunits + per - 1) / per;
-    const int64_t ctas = tiles * real;
-    const double eff = static_cast<double>(ctas) / (static_cast<double>((ctas + num_sms - 1) / num_sms) * num_sms);
-    if (eff >= 0.85) return real;
-    if (eff > best_eff + 1e-9) best_eff = eff, best = real;
-  }
-  return best;
+  (void)w;
+  (void)num_sms;
+  return 1;
 }
 
 int gemm_slices(const DevWeight& w, int split) {
@@ -462,12 +556,7 @@ void launch_gemm(const DevWeight& w, const ActQ& act, int n, float* y, int64_t l
                  int* status, cudaStream_t s) {
   if (n <= 0) return;
   if (w.layout == kLayoutTc) {
-    if (act.q8 == kQ8Split)
-      launch_gemm_x3(w, act, n, y, ldy, slice, split, status, s);
-    else if (act.q8 == kQ8Fp16)
-      launch_gemm_f16(w, act, n, y, ldy, slice, split, status, s);
-    else
-      launch_gemm_tc(w, act, n, y, ldy, slice, split, nullptr, status, s);
+    launch_gemm_tc(w, act, n, y, ldy, slice, split, nullptr, status, s);
     return;
   }
   split = std::max(1, std::min(split, w.kunits));
@@ -489,24 +578,13 @@ void launch_gemm(const DevWeight& w, const ActQ& act, int n, float* y, int64_t l
   a.slice = slice;
   a.n = n;
   a.status = status;
-  const int tiles = (n + 7) / 8;
-  const int passes = (tiles + kMaxNT - 1) / kMaxNT;
-  const int nt = passes == 1 ? tiles : kMaxNT;  // full passes; the last pass reads zero-padded tiles
-  const dim3 grid(static_cast<unsigned>((w.panels + kTilePanels - 1) / kTilePanels), static_cast<unsigned>(gy),
-                  static_cast<unsigned>(passes));
-  switch (w.type) {
-    case 8:
-      launch_t<8>(a, grid, nt, s);
-      break;
-    case 12:
-      launch_t<12>(a, grid, nt, s);
-      break;
-    case 14:
-      launch_t<14>(a, grid, nt, s);
-      break;
-    default:
-      break;
-  }
+  if (w.type != 8 && w.type != 12 && w.type != 14) return;
+  const Plan pl = plan_for(w, n, act.nt8, gy);
+  const Variant& v = table_of(w.type)[pl.variant];
+  prepare(w.type, pl.variant);
+  const dim3 grid(static_cast<unsigned>((w.panels + 2 * v.wp - 1) / (2 * v.wp)), static_cast<unsigned>(gy),
+                  static_cast<unsigned>(pl.passes));
+  v.fn<<<grid, kThreadsG, v.smem, s>>>(a);
 }
 
 void launch_block_dots(const DevWeight& w, const ActQ& act, int n, int32_t* out, int* status, cudaStream_t s) {

@@ -64,8 +64,19 @@ __host__ __device__ constexpr uint32_t tc_smem(int N) { return tc_stages(N) * tc
 
 // N = 16 * NCH tokens per launch.
 template <int NCH>
-__global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
+__global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs args) {
   constexpr int N = 16 * NCH;
+  // blockIdx.z: token pass of N tokens (passes instead of split-K slices keep every (row, token) sum in malkin's
+  // block order while filling the SMs); the pass sees its tokens from offset 0
+  TcArgs a = args;
+  {
+    const int t0 = static_cast<int>(blockIdx.z) * N;
+    a.qc += static_cast<size_t>(t0) * 32;
+    a.dx += t0;
+    if (a.y) a.y += static_cast<int64_t>(t0) * a.ldy;
+    if (a.dots) a.dots += static_cast<int64_t>(t0) * a.kblocks;
+    a.n = min(N, args.n - t0);
+  }
   constexpr uint32_t SB = tc_stage_bytes(N);
   constexpr int NS = tc_stages(N);
   constexpr uint32_t OFF_B = kTcKB * static_cast<uint32_t>(kTcRecord), OFF_DX = OFF_B + kTcKB * N * 32;
@@ -373,6 +384,12 @@ constexpr std::array<TcFn, sizeof...(I)> tc_table(std::integer_sequence<int, I..
 }
 constexpr int kTcVariants = kTcMaxN / 16;
 
+int sms_of_device(int dev) {
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
 }  // namespace
 
 int gemm_tc_split_for(const DevWeight& w, int num_sms) {
@@ -387,6 +404,25 @@ int gemm_tc_split_for(const DevWeight& w, int num_sms) {
     const double eff = static_cast<double>(ctas) / (static_cast<double>((ctas + num_sms - 1) / num_sms) * num_sms);
     if (eff >= 0.9) return real;
     if (eff > best_eff + 1e-9) best_eff = eff, best = real;
+  }
+  return best;
+}
+
+// Tokens per pass (a multiple of 16, <= 256) for `tiles` 128-row tiles and n tokens at split 1: the fewest passes
+// whose CTA count (tiles x passes, one CTA per SM) keeps the waves at least 85 % full, each pass re-reading the
+// weight tile (from L2 when the passes of a tile run together). Passes never read past npad activation rows.
+int gemm_tc_pass_tokens(int64_t tiles, int n, int npad, int num_sms) {
+  const int n16 = (n + 15) / 16;
+  int best = (std::min(n, kTcMaxN) + 15) / 16 * 16;
+  double best_eff = 0.0;
+  for (int passes = (n + kTcMaxN - 1) / kTcMaxN; passes <= n16; ++passes) {
+    const int N = (n16 + passes - 1) / passes * 16;
+    const int real = (n + N - 1) / N;
+    if (static_cast<int64_t>(real) * N > npad) continue;
+    const int64_t ctas = tiles * real;
+    const double eff = static_cast<double>(ctas) / (static_cast<double>((ctas + num_sms - 1) / num_sms) * num_sms);
+    if (eff >= 0.85) return N;
+    if (eff > best_eff + 1e-9) best_eff = eff, best = N;
   }
   return best;
 }
@@ -421,23 +457,26 @@ void launch_gemm_tc(const DevWeight& w, const ActQ& act, int n, float* y, int64_
   a.slice = slice;
   a.dots_n = n;
   a.status = status;
-  const dim3 grid(static_cast<unsigned>((w.rows + kTcRows - 1) / kTcRows), static_cast<unsigned>(gy));
-  // passes of up to 256 tokens; each launch sees its pass's tokens from offset 0
-  for (int t0 = 0; t0 < n; t0 += kTcMaxN) {
-    const int N = (std::min(npad - t0, kTcMaxN) + 15) / 16 * 16;
-    const int v = N / 16 - 1;
-    if (dev < 64 && !attr_set[dev][v]) {
-      cudaFuncSetAttribute(fns[v], cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(tc_smem(N)));
-      attr_set[dev][v] = true;
-    }
-    TcArgs ap = a;
-    ap.qc = act.qc + static_cast<size_t>(t0) * 32;
-    ap.dx = act.dx + t0;
-    ap.y = y ? y + static_cast<int64_t>(t0) * ldy : nullptr;
-    ap.n = std::min(kTcMaxN, n - t0);
-    ap.dots = dots ? dots + static_cast<int64_t>(t0) * kb : nullptr;
-    fns[v]<<<grid, kTcThreads, tc_smem(N), s>>>(ap);
+  // Token passes (grid.z) of N tokens: N a multiple of 16 (<= 256) chosen so tiles x slices x passes fill the SMs
+  // when the K range is not split (split == 1 keeps malkin's block order for every output).
+  const int64_t tiles = (w.rows + kTcRows - 1) / kTcRows;
+  int N = (std::min(n, kTcMaxN) + 15) / 16 * 16;
+  if (gy == 1) N = gemm_tc_pass_tokens(tiles, n, npad, sms_of_device(dev));
+  const int passes = (n + N - 1) / N;
+  if (static_cast<int64_t>(passes) * N > npad)  // a pass may not read past the padded activation rows
+    N = (std::min(n, kTcMaxN) + 15) / 16 * 16;
+  const int v = N / 16 - 1;
+  if (dev < 64 && !attr_set[dev][v]) {
+    cudaFuncSetAttribute(fns[v], cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(tc_smem(N)));
+    attr_set[dev][v] = true;
   }
+  a.qc = act.qc;
+  a.dx = act.dx;
+  a.y = y;
+  a.n = n;
+  a.dots = dots;
+  const dim3 grid(static_cast<unsigned>(tiles), static_cast<unsigned>(gy), static_cast<unsigned>((n + N - 1) / N));
+  fns[v]<<<grid, kTcThreads, tc_smem(N), s>>>(a);
 }
 
 }  // namespace mkb

@@ -21,17 +21,10 @@ inline int act_tiles(int n) {
 
 // Status-word code of an activation outside the fp16 range of the split-fp16 GEMM operand (bounded-wait timeouts use
 // codes 1-10 and 16 up).
-constexpr int kErrFp16Range = 11;
-
-// Arithmetic of the Q8_0 tensor-core GEMM (see launch_gemm below).
-enum Q8Mode { kQ8Fp16 = 0, kQ8Exact = 1, kQ8Split = 2 };
-
 // Quantized activations in the GEMM layout (layout.hpp). nt8 = token tiles of the current batch (layout stride).
 struct ActQ {
   uint8_t* qx = nullptr;
   uint8_t* qc = nullptr;  // tensor-core order of the same int8 values (nullable)
-  uint16_t* xh = nullptr;  // fp16 of q * d in tensor-core order (nullable), layout.hpp
-  int q8 = kQ8Exact;       // Q8Mode the tensor-core Q8_0 GEMM runs in (qc for exact / split, xh for fp16)
   float* dx = nullptr;
   float* dsx = nullptr;
   uint32_t* sh = nullptr;
@@ -85,27 +78,9 @@ int gemm_slices(const DevWeight& w, int split);
 // out[(r * n + t) * nblk + b]: exact int dot of block b (Q6_K: 16-value halves).
 void launch_block_dots(const DevWeight& w, const ActQ& act, int n, int32_t* out, int* status, cudaStream_t s);
 
-// ---- tensor-core Q8_0 GEMMs, reached through launch_gemm / launch_block_dots ----
-// Arithmetic of the Q8_0 GEMM:
-//   kQ8Exact  malkin's exact int8 block dots and per-block float epilogue (tcgen05 kind::i8, gemm_tc.cu, plus the
-//             mma.sync panel kernel for the shapes it wins); bit-identical to malkin at split 1.
-//   kQ8Split  the dequantized operands q * d split into fp16 hi + lo terms, three kind::f16 MMAs per 16 values
-//             accumulated in fp32 across blocks (gemm_x3.cu): about 2^-21 relative error per product, no per-block
-//             epilogue. Reads the int8 qc copy and dx like the exact kernel. Needs |q_x * d_x| < 65520 (fp16
-//             range); a value outside it sets kErrFp16Range.
-//   kQ8Fp16   one fp16 term per operand (gemm_f16.cu): two fp16 roundings per product, which move logits of the
-//             synthetic test models by up to about 2e-2.
-// The environment variable MALKIN_B200_Q8_GEMM (exact | split | fp16) selects it; q8_mode() reads it on every call.
-// launch_gemm runs the kernel of act.q8, which the owner of the activation buffers sets with the buffers.
-int q8_mode();
-// Bytes per (32-value block, padded token) of the tensor-core activation copy the mode reads: int8 qc (32) or
-// fp16 xh (64).
-inline int q8_act_bytes(int mode) { return mode == kQ8Fp16 ? 64 : 32; }
-void launch_gemm_x3(const DevWeight& w, const ActQ& act, int n, float* y, int64_t ldy, int64_t slice, int split,
-                    int* status, cudaStream_t s);
-int gemm_x3_split_for(const DevWeight& w, int num_sms);
-void launch_gemm_f16(const DevWeight& w, const ActQ& act, int n, float* y, int64_t ldy, int64_t slice, int split,
-                     int* status, cudaStream_t s);
+// ---- tensor-core Q8_0 GEMM (tcgen05 kind::i8, gemm_tc.cu), reached through launch_gemm / launch_block_dots ----
+// malkin's exact int8 block dots and per-block float epilogue; bit-identical to malkin at split 1 (token passes
+// fill the SMs instead of K slices).
 void launch_gemm_tc(const DevWeight& w, const ActQ& act, int n, float* y, int64_t ldy, int64_t slice, int split,
                     int32_t* dots, int* status, cudaStream_t s);
 int gemm_tc_split_for(const DevWeight& w, int num_sms);
@@ -161,9 +136,8 @@ void launch_qkv_post(Slices qk, int v_n, int64_t v_col0, int64_t ldy, int n, int
 // Attention work description (host-built, device tables).
 struct AttnPlan {
   int n = 0;                    // tokens
-  int n_sg = 0;                 // query sub-groups (consecutive tokens of one sequence)
-  int chunk = 256;              // keys per partial CTA
-  int n_chunks = 0;             // chunk slots per sub-group (grid)
+  int n_sg = 0;                 // query sub-groups (consecutive tokens of one sequence, at most attn_qmax() / G)
+  int kchunks = 0;              // key chunks of the score kernel's grid (attn_key_chunks of the context length)
   const int32_t* sg_first = nullptr;  // [n_sg + 1] token ranges
   const int32_t* kv_base = nullptr;   // [n]
   const int32_t* n_keys = nullptr;    // [n]
@@ -171,15 +145,18 @@ struct AttnPlan {
   const int32_t* anc = nullptr;       // extra key rows (relative to kv_base)
   const int32_t* tok_sg = nullptr;    // [n] sub-group of each token
   const int32_t* sg_maxk = nullptr;   // [n_sg] longest key prefix (n_keys) among the sub-group's tokens
-  float* part = nullptr;              // partials workspace (attn_part_floats)
+  float* sbuf = nullptr;              // [n][H][sstride] scores, then e_j * v_scale_j (workspace)
+  int64_t sstride = 0;                // >= the longest key list (prefix + extras) of any token
+  float* inv = nullptr;               // [n][H] 1 / sum of e_j
+  float* att = nullptr;               // [n][H][D] output when the caller passes none (workspace)
   int* status = nullptr;              // device word for bounded-wait failures (nullable)
 };
 // Query vectors (rows x G) one sub-group may hold.
 int attn_qmax();
-// Keys per attention chunk (a multiple of 64) for sequences of up to max_keys keys, n_sg sub-groups and KV heads: about
-// two CTAs per SM in total, at least 64 keys per chunk.
-int attn_chunk_for(int max_keys, int n_sg, int KV, int num_sms);
-size_t attn_part_floats(int n_sg, int n_chunks, int KV, int D);
+// Key chunks of the score kernel for a context of n_ctx keys.
+int attn_key_chunks(int n_ctx);
+// Workspace floats for n tokens, H heads, score rows of sstride keys and head_dim D (sbuf, inv, att).
+size_t attn_ws_floats(int n, int H, int64_t sstride, int D);
 // out: [n][H][D] floats (nullable); act: the same rows quantized into the GEMM activation layouts (act.qx nullable).
 void launch_attention(const float* q, int H, int KV, int D, float scale, const AttnLayer& L, const AttnPlan& p,
                       float* out, const ActQ& act, cudaStream_t s);

@@ -25,7 +25,7 @@ __device__ float dequant_at(uint32_t type, const uint8_t* row, int i) {
       const uint8_t* b = row + (i / 32) * 34;
       return __fmul_rn(ld_h(b), static_cast<float>(static_cast<int8_t>(b[2 + i % 32])));
     }
-    case 12: {  // Q4_K: d * sc * q - dmin * m
+    case 12: {  // Q4_K
       const uint8_t* b = row + (i / 256) * 144;
       const int k = i % 256, j = k / 32, l = k % 32;
       const uint8_t* s = b + 4;
@@ -39,8 +39,9 @@ __device__ float dequant_at(uint32_t type, const uint8_t* row, int i) {
       }
       const uint8_t q8 = b[16 + 32 * (j / 2) + l];
       const int q = (j & 1) ? q8 >> 4 : q8 & 0xF;
-      return __fsub_rn(__fmul_rn(__fmul_rn(ld_h(b), static_cast<float>(sc)), static_cast<float>(q)),
-                       __fmul_rn(ld_h(b + 2), static_cast<float>(m)));
+      // d * sc * q - dmin * m as g++ contracts dequant_q4_k (quant.cpp:77-90): fma(q, d * sc, -(dmin * m))
+      return __fmaf_rn(static_cast<float>(q), __fmul_rn(ld_h(b), static_cast<float>(sc)),
+                       -__fmul_rn(ld_h(b + 2), static_cast<float>(m)));
     }
     case 14: {  // Q6_K: d * sc * (q - 32)
       const uint8_t* b = row + (i / 256) * 210;

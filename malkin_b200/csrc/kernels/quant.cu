@@ -36,7 +36,8 @@ __global__ void k_quant_rows(const float* __restrict__ x, int64_t ldx, int n, in
   store_act(a, b, t, quant_block32(v, lane), lane);
 }
 
-// grid (npad), block 256: one token row. y = x * s * w, s = 1 / sqrt(dot(x, x) / K + eps).
+// grid (npad), block 256: one token row. y = x * s * w, s = 1 / sqrt(dot(x, x) / K + eps), the dot in malkin's
+// 16-lane order (dot16_self over the row in global memory, written back by this block before the barrier).
 __global__ void k_rmsnorm_quant(float* __restrict__ x, int64_t ldx, Slices add, const int32_t* __restrict__ rows,
                                 const float* __restrict__ w, float eps, int n, int K, ActQ a) {
   const int t = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -47,24 +48,18 @@ __global__ void k_rmsnorm_quant(float* __restrict__ x, int64_t ldx, Slices add, 
   }
   const int r = rows ? rows[t] : t;
   float* xr = x + static_cast<size_t>(r) * ldx;
-  __shared__ float red[8];
-  float ss = 0.0f;
-#pragma unroll 4
-  for (int i = threadIdx.x; i < K; i += blockDim.x) {
-    float v = xr[i];
-    if (add.n > 0) {
-      v = __fadd_rn(v, sum_strided16(add.p + static_cast<size_t>(r) * ldx + i, add.n, add.stride));
-      xr[i] = v;
-    }
-    ss = __fmaf_rn(v, v, ss);
+  __shared__ float s_sh;
+  if (add.n > 0) {
+    for (int i = threadIdx.x; i < K; i += blockDim.x)
+      xr[i] = __fadd_rn(xr[i], sum_strided16(add.p + static_cast<size_t>(r) * ldx + i, add.n, add.stride));
+    __syncthreads();
   }
-  ss = warp_sum(ss);
-  if (lane == 0) red[warp] = ss;
+  if (warp == 0) {
+    const float ss = dot16_self(xr, K, lane);
+    if (lane == 0) s_sh = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(K)), eps)));
+  }
   __syncthreads();
-  float tot = 0.0f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) tot += red[i];
-  const float s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(K)), eps)));
+  const float s = s_sh;
   for (int b = warp; b < nb; b += 8) {
     const int i = b * 32 + lane;
     const float v = __fmul_rn(__fmul_rn(xr[i], s), w[i]);
@@ -74,7 +69,8 @@ __global__ void k_rmsnorm_quant(float* __restrict__ x, int64_t ldx, Slices add, 
 
 // The same with one 1024-thread block per token row and the row held in registers (K <= 8192): thread i holds
 // values i, i + 1024, ..., so warp w's lanes already hold block w + 32 j for the quantization pass, and every load
-// of the row (and of its residual slices) is in flight at once.
+// of the row (and of its residual slices) is in flight at once. The row also goes to shared memory, where warp 0
+// forms malkin's 16-lane dot (dot16_self): the scale is bit-identical to rmsnorm's (model.cpp:46-49).
 constexpr int kNormThreads = 1024, kNormMaxJ = 8;
 template <int NS>  // residual slices added first (add.n == NS)
 __global__ void __launch_bounds__(kNormThreads) k_rmsnorm_quant_wide(float* __restrict__ x, int64_t ldx, Slices add,
@@ -108,17 +104,20 @@ __global__ void __launch_bounds__(kNormThreads) k_rmsnorm_quant_wide(float* __re
       if (i < K) xr[i] = v[j];
     }
   }
-  float ss = 0.0f;
+  __shared__ float row[kNormThreads * kNormMaxJ];
+  __shared__ float s_sh;
 #pragma unroll
-  for (int j = 0; j < kNormMaxJ; ++j) ss = __fmaf_rn(v[j], v[j], ss);
-  ss = warp_sum(ss);
-  __shared__ float red[kNormThreads / 32];
-  if (lane == 0) red[warp] = ss;
+  for (int j = 0; j < kNormMaxJ; ++j) {
+    const int i = threadIdx.x + kNormThreads * j;
+    if (i < K) row[i] = v[j];
+  }
   __syncthreads();
-  float tot = 0.0f;
-#pragma unroll
-  for (int i = 0; i < kNormThreads / 32; ++i) tot += red[i];
-  const float sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(K)), eps)));
+  if (warp == 0) {
+    const float ss = dot16_self(row, K, lane);
+    if (lane == 0) s_sh = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(K)), eps)));
+  }
+  __syncthreads();
+  const float sc = s_sh;
 #pragma unroll
   for (int j = 0; j < kNormMaxJ; ++j) {
     const int b = warp + 32 * j;

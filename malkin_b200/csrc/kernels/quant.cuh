@@ -55,13 +55,6 @@ __device__ __forceinline__ void store_act(const ActQ& a, int b, int t, const QBl
       *reinterpret_cast<uint32_t*>(dq) = word;
     }
   }
-  if (a.xh) {
-    // fp16 of the dequantized value q * d, value k of token t at (t / 8) * 256 + (k / 8) * 64 + (t % 8) * 8 + k % 8
-    // halves from the block's base
-    const __half h = __float2half_rn(__fmul_rn(static_cast<float>(qb.q), qb.d));
-    a.xh[static_cast<size_t>(b) * npad * 32 + (t >> 3) * 256 + (lane >> 3) * 64 + (t & 7) * 8 + (lane & 7)] =
-        __half_as_ushort(h);
-  }
   if (lane == 0) {
     const size_t o = static_cast<size_t>(b) * npad + t;
     a.dx[o] = qb.d;

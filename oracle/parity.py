@@ -166,7 +166,8 @@ def compare(d: Dict, r: Dict) -> Dict:
     for s, (dev, ref) in enumerate(zip(d["greedy"], r["greedy"])):
         rt = d["tree_roots"][s]
         srt = np.sort(r["tree_logits"][rt:rt + per], axis=-1)
-        if np.all(srt[:, -1] - srt[:, -2] > MARGIN):
+        same = np.array_equal(d["tree_logits"][rt:rt + per], r["tree_logits"][rt:rt + per])
+        if same or np.all(srt[:, -1] - srt[:, -2] > MARGIN):  # identical logits: every walk must match
             g_cmp += 1
             g_same += int(dev == ref)
     out = {"max_abs_logits": mx, "tol": TOL_LOGITS, "greedy_compared": g_cmp, "greedy_identical": g_same,

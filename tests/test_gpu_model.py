@@ -1,12 +1,12 @@
-"""Model-level parity of the sm_100a path through the C ABI: prefill and tree-verify logits within 2e-2 of malkin's
-(golden) after the final norm, greedy accepted paths identical where malkin's top-1 margin exceeds 1e-2, KV
-compaction (move_kv) correct (the next step matches), sampled decisions identical given the same uniforms."""
+"""Model-level parity of the sm_100a path through the C ABI: prefill and tree-verify logits bit-identical to malkin's
+(golden) - every float operation runs in malkin's order - greedy accepted paths identical, KV compaction (move_kv)
+correct (the next step matches), sampled decisions identical given the same uniforms."""
 import numpy as np
 import pytest
 
 pytestmark = pytest.mark.gpu
 
-TOL = 2e-2  # max-abs logits tolerance after the final norm (north star)
+TOL = 2e-2  # the north star's max-abs logits tolerance; the path is bit-exact, so the tests require equality
 
 
 def load(mk, path, n_ctx=64, n_seq=2, max_batch=256):
@@ -26,11 +26,11 @@ def margin_ok(logits_rows):
 def test_verify_step_matches_reference(mk, golden, model_paths, name, torch_cuda):
     m = load(mk, model_paths[name])
     pl = m.forward(batch_of(mk, golden[f"m_{name}_pre"]))
-    assert np.abs(pl - golden[f"m_{name}_pre_logits"]).max() < TOL
+    assert np.array_equal(pl, golden[f"m_{name}_pre_logits"])
     tree = golden[f"m_{name}_tree"]
     tl = m.forward(batch_of(mk, tree))
     gl = golden[f"m_{name}_tree_logits"]
-    assert np.abs(tl - gl).max() < TOL
+    assert np.array_equal(tl, gl)
     kk = 4
     props = []
     for root in golden[f"m_{name}_roots"]:
@@ -40,15 +40,13 @@ def test_verify_step_matches_reference(mk, golden, model_paths, name, torch_cuda
                                  alt=alt))
     res = m.accept(props)
     for j, (r, root) in enumerate(zip(res, golden[f"m_{name}_roots"])):
-        if not margin_ok(gl[root:root + 2 * kk + 1]):
-            continue
         n = int(golden[f"m_{name}_acc_n"][j])
         assert r.ids == list(golden[f"m_{name}_acc_ids"][j][:n])
         assert r.next == int(golden[f"m_{name}_acc_next"][j])
         assert r.cache_len == int(golden[f"m_{name}_acc_cache"][j])
     # next step reads the compacted KV rows
     l2 = m.forward(batch_of(mk, golden[f"m_{name}_step2"]))
-    assert np.abs(l2 - golden[f"m_{name}_step2_logits"]).max() < TOL
+    assert np.array_equal(l2, golden[f"m_{name}_step2_logits"])
     m.close()
 
 
@@ -64,7 +62,7 @@ def test_verify_step_matches_oracle_fresh(mk, oracle, model_paths, torch_cuda):
         pre += [(int(t), seq, i, int(i == L - 1), -1, -1) for i, t in enumerate(rng.integers(0, 1000, L))]
     a = m.forward(batch_of(mk, pre))
     b = om.forward(pre)
-    assert np.abs(a - b).max() < TOL
+    assert np.array_equal(a, b)
     lens = (20, 33, 7)
     rows, props = [], []
     for seq in range(3):
@@ -80,7 +78,7 @@ def test_verify_step_matches_oracle_fresh(mk, oracle, model_paths, torch_cuda):
         props.append((seq, root, P, chain, alt))
     ta = m.forward(batch_of(mk, rows))
     tb = om.forward(rows)
-    assert np.abs(ta - tb).max() < TOL
+    assert np.array_equal(ta, tb)
     res = m.accept([mk.Proposal(seq=s, root=r, cache_len=P, chain=c, alt=al) for s, r, P, c, al in props])
     for (s, r, P, c, al), got in zip(props, res):
         ids, nxt, _ = oracle.accept_greedy(ta[r:r + 7], c, al)  # identical logits -> identical walk
@@ -159,8 +157,8 @@ def test_continuous_batch_equals_separate(mk, model_paths, torch_cuda):
     m2 = load(mk, path)
     a = m2.forward(batch_of(mk, ta))
     b = m2.forward(batch_of(mk, tb))
-    # int8 activation rounding can flip on float-summation-order noise, so the bound is the logits tolerance
-    assert np.abs(both - np.concatenate([a, b])).max() < TOL
+    # every row's arithmetic is independent of the other rows in the batch
+    assert np.array_equal(both, np.concatenate([a, b]))
 
 
 def test_profile_and_launch_count(mk, model_paths, torch_cuda):
