@@ -432,9 +432,9 @@ int mk_attention(const float* dev_q, int n, int H, int KV, int D, const int8_t* 
     mkb::cuda_check(cudaMemcpy(ao.data(), dev_anc_off, (n + 1) * 4, cudaMemcpyDeviceToHost), "attention");
     const int G = H / KV, rows = std::max(1, mkb::attn_qmax() / G);
     std::vector<int32_t> sgf, tsg(n), sgm;
-    int maxk = 1, maxlist = 1;
+    int maxk = 1, maxex = 1;
     for (int t = 0; t < n; ++t) {
-      maxlist = std::max(maxlist, nk[t] + ao[t + 1] - ao[t]);
+      maxex = std::max(maxex, ao[t + 1] - ao[t]);
       if (t == 0 || kvb[t] != kvb[t - 1] || t - sgf.back() >= rows) {
         sgf.push_back(t);
         sgm.push_back(0);
@@ -445,19 +445,33 @@ int mk_attention(const float* dev_q, int n, int H, int KV, int D, const int8_t* 
     }
     const int n_sg = static_cast<int>(sgf.size());
     sgf.push_back(n);
+    std::vector<int32_t> stoff(static_cast<size_t>(n_sg) + 1, 0);
+    int64_t st_total = 0;
+    for (int g = 0; g < n_sg; ++g) {
+      stoff[static_cast<size_t>(g)] = static_cast<int32_t>(st_total);
+      st_total += mkb::attn_st_floats(sgf[static_cast<size_t>(g) + 1] - sgf[static_cast<size_t>(g)], G, KV,
+                                      sgm[static_cast<size_t>(g)]);
+    }
+    if (st_total > INT32_MAX) throw mkb::ArgError("attention: score tables too large");
+    stoff[static_cast<size_t>(n_sg)] = static_cast<int32_t>(st_total);
     mkb::AttnPlan p;
     p.n = n;
     p.n_sg = n_sg;
     p.kchunks = mkb::attn_key_chunks(maxk);
-    mkb::DevBuf tabs((sgf.size() + tsg.size() + sgm.size()) * 4);
+    mkb::DevBuf tabs((sgf.size() + tsg.size() + sgm.size() + stoff.size()) * 4);
     mkb::cuda_check(cudaMemcpy(tabs.get(), sgf.data(), sgf.size() * 4, cudaMemcpyHostToDevice), "attention");
     mkb::cuda_check(cudaMemcpy(tabs.get<int32_t>() + sgf.size(), tsg.data(), tsg.size() * 4, cudaMemcpyHostToDevice),
                     "attention");
     mkb::cuda_check(cudaMemcpy(tabs.get<int32_t>() + sgf.size() + tsg.size(), sgm.data(), sgm.size() * 4,
                                cudaMemcpyHostToDevice),
                     "attention");
-    const int64_t sstride = (maxlist + 3) / 4 * 4;
-    mkb::DevBuf ws(mkb::attn_ws_floats(n, H, sstride, D) * 4);
+    mkb::cuda_check(cudaMemcpy(tabs.get<int32_t>() + sgf.size() + tsg.size() + sgm.size(), stoff.data(),
+                               stoff.size() * 4, cudaMemcpyHostToDevice),
+                    "attention");
+    const int64_t exs = (maxex + 3) / 4 * 4;
+    const size_t ws_floats = static_cast<size_t>(st_total) + static_cast<size_t>(n) * H * exs +
+                             static_cast<size_t>(n) * H + static_cast<size_t>(n) * H * D;
+    mkb::DevBuf ws(ws_floats * 4);
     p.sg_first = tabs.get<int32_t>();
     p.tok_sg = tabs.get<int32_t>() + sgf.size();
     p.sg_maxk = tabs.get<int32_t>() + sgf.size() + tsg.size();
@@ -465,9 +479,11 @@ int mk_attention(const float* dev_q, int n, int H, int KV, int D, const int8_t* 
     p.n_keys = dev_n_keys;
     p.anc_off = dev_anc_off;
     p.anc = dev_anc;
-    p.sbuf = ws.get<float>();
-    p.sstride = sstride;
-    p.inv = p.sbuf + static_cast<size_t>(n) * H * sstride;
+    p.st = ws.get<float>();
+    p.st_off = tabs.get<int32_t>() + sgf.size() + tsg.size() + sgm.size();
+    p.ex = p.st + st_total;
+    p.ex_stride = static_cast<int>(exs);
+    p.inv = p.ex + static_cast<size_t>(n) * H * exs;
     p.att = p.inv + static_cast<size_t>(n) * H;
     mkb::AttnLayer L{const_cast<int8_t*>(dev_k), const_cast<int8_t*>(dev_v), const_cast<float*>(dev_ks),
                      const_cast<float*>(dev_vs), n_rows};

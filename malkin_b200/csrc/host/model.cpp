@@ -427,16 +427,23 @@ void Model::alloc_kv(int n_ctx, int n_seq, int max_batch) {
   // attention plan geometry
   const int G = c.n_head / c.n_head_kv;
   sg_rows_ = std::max(1, attn_qmax() / G);
-  // attention workspace: a score row per (token, head) long enough for any key list (prefix + extra rows)
-  attn_sstride_ = static_cast<int64_t>(n_ctx) + max_batch;
-  attn_ws_ = DevBuf(attn_ws_floats(max_batch, Hl_, attn_sstride_, D) * sizeof(float));
+  // attention workspace: the key-major score tables of every sub-group (at most one per token, each row padded to
+  // att_nqp slots), the extra keys' scores, 1 / sums and the output rows
+  {
+    const int GA = (G + 1) / 2 * 2;
+    attn_st_cap_ = static_cast<int64_t>(KVl_) * n_ctx * max_batch * (GA + 4);
+    attn_ex_stride_ = max_batch;
+    const int64_t ex = static_cast<int64_t>(max_batch) * Hl_ * attn_ex_stride_;
+    const int64_t inv = static_cast<int64_t>(max_batch) * Hl_, att = static_cast<int64_t>(max_batch) * Hl_ * D;
+    attn_ws_ = DevBuf(static_cast<size_t>(attn_st_cap_ + ex + inv + att) * sizeof(float));
+  }
   meta_cap_ = 0;
   ensure_meta(static_cast<size_t>(max_batch) * 16);
 }
 
 void Model::ensure_meta(size_t anc_cap) {
   const size_t MB = static_cast<size_t>(max_batch_);
-  const size_t need = 10 * MB + 2 + anc_cap;
+  const size_t need = 11 * MB + 3 + anc_cap;
   if (need <= meta_cap_) return;
   for (auto& [k, g] : graphs_) cudaGraphExecDestroy(g);
   graphs_.clear();
@@ -457,7 +464,8 @@ void Model::ensure_meta(size_t anc_cap) {
   d_toksg_ = m + 7 * MB + 2;
   d_outrows_ = m + 8 * MB + 2;
   d_sgmaxk_ = m + 9 * MB + 2;
-  d_anc_ = m + 10 * MB + 2;
+  d_stoff_ = m + 10 * MB + 2;
+  d_anc_ = m + 11 * MB + 3;
 }
 
 void Model::stage(int i) {
@@ -688,6 +696,18 @@ void Model::forward(const mk_batch_token* batch, int n, float* host_logits) {
   }
   const int n_sg = static_cast<int>(sgfirst.size());
   sgfirst.push_back(n);
+  // offsets of the sub-groups' attention score tables
+  std::vector<int32_t> stoff(static_cast<size_t>(n_sg) + 1, 0);
+  {
+    int64_t off = 0;
+    for (int g = 0; g < n_sg; ++g) {
+      stoff[static_cast<size_t>(g)] = static_cast<int32_t>(off);
+      off += attn_st_floats(sgfirst[static_cast<size_t>(g) + 1] - sgfirst[static_cast<size_t>(g)],
+                            cfg_.n_head / cfg_.n_head_kv, KVl_, sgmaxk[static_cast<size_t>(g)]);
+    }
+    if (off > attn_st_cap_ || off > INT32_MAX) throw ArgError("forward: attention workspace exceeded");
+    stoff[static_cast<size_t>(n_sg)] = static_cast<int32_t>(off);
+  }
   const int m = static_cast<int>(outrows.size());
   ensure_meta(anc.size());
   // pinned staging -> one copy
@@ -703,10 +723,11 @@ void Model::forward(const mk_batch_token* batch, int n, float* host_logits) {
   std::copy(toksg.begin(), toksg.end(), h + 7 * MB + 2);
   std::copy(outrows.begin(), outrows.end(), h + 8 * MB + 2);
   std::copy(sgmaxk.begin(), sgmaxk.end(), h + 9 * MB + 2);
-  std::copy(anc.begin(), anc.end(), h + 10 * MB + 2);
-  cuda_check(cudaMemcpyAsync(meta_.get(), h, (10 * MB + 2 + anc.size()) * 4, cudaMemcpyHostToDevice, stream_),
+  std::copy(stoff.begin(), stoff.end(), h + 10 * MB + 2);
+  std::copy(anc.begin(), anc.end(), h + 11 * MB + 3);
+  cuda_check(cudaMemcpyAsync(meta_.get(), h, (11 * MB + 3 + anc.size()) * 4, cudaMemcpyHostToDevice, stream_),
              "meta upload");
-  h2d_bytes_ += static_cast<int64_t>((10 * MB + 2 + anc.size()) * 4);
+  h2d_bytes_ += static_cast<int64_t>((11 * MB + 3 + anc.size()) * 4);
   plan_.n = n;
   plan_.n_sg = n_sg;
   plan_.kchunks = attn_key_chunks(n_ctx_);
@@ -719,11 +740,12 @@ void Model::forward(const mk_batch_token* batch, int n, float* host_logits) {
   plan_.sg_maxk = d_sgmaxk_;
   {
     float* ws = attn_ws_.get<float>();
-    const size_t sb = static_cast<size_t>(max_batch_) * Hl_ * static_cast<size_t>(attn_sstride_);
-    plan_.sbuf = ws;
-    plan_.sstride = attn_sstride_;
-    plan_.inv = ws + sb;
-    plan_.att = ws + sb + static_cast<size_t>(max_batch_) * Hl_;
+    plan_.st = ws;
+    plan_.st_off = d_stoff_;
+    plan_.ex = ws + attn_st_cap_;
+    plan_.ex_stride = attn_ex_stride_;
+    plan_.inv = plan_.ex + static_cast<size_t>(max_batch_) * Hl_ * attn_ex_stride_;
+    plan_.att = plan_.inv + static_cast<size_t>(max_batch_) * Hl_;
   }
   plan_.status = status_;
 

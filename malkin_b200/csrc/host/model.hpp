@@ -187,9 +187,10 @@ class Model {
   int32_t* meta_host_ = nullptr;
   size_t meta_cap_ = 0;  // int32 entries
   int32_t *d_ids_ = nullptr, *d_rpos_ = nullptr, *d_kvat_ = nullptr, *d_kvbase_ = nullptr, *d_nkeys_ = nullptr,
-          *d_ancoff_ = nullptr, *d_sgfirst_ = nullptr, *d_toksg_ = nullptr, *d_outrows_ = nullptr, *d_sgmaxk_ = nullptr, *d_anc_ = nullptr;
-  DevBuf attn_ws_;             // attention scores / probabilities, inverses, output (attn_ws_floats)
-  int64_t attn_sstride_ = 0;
+          *d_ancoff_ = nullptr, *d_sgfirst_ = nullptr, *d_toksg_ = nullptr, *d_outrows_ = nullptr, *d_sgmaxk_ = nullptr, *d_stoff_ = nullptr, *d_anc_ = nullptr;
+  DevBuf attn_ws_;             // attention score tables, extra-key scores, 1 / sums, output rows
+  int64_t attn_st_cap_ = 0;     // floats of the score tables
+  int attn_ex_stride_ = 0;
   AttnPlan plan_;
   int sg_rows_ = 0;
 

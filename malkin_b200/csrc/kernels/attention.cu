@@ -20,6 +20,7 @@
 #include "common.cuh"
 #include "kernels.hpp"
 #include "quant.cuh"
+#include "pipeline.cuh"
 
 namespace mkb {
 
@@ -97,17 +98,21 @@ __global__ void k_qkv_post(Slices qk, int v_n, int64_t v_col0, int64_t ldy, int 
 //   e_j  = exp(s_j - max_j s_j)                      (malkin's exp)
 //   inv  = 1 / reduce16(sums), sum l adds e_j for j = l, l + 16, ... in order
 //   out  = (acc over j in order: acc = fma(e_j * v_scale_j, v_j, acc), from 0) * inv
-// Every float operation is malkin's, in malkin's order, so the output is bit-identical. Three kernels:
+// Every float operation is malkin's, in malkin's order, so the output is bit-identical. Four kernels:
 //   k_att_scores   one thread per prefix key of a (sub-group, KV head): the key row in registers, every query vector
-//                  of the sub-group (rows x G heads) broadcast from shared memory; scores to a workspace row per (t, h)
-//   k_att_softmax  one warp per (t, h): the extra keys' scores, the maximum, e_j, the 16 lane-striped sums (one
-//                  sequential chain per lane, as malkin's vector lanes), e_j * v_scale_j in place of s_j, and inv
-//   k_att_pv       one thread per (row, 4 output values) of a (sub-group, KV head, 32-value slice of D): the G heads'
-//                  chains over the shared prefix keys from shared-memory tiles, then each row's extra keys.
+//                  of the sub-group (rows x G heads) broadcast from shared memory; scores into the sub-group's
+//                  key-major table ST[j][slot] (slot = row * GA + head, GA = G rounded up to even)
+//   k_att_extras   one warp per (t, h): the scores of the token's extra (ancestor) keys, as 16 chains on a half-warp
+//   k_att_softmax  one CTA per (sub-group, KV head): warp l runs malkin's vector lane l - the lane-striped maximum and
+//                  sum of every slot - with 32 slots side by side, then e_j * v_scale_j in place of s_j and 1 / sum
+//   k_att_pv       one CTA per (sub-group, KV head, 32 of the D values): TMA bulk copies bring key tiles of the
+//                  probabilities (ST rows) and of the int8 values two tiles ahead; the chains of two heads advance
+//                  in one f32x2 FMA (each lane of the pair its own IEEE fma, in key order); then each row's extras.
 constexpr int kQMax = 96;         // query vectors (rows x G) per sub-group
 constexpr int kScoreKeys = 128;   // keys (threads) per score CTA
-constexpr int kPvTile = 64;       // keys per shared-memory tile of the P.V kernel
+constexpr int kPvTile = 64;       // keys per P.V tile
 constexpr int kPvSlice = 32;      // output values per P.V CTA
+constexpr int kErrAttWait = 24;   // status code: a P.V tile copy never landed
 
 struct AttArgs {
   const float* q;  // [n][H][D]
@@ -118,20 +123,20 @@ struct AttArgs {
   float* out;      // [n][H][D]
 };
 
-// malkin's _mm512_reduce_add_ps on 16 values held by one thread: (0+8, 4+12, 2+10, 6+14, 1+9, 5+13, 3+11, 7+15)
-// pairwise as the vector reduction pairs them.
-__device__ __forceinline__ float tree16(const float (&a)[16]) {
-  float b[8], c[4];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) b[i] = __fadd_rn(a[i + 8], a[i]);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) c[i] = __fadd_rn(b[i + 4], b[i]);
-  return __fadd_rn(__fadd_rn(c[0], c[2]), __fadd_rn(c[1], c[3]));
-}
+// Slots of a sub-group's key-major probability table: row r, head g at r * GA + g; rows padded to 4 slots.
+__host__ __device__ constexpr int att_ga(int G) { return (G + 1) / 2 * 2; }
+__host__ __device__ constexpr int att_nqp(int rows, int G) { return (rows * att_ga(G) + 3) / 4 * 4; }
 
 __device__ __forceinline__ float i8f(int8_t v) { return static_cast<float>(v); }
 
-// grid (key chunks, n_sg, KV), block kScoreKeys; dynamic smem: nq x D query floats + nq key limits.
+// ST of (sub-group sg, KV head kvh): maxk_sg rows of nqp floats.
+__device__ __forceinline__ float* st_of(const AttArgs& a, int sg, int kvh, int maxk, int nqp) {
+  return a.p.st + a.p.st_off[sg] + static_cast<int64_t>(kvh) * maxk * nqp;
+}
+
+// grid (key chunks, n_sg, KV), block kScoreKeys; dynamic smem: kQMax x D query floats + kQMax key limits. The 16 chains
+// of a score run as 8 packed f32x2 pairs (chains 2m and 2m + 1 share an instruction; each lane of the pair is its
+// own IEEE operation, so the values are malkin's) and the horizontal sum is done pairwise the same way.
 template <int D>
 __global__ void __launch_bounds__(kScoreKeys) k_att_scores(AttArgs a) {
   constexpr int DC = D / 16;
@@ -152,7 +157,7 @@ __global__ void __launch_bounds__(kScoreKeys) k_att_scores(AttArgs a) {
   const int j = j0 + threadIdx.x;
   if (j >= maxk) return;
   const size_t row = static_cast<size_t>(kvh) * a.L.n_rows + a.p.kv_base[t0] + j;
-  float kf[D];
+  f2 kf[D / 2];  // (k[2m], k[2m + 1])
   {
     const int4* kr = reinterpret_cast<const int4*>(a.L.k + row * D);
 #pragma unroll
@@ -160,93 +165,160 @@ __global__ void __launch_bounds__(kScoreKeys) k_att_scores(AttArgs a) {
       const int4 w = kr[c];
       const int8_t* b = reinterpret_cast<const int8_t*>(&w);
 #pragma unroll
-      for (int e = 0; e < 16; ++e) kf[16 * c + e] = i8f(b[e]);
+      for (int e = 0; e < 8; ++e) kf[8 * c + e] = f2_make(i8f(b[2 * e]), i8f(b[2 * e + 1]));
     }
   }
   const float ks = __fmul_rn(a.L.ks[row], a.scale);
+  const int ga = att_ga(a.G), nqp = att_nqp(t1 - t0, a.G);
+  float* srow = st_of(a, sg, kvh, maxk, nqp) + static_cast<int64_t>(j) * nqp;
   for (int v = 0; v < nq; ++v) {
     if (j >= nkq[v]) continue;
-    const float4* qv = reinterpret_cast<const float4*>(qs + v * D);
-    float acc[16];
+    const ulonglong2* qv = reinterpret_cast<const ulonglong2*>(qs + v * D);  // pairs (q[2m], q[2m + 1])
+    f2 acc[8];
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-      const float4 x = qv[c];
-      acc[4 * c] = __fmul_rn(x.x, kf[4 * c]);
-      acc[4 * c + 1] = __fmul_rn(x.y, kf[4 * c + 1]);
-      acc[4 * c + 2] = __fmul_rn(x.z, kf[4 * c + 2]);
-      acc[4 * c + 3] = __fmul_rn(x.w, kf[4 * c + 3]);
+      const ulonglong2 x = qv[c];
+      acc[2 * c] = f2_mul(x.x, kf[2 * c]);
+      acc[2 * c + 1] = f2_mul(x.y, kf[2 * c + 1]);
     }
 #pragma unroll
     for (int i = 1; i < DC; ++i)
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        const float4 x = qv[4 * i + c];
-        acc[4 * c] = __fmaf_rn(x.x, kf[16 * i + 4 * c], acc[4 * c]);
-        acc[4 * c + 1] = __fmaf_rn(x.y, kf[16 * i + 4 * c + 1], acc[4 * c + 1]);
-        acc[4 * c + 2] = __fmaf_rn(x.z, kf[16 * i + 4 * c + 2], acc[4 * c + 2]);
-        acc[4 * c + 3] = __fmaf_rn(x.w, kf[16 * i + 4 * c + 3], acc[4 * c + 3]);
+        const ulonglong2 x = qv[4 * i + c];
+        acc[2 * c] = f2_fma(x.x, kf[8 * i + 2 * c], acc[2 * c]);
+        acc[2 * c + 1] = f2_fma(x.y, kf[8 * i + 2 * c + 1], acc[2 * c + 1]);
       }
-    const int t = t0 + v / a.G, h = kvh * a.G + v % a.G;
-    a.p.sbuf[(static_cast<size_t>(t) * a.H + h) * a.p.sstride + j] = __fmul_rn(tree16(acc), ks);
+    // tree16 in pairs: lanes i + 8 and i (pairs p + 4 and p), then i + 4 and i, then (0 + 2, 1 + 3), then 0 + 1
+    f2 b2[4], c2[2];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) b2[p] = f2_add(acc[p + 4], acc[p]);
+#pragma unroll
+    for (int p = 0; p < 2; ++p) c2[p] = f2_add(b2[p + 2], b2[p]);
+    const f2 d2 = f2_add(c2[0], c2[1]);
+    srow[(v / a.G) * ga + v % a.G] = __fmul_rn(__fadd_rn(f2_lo(d2), f2_hi(d2)), ks);
   }
 }
 
-// grid (n, ceil(H / 4)), block 128: warp w handles (t = blockIdx.x, h = blockIdx.y * 4 + w).
+// grid (n, ceil(H / 4)), block 128: warp w computes the extra keys' scores of (t = blockIdx.x, h = blockIdx.y * 4 + w)
+// into ex[t][h][e]: lane l < 16 runs chain l (the lanes of malkin's vector), reduce16 across the half-warp.
 template <int D>
-__global__ void __launch_bounds__(128) k_att_softmax(AttArgs a) {
+__global__ void __launch_bounds__(128) k_att_extras(AttArgs a) {
   constexpr int DC = D / 16;
   const int t = blockIdx.x, lane = threadIdx.x & 31;
   const int h = blockIdx.y * 4 + (threadIdx.x >> 5);
   if (h >= a.H) return;
-  const int kvh = h / a.G;
-  const int n0 = a.p.n_keys[t], e0 = a.p.anc_off[t], ne = a.p.anc_off[t + 1] - e0, nk = n0 + ne;
-  const size_t hb = static_cast<size_t>(kvh) * a.L.n_rows + a.p.kv_base[t];
-  float* sr = a.p.sbuf + (static_cast<size_t>(t) * a.H + h) * a.p.sstride;
-  // extra keys: lane l < 16 runs chain l (the lanes of malkin's vector), reduce16 across the half-warp
-  if (ne > 0) {
-    const float* qv = a.q + (static_cast<size_t>(t) * a.H + h) * D;
-    float q[DC];
+  const int e0 = a.p.anc_off[t], ne = a.p.anc_off[t + 1] - e0;
+  if (ne == 0) return;
+  const size_t hb = static_cast<size_t>(h / a.G) * a.L.n_rows + a.p.kv_base[t];
+  const float* qv = a.q + (static_cast<size_t>(t) * a.H + h) * D;
+  float q[DC];
 #pragma unroll
-    for (int i = 0; i < DC; ++i) q[i] = qv[16 * i + (lane & 15)];
-    for (int e = 0; e < ne; ++e) {
-      const size_t row = hb + a.p.anc[e0 + e];
-      const int8_t* kr = a.L.k + row * D;
-      float acc = __fmul_rn(q[0], i8f(kr[lane & 15]));
+  for (int i = 0; i < DC; ++i) q[i] = qv[16 * i + (lane & 15)];
+  float* er = a.p.ex + (static_cast<size_t>(t) * a.H + h) * a.p.ex_stride;
+  for (int e = 0; e < ne; ++e) {
+    const size_t row = hb + a.p.anc[e0 + e];
+    const int8_t* kr = a.L.k + row * D;
+    float acc = __fmul_rn(q[0], i8f(kr[lane & 15]));
 #pragma unroll
-      for (int i = 1; i < DC; ++i) acc = __fmaf_rn(q[i], i8f(kr[16 * i + (lane & 15)]), acc);
-      acc = reduce16(acc);
-      if (lane == 0) sr[n0 + e] = __fmul_rn(acc, __fmul_rn(a.L.ks[row], a.scale));
-    }
-    __syncwarp();
+    for (int i = 1; i < DC; ++i) acc = __fmaf_rn(q[i], i8f(kr[16 * i + (lane & 15)]), acc);
+    acc = reduce16(acc);
+    if (lane == 0) er[e] = __fmul_rn(acc, __fmul_rn(a.L.ks[row], a.scale));
   }
-  float mx = -INFINITY;
-  for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, sr[j]);
-  mx = warp_max(mx);
-  for (int j = lane; j < nk; j += 32) sr[j] = exp_malkin(__fsub_rn(sr[j], mx));
-  __syncwarp();
-  // 16 lane-striped sums in key order (malkin's vector lanes), and p_j = e_j * v_scale_j for the P.V chains
-  float sum = 0.0f;
-  if (lane < 16) {
-    for (int j = lane; j < nk; j += 16) {
-      const float e = sr[j];
-      sum = __fadd_rn(sum, e);
-      const size_t row = j < n0 ? hb + j : hb + a.p.anc[e0 + j - n0];
-      sr[j] = __fmul_rn(e, a.L.vs[row]);
+}
+
+// grid (n_sg, KV), block 512: warp l (0..15) plays malkin's vector lane l for 32 slots at a time (lane = slot): the
+// maximum over the slot's keys (any order), then e_j = exp(s_j - max) and the lane-striped sum over keys j = l, l + 16,
+// ... in order (prefix keys from ST, extras from ex), p_j = e_j * v_scale_j written in place; then 1 / reduce16 of
+// the 16 sums.
+__global__ void __launch_bounds__(512) k_att_softmax(AttArgs a) {
+  __shared__ float red[16][33];
+  const int sg = blockIdx.x, kvh = blockIdx.y;
+  const int l = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t0 = a.p.sg_first[sg], rows = a.p.sg_first[sg + 1] - t0;
+  const int maxk = a.p.sg_maxk[sg];
+  const int ga = att_ga(a.G), nqp = att_nqp(rows, a.G);
+  float* st = st_of(a, sg, kvh, maxk, nqp);
+  const size_t hb = static_cast<size_t>(kvh) * a.L.n_rows + a.p.kv_base[t0];
+  for (int s0 = 0; s0 < rows * ga; s0 += 32) {
+    const int slot = s0 + lane, r = slot / ga, g = slot % ga;
+    const bool valid = r < rows && g < a.G;
+    const int t = t0 + (valid ? r : 0), h = kvh * a.G + (valid ? g : 0);
+    const int n0 = valid ? a.p.n_keys[t] : 0;
+    const int e0 = a.p.anc_off[t], ne = valid ? a.p.anc_off[t + 1] - e0 : 0, nk = n0 + ne;
+    float* er = a.p.ex + (static_cast<size_t>(t) * a.H + h) * a.p.ex_stride;
+    // maximum (of this lane's stripe, then over the 16 stripes)
+    float mx = -INFINITY;
+#pragma unroll 4
+    for (int j = l; j < nk; j += 16) mx = fmaxf(mx, j < n0 ? st[static_cast<int64_t>(j) * nqp + slot] : er[j - n0]);
+    red[l][lane] = mx;
+    __syncthreads();
+    mx = red[0][lane];
+#pragma unroll
+    for (int i = 1; i < 16; ++i) mx = fmaxf(mx, red[i][lane]);
+    __syncthreads();
+    // lane-striped sum in key order; eight keys of the stripe loaded at once, only the sum runs in sequence
+    float sum = 0.0f;
+    for (int jb = l; jb < nk; jb += 16 * 8) {
+      float sv[8], vv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int j = jb + 16 * u;
+        sv[u] = j < nk ? (j < n0 ? st[static_cast<int64_t>(j) * nqp + slot] : er[j - n0]) : 0.0f;
+        vv[u] = j < nk ? a.L.vs[j < n0 ? hb + j : hb + a.p.anc[e0 + j - n0]] : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int j = jb + 16 * u;
+        if (j < nk) {
+          const float e = exp_malkin(__fsub_rn(sv[u], mx));
+          sum = __fadd_rn(sum, e);
+          const float p = __fmul_rn(e, vv[u]);
+          if (j < n0)
+            st[static_cast<int64_t>(j) * nqp + slot] = p;
+          else
+            er[j - n0] = p;
+        }
+      }
     }
+    red[l][lane] = sum;
+    __syncthreads();
+    if (l == 0 && valid) {
+      float b8[8], c4[4];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) b8[i] = __fadd_rn(red[i + 8][lane], red[i][lane]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) c4[i] = __fadd_rn(b8[i + 4], b8[i]);
+      const float tot = __fadd_rn(__fadd_rn(c4[0], c4[2]), __fadd_rn(c4[1], c4[3]));
+      a.p.inv[static_cast<size_t>(t) * a.H + h] = __fdiv_rn(1.0f, tot);
+    }
+    __syncthreads();
   }
-  sum = reduce16(sum);
-  if (lane == 0) a.p.inv[static_cast<size_t>(t) * a.H + h] = __fdiv_rn(1.0f, sum);
 }
 
 // grid (n_sg, KV, D / kPvSlice), block rows x 8 (rows = kQMax / G): thread (r, u) owns values u*4 .. u*4+3 of the
-// slice for the G heads of row t0 + r. dynamic smem: V tile [kPvTile][kPvSlice] floats, P tile [kPvTile][rows * G].
+// slice for the G heads of row t0 + r. Thread 0 keeps two tiles of kPvTile keys in flight with TMA bulk copies (the
+// ST rows and the raw int8 value rows); every thread converts its share of a landed value tile into a shared float
+// buffer holding each value twice (v, v), so one f32x2 FMA advances the chains of two heads (each lane of the pair
+// is its own IEEE fma, in key order: malkin's acc = fma(p_j, v_j, acc)).
+constexpr int kVS2 = 2 * kPvSlice + 8;  // float value buffer row stride (32 values duplicated + padding)
 template <int D, int G>
-__global__ void k_att_pv(AttArgs a) {
-  constexpr int ROWS = kQMax / G;
-  extern __shared__ __align__(16) float pvs[];
-  constexpr int PS = ROWS * G + 1;       // P tile row stride (odd: conflict-free stores)
-  float* vt = pvs;                       // [kPvTile][kPvSlice]
-  float* pt = pvs + kPvTile * kPvSlice;  // [kPvTile][PS]
+struct PvGeom {
+  static constexpr int ROWS = kQMax / G, NT = ROWS * 8, GA = att_ga(G);
+  static constexpr int NQP = att_nqp(ROWS, G);                // largest P row (floats)
+  static constexpr uint32_t PBYTES = kPvTile * NQP * 4, VBYTES = kPvTile * D;
+  static constexpr uint32_t STAGE = PBYTES + VBYTES;           // one stage: P rows then raw values
+  static constexpr uint32_t VF = 2 * STAGE;                    // float value buffer offset
+  static constexpr uint32_t BAR = VF + kPvTile * kVS2 * 4;     // two mbarriers
+  static constexpr uint32_t SMEM = BAR + 16;
+};
+template <int D, int G>
+__global__ void __launch_bounds__(kQMax / G * 8) k_att_pv(AttArgs a) {
+  using Gm = PvGeom<D, G>;
+  constexpr int GP = G / 2;  // head pairs
+  extern __shared__ __align__(128) uint8_t sm[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + Gm::BAR);
+  float* vf = reinterpret_cast<float*>(sm + Gm::VF);
   const int sg = blockIdx.x, kvh = blockIdx.y, d0 = blockIdx.z * kPvSlice;
   const int t0 = a.p.sg_first[sg], t1 = a.p.sg_first[sg + 1], nr = t1 - t0;
   const int r = threadIdx.x >> 3, u = threadIdx.x & 7;
@@ -254,83 +326,123 @@ __global__ void k_att_pv(AttArgs a) {
   const bool active = r < nr;
   const int maxk = a.p.sg_maxk[sg];
   const int n0 = active ? a.p.n_keys[t] : 0;
+  const int nqp = att_nqp(nr, G);
+  const float* st = st_of(a, sg, kvh, maxk, nqp);
   const size_t hb = static_cast<size_t>(kvh) * a.L.n_rows + a.p.kv_base[t0];
-  float acc[G][4];
+  const int ntiles = (maxk + kPvTile - 1) / kPvTile;
+  if (threadIdx.x == 0) {
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  auto issue = [&](int it) {  // thread 0
+    const int s = it & 1, k0 = it * kPvTile, nkt = min(kPvTile, maxk - k0);
+    uint8_t* stg = sm + s * Gm::STAGE;
+    const uint32_t pb = static_cast<uint32_t>(nkt) * nqp * 4, vb = static_cast<uint32_t>(nkt) * D;
+    mbar_arrive_expect_tx(&full[s], pb + vb);
+    bulk_g2s(stg, st + static_cast<int64_t>(k0) * nqp, pb, &full[s]);
+    bulk_g2s(stg + Gm::PBYTES, a.L.v + (hb + k0) * D, vb, &full[s]);
+  };
+  if (threadIdx.x == 0)
+    for (int it = 0; it < 2 && it < ntiles; ++it) issue(it);
+  f2 acc2[GP > 0 ? GP : 1][4];  // (head 2 hp, head 2 hp + 1) at output value e
+  float acc1[4];                // the last head when G is odd
 #pragma unroll
-  for (int g = 0; g < G; ++g) acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.0f;
-  for (int k0 = 0; k0 < maxk; k0 += kPvTile) {
-    const int nkt = min(kPvTile, maxk - k0);
-    // V tile: 8-byte groups of the slice, converted exactly
-    for (int i = threadIdx.x; i < kPvTile * (kPvSlice / 8); i += blockDim.x) {
-      const int jj = i / (kPvSlice / 8), c = i % (kPvSlice / 8);
-      float* dst = vt + jj * kPvSlice + 8 * c;
-      if (jj < nkt) {
-        const int2 w = *reinterpret_cast<const int2*>(a.L.v + (hb + k0 + jj) * D + d0 + 8 * c);
-        const int8_t* b = reinterpret_cast<const int8_t*>(&w);
+  for (int e = 0; e < 4; ++e) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) dst[e] = i8f(b[e]);
-      }
-    }
-    // P tile: p_j of every (row, head) of the sub-group for these keys
-    for (int i = threadIdx.x; i < nr * G * kPvTile; i += blockDim.x) {
-      const int v = i / kPvTile, jj = i % kPvTile;
-      if (jj < nkt)
-        pt[jj * PS + v] =
-            a.p.sbuf[(static_cast<size_t>(t0 + v / G) * a.H + kvh * G + v % G) * a.p.sstride + k0 + jj];
+    for (int hp = 0; hp < GP; ++hp) acc2[hp][e] = f2_make(0.0f, 0.0f);
+    acc1[e] = 0.0f;
+  }
+  bool ok = true;
+  for (int it = 0; it < ntiles; ++it) {
+    const int s = it & 1, k0 = it * kPvTile, nkt = min(kPvTile, maxk - k0);
+    ok = ok && mbar_wait(&full[s], (it >> 1) & 1, a.p.status, kErrAttWait);
+    const uint8_t* stg = sm + s * Gm::STAGE;
+    // value slice of the landed tile -> floats, each twice
+    const int8_t* vraw = reinterpret_cast<const int8_t*>(stg + Gm::PBYTES);
+    for (int i = threadIdx.x; i < nkt * (kPvSlice / 4); i += blockDim.x) {
+      const int jj = i / (kPvSlice / 4), c = i % (kPvSlice / 4);
+      const char4 w = *reinterpret_cast<const char4*>(vraw + jj * D + d0 + 4 * c);
+      float4* dst = reinterpret_cast<float4*>(vf + jj * kVS2 + 8 * c);
+      dst[0] = make_float4(i8f(w.x), i8f(w.x), i8f(w.y), i8f(w.y));
+      dst[1] = make_float4(i8f(w.z), i8f(w.z), i8f(w.w), i8f(w.w));
     }
     __syncthreads();
-    if (active) {
+    if (active && ok) {
+      const float* pt = reinterpret_cast<const float*>(stg);
       const int lim = min(nkt, n0 - k0);
+#pragma unroll 2
       for (int jj = 0; jj < lim; ++jj) {
-        const float4 vv = *reinterpret_cast<const float4*>(vt + jj * kPvSlice + 4 * u);
-        const float* pp = pt + jj * PS + r * G;
+        const ulonglong2* vv = reinterpret_cast<const ulonglong2*>(vf + jj * kVS2 + 8 * u);  // (v_e, v_e), e = 0..3
+        const ulonglong2 va = vv[0], vb = vv[1];
+        const float* pp = pt + jj * nqp + r * Gm::GA;
+        const f2 V[4] = {va.x, va.y, vb.x, vb.y};
 #pragma unroll
-        for (int g = 0; g < G; ++g) {
-          const float p = pp[g];
-          acc[g][0] = __fmaf_rn(p, vv.x, acc[g][0]);
-          acc[g][1] = __fmaf_rn(p, vv.y, acc[g][1]);
-          acc[g][2] = __fmaf_rn(p, vv.z, acc[g][2]);
-          acc[g][3] = __fmaf_rn(p, vv.w, acc[g][3]);
+        for (int hp = 0; hp < GP; ++hp) {
+          const f2 P = *reinterpret_cast<const f2*>(pp + 2 * hp);  // (p_2hp, p_2hp+1)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc2[hp][e] = f2_fma(P, V[e], acc2[hp][e]);
+        }
+        if constexpr (G % 2) {
+          const float p = pp[G - 1];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc1[e] = __fmaf_rn(p, f2_lo(V[e]), acc1[e]);
         }
       }
     }
-    __syncthreads();
+    __syncthreads();  // stage s and the value buffer are free
+    if (threadIdx.x == 0 && it + 2 < ntiles && ok) issue(it + 2);
   }
-  if (!active) return;
+  if (!active || !ok) return;
   // the row's extra keys, in order
   const int e0 = a.p.anc_off[t], ne = a.p.anc_off[t + 1] - e0;
   for (int e = 0; e < ne; ++e) {
     const size_t row = hb + a.p.anc[e0 + e];
     const int8_t* vr = a.L.v + row * D + d0 + 4 * u;
-    const float v0 = i8f(vr[0]), v1 = i8f(vr[1]), v2 = i8f(vr[2]), v3 = i8f(vr[3]);
+    const f2 V[4] = {f2_make(i8f(vr[0]), i8f(vr[0])), f2_make(i8f(vr[1]), i8f(vr[1])),
+                     f2_make(i8f(vr[2]), i8f(vr[2])), f2_make(i8f(vr[3]), i8f(vr[3]))};
+    const float* pr = a.p.ex + (static_cast<size_t>(t) * a.H + kvh * G) * a.p.ex_stride + e;
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float p = a.p.sbuf[(static_cast<size_t>(t) * a.H + kvh * G + g) * a.p.sstride + n0 + e];
-      acc[g][0] = __fmaf_rn(p, v0, acc[g][0]);
-      acc[g][1] = __fmaf_rn(p, v1, acc[g][1]);
-      acc[g][2] = __fmaf_rn(p, v2, acc[g][2]);
-      acc[g][3] = __fmaf_rn(p, v3, acc[g][3]);
+    for (int hp = 0; hp < GP; ++hp) {
+      const f2 P = f2_make(pr[(2 * hp) * a.p.ex_stride], pr[(2 * hp + 1) * a.p.ex_stride]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc2[hp][q] = f2_fma(P, V[q], acc2[hp][q]);
+    }
+    if constexpr (G % 2) {
+      const float p = pr[(G - 1) * a.p.ex_stride];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc1[q] = __fmaf_rn(p, f2_lo(V[q]), acc1[q]);
     }
   }
 #pragma unroll
   for (int g = 0; g < G; ++g) {
     const int h = kvh * G + g;
     const float iv = a.p.inv[static_cast<size_t>(t) * a.H + h];
-    float4 o;
-    o.x = __fmul_rn(acc[g][0], iv);
-    o.y = __fmul_rn(acc[g][1], iv);
-    o.z = __fmul_rn(acc[g][2], iv);
-    o.w = __fmul_rn(acc[g][3], iv);
-    *reinterpret_cast<float4*>(a.out + (static_cast<size_t>(t) * a.H + h) * D + d0 + 4 * u) = o;
+    float o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float x = (G % 2 && g == G - 1) ? acc1[e] : ((g & 1) ? f2_hi(acc2[g / 2 < GP ? g / 2 : 0][e])
+                                                                  : f2_lo(acc2[g / 2 < GP ? g / 2 : 0][e]));
+      o[e] = __fmul_rn(x, iv);
+    }
+    *reinterpret_cast<float4*>(a.out + (static_cast<size_t>(t) * a.H + h) * D + d0 + 4 * u) =
+        make_float4(o[0], o[1], o[2], o[3]);
   }
 }
 
 template <int D, int G>
 void launch_pv(const AttArgs& a, cudaStream_t s) {
-  constexpr int ROWS = kQMax / G;
-  const size_t smem = (kPvTile * kPvSlice + kPvTile * (ROWS * G + 1)) * sizeof(float);
+  using Gm = PvGeom<D, G>;
+  static bool attr[kMaxDevices] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < kMaxDevices && !attr[dev]) {
+    cudaFuncSetAttribute(k_att_pv<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(Gm::SMEM));
+    attr[dev] = true;
+  }
   const dim3 g(a.p.n_sg, a.KV, D / kPvSlice);
-  k_att_pv<D, G><<<g, ROWS * 8, smem, s>>>(a);
+  k_att_pv<D, G><<<g, Gm::NT, Gm::SMEM, s>>>(a);
 }
 
 template <int D>
@@ -347,7 +459,8 @@ void run_attention(const float* q, int H, int KV, float scale, const AttnLayer& 
     attr[dev] = true;
   }
   if (p.n_sg > 0 && p.kchunks > 0) k_att_scores<D><<<dim3(p.kchunks, p.n_sg, KV), kScoreKeys, qsmem, s>>>(a);
-  k_att_softmax<D><<<dim3(p.n, (H + 3) / 4), 128, 0, s>>>(a);
+  k_att_extras<D><<<dim3(p.n, (H + 3) / 4), 128, 0, s>>>(a);
+  if (p.n_sg > 0) k_att_softmax<<<dim3(p.n_sg, KV), 512, 0, s>>>(a);
   switch (a.G) {
     case 1: launch_pv<D, 1>(a, s); break;
     case 2: launch_pv<D, 2>(a, s); break;
@@ -368,9 +481,8 @@ int attn_qmax() { return kQMax; }
 
 int attn_key_chunks(int n_ctx) { return (n_ctx + kScoreKeys - 1) / kScoreKeys; }
 
-size_t attn_ws_floats(int n, int H, int64_t sstride, int D) {
-  return static_cast<size_t>(n) * H * static_cast<size_t>(sstride) + static_cast<size_t>(n) * H +
-         static_cast<size_t>(n) * H * D;
+int64_t attn_st_floats(int rows, int G, int KV, int maxk) {
+  return static_cast<int64_t>(KV) * maxk * att_nqp(rows, G);
 }
 
 void launch_qkv_post(Slices qk, int v_n, int64_t v_col0, int64_t ldy, int n, int H, int KV, int D, const float* q_norm,

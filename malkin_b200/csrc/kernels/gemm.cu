@@ -76,16 +76,21 @@ struct GemmArgs {
   int* status;
 };
 
-// Shared-memory layout of one stage (NT token tiles, TP panels).
-template <uint32_t T, int NT, int TP = kTilePanels>
+// Shared-memory layout of one stage (NT token tiles, TP panels, KSX k-units per stage; 0 = the type's default) and
+// the ring depth: the type's default, fewer stages when a stage is large (at most ~200 KB in all, at least 2).
+template <uint32_t T, int NT, int TP = kTilePanels, int KSX = 0>
 struct Stage {
   using C = TypeCfg<T>;
-  static constexpr uint32_t A = TP * C::KS * C::UNIT;
-  static constexpr uint32_t B = C::KS * C::BPU * NT * 256;
-  static constexpr uint32_t DX = C::KS * C::BPU * NT * 8 * 4;
+  static constexpr int KS = KSX ? KSX : C::KS;
+  static constexpr uint32_t A = TP * KS * C::UNIT;
+  static constexpr uint32_t B = KS * C::BPU * NT * 256;
+  static constexpr uint32_t DX = KS * C::BPU * NT * 8 * 4;
   static constexpr uint32_t EX = (C::kDsx || C::kSh) ? DX : 0;
   static constexpr uint32_t BYTES = A + B + DX + EX;
-  static constexpr uint32_t SMEM = C::NS * BYTES + 2 * C::NS * 8;
+  // the type's ring depth when it fits 2 CTAs per SM or only 1 CTA fits anyway; else 2 stages, so 2 CTAs share an SM
+  static constexpr int NS = C::NS * BYTES <= 110u * 1024 ? C::NS
+                            : (2 * BYTES <= 110u * 1024 ? 2 : (C::NS * BYTES <= 200u * 1024 ? C::NS : 2));
+  static constexpr uint32_t SMEM = NS * BYTES + 2 * NS * 8;
 };
 
 // scale_min_k4 (kernels.h:18-26) on the 12 packed bytes held in words w1 (bytes 4-7), w2 (8-11), w3 (12-15).
@@ -100,25 +105,29 @@ __device__ __forceinline__ void q4k_scale_min(int j, uint32_t w1, uint32_t w2, u
   }
 }
 
-// NTW token tiles per warp, WP panel pairs per CTA (WT = 8 / WP warps along the tokens).
-template <uint32_t T, int NTW, int WP>
-__global__ void __launch_bounds__(kThreadsG, 1) k_gemm(GemmArgs a) {
+// NTW token tiles per warp, WP panel pairs per CTA (WT = 8 / WP warps along the tokens), KSX k-units per stage
+// (0: the type's default; narrow tiles take more per stage, so a stage's work outweighs its barrier).
+template <uint32_t T, int NTW, int WP, int KSX>
+__global__ void __launch_bounds__(kThreadsG, NTW <= 7 ? 2 : 1) k_gemm(GemmArgs a) {
   using C = TypeCfg<T>;
   constexpr int WT = kConsumers / WP, NT = WT * NTW, TP = 2 * WP;
-  using S = Stage<T, NT, TP>;
+  using S = Stage<T, NT, TP, KSX>;
+  static_assert(S::NS >= 2, "stage ring too small");
   extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::NS * S::BYTES);
-  uint64_t* empty = full + C::NS;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::NS * S::BYTES);
+  uint64_t* empty = full + S::NS;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
-  const int64_t p0 = static_cast<int64_t>(blockIdx.x) * TP;
+  // grid (passes, slices, row tiles): the passes of one tile are launched together, so after the first one reads
+  // the tile's weights from HBM the others find them in L2
+  const int64_t p0 = static_cast<int64_t>(blockIdx.z) * TP;
   const int tile_panels = static_cast<int>(a.panels - p0 < TP ? a.panels - p0 : TP);
   const int u0 = blockIdx.y * a.per_split, u1 = min(a.kunits, u0 + a.per_split);
-  const int t0 = blockIdx.z * (NT * 8);  // first token of this pass
+  const int t0 = blockIdx.x * (NT * 8);  // first token of this pass
   const int jt0 = (warp / WP) * NTW;     // this warp's first token tile within the pass
   const int npad = a.nt8 * 8;
-  const int n_it = (u1 - u0 + C::KS - 1) / C::KS;
+  const int n_it = (u1 - u0 + S::KS - 1) / S::KS;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < C::NS; ++s) {
+    for (int s = 0; s < S::NS; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumers);
     }
@@ -129,33 +138,36 @@ __global__ void __launch_bounds__(kThreadsG, 1) k_gemm(GemmArgs a) {
   // Stage refill, issued by warp 0: lane 0 arms the full barrier with the byte count, lanes 0-15 copy the tile's
   // weight chunks (one per panel), lanes 16-23 the activation blocks, dx (and dsx / sh) of each 32-value block.
   auto issue = [&](int it) {
-    const int s = it % C::NS;
-    const int ua = u0 + it * C::KS, uk = min(C::KS, u1 - ua);  // units in this stage
+    const int s = it % S::NS;
+    const int ua = u0 + it * S::KS, uk = min(S::KS, u1 - ua);  // units in this stage
     const int nb = uk * C::BPU;                                // 32-value blocks in this stage
+    // token tiles this pass reads: a last pass past the padded activation rows reads only those that exist (the
+    // columns of the missing tiles hold stale shared memory; their outputs are tokens >= n and are never stored)
+    const int ntp = min(NT, a.nt8 - t0 / 8);
     const uint32_t bytes = static_cast<uint32_t>(tile_panels) * uk * C::UNIT +
-                           static_cast<uint32_t>(nb) * NT * (256 + 32 + ((C::kDsx || C::kSh) ? 32 : 0));
+                           static_cast<uint32_t>(nb) * ntp * (256 + 32 + ((C::kDsx || C::kSh) ? 32 : 0));
     uint8_t* st = smem + static_cast<size_t>(s) * S::BYTES;
     if (lane == 0) mbar_arrive_expect_tx(&full[s], bytes);
     __syncwarp();
     if (lane < tile_panels)
-      bulk_g2s(st + lane * (C::KS * C::UNIT), a.w + (static_cast<size_t>(p0 + lane) * a.kunits + ua) * C::UNIT,
+      bulk_g2s(st + lane * (S::KS * C::UNIT), a.w + (static_cast<size_t>(p0 + lane) * a.kunits + ua) * C::UNIT,
                uk * C::UNIT, &full[s]);
     const int blk0 = ua * C::BPU;
     if (lane >= 16 && lane - 16 < nb) {
       const int b = lane - 16;
-      bulk_g2s(st + S::A + b * NT * 256, a.qx + (static_cast<size_t>(blk0 + b) * a.nt8 + t0 / 8) * 256, NT * 256,
+      bulk_g2s(st + S::A + b * NT * 256, a.qx + (static_cast<size_t>(blk0 + b) * a.nt8 + t0 / 8) * 256, ntp * 256,
                &full[s]);
-      bulk_g2s(st + S::A + S::B + b * NT * 32, a.dx + static_cast<size_t>(blk0 + b) * npad + t0, NT * 32, &full[s]);
+      bulk_g2s(st + S::A + S::B + b * NT * 32, a.dx + static_cast<size_t>(blk0 + b) * npad + t0, ntp * 32, &full[s]);
       if (C::kDsx)
-        bulk_g2s(st + S::A + S::B + S::DX + b * NT * 32, a.dsx + static_cast<size_t>(blk0 + b) * npad + t0, NT * 32,
+        bulk_g2s(st + S::A + S::B + S::DX + b * NT * 32, a.dsx + static_cast<size_t>(blk0 + b) * npad + t0, ntp * 32,
                  &full[s]);
       if (C::kSh)
-        bulk_g2s(st + S::A + S::B + S::DX + b * NT * 32, a.sh + static_cast<size_t>(blk0 + b) * npad + t0, NT * 32,
+        bulk_g2s(st + S::A + S::B + S::DX + b * NT * 32, a.sh + static_cast<size_t>(blk0 + b) * npad + t0, ntp * 32,
                  &full[s]);
     }
   };
   if (warp == 0)
-    for (int it = 0; it < C::NS && it < n_it; ++it) issue(it);
+    for (int it = 0; it < S::NS && it < n_it; ++it) issue(it);
 
   // ---------------- consumers: warp owns panels pw, pw + 1 of the tile x token tiles jt0 .. jt0 + NTW - 1 ----------------
   const int pw = 2 * (warp % WP);
@@ -168,13 +180,13 @@ __global__ void __launch_bounds__(kThreadsG, 1) k_gemm(GemmArgs a) {
     for (int j = 0; j < NTW; ++j) acc[q][j][0] = acc[q][j][1] = f2_make(0.0f, 0.0f);
 
   for (int it = 0; it < n_it; ++it) {
-    const int s = it % C::NS, r = it / C::NS;
+    const int s = it % S::NS, r = it / S::NS;
     if (!mbar_wait(&full[s], r & 1, a.status, kErrWaitFull)) break;
     const uint8_t* st = smem + static_cast<size_t>(s) * S::BYTES;
-    const int uk = min(C::KS, u1 - (u0 + it * C::KS));
+    const int uk = min(S::KS, u1 - (u0 + it * S::KS));
     if (has0) {
-      const uint8_t* sa0 = st + pw * (C::KS * C::UNIT);
-      const uint8_t* sa1 = sa0 + C::KS * C::UNIT;
+      const uint8_t* sa0 = st + pw * (S::KS * C::UNIT);
+      const uint8_t* sa1 = sa0 + S::KS * C::UNIT;
       const uint8_t* sb = st + S::A + jt0 * 256 + lane * 8;
       const float* sdx = reinterpret_cast<const float*>(st + S::A + S::B) + 8 * jt0 + 2 * c;
       const float* sex = reinterpret_cast<const float*>(st + S::A + S::B + S::DX) + 8 * jt0 + 2 * c;
@@ -320,9 +332,9 @@ __global__ void __launch_bounds__(kThreadsG, 1) k_gemm(GemmArgs a) {
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
     // warp 0 refills this stage for iteration it + NS once all warps have released it
-    if (warp == 0 && it + C::NS < n_it) {
+    if (warp == 0 && it + S::NS < n_it) {
       if (!mbar_wait(&empty[s], r & 1, a.status, kErrWaitEmpty)) break;
-      issue(it + C::NS);
+      issue(it + S::NS);
     }
   }
   // ---------------- epilogue: this slice's partial sums ----------------
@@ -414,19 +426,29 @@ struct Variant {
   uint32_t smem;
   int wp, ntw;
 };
-constexpr int kVariants = kMaxNT + 4 + 3;
+// WP = 8 (16-panel tiles): NTW 1..18, default stage depth. WP = 4 (8 panels): NTW 4..9; WP = 2 (4 panels): NTW 2..5;
+// WP = 1 (2 panels): NTW 1..3; the narrow Q8_0 tiles with 8 blocks per stage.
+constexpr int kVariants = kMaxNT + 6 + 4 + 3;
 
-template <uint32_t T, int WP, int... N>
+template <uint32_t T>
+constexpr int narrow_ks() {
+  return T == 8 ? 8 : 0;  // K-quant stages already hold 8 blocks (one super-block)
+}
+
+template <uint32_t T, int WP, int N0, int KSX, int... N>
 constexpr void fill(Variant* v, std::integer_sequence<int, N...>) {
-  ((v[N] = Variant{&k_gemm<T, N + 1, WP>, Stage<T, (kConsumers / WP) * (N + 1), 2 * WP>::SMEM, WP, N + 1}), ...);
+  ((v[N] = Variant{&k_gemm<T, N + N0, WP, KSX>, Stage<T, (kConsumers / WP) * (N + N0), 2 * WP, KSX>::SMEM, WP,
+                   N + N0}),
+   ...);
 }
 
 template <uint32_t T>
 constexpr std::array<Variant, kVariants> variants() {
   std::array<Variant, kVariants> v{};
-  fill<T, 8>(v.data(), std::make_integer_sequence<int, kMaxNT>{});
-  fill<T, 2>(v.data() + kMaxNT, std::make_integer_sequence<int, 4>{});
-  fill<T, 1>(v.data() + kMaxNT + 4, std::make_integer_sequence<int, 3>{});
+  fill<T, 8, 1, 0>(v.data(), std::make_integer_sequence<int, kMaxNT>{});
+  fill<T, 4, 4, narrow_ks<T>()>(v.data() + kMaxNT, std::make_integer_sequence<int, 6>{});
+  fill<T, 2, 2, narrow_ks<T>()>(v.data() + kMaxNT + 6, std::make_integer_sequence<int, 4>{});
+  fill<T, 1, 1, narrow_ks<T>()>(v.data() + kMaxNT + 10, std::make_integer_sequence<int, 3>{});
   return v;
 }
 
@@ -502,8 +524,8 @@ Plan plan_for(const DevWeight& w, int n, int nt8, int split) {
     if (std::sscanf(e, "%d:%d", &wp, &ntw) == 2)
       for (int i = 0; i < kVariants; ++i)
         if (tab[i].wp == wp && tab[i].ntw == ntw) {
-          const int nt = (kConsumers / wp) * ntw, passes = (tiles + nt - 1) / nt;
-          if (passes * nt <= nt8) return Plan{i, passes};
+          const int nt = (kConsumers / wp) * ntw;
+          return Plan{i, (tiles + nt - 1) / nt};
         }
   }
   int dev = 0;
@@ -518,7 +540,6 @@ Plan plan_for(const DevWeight& w, int n, int nt8, int split) {
     const int nt = (kConsumers / v.wp) * v.ntw;  // token tiles per CTA
     if (nt > 2 * tiles + 1 && i != 0) continue;  // far more token columns than tokens
     const int passes = (tiles + nt - 1) / nt;
-    if (passes * nt > nt8) continue;  // a pass may not read past the padded activation rows
     const int64_t rtiles = (w.panels + 2 * v.wp - 1) / (2 * v.wp);
     const int64_t ctas = rtiles * passes;
     const int occ = prepare(w.type, i);
@@ -582,8 +603,8 @@ void launch_gemm(const DevWeight& w, const ActQ& act, int n, float* y, int64_t l
   const Plan pl = plan_for(w, n, act.nt8, gy);
   const Variant& v = table_of(w.type)[pl.variant];
   prepare(w.type, pl.variant);
-  const dim3 grid(static_cast<unsigned>((w.panels + 2 * v.wp - 1) / (2 * v.wp)), static_cast<unsigned>(gy),
-                  static_cast<unsigned>(pl.passes));
+  const dim3 grid(static_cast<unsigned>(pl.passes), static_cast<unsigned>(gy),
+                  static_cast<unsigned>((w.panels + 2 * v.wp - 1) / (2 * v.wp)));
   v.fn<<<grid, kThreadsG, v.smem, s>>>(a);
 }
 

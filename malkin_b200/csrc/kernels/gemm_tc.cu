@@ -16,6 +16,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <array>
 #include <utility>
 
@@ -461,7 +462,14 @@ void launch_gemm_tc(const DevWeight& w, const ActQ& act, int n, float* y, int64_
   // when the K range is not split (split == 1 keeps malkin's block order for every output).
   const int64_t tiles = (w.rows + kTcRows - 1) / kTcRows;
   int N = (std::min(n, kTcMaxN) + 15) / 16 * 16;
-  if (gy == 1) N = gemm_tc_pass_tokens(tiles, n, npad, sms_of_device(dev));
+  if (gy == 1) {
+    N = gemm_tc_pass_tokens(tiles, n, npad, sms_of_device(dev));
+    // MALKIN_B200_TC_PASS=<tokens> forces the pass size (tests and measurements), when it fits the padded rows
+    if (const char* e = std::getenv("MALKIN_B200_TC_PASS")) {
+      const int f = (std::atoi(e) + 15) / 16 * 16;
+      if (f >= 16 && f <= kTcMaxN && static_cast<int64_t>((n + f - 1) / f) * f <= npad) N = f;
+    }
+  }
   const int passes = (n + N - 1) / N;
   if (static_cast<int64_t>(passes) * N > npad)  // a pass may not read past the padded activation rows
     N = (std::min(n, kTcMaxN) + 15) / 16 * 16;

@@ -145,8 +145,10 @@ struct AttnPlan {
   const int32_t* anc = nullptr;       // extra key rows (relative to kv_base)
   const int32_t* tok_sg = nullptr;    // [n] sub-group of each token
   const int32_t* sg_maxk = nullptr;   // [n_sg] longest key prefix (n_keys) among the sub-group's tokens
-  float* sbuf = nullptr;              // [n][H][sstride] scores, then e_j * v_scale_j (workspace)
-  int64_t sstride = 0;                // >= the longest key list (prefix + extras) of any token
+  float* st = nullptr;                // key-major score / probability tables, one per (sub-group, KV head)
+  const int32_t* st_off = nullptr;    // [n_sg] float offset of each sub-group's tables (attn_st_floats each)
+  float* ex = nullptr;                // [n][H][ex_stride] the extra keys' scores, then probabilities
+  int ex_stride = 0;                  // >= the most extra keys of any token
   float* inv = nullptr;               // [n][H] 1 / sum of e_j
   float* att = nullptr;               // [n][H][D] output when the caller passes none (workspace)
   int* status = nullptr;              // device word for bounded-wait failures (nullable)
@@ -155,8 +157,8 @@ struct AttnPlan {
 int attn_qmax();
 // Key chunks of the score kernel for a context of n_ctx keys.
 int attn_key_chunks(int n_ctx);
-// Workspace floats for n tokens, H heads, score rows of sstride keys and head_dim D (sbuf, inv, att).
-size_t attn_ws_floats(int n, int H, int64_t sstride, int D);
+// Floats of the score / probability tables of one sub-group of `rows` tokens with keys 0 .. maxk - 1 (all KV heads).
+int64_t attn_st_floats(int rows, int G, int KV, int maxk);
 // out: [n][H][D] floats (nullable); act: the same rows quantized into the GEMM activation layouts (act.qx nullable).
 void launch_attention(const float* q, int H, int KV, int D, float scale, const AttnLayer& L, const AttnPlan& p,
                       float* out, const ActQ& act, cudaStream_t s);

@@ -93,7 +93,7 @@ def test_matmul_shapes_vs_oracle(mk, oracle, torch_cuda, monkeypatch, t, n):
     assert np.array_equal(y.cpu().numpy(), oracle.matmul(t, w, rows, cols, x))
 
 
-GEMM_SHAPES = [(8, wp, ntw) for wp, nmax in ((8, 18), (2, 4), (1, 3)) for ntw in range(1, nmax + 1)]
+GEMM_SHAPES = [(8, wp, ntw) for wp, lo, hi in ((8, 1, 18), (4, 4, 9), (2, 2, 5), (1, 1, 3)) for ntw in range(lo, hi + 1)]
 
 
 @pytest.mark.parametrize("t", TYPES)
