@@ -227,7 +227,8 @@ __global__ void __launch_bounds__(128) k_att_extras(AttArgs a) {
   }
 }
 
-// grid (n_sg, KV), block 512: warp l (0..15) plays malkin's vector lane l for 32 slots at a time (lane = slot): the
+// grid (n_sg, KV, slot groups of 32), block 512: warp l (0..15) plays malkin's vector lane l for the CTA's 32 slots
+// (lane = slot): the
 // maximum over the slot's keys (any order), then e_j = exp(s_j - max) and the lane-striped sum over keys j = l, l + 16,
 // ... in order (prefix keys from ST, extras from ex), p_j = e_j * v_scale_j written in place; then 1 / reduce16 of
 // the 16 sums.
@@ -240,7 +241,7 @@ __global__ void __launch_bounds__(512) k_att_softmax(AttArgs a) {
   const int ga = att_ga(a.G), nqp = att_nqp(rows, a.G);
   float* st = st_of(a, sg, kvh, maxk, nqp);
   const size_t hb = static_cast<size_t>(kvh) * a.L.n_rows + a.p.kv_base[t0];
-  for (int s0 = 0; s0 < rows * ga; s0 += 32) {
+  for (int s0 = blockIdx.z * 32; s0 < rows * ga && s0 < (blockIdx.z + 1) * 32; s0 += 32) {
     const int slot = s0 + lane, r = slot / ga, g = slot % ga;
     const bool valid = r < rows && g < a.G;
     const int t = t0 + (valid ? r : 0), h = kvh * a.G + (valid ? g : 0);
@@ -372,8 +373,35 @@ __global__ void __launch_bounds__(kQMax / G * 8) k_att_pv(AttArgs a) {
     if (active && ok) {
       const float* pt = reinterpret_cast<const float*>(stg);
       const int lim = min(nkt, n0 - k0);
-#pragma unroll 2
-      for (int jj = 0; jj < lim; ++jj) {
+      // keys in groups of kB: every shared-memory load of the group is issued before its FMAs (which run in key order)
+      constexpr int kB = 4;
+      int jj = 0;
+      for (; jj + kB <= lim; jj += kB) {
+        f2 V[kB][4], P[kB][GP > 0 ? GP : 1];
+        float P1[kB];
+#pragma unroll
+        for (int b = 0; b < kB; ++b) {
+          const ulonglong2* vv = reinterpret_cast<const ulonglong2*>(vf + (jj + b) * kVS2 + 8 * u);
+          const ulonglong2 va = vv[0], vb = vv[1];
+          V[b][0] = va.x, V[b][1] = va.y, V[b][2] = vb.x, V[b][3] = vb.y;
+          const float* pp = pt + (jj + b) * nqp + r * Gm::GA;
+#pragma unroll
+          for (int hp = 0; hp < GP; ++hp) P[b][hp] = *reinterpret_cast<const f2*>(pp + 2 * hp);
+          P1[b] = (G % 2) ? pp[G - 1] : 0.0f;
+        }
+#pragma unroll
+        for (int b = 0; b < kB; ++b) {
+#pragma unroll
+          for (int hp = 0; hp < GP; ++hp)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc2[hp][e] = f2_fma(P[b][hp], V[b][e], acc2[hp][e]);
+          if constexpr (G % 2) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc1[e] = __fmaf_rn(P1[b], f2_lo(V[b][e]), acc1[e]);
+          }
+        }
+      }
+      for (; jj < lim; ++jj) {
         const ulonglong2* vv = reinterpret_cast<const ulonglong2*>(vf + jj * kVS2 + 8 * u);  // (v_e, v_e), e = 0..3
         const ulonglong2 va = vv[0], vb = vv[1];
         const float* pp = pt + jj * nqp + r * Gm::GA;
@@ -460,7 +488,7 @@ void run_attention(const float* q, int H, int KV, float scale, const AttnLayer& 
   }
   if (p.n_sg > 0 && p.kchunks > 0) k_att_scores<D><<<dim3(p.kchunks, p.n_sg, KV), kScoreKeys, qsmem, s>>>(a);
   k_att_extras<D><<<dim3(p.n, (H + 3) / 4), 128, 0, s>>>(a);
-  if (p.n_sg > 0) k_att_softmax<<<dim3(p.n_sg, KV), 512, 0, s>>>(a);
+  if (p.n_sg > 0) k_att_softmax<<<dim3(p.n_sg, KV, (kQMax / (H / KV) * att_ga(H / KV) + 31) / 32), 512, 0, s>>>(a);
   switch (a.G) {
     case 1: launch_pv<D, 1>(a, s); break;
     case 2: launch_pv<D, 2>(a, s); break;
