@@ -315,6 +315,7 @@ int mk_matmul(const mk_weight* w, const float* dev_x, int n, float* dev_y, int s
     const int64_t slice = static_cast<int64_t>(n) * w->w.rows;
     mkb::DevBuf slices(split > 1 ? static_cast<size_t>(split) * slice * 4 : 0);
     float* out = split > 1 ? slices.get<float>() : dev_y;
+    if (split == 1) mkb::gemm_tune(w->w, t.act, n, out, w->w.rows, status.get<int>(), s);
     mkb::launch_gemm(w->w, t.act, n, out, w->w.rows, slice, split, status.get<int>(), s);
     if (split > 1) mkb::launch_sum_slices(mkb::Slices{out, split, slice}, w->w.rows, n, static_cast<int>(w->w.rows), dev_y, s);
     mkb::cuda_check(cudaGetLastError(), "matmul");

@@ -428,10 +428,10 @@ void Model::alloc_kv(int n_ctx, int n_seq, int max_batch) {
   const int G = c.n_head / c.n_head_kv;
   sg_rows_ = std::max(1, attn_qmax() / G);
   // attention workspace: the key-major score tables of every sub-group (at most one per token, each row padded to
-  // att_nqp slots), the extra keys' scores, 1 / sums and the output rows
+  // att_nqp slots, plus a chunk-maximum row per 128 keys), the extra keys' scores, 1 / sums and the output rows
   {
     const int GA = (G + 1) / 2 * 2;
-    attn_st_cap_ = static_cast<int64_t>(KVl_) * n_ctx * max_batch * (GA + 4);
+    attn_st_cap_ = static_cast<int64_t>(KVl_) * (n_ctx + attn_key_chunks(n_ctx)) * max_batch * (GA + 4);
     attn_ex_stride_ = max_batch;
     const int64_t ex = static_cast<int64_t>(max_batch) * Hl_ * attn_ex_stride_;
     const int64_t inv = static_cast<int64_t>(max_batch) * Hl_, att = static_cast<int64_t>(max_batch) * Hl_ * D;
@@ -587,6 +587,23 @@ void Model::allreduce(float* buf, size_t count) {
 
 void Model::gemm(const DevWeight& w, int split, int n, float* y, int64_t ldy, int64_t slice) {
   launch_gemm(w, act_, n, y, ldy, slice, split, status_, stream_);
+}
+
+void Model::tune_gemms(int n, int m) {
+  const Layer& L = layers_[0];  // every layer has the same shapes
+  const int E = cfg_.n_embd;
+  act_.nt8 = act_tiles(n);
+  for (int i = 0; i < L.n_qkv; ++i)
+    if (L.qkv_split[i] == 1) gemm_tune(L.qkv[i], act_, n, yqkv_ + L.qkv_col[i], qkv_ld_, status_, stream_);
+  if (L.wo_split == 1) gemm_tune(L.wo, act_, n, part_, E, status_, stream_);
+  for (int i = 0; i < L.n_gu; ++i)
+    if (L.gu_split[i] == 1)
+      gemm_tune(L.gu[i], act_, n, ygu_ + L.gu_col[i], 2 * static_cast<int64_t>(Fl_), status_, stream_);
+  if (L.down_split == 1) gemm_tune(L.down, act_, n, part_, E, status_, stream_);
+  if (m > 0) {
+    act_.nt8 = act_tiles(m);
+    gemm_tune(lm_head_, act_, m, logits_, Vl_, status_, stream_);
+  }
 }
 
 void Model::run_forward(int n, int m) {
@@ -749,6 +766,8 @@ void Model::forward(const mk_batch_token* batch, int n, float* host_logits) {
   }
   plan_.status = status_;
 
+  // kernel shapes measured on first sight of a batch shape (scratch operands; every shape gives identical results)
+  if (profile_ || graphs_.find(std::make_tuple(n, m, n_sg)) == graphs_.end()) tune_gemms(n, m);
   if (profile_) {
     run_forward(n, m);
     cuda_check(cudaStreamSynchronize(stream_), "forward");

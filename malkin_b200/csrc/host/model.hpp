@@ -128,6 +128,7 @@ class Model {
   };
 
   void run_forward(int n, int m);               // kernel sequence (captured or direct)
+  void tune_gemms(int n, int m);                // measured kernel shapes for n rows (m output rows), before capture
   // y slices = W x: slice s at y + s * slice (split-K partial sums, summed in order by the consumer)
   void gemm(const DevWeight& w, int split, int n, float* y, int64_t ldy, int64_t slice);
   void allreduce(float* buf, size_t count);

@@ -99,20 +99,26 @@ __global__ void k_qkv_post(Slices qk, int v_n, int64_t v_col0, int64_t ldy, int 
 //   inv  = 1 / reduce16(sums), sum l adds e_j for j = l, l + 16, ... in order
 //   out  = (acc over j in order: acc = fma(e_j * v_scale_j, v_j, acc), from 0) * inv
 // Every float operation is malkin's, in malkin's order, so the output is bit-identical. Four kernels:
-//   k_att_scores   one thread per prefix key of a (sub-group, KV head): the key row in registers, every query vector
-//                  of the sub-group (rows x G heads) broadcast from shared memory; scores into the sub-group's
-//                  key-major table ST[j][slot] (slot = row * GA + head, GA = G rounded up to even)
+//   k_att_scores   a thread pair per two prefix keys of a (sub-group, KV head, half of its rows): each thread holds
+//                  eight of the 16 chains of both keys in registers, the query vectors come from shared memory; the
+//                  scores of 128 keys are staged in shared memory, written out as whole rows of the sub-group's
+//                  key-major table ST[j][slot] (slot = row * GA + head, GA = G rounded up to even), followed by
+//                  the chunk's maximum of every slot (a row after the table's maxk rows per 128 keys)
 //   k_att_extras   one warp per (t, h): the scores of the token's extra (ancestor) keys, as 16 chains on a half-warp
-//   k_att_softmax  one CTA per (sub-group, KV head): warp l runs malkin's vector lane l - the lane-striped maximum and
-//                  sum of every slot - with 32 slots side by side, then e_j * v_scale_j in place of s_j and 1 / sum
-//   k_att_pv       one CTA per (sub-group, KV head, 32 of the D values): TMA bulk copies bring key tiles of the
-//                  probabilities (ST rows) and of the int8 values two tiles ahead; the chains of two heads advance
-//                  in one f32x2 FMA (each lane of the pair its own IEEE fma, in key order); then each row's extras.
+//   k_att_softmax  one CTA per (sub-group, KV head, 32 slots): warp l runs malkin's vector lane l - the lane-striped
+//                  sum of every slot - with 32 slots side by side, the maximum from the chunk maxima; then
+//                  e_j * v_scale_j in place of s_j and 1 / sum
+//   k_att_pv       one CTA per (sub-group, KV head, 32 of the D values): a producer warp keeps key tiles of the
+//                  probabilities (ST rows) and of the int8 values in flight with TMA bulk copies and converts each
+//                  landed value tile to floats; the consumer warps advance the chains of two heads in one f32x2 FMA
+//                  (each lane of the pair its own IEEE fma, in key order); then each row's extras.
 constexpr int kQMax = 96;         // query vectors (rows x G) per sub-group
-constexpr int kScoreKeys = 128;   // keys (threads) per score CTA
-constexpr int kPvTile = 64;       // keys per P.V tile
+constexpr int kScoreKeys = 128;   // keys per score CTA (and per chunk maximum)
+constexpr int kScoreParts = 2;    // score CTAs that split a sub-group's rows
+constexpr int kPvTile = 32;       // keys per P.V stage
+constexpr int kPvStages = 3;      // P.V ring depth
 constexpr int kPvSlice = 32;      // output values per P.V CTA
-constexpr int kErrAttWait = 24;   // status code: a P.V tile copy never landed
+constexpr int kErrAttWait = 24;   // status code: a P.V stage never landed or was never released
 
 struct AttArgs {
   const float* q;  // [n][H][D]
@@ -126,77 +132,140 @@ struct AttArgs {
 // Slots of a sub-group's key-major probability table: row r, head g at r * GA + g; rows padded to 4 slots.
 __host__ __device__ constexpr int att_ga(int G) { return (G + 1) / 2 * 2; }
 __host__ __device__ constexpr int att_nqp(int rows, int G) { return (rows * att_ga(G) + 3) / 4 * 4; }
+// chunk maxima rows after a table of maxk key rows
+__host__ __device__ constexpr int att_nch(int maxk) { return (maxk + kScoreKeys - 1) / kScoreKeys; }
+// rows of one score CTA (a part of the sub-group) and its staging tile stride (odd: 32 keys at one slot, 32 banks)
+__host__ __device__ constexpr int sc_part_rows(int G) { return (kQMax / G + kScoreParts - 1) / kScoreParts; }
+__host__ __device__ constexpr int sc_stride(int G) { return sc_part_rows(G) * att_ga(G) + 1; }
+__host__ __device__ constexpr int sc_smem(int G, int D) {
+  return (sc_part_rows(G) * G * D + kScoreKeys * sc_stride(G)) * 4;
+}
 
 __device__ __forceinline__ float i8f(int8_t v) { return static_cast<float>(v); }
 
-// ST of (sub-group sg, KV head kvh): maxk_sg rows of nqp floats.
+// ST of (sub-group sg, KV head kvh): maxk key rows of nqp floats, then att_nch(maxk) chunk-maximum rows.
 __device__ __forceinline__ float* st_of(const AttArgs& a, int sg, int kvh, int maxk, int nqp) {
-  return a.p.st + a.p.st_off[sg] + static_cast<int64_t>(kvh) * maxk * nqp;
+  return a.p.st + a.p.st_off[sg] + static_cast<int64_t>(kvh) * (maxk + att_nch(maxk)) * nqp;
 }
 
-// grid (key chunks, n_sg, KV), block kScoreKeys; dynamic smem: kQMax x D query floats + kQMax key limits. The 16 chains
-// of a score run as 8 packed f32x2 pairs (chains 2m and 2m + 1 share an instruction; each lane of the pair is its
-// own IEEE operation, so the values are malkin's) and the horizontal sum is done pairwise the same way.
+// grid (key chunks, n_sg x kScoreParts, KV), block 2 x kScoreKeys / KP. Thread c (0, 1) of a pair holds the chain
+// pairs m = c, c + 2, c + 4, c + 6 (chains 2m, 2m + 1, one f32x2 register per step of 16 values) of KP keys, so a
+// 16-byte load of the query vector feeds 2 KP packed FMAs. malkin's horizontal sum pairs chain i + 8 with i, then
+// i + 4 with i, then (0 + 2, 1 + 3), then 0 + 1: in chain pairs that is m + 4 with m, m + 2 with m (both inside a
+// thread), then pair 0 with pair 1 (across the thread pair) and the two lanes - the same operations in the same
+// order, so the scores are malkin's.
 template <int D>
-__global__ void __launch_bounds__(kScoreKeys) k_att_scores(AttArgs a) {
-  constexpr int DC = D / 16;
-  extern __shared__ __align__(16) float qs[];
-  int* nkq = reinterpret_cast<int*>(qs + kQMax * D);
-  const int sg = blockIdx.y, kvh = blockIdx.z;
-  const int t0 = a.p.sg_first[sg], t1 = a.p.sg_first[sg + 1];
-  const int nq = (t1 - t0) * a.G;
+constexpr int sc_kp() { return D <= 128 ? 2 : 1; }
+// three CTAs per SM for D <= 128 (167 registers, no spills): measured faster than two CTAs with more registers and
+// than one key per thread
+template <int D>
+__global__ void __launch_bounds__(2 * kScoreKeys / sc_kp<D>(), D <= 128 ? 3 : 1) k_att_scores(AttArgs a) {
+  constexpr int DC = D / 16, KP = sc_kp<D>(), NTH = 2 * kScoreKeys / KP;
+  extern __shared__ __align__(16) float qs[];  // [v][D] permuted per step: (c, mm, lane) at c * 8 + mm * 2 + lane
+  __shared__ int64_t qrow[kQMax];              // global offset of each query vector of this part
+  const int G = a.G, GA = att_ga(G);
+  const int sg = blockIdx.y / kScoreParts, part = blockIdx.y % kScoreParts, kvh = blockIdx.z;
+  const int t0 = a.p.sg_first[sg], nr = a.p.sg_first[sg + 1] - t0;
   const int maxk = a.p.sg_maxk[sg];
   const int j0 = blockIdx.x * kScoreKeys;
-  if (j0 >= maxk) return;
-  for (int i = threadIdx.x; i < nq * D; i += kScoreKeys) {
-    const int v = i / D, d = i % D;
-    qs[i] = a.q[(static_cast<size_t>(t0 + v / a.G) * a.H + kvh * a.G + v % a.G) * D + d];
-  }
-  for (int v = threadIdx.x; v < nq; v += kScoreKeys) nkq[v] = a.p.n_keys[t0 + v / a.G];
+  const int pr = (nr + kScoreParts - 1) / kScoreParts;
+  const int ra = part * pr, rb = min(nr, ra + pr);
+  if (j0 >= maxk || ra >= rb) return;
+  const int nq = (rb - ra) * G, sst = sc_stride(G);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* sc = qs + sc_part_rows(G) * G * D;  // [kScoreKeys][sst]: scores of this CTA's keys at its slots
+  for (int r = warp; r < rb - ra; r += NTH / 32)
+    if (lane < G) qrow[r * G + lane] = (static_cast<int64_t>(t0 + ra + r) * a.H + kvh * G + lane) * D;
   __syncthreads();
-  const int j = j0 + threadIdx.x;
-  if (j >= maxk) return;
-  const size_t row = static_cast<size_t>(kvh) * a.L.n_rows + a.p.kv_base[t0] + j;
-  f2 kf[D / 2];  // (k[2m], k[2m + 1])
-  {
-    const int4* kr = reinterpret_cast<const int4*>(a.L.k + row * D);
+  // query vectors, 4 values per load: values e .. e + 3 are pairs m, m + 1 (m even) of a 16-value step
+  for (int i = threadIdx.x; i < nq * (D / 4); i += NTH) {
+    const int v = i / (D / 4), e = 4 * (i % (D / 4)), m = (e & 15) >> 1;
+    const float4 x = *reinterpret_cast<const float4*>(a.q + qrow[v] + e);
+    float* dst = qs + v * D + (e & ~15) + (m >> 1) * 2;
+    *reinterpret_cast<float2*>(dst) = make_float2(x.x, x.y);      // pair m: c = 0
+    *reinterpret_cast<float2*>(dst + 8) = make_float2(x.z, x.w);  // pair m + 1: c = 1
+  }
+  const int pi = threadIdx.x >> 1, c = threadIdx.x & 1;
+  const size_t hb = static_cast<size_t>(kvh) * a.L.n_rows + a.p.kv_base[t0];
+  f2 kf[KP][DC][4];
 #pragma unroll
-    for (int c = 0; c < D / 16; ++c) {
-      const int4 w = kr[c];
-      const int8_t* b = reinterpret_cast<const int8_t*>(&w);
+  for (int k = 0; k < KP; ++k) {
+    const int j = min(j0 + pi * KP + k, maxk - 1);  // keys past the table compute on a real row and are not stored
+    const int4* kr = reinterpret_cast<const int4*>(a.L.k + (hb + j) * D);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) kf[8 * c + e] = f2_make(i8f(b[2 * e]), i8f(b[2 * e + 1]));
+    for (int i = 0; i < DC; ++i) {
+      const int4 w = kr[i];
+      const int ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int mm = 0; mm < 4; ++mm) {  // pair m = c + 2 mm: bytes 2m, 2m + 1 = half c of word mm
+        const int h = ws[mm] >> (16 * c);
+        kf[k][i][mm] = f2_make(i8f(static_cast<int8_t>(h & 0xFF)), i8f(static_cast<int8_t>((h >> 8) & 0xFF)));
+      }
     }
   }
-  const float ks = __fmul_rn(a.L.ks[row], a.scale);
-  const int ga = att_ga(a.G), nqp = att_nqp(t1 - t0, a.G);
-  float* srow = st_of(a, sg, kvh, maxk, nqp) + static_cast<int64_t>(j) * nqp;
-  for (int v = 0; v < nq; ++v) {
-    if (j >= nkq[v]) continue;
-    const ulonglong2* qv = reinterpret_cast<const ulonglong2*>(qs + v * D);  // pairs (q[2m], q[2m + 1])
-    f2 acc[8];
+  const int jl = pi * KP + (KP == 2 ? c : 0);  // the key this thread finishes
+  const float ksc = __fmul_rn(a.L.ks[hb + min(j0 + jl, maxk - 1)], a.scale);
+  __syncthreads();
+  float* srow = sc + jl * sst;
+  for (int r = 0; r < rb - ra; ++r) {
+    for (int g = 0; g < G; ++g) {
+      const ulonglong2* qv = reinterpret_cast<const ulonglong2*>(qs + (r * G + g) * D + c * 8);
+      f2 acc[KP][4];
+      {
+        const ulonglong2 x0 = qv[0], x1 = qv[1];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const ulonglong2 x = qv[c];
-      acc[2 * c] = f2_mul(x.x, kf[2 * c]);
-      acc[2 * c + 1] = f2_mul(x.y, kf[2 * c + 1]);
-    }
-#pragma unroll
-    for (int i = 1; i < DC; ++i)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const ulonglong2 x = qv[4 * i + c];
-        acc[2 * c] = f2_fma(x.x, kf[8 * i + 2 * c], acc[2 * c]);
-        acc[2 * c + 1] = f2_fma(x.y, kf[8 * i + 2 * c + 1], acc[2 * c + 1]);
+        for (int k = 0; k < KP; ++k) {
+          acc[k][0] = f2_mul(x0.x, kf[k][0][0]);
+          acc[k][1] = f2_mul(x0.y, kf[k][0][1]);
+          acc[k][2] = f2_mul(x1.x, kf[k][0][2]);
+          acc[k][3] = f2_mul(x1.y, kf[k][0][3]);
+        }
       }
-    // tree16 in pairs: lanes i + 8 and i (pairs p + 4 and p), then i + 4 and i, then (0 + 2, 1 + 3), then 0 + 1
-    f2 b2[4], c2[2];
 #pragma unroll
-    for (int p = 0; p < 4; ++p) b2[p] = f2_add(acc[p + 4], acc[p]);
+      for (int i = 1; i < DC; ++i) {
+        const ulonglong2 x0 = qv[4 * i], x1 = qv[4 * i + 1];
 #pragma unroll
-    for (int p = 0; p < 2; ++p) c2[p] = f2_add(b2[p + 2], b2[p]);
-    const f2 d2 = f2_add(c2[0], c2[1]);
-    srow[(v / a.G) * ga + v % a.G] = __fmul_rn(__fadd_rn(f2_lo(d2), f2_hi(d2)), ks);
+        for (int k = 0; k < KP; ++k) {
+          acc[k][0] = f2_fma(x0.x, kf[k][i][0], acc[k][0]);
+          acc[k][1] = f2_fma(x0.y, kf[k][i][1], acc[k][1]);
+          acc[k][2] = f2_fma(x1.x, kf[k][i][2], acc[k][2]);
+          acc[k][3] = f2_fma(x1.y, kf[k][i][3], acc[k][3]);
+        }
+      }
+      f2 c2[KP];  // level 2 of the tree for pair c: (pairs c+2, c+6) + (pairs c, c+4)
+#pragma unroll
+      for (int k = 0; k < KP; ++k) c2[k] = f2_add(f2_add(acc[k][3], acc[k][1]), f2_add(acc[k][2], acc[k][0]));
+      f2 mine, other;
+      if constexpr (KP == 2) {  // thread c finishes key c of the pair
+        mine = c ? c2[1] : c2[0];
+        other = __shfl_xor_sync(0xffffffffu, c ? c2[0] : c2[1], 1);
+      } else {
+        mine = c2[0];
+        other = __shfl_xor_sync(0xffffffffu, c2[0], 1);
+      }
+      const f2 d2 = f2_add(mine, other);
+      if (KP == 2 || c == 0) srow[g] = __fmul_rn(__fadd_rn(f2_lo(d2), f2_hi(d2)), ksc);
+    }
+    srow += GA;
+  }
+  __syncthreads();
+  // write-out: rows j0 .. j0 + kn - 1 of the table at this part's slots, a warp per row (GA even: 8-byte pairs)
+  const int nqp = att_nqp(nr, G);
+  float* st = st_of(a, sg, kvh, maxk, nqp);
+  const int kn = min(kScoreKeys, maxk - j0), np = (rb - ra) * GA / 2;
+  for (int k = warp; k < kn; k += NTH / 32) {
+    float2* dst = reinterpret_cast<float2*>(st + static_cast<int64_t>(j0 + k) * nqp + ra * GA);
+    for (int q = lane; q < np; q += 32) dst[q] = make_float2(sc[k * sst + 2 * q], sc[k * sst + 2 * q + 1]);
+  }
+  // chunk maxima: warp w takes slots w, w + NTH / 32, ...; lane l the keys l, l + 32, ... below the row's n_keys
+  float* pm = st + static_cast<int64_t>(maxk + blockIdx.x) * nqp + ra * GA;
+  for (int sl = warp; sl < (rb - ra) * GA; sl += NTH / 32) {
+    const int r = sl / GA, g = sl - r * GA;
+    const int lim = g < G ? min(kn, a.p.n_keys[t0 + ra + r] - j0) : 0;
+    float mx = -INFINITY;
+    for (int k = lane; k < lim; k += 32) mx = fmaxf(mx, sc[k * sst + sl]);
+    mx = warp_max(mx);
+    if (lane == 0) pm[sl] = mx;
   }
 }
 
@@ -228,219 +297,245 @@ __global__ void __launch_bounds__(128) k_att_extras(AttArgs a) {
 }
 
 // grid (n_sg, KV, slot groups of 32), block 512: warp l (0..15) plays malkin's vector lane l for the CTA's 32 slots
-// (lane = slot): the
-// maximum over the slot's keys (any order), then e_j = exp(s_j - max) and the lane-striped sum over keys j = l, l + 16,
-// ... in order (prefix keys from ST, extras from ex), p_j = e_j * v_scale_j written in place; then 1 / reduce16 of
-// the 16 sums.
+// (lane = slot): the maximum over the slot's keys (any order: the chunk maxima of the score kernel and the extras),
+// then e_j = exp(s_j - max) and the lane-striped sum over keys j = l, l + 16, ... in order (prefix keys from ST,
+// extras from ex), p_j = e_j * v_scale_j written in place; then 1 / reduce16 of the 16 sums.
 __global__ void __launch_bounds__(512) k_att_softmax(AttArgs a) {
   __shared__ float red[16][33];
   const int sg = blockIdx.x, kvh = blockIdx.y;
   const int l = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = a.p.sg_first[sg], rows = a.p.sg_first[sg + 1] - t0;
-  const int maxk = a.p.sg_maxk[sg];
+  const int maxk = a.p.sg_maxk[sg], nch = att_nch(maxk);
   const int ga = att_ga(a.G), nqp = att_nqp(rows, a.G);
   float* st = st_of(a, sg, kvh, maxk, nqp);
+  const float* pm = st + static_cast<int64_t>(maxk) * nqp;
   const size_t hb = static_cast<size_t>(kvh) * a.L.n_rows + a.p.kv_base[t0];
-  for (int s0 = blockIdx.z * 32; s0 < rows * ga && s0 < (blockIdx.z + 1) * 32; s0 += 32) {
-    const int slot = s0 + lane, r = slot / ga, g = slot % ga;
-    const bool valid = r < rows && g < a.G;
-    const int t = t0 + (valid ? r : 0), h = kvh * a.G + (valid ? g : 0);
-    const int n0 = valid ? a.p.n_keys[t] : 0;
-    const int e0 = a.p.anc_off[t], ne = valid ? a.p.anc_off[t + 1] - e0 : 0, nk = n0 + ne;
-    float* er = a.p.ex + (static_cast<size_t>(t) * a.H + h) * a.p.ex_stride;
-    // maximum (of this lane's stripe, then over the 16 stripes)
-    float mx = -INFINITY;
-#pragma unroll 4
-    for (int j = l; j < nk; j += 16) mx = fmaxf(mx, j < n0 ? st[static_cast<int64_t>(j) * nqp + slot] : er[j - n0]);
-    red[l][lane] = mx;
-    __syncthreads();
-    mx = red[0][lane];
+  const int s0 = blockIdx.z * 32;
+  if (s0 >= rows * ga) return;
+  const int slot = s0 + lane, r = slot / ga, g = slot % ga;
+  const bool valid = r < rows && g < a.G;
+  const int t = t0 + (valid ? r : 0), h = kvh * a.G + (valid ? g : 0);
+  const int n0 = valid ? a.p.n_keys[t] : 0;
+  const int e0 = a.p.anc_off[t], ne = valid ? a.p.anc_off[t + 1] - e0 : 0, nk = n0 + ne;
+  float* er = a.p.ex + (static_cast<size_t>(t) * a.H + h) * a.p.ex_stride;
+  // maximum: chunk maxima (chunks with keys below n0) and the extras, striped over the warps
+  float mx = -INFINITY;
+  const int nc = valid ? min(nch, (n0 + kScoreKeys - 1) / kScoreKeys) : 0;
+  for (int cc = l; cc < nc; cc += 16) mx = fmaxf(mx, pm[static_cast<int64_t>(cc) * nqp + slot]);
+  for (int e = l; e < ne; e += 16) mx = fmaxf(mx, er[e]);
+  red[l][lane] = mx;
+  __syncthreads();
+  mx = red[0][lane];
 #pragma unroll
-    for (int i = 1; i < 16; ++i) mx = fmaxf(mx, red[i][lane]);
-    __syncthreads();
-    // lane-striped sum in key order; eight keys of the stripe loaded at once, only the sum runs in sequence
-    float sum = 0.0f;
-    for (int jb = l; jb < nk; jb += 16 * 8) {
-      float sv[8], vv[8];
+  for (int i = 1; i < 16; ++i) mx = fmaxf(mx, red[i][lane]);
+  __syncthreads();
+  // lane-striped sum in key order; sixteen keys of the stripe loaded at once, only the sum runs in sequence
+  constexpr int kU = 16;
+  float sum = 0.0f;
+  for (int jb = l; jb < nk; jb += 16 * kU) {
+    float sv[kU], vv[kU];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int j = jb + 16 * u;
-        sv[u] = j < nk ? (j < n0 ? st[static_cast<int64_t>(j) * nqp + slot] : er[j - n0]) : 0.0f;
-        vv[u] = j < nk ? a.L.vs[j < n0 ? hb + j : hb + a.p.anc[e0 + j - n0]] : 0.0f;
-      }
+    for (int u = 0; u < kU; ++u) {
+      const int j = jb + 16 * u;
+      sv[u] = j < nk ? (j < n0 ? st[static_cast<int64_t>(j) * nqp + slot] : er[j - n0]) : 0.0f;
+      vv[u] = j < nk ? a.L.vs[j < n0 ? hb + j : hb + a.p.anc[e0 + j - n0]] : 0.0f;
+    }
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int j = jb + 16 * u;
-        if (j < nk) {
-          const float e = exp_malkin(__fsub_rn(sv[u], mx));
-          sum = __fadd_rn(sum, e);
-          const float p = __fmul_rn(e, vv[u]);
-          if (j < n0)
-            st[static_cast<int64_t>(j) * nqp + slot] = p;
-          else
-            er[j - n0] = p;
-        }
+    for (int u = 0; u < kU; ++u) {
+      const int j = jb + 16 * u;
+      if (j < nk) {
+        const float e = exp_malkin(__fsub_rn(sv[u], mx));
+        sum = __fadd_rn(sum, e);
+        const float p = __fmul_rn(e, vv[u]);
+        if (j < n0)
+          st[static_cast<int64_t>(j) * nqp + slot] = p;
+        else
+          er[j - n0] = p;
       }
     }
-    red[l][lane] = sum;
-    __syncthreads();
-    if (l == 0 && valid) {
-      float b8[8], c4[4];
+  }
+  red[l][lane] = sum;
+  __syncthreads();
+  if (l == 0 && valid) {
+    float b8[8], c4[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) b8[i] = __fadd_rn(red[i + 8][lane], red[i][lane]);
+    for (int i = 0; i < 8; ++i) b8[i] = __fadd_rn(red[i + 8][lane], red[i][lane]);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) c4[i] = __fadd_rn(b8[i + 4], b8[i]);
-      const float tot = __fadd_rn(__fadd_rn(c4[0], c4[2]), __fadd_rn(c4[1], c4[3]));
-      a.p.inv[static_cast<size_t>(t) * a.H + h] = __fdiv_rn(1.0f, tot);
-    }
-    __syncthreads();
+    for (int i = 0; i < 4; ++i) c4[i] = __fadd_rn(b8[i + 4], b8[i]);
+    const float tot = __fadd_rn(__fadd_rn(c4[0], c4[2]), __fadd_rn(c4[1], c4[3]));
+    a.p.inv[static_cast<size_t>(t) * a.H + h] = __fdiv_rn(1.0f, tot);
   }
 }
 
-// grid (n_sg, KV, D / kPvSlice), block rows x 8 (rows = kQMax / G): thread (r, u) owns values u*4 .. u*4+3 of the
-// slice for the G heads of row t0 + r. Thread 0 keeps two tiles of kPvTile keys in flight with TMA bulk copies (the
-// ST rows and the raw int8 value rows); every thread converts its share of a landed value tile into a shared float
-// buffer holding each value twice (v, v), so one f32x2 FMA advances the chains of two heads (each lane of the pair
-// is its own IEEE fma, in key order: malkin's acc = fma(p_j, v_j, acc)).
-constexpr int kVS2 = 2 * kPvSlice + 8;  // float value buffer row stride (32 values duplicated + padding)
+// grid (n_sg, KV, D / kPvSlice), block 32 + rows x 8 (rows = kQMax / G). Warp 0 is the producer: lane 0 keeps
+// kPvStages tiles of kPvTile keys in flight with TMA bulk copies (the ST rows and the raw int8 value rows), the warp
+// converts the slice of each landed value tile into floats held twice, (v, v), and signals `ready`. Consumer thread
+// (r, u) owns values 4u .. 4u + 3 of the slice for the G heads of row t0 + r: one f32x2 FMA advances the chains of
+// two heads (heads 2i, 2i + 1; for odd G the last pair's second lane is a padding slot whose result is discarded).
+// Each lane of the pair is its own IEEE fma in key order: malkin's acc = fma(p_j, v_j, acc). Converted value row:
+// (v0 v0 v1 v1) of every u in the first 128 bytes, (v2 v2 v3 v3) in the next, so each 16-byte load of a warp
+// reads 128 contiguous bytes.
+constexpr int kVfRow = 2 * kPvSlice;  // floats per converted value row
 template <int D, int G>
 struct PvGeom {
-  static constexpr int ROWS = kQMax / G, NT = ROWS * 8, GA = att_ga(G);
-  static constexpr int NQP = att_nqp(ROWS, G);                // largest P row (floats)
-  static constexpr uint32_t PBYTES = kPvTile * NQP * 4, VBYTES = kPvTile * D;
-  static constexpr uint32_t STAGE = PBYTES + VBYTES;           // one stage: P rows then raw values
-  static constexpr uint32_t VF = 2 * STAGE;                    // float value buffer offset
-  static constexpr uint32_t BAR = VF + kPvTile * kVS2 * 4;     // two mbarriers
-  static constexpr uint32_t SMEM = BAR + 16;
+  static constexpr int ROWS = kQMax / G, CW = (ROWS * 8 + 31) / 32, NT = 32 * (1 + CW);
+  static constexpr int GA = att_ga(G), NQP = att_nqp(ROWS, G);
+  static constexpr uint32_t PB = kPvTile * NQP * 4, VB = kPvTile * D, FB = kPvTile * kVfRow * 4;
+  static constexpr uint32_t STAGE = (PB + VB + FB + 127) / 128 * 128;  // P rows | raw values | converted values
+  static constexpr uint32_t BAR = kPvStages * STAGE;
+  static constexpr uint32_t SMEM = BAR + 3 * kPvStages * 8;
 };
+// Lane 0 of the producer: tile `it` (kPvTile keys from key it * kPvTile) of the P rows and the raw value rows into
+// the stage at stg (values at stg + pb_off), completion counted on bar.
+template <int D>
+__device__ __forceinline__ void pv_issue(uint8_t* stg, uint32_t pb_off, uint64_t* bar, const float* st,
+                                         const int8_t* vsrc, int it, int maxk, int nqp) {
+  const int k0 = it * kPvTile, nkt = min(kPvTile, maxk - k0);
+  const uint32_t pb = static_cast<uint32_t>(nkt) * nqp * 4, vb = static_cast<uint32_t>(nkt) * D;
+  mbar_arrive_expect_tx(bar, pb + vb);
+  bulk_g2s(stg, st + static_cast<int64_t>(k0) * nqp, pb, bar);
+  bulk_g2s(stg + pb_off, vsrc + static_cast<int64_t>(k0) * D, vb, bar);
+}
+
 template <int D, int G>
-__global__ void __launch_bounds__(kQMax / G * 8) k_att_pv(AttArgs a) {
+__global__ void __launch_bounds__(PvGeom<D, G>::NT) k_att_pv(AttArgs a) {
   using Gm = PvGeom<D, G>;
-  constexpr int GP = G / 2;  // head pairs
+  constexpr int GP = Gm::GA / 2;        // head pairs (the last one padded for odd G)
+  constexpr int KB = G <= 4 ? 4 : 2;    // keys whose loads are issued together
   extern __shared__ __align__(128) uint8_t sm[];
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + Gm::BAR);
-  float* vf = reinterpret_cast<float*>(sm + Gm::VF);
+  uint64_t* ready = full + kPvStages;
+  uint64_t* empty = ready + kPvStages;
   const int sg = blockIdx.x, kvh = blockIdx.y, d0 = blockIdx.z * kPvSlice;
-  const int t0 = a.p.sg_first[sg], t1 = a.p.sg_first[sg + 1], nr = t1 - t0;
-  const int r = threadIdx.x >> 3, u = threadIdx.x & 7;
-  const int t = t0 + r;
-  const bool active = r < nr;
+  const int t0 = a.p.sg_first[sg], nr = a.p.sg_first[sg + 1] - t0;
   const int maxk = a.p.sg_maxk[sg];
-  const int n0 = active ? a.p.n_keys[t] : 0;
   const int nqp = att_nqp(nr, G);
   const float* st = st_of(a, sg, kvh, maxk, nqp);
   const size_t hb = static_cast<size_t>(kvh) * a.L.n_rows + a.p.kv_base[t0];
   const int ntiles = (maxk + kPvTile - 1) / kPvTile;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cwarps = (nr * 8 + 31) / 32;  // consumer warps with at least one row
   if (threadIdx.x == 0) {
-    mbar_init(&full[0], 1);
-    mbar_init(&full[1], 1);
+    for (int s = 0; s < kPvStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&ready[s], 32);
+      mbar_init(&empty[s], cwarps);
+    }
     mbar_fence_init();
   }
   __syncthreads();
-  auto issue = [&](int it) {  // thread 0
-    const int s = it & 1, k0 = it * kPvTile, nkt = min(kPvTile, maxk - k0);
-    uint8_t* stg = sm + s * Gm::STAGE;
-    const uint32_t pb = static_cast<uint32_t>(nkt) * nqp * 4, vb = static_cast<uint32_t>(nkt) * D;
-    mbar_arrive_expect_tx(&full[s], pb + vb);
-    bulk_g2s(stg, st + static_cast<int64_t>(k0) * nqp, pb, &full[s]);
-    bulk_g2s(stg + Gm::PBYTES, a.L.v + (hb + k0) * D, vb, &full[s]);
-  };
-  if (threadIdx.x == 0)
-    for (int it = 0; it < 2 && it < ntiles; ++it) issue(it);
-  f2 acc2[GP > 0 ? GP : 1][4];  // (head 2 hp, head 2 hp + 1) at output value e
-  float acc1[4];                // the last head when G is odd
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-#pragma unroll
-    for (int hp = 0; hp < GP; ++hp) acc2[hp][e] = f2_make(0.0f, 0.0f);
-    acc1[e] = 0.0f;
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    const int8_t* vsrc = a.L.v + hb * D;
+    int issued = min(kPvStages, ntiles), landed = 0;
+    if (lane == 0)
+      for (int it = 0; it < issued; ++it) pv_issue<D>(sm + (it % kPvStages) * Gm::STAGE, Gm::PB, &full[it % kPvStages], st, vsrc, it, maxk, nqp);
+    bool ok = true;
+    for (int it = 0; it < ntiles; ++it) {
+      const int s = it % kPvStages;
+      if (!(ok = mbar_wait_warp(&full[s], (it / kPvStages) & 1, a.p.status, kErrAttWait))) break;
+      landed = it + 1;
+      const uint8_t* stg = sm + s * Gm::STAGE;
+      const int8_t* vraw = reinterpret_cast<const int8_t*>(stg + Gm::PB);
+      float4* vf = reinterpret_cast<float4*>(sm + s * Gm::STAGE + Gm::PB + Gm::VB);
+      const int nkt = min(kPvTile, maxk - it * kPvTile);
+      for (int i = lane; i < nkt * 8; i += 32) {
+        const int jj = i >> 3, u = i & 7;
+        const char4 w = *reinterpret_cast<const char4*>(vraw + jj * D + d0 + 4 * u);
+        vf[jj * (kVfRow / 4) + u] = make_float4(i8f(w.x), i8f(w.x), i8f(w.y), i8f(w.y));
+        vf[jj * (kVfRow / 4) + 8 + u] = make_float4(i8f(w.z), i8f(w.z), i8f(w.w), i8f(w.w));
+      }
+      mbar_arrive(&ready[s]);  // every lane: its conversions happen before the consumers' reads
+      // refill the stage of the previous tile once its consumers have released it
+      const int nxt = it - 1 + kPvStages;
+      if (it >= 1 && nxt < ntiles) {
+        const int sp = (it - 1) % kPvStages;
+        if (!(ok = mbar_wait_warp(&empty[sp], ((it - 1) / kPvStages) & 1, a.p.status, kErrAttWait))) break;
+        if (lane == 0) pv_issue<D>(sm + sp * Gm::STAGE, Gm::PB, &full[sp], st, vsrc, nxt, maxk, nqp);
+        issued = nxt + 1;
+      }
+    }
+    if (!ok)  // copies still in flight land before the CTA exits (bounded)
+      for (int it = landed; it < issued; ++it)
+        mbar_wait_warp(&full[it % kPvStages], (it / kPvStages) & 1, nullptr, 0);
+    return;
   }
+  // ---------------- consumers ----------------
+  if (warp - 1 >= cwarps) return;
+  const int ct = threadIdx.x - 32, r = ct >> 3, u = ct & 7;
+  const int t = t0 + r;
+  const bool active = r < nr;
+  const int n0 = active ? a.p.n_keys[t] : 0;
+  f2 acc[GP][4];  // (head 2i, head 2i + 1) at output value 4u + e
+#pragma unroll
+  for (int i = 0; i < GP; ++i)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[i][e] = f2_make(0.0f, 0.0f);
   bool ok = true;
   for (int it = 0; it < ntiles; ++it) {
-    const int s = it & 1, k0 = it * kPvTile, nkt = min(kPvTile, maxk - k0);
-    ok = ok && mbar_wait(&full[s], (it >> 1) & 1, a.p.status, kErrAttWait);
+    const int s = it % kPvStages;
+    const uint32_t par = (it / kPvStages) & 1;
+    if (!(ok = mbar_wait(&full[s], par, a.p.status, kErrAttWait) && mbar_wait(&ready[s], par, a.p.status, kErrAttWait)))
+      break;
     const uint8_t* stg = sm + s * Gm::STAGE;
-    // value slice of the landed tile -> floats, each twice
-    const int8_t* vraw = reinterpret_cast<const int8_t*>(stg + Gm::PBYTES);
-    for (int i = threadIdx.x; i < nkt * (kPvSlice / 4); i += blockDim.x) {
-      const int jj = i / (kPvSlice / 4), c = i % (kPvSlice / 4);
-      const char4 w = *reinterpret_cast<const char4*>(vraw + jj * D + d0 + 4 * c);
-      float4* dst = reinterpret_cast<float4*>(vf + jj * kVS2 + 8 * c);
-      dst[0] = make_float4(i8f(w.x), i8f(w.x), i8f(w.y), i8f(w.y));
-      dst[1] = make_float4(i8f(w.z), i8f(w.z), i8f(w.w), i8f(w.w));
-    }
-    __syncthreads();
-    if (active && ok) {
-      const float* pt = reinterpret_cast<const float*>(stg);
-      const int lim = min(nkt, n0 - k0);
-      // keys in groups of kB: every shared-memory load of the group is issued before its FMAs (which run in key order)
-      constexpr int kB = 4;
-      int jj = 0;
-      for (; jj + kB <= lim; jj += kB) {
-        f2 V[kB][4], P[kB][GP > 0 ? GP : 1];
-        float P1[kB];
+    const float* pt = reinterpret_cast<const float*>(stg) + r * Gm::GA;
+    const float* vf = reinterpret_cast<const float*>(stg + Gm::PB + Gm::VB) + 4 * u;
+    const int lim = active ? min(kPvTile, n0 - it * kPvTile) : 0;
+    int jj = 0;
+    for (; jj + KB <= lim; jj += KB) {
+      f2 V[KB][4], P[KB][GP];
 #pragma unroll
-        for (int b = 0; b < kB; ++b) {
-          const ulonglong2* vv = reinterpret_cast<const ulonglong2*>(vf + (jj + b) * kVS2 + 8 * u);
-          const ulonglong2 va = vv[0], vb = vv[1];
-          V[b][0] = va.x, V[b][1] = va.y, V[b][2] = vb.x, V[b][3] = vb.y;
-          const float* pp = pt + (jj + b) * nqp + r * Gm::GA;
+      for (int b = 0; b < KB; ++b) {
+        const ulonglong2 va = *reinterpret_cast<const ulonglong2*>(vf + (jj + b) * kVfRow);
+        const ulonglong2 vb = *reinterpret_cast<const ulonglong2*>(vf + (jj + b) * kVfRow + 32);
+        V[b][0] = va.x, V[b][1] = va.y, V[b][2] = vb.x, V[b][3] = vb.y;
+        const float* pp = pt + (jj + b) * nqp;
+        if constexpr (Gm::GA % 4 == 0) {
 #pragma unroll
-          for (int hp = 0; hp < GP; ++hp) P[b][hp] = *reinterpret_cast<const f2*>(pp + 2 * hp);
-          P1[b] = (G % 2) ? pp[G - 1] : 0.0f;
-        }
-#pragma unroll
-        for (int b = 0; b < kB; ++b) {
-#pragma unroll
-          for (int hp = 0; hp < GP; ++hp)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) acc2[hp][e] = f2_fma(P[b][hp], V[b][e], acc2[hp][e]);
-          if constexpr (G % 2) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) acc1[e] = __fmaf_rn(P1[b], f2_lo(V[b][e]), acc1[e]);
+          for (int i = 0; i < GP / 2; ++i) {
+            const ulonglong2 x = reinterpret_cast<const ulonglong2*>(pp)[i];
+            P[b][2 * i] = x.x, P[b][2 * i + 1] = x.y;
           }
+        } else {
+#pragma unroll
+          for (int i = 0; i < GP; ++i) P[b][i] = reinterpret_cast<const f2*>(pp)[i];
         }
       }
-      for (; jj < lim; ++jj) {
-        const ulonglong2* vv = reinterpret_cast<const ulonglong2*>(vf + jj * kVS2 + 8 * u);  // (v_e, v_e), e = 0..3
-        const ulonglong2 va = vv[0], vb = vv[1];
-        const float* pp = pt + jj * nqp + r * Gm::GA;
-        const f2 V[4] = {va.x, va.y, vb.x, vb.y};
 #pragma unroll
-        for (int hp = 0; hp < GP; ++hp) {
-          const f2 P = *reinterpret_cast<const f2*>(pp + 2 * hp);  // (p_2hp, p_2hp+1)
+      for (int b = 0; b < KB; ++b)
 #pragma unroll
-          for (int e = 0; e < 4; ++e) acc2[hp][e] = f2_fma(P, V[e], acc2[hp][e]);
-        }
-        if constexpr (G % 2) {
-          const float p = pp[G - 1];
+        for (int i = 0; i < GP; ++i)
 #pragma unroll
-          for (int e = 0; e < 4; ++e) acc1[e] = __fmaf_rn(p, f2_lo(V[e]), acc1[e]);
-        }
+          for (int e = 0; e < 4; ++e) acc[i][e] = f2_fma(P[b][i], V[b][e], acc[i][e]);
+    }
+    for (; jj < lim; ++jj) {
+      const ulonglong2 va = *reinterpret_cast<const ulonglong2*>(vf + jj * kVfRow);
+      const ulonglong2 vb = *reinterpret_cast<const ulonglong2*>(vf + jj * kVfRow + 32);
+      const f2 V[4] = {va.x, va.y, vb.x, vb.y};
+      const f2* pp = reinterpret_cast<const f2*>(pt + jj * nqp);
+#pragma unroll
+      for (int i = 0; i < GP; ++i) {
+        const f2 P = pp[i];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[i][e] = f2_fma(P, V[e], acc[i][e]);
       }
     }
-    __syncthreads();  // stage s and the value buffer are free
-    if (threadIdx.x == 0 && it + 2 < ntiles && ok) issue(it + 2);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
   }
   if (!active || !ok) return;
   // the row's extra keys, in order
   const int e0 = a.p.anc_off[t], ne = a.p.anc_off[t + 1] - e0;
+  const float* pr = a.p.ex + (static_cast<size_t>(t) * a.H + kvh * G) * a.p.ex_stride;
   for (int e = 0; e < ne; ++e) {
-    const size_t row = hb + a.p.anc[e0 + e];
-    const int8_t* vr = a.L.v + row * D + d0 + 4 * u;
+    const int8_t* vr = a.L.v + (hb + a.p.anc[e0 + e]) * D + d0 + 4 * u;
     const f2 V[4] = {f2_make(i8f(vr[0]), i8f(vr[0])), f2_make(i8f(vr[1]), i8f(vr[1])),
                      f2_make(i8f(vr[2]), i8f(vr[2])), f2_make(i8f(vr[3]), i8f(vr[3]))};
-    const float* pr = a.p.ex + (static_cast<size_t>(t) * a.H + kvh * G) * a.p.ex_stride + e;
 #pragma unroll
-    for (int hp = 0; hp < GP; ++hp) {
-      const f2 P = f2_make(pr[(2 * hp) * a.p.ex_stride], pr[(2 * hp + 1) * a.p.ex_stride]);
+    for (int i = 0; i < GP; ++i) {
+      const f2 P = f2_make(pr[(2 * i) * a.p.ex_stride + e], 2 * i + 1 < G ? pr[(2 * i + 1) * a.p.ex_stride + e] : 0.0f);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) acc2[hp][q] = f2_fma(P, V[q], acc2[hp][q]);
-    }
-    if constexpr (G % 2) {
-      const float p = pr[(G - 1) * a.p.ex_stride];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) acc1[q] = __fmaf_rn(p, f2_lo(V[q]), acc1[q]);
+      for (int q = 0; q < 4; ++q) acc[i][q] = f2_fma(P, V[q], acc[i][q]);
     }
   }
 #pragma unroll
@@ -449,11 +544,7 @@ __global__ void __launch_bounds__(kQMax / G * 8) k_att_pv(AttArgs a) {
     const float iv = a.p.inv[static_cast<size_t>(t) * a.H + h];
     float o[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float x = (G % 2 && g == G - 1) ? acc1[e] : ((g & 1) ? f2_hi(acc2[g / 2 < GP ? g / 2 : 0][e])
-                                                                  : f2_lo(acc2[g / 2 < GP ? g / 2 : 0][e]));
-      o[e] = __fmul_rn(x, iv);
-    }
+    for (int e = 0; e < 4; ++e) o[e] = __fmul_rn((g & 1) ? f2_hi(acc[g / 2][e]) : f2_lo(acc[g / 2][e]), iv);
     *reinterpret_cast<float4*>(a.out + (static_cast<size_t>(t) * a.H + h) * D + d0 + 4 * u) =
         make_float4(o[0], o[1], o[2], o[3]);
   }
@@ -478,17 +569,20 @@ void run_attention(const float* q, int H, int KV, float scale, const AttnLayer& 
                    const ActQ& act, cudaStream_t s) {
   AttArgs a{q, H, KV, H / KV, scale, L, p, out ? out : p.att};
   if (p.n <= 0) return;
-  const size_t qsmem = kQMax * D * sizeof(float) + kQMax * sizeof(int);
+  constexpr int KP = sc_kp<D>();
   static bool attr[kMaxDevices] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < kMaxDevices && !attr[dev]) {
-    cudaFuncSetAttribute(k_att_scores<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(qsmem));
+    int mx = 0;
+    for (int g = 1; g <= 8; ++g) mx = std::max(mx, sc_smem(g, D));
+    cudaFuncSetAttribute(k_att_scores<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
     attr[dev] = true;
   }
-  if (p.n_sg > 0 && p.kchunks > 0) k_att_scores<D><<<dim3(p.kchunks, p.n_sg, KV), kScoreKeys, qsmem, s>>>(a);
+  if (p.n_sg > 0 && p.kchunks > 0)
+    k_att_scores<D><<<dim3(p.kchunks, p.n_sg * kScoreParts, KV), 2 * kScoreKeys / KP, sc_smem(a.G, D), s>>>(a);
   k_att_extras<D><<<dim3(p.n, (H + 3) / 4), 128, 0, s>>>(a);
-  if (p.n_sg > 0) k_att_softmax<<<dim3(p.n_sg, KV, (kQMax / (H / KV) * att_ga(H / KV) + 31) / 32), 512, 0, s>>>(a);
+  if (p.n_sg > 0) k_att_softmax<<<dim3(p.n_sg, KV, (kQMax / a.G * att_ga(a.G) + 31) / 32), 512, 0, s>>>(a);
   switch (a.G) {
     case 1: launch_pv<D, 1>(a, s); break;
     case 2: launch_pv<D, 2>(a, s); break;
@@ -510,7 +604,7 @@ int attn_qmax() { return kQMax; }
 int attn_key_chunks(int n_ctx) { return (n_ctx + kScoreKeys - 1) / kScoreKeys; }
 
 int64_t attn_st_floats(int rows, int G, int KV, int maxk) {
-  return static_cast<int64_t>(KV) * maxk * att_nqp(rows, G);
+  return static_cast<int64_t>(KV) * (maxk + att_nch(maxk)) * att_nqp(rows, G);
 }
 
 void launch_qkv_post(Slices qk, int v_n, int64_t v_col0, int64_t ldy, int n, int H, int KV, int D, const float* q_norm,

@@ -26,6 +26,10 @@
 #include <string>
 #include <array>
 #include <utility>
+#include <map>
+#include <mutex>
+#include <tuple>
+#include <vector>
 
 #include "common.cuh"
 #include "kernels.hpp"
@@ -528,6 +532,11 @@ Plan plan_for(const DevWeight& w, int n, int nt8, int split) {
           return Plan{i, (tiles + nt - 1) / nt};
         }
   }
+  // the measured shape (gemm_tune)
+  if (const int ch = gemm_choice(w, n); ch >= 0 && ch < kVariants) {
+    const int nt = (kConsumers / tab[ch].wp) * tab[ch].ntw;
+    return Plan{ch, (tiles + nt - 1) / nt};
+  }
   int dev = 0;
   cudaGetDevice(&dev);
   const int sms = dev_info(dev).sms;
@@ -555,7 +564,110 @@ Plan plan_for(const DevWeight& w, int n, int nt8, int split) {
   return best;
 }
 
+// ---- kernel-shape tuning ----
+using TuneKey = std::tuple<int, uint32_t, int, int64_t, int, int>;  // device, type, layout, rows, k units, tiles
+std::mutex g_tune_mu;
+std::map<TuneKey, int> g_tuned;
+thread_local int g_force = -1;
+constexpr size_t kFlushBytes = size_t{256} << 20;  // > L2 (126 MB)
+
+TuneKey tune_key(const DevWeight& w, int n) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return TuneKey{dev, w.type, w.layout, w.rows, w.kunits, (n + 7) / 8};
+}
+
+void* flush_buffer(int dev) {
+  static void* buf[kMaxDevices] = {};
+  static bool tried[kMaxDevices] = {};
+  if (dev >= kMaxDevices) return nullptr;
+  if (!tried[dev]) {
+    tried[dev] = true;
+    if (cudaMalloc(&buf[dev], kFlushBytes) != cudaSuccess) {
+      cudaGetLastError();
+      buf[dev] = nullptr;
+    }
+  }
+  return buf[dev];
+}
+
 }  // namespace
+
+int gemm_choice(const DevWeight& w, int n) {
+  if (g_force >= 0) return g_force;
+  std::lock_guard<std::mutex> lk(g_tune_mu);
+  const auto it = g_tuned.find(tune_key(w, n));
+  return it == g_tuned.end() ? -1 : it->second;
+}
+
+void gemm_tune(const DevWeight& w, const ActQ& act, int n, float* y, int64_t ldy, int* status, cudaStream_t s) {
+  static const bool off = [] {
+    const char* e = std::getenv("MALKIN_B200_GEMM_TUNE");
+    return e && std::string(e) == "0";
+  }();
+  if (off || n <= 0 || w.rows <= 0 || w.kunits <= 0) return;
+  if (w.layout != kLayoutTc && w.type != 8 && w.type != 12 && w.type != 14) return;
+  if (gemm_choice(w, n) >= 0) return;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return;
+  }
+  const int tiles = (n + 7) / 8;
+  std::vector<int> cand;
+  if (w.layout == kLayoutTc) {  // pass sizes: multiples of 16 up to the one that covers n at once
+    const int npad = act.nt8 * 8;
+    for (int N = 16; N <= gemm_tc_max_tokens() && N < n + 16; N += 16)
+      if (static_cast<int64_t>((n + N - 1) / N) * N <= npad) cand.push_back(N);
+  } else {  // panel variants with at most about twice the token columns needed
+    const auto& tab = table_of(w.type);
+    for (int i = 0; i < kVariants; ++i)
+      if ((kConsumers / tab[i].wp) * tab[i].ntw <= std::max(8, 2 * tiles + 1)) cand.push_back(i);
+  }
+  if (cand.empty()) return;
+  const TuneKey key = tune_key(w, n);
+  if (cand.size() == 1) {
+    std::lock_guard<std::mutex> lk(g_tune_mu);
+    g_tuned[key] = cand[0];
+    return;
+  }
+  void* flush = flush_buffer(std::get<0>(key));
+  constexpr int kReps = 2;
+  const size_t C = cand.size();
+  std::vector<cudaEvent_t> ev(2 * C * kReps, nullptr);
+  bool ok = true;
+  for (auto& e : ev) ok = ok && cudaEventCreate(&e) == cudaSuccess;
+  for (int r = 0; r < kReps && ok; ++r)
+    for (size_t c = 0; c < C && ok; ++c) {
+      if (flush) ok = cudaMemsetAsync(flush, r + 1, kFlushBytes, s) == cudaSuccess;
+      g_force = cand[c];
+      ok = ok && cudaEventRecord(ev[2 * (r * C + c)], s) == cudaSuccess;
+      launch_gemm(w, act, n, y, ldy, 0, 1, status, s);
+      ok = ok && cudaGetLastError() == cudaSuccess;
+      ok = ok && cudaEventRecord(ev[2 * (r * C + c) + 1], s) == cudaSuccess;
+      g_force = -1;
+    }
+  ok = ok && cudaStreamSynchronize(s) == cudaSuccess;
+  int best = -1;
+  float best_ms = 0.0f;
+  for (size_t c = 0; c < C && ok; ++c) {
+    float t = 0.0f;
+    for (int r = 0; r < kReps; ++r) {
+      float ms = 0.0f;
+      if (cudaEventElapsedTime(&ms, ev[2 * (r * C + c)], ev[2 * (r * C + c) + 1]) != cudaSuccess) ok = false;
+      t = r == 0 ? ms : std::min(t, ms);
+    }
+    if (best < 0 || t < best_ms) best = cand[c], best_ms = t;
+  }
+  for (auto& e : ev)
+    if (e) cudaEventDestroy(e);
+  if (!ok) {
+    cudaGetLastError();
+    return;
+  }
+  std::lock_guard<std::mutex> lk(g_tune_mu);
+  g_tuned[key] = best;
+}
 
 // Split-K is never chosen automatically: token passes and narrow tiles fill the SMs (plan_for) and keep every
 // (row, token) sum in malkin's block order, so results are bit-identical to its compact panel kernels. An explicit

@@ -428,6 +428,8 @@ int gemm_tc_pass_tokens(int64_t tiles, int n, int npad, int num_sms) {
   return best;
 }
 
+int gemm_tc_max_tokens() { return kTcMaxN; }
+
 int gemm_tc_slices(const DevWeight& w, int split) {
   const int kb = w.kunits;
   split = std::max(1, std::min(split, kb));
@@ -464,6 +466,9 @@ void launch_gemm_tc(const DevWeight& w, const ActQ& act, int n, float* y, int64_
   int N = (std::min(n, kTcMaxN) + 15) / 16 * 16;
   if (gy == 1) {
     N = gemm_tc_pass_tokens(tiles, n, npad, sms_of_device(dev));
+    if (const int ch = gemm_choice(w, n); ch >= 16 && ch <= kTcMaxN && ch % 16 == 0 &&
+                                          static_cast<int64_t>((n + ch - 1) / ch) * ch <= npad)
+      N = ch;  // the measured pass size (gemm_tune)
     // MALKIN_B200_TC_PASS=<tokens> forces the pass size (tests and measurements), when it fits the padded rows
     if (const char* e = std::getenv("MALKIN_B200_TC_PASS")) {
       const int f = (std::atoi(e) + 15) / 16 * 16;

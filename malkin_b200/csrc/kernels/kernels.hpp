@@ -75,6 +75,16 @@ void launch_gemm(const DevWeight& w, const ActQ& act, int n, float* y, int64_t l
 // Split that fills the GPU for this weight (>= 1), and the slices a split request produces.
 int gemm_split_for(const DevWeight& w, int num_sms);
 int gemm_slices(const DevWeight& w, int split);
+// Kernel-shape tuning: times every kernel shape of w's layout (panel tile and token pass; tensor-core pass size) for
+// n tokens on stream s with the operands launch_gemm would get (y is overwritten with the product, which every shape
+// computes bit-identically, so the choice never changes a result) and keeps the fastest for (device, weight shape,
+// token tiles); split-1 launches of that shape use it from then on. L2 is flushed before every timed launch, so the
+// weights stream from HBM as they do inside a forward. No-op when the shape is tuned already, s is capturing, or
+// MALKIN_B200_GEMM_TUNE=0; otherwise it allocates a 256 MiB flush buffer on first use and synchronizes s.
+void gemm_tune(const DevWeight& w, const ActQ& act, int n, float* y, int64_t ldy, int* status, cudaStream_t s);
+// The tuned (or, while tuning, the forced) shape for w at n tokens: a panel variant index or tensor-core pass
+// tokens; -1 if none.
+int gemm_choice(const DevWeight& w, int n);
 // out[(r * n + t) * nblk + b]: exact int dot of block b (Q6_K: 16-value halves).
 void launch_block_dots(const DevWeight& w, const ActQ& act, int n, int32_t* out, int* status, cudaStream_t s);
 
@@ -85,6 +95,7 @@ void launch_gemm_tc(const DevWeight& w, const ActQ& act, int n, float* y, int64_
                     int32_t* dots, int* status, cudaStream_t s);
 int gemm_tc_split_for(const DevWeight& w, int num_sms);
 int gemm_tc_slices(const DevWeight& w, int split);
+int gemm_tc_max_tokens();  // largest pass size (tokens)
 
 // ---- tensor-parallel sum over NVLink peer memory (tp_reduce.cu) ----
 // Rank r's exchange buffer: data[r] = two halves of `cap` floats, flags[r] = one int per rank (the last epoch that

@@ -151,10 +151,11 @@ def test_attention_golden(mk, golden, torch_cuda):
         assert np.array_equal(out.reshape(-1), golden[f"att{i}_out"])  # malkin's operation order: bit-identical
 
 
-@pytest.mark.parametrize("H,KV,D", [(8, 2, 128), (16, 8, 128), (40, 8, 128), (64, 8, 128), (4, 2, 64), (4, 1, 256)])
+@pytest.mark.parametrize("H,KV,D", [(8, 2, 128), (16, 8, 128), (40, 8, 128), (64, 8, 128), (8, 8, 128), (24, 8, 64),
+                                     (4, 2, 64), (4, 1, 256)])
 def test_attention_tree_batch_vs_oracle(mk, oracle, torch_cuda, H, KV, D):
     """Two sequences, a 9-node tree on one and a 5-token prompt chunk on the other, long prefix (several key chunks
-    and P.V tiles): bit-identical to the oracle's restatement of attend_gqa for G = 1, 2, 4, 5, 8 and D = 64, 128, 256."""
+    and P.V tiles): bit-identical to the oracle's restatement of attend_gqa for G = 1, 2, 3, 4, 5, 8 and D = 64, 128, 256."""
     torch = torch_cuda
     rng = np.random.default_rng(5 + H + D)
     n_ctx = 700
