@@ -60,6 +60,8 @@ typedef struct mk_synth_spec {
   int32_t type_embd;      /* token_embd.weight when not tied */
   float sigma;            /* weights ~ N(0, sigma) */
   uint64_t seed;
+  int32_t has_eos;        /* 1: write eos_token_id as tokenizer.ggml.eos_token_id (an end-of-generation token) */
+  int32_t eos_token_id;
 } mk_synth_spec;
 
 /* Writes the model to path with n_threads host threads (0 = all). */
@@ -195,6 +197,66 @@ int mk_rng_uniforms(uint64_t seed, int64_t skip, int n, double* out);
  * engine.cpp:397-421 minus the host-side emit). */
 int mk_verify_step(mk_ctx* ctx, const mk_batch_token* batch, int n, const mk_proposal* props, int n_props,
                    mk_accept_result* out);
+
+/* ---------------------------------------------------------------------------------------------------------
+ * Engine: continuous batching with speculative decoding over device models, malkin::Engine (engine.h:47-141,
+ * engine.cpp:191-559) at the token level. One target context and an optional draft context (same vocabulary,
+ * same n_ctx and n_seq, on the same GPU); one KV sequence per slot. Each mk_engine_step is Engine::worker_loop's
+ * admission plus Engine::step: waiting requests go to idle slots with the longest common prompt prefix, decoding
+ * slots get an adaptive draft length (plan_drafts), the draft proposes (greedy: top-1 chain and top-2 siblings;
+ * sampled: a chain drawn from the draft's distribution with its own seed + 1 stream), one target batch holds the
+ * trees / chains and then prompt chunks, acceptance runs on the device, emission on the host.
+ * Detokenization, stop strings and chat templates stay with the caller: it passes the end-of-generation ids and
+ * ends a request with mk_engine_cancel (malkin's on_text returning false). Calls on one engine are not thread-safe.
+ * ------------------------------------------------------------------------------------------------------- */
+#define MK_FINISH_STOP 1      /* end-of-generation token (finish_reason "stop") */
+#define MK_FINISH_LENGTH 2    /* max_tokens reached or the context is full ("length") */
+#define MK_FINISH_CANCELLED 3 /* mk_engine_cancel ("cancelled") */
+
+typedef struct mk_gen_request { /* GenRequest (engine.h:29-34) with token ids */
+  const int32_t* prompt;
+  int32_t n_prompt;           /* 1 .. n_ctx - 1 */
+  int32_t max_tokens;         /* 0: until the context ends */
+  mk_sampling sampling;       /* temperature <= 0: greedy; else top_k 1 .. MK_MAX_TOPK; penalties 0 */
+  uint64_t seed;              /* SamplingParams::seed (sampler.h:17); 0: random */
+  const int32_t* eog;         /* end-of-generation token ids (Tokenizer::is_eog) */
+  int32_t n_eog;
+} mk_gen_request;
+
+typedef struct mk_gen_event {
+  int32_t request;
+  int32_t token;   /* an emitted token, or -1 when the request finished */
+  int32_t finish;  /* 0 for a token, else MK_FINISH_* */
+} mk_gen_event;
+
+typedef struct mk_gen_stats { /* GenResult's counters (engine.h:36-42) */
+  int32_t prompt_tokens, cached_tokens, completion_tokens, drafted, accepted;
+  int32_t finish; /* 0 while running */
+} mk_gen_stats;
+
+typedef struct mk_engine mk_engine;
+
+/* draft may be NULL (plain decoding). n_draft: largest draft length (0: malkin's default 8; at most MK_MAX_DRAFT). */
+int mk_engine_create(mk_ctx* target, mk_ctx* draft, int n_draft, mk_engine** out);
+int mk_engine_destroy(mk_engine* e);
+/* Queues a request (Engine::generate, engine.cpp:227-242); MK_ERR_ARG for an empty prompt or one that fills the
+ * context, MK_ERR_UNSUPPORTED for penalties or a top_k the device accept cannot take. */
+int mk_engine_submit(mk_engine* e, const mk_gen_request* r, int32_t* request_id);
+/* One step; then up to cap queued events in emission order (tokens of a request in order, its finish last). Events
+ * that do not fit stay queued for the next call (cap 0 just steps). */
+int mk_engine_step(mk_engine* e, mk_gen_event* events, int cap, int* n_events);
+/* Queued events without stepping. */
+int mk_engine_events(mk_engine* e, mk_gen_event* events, int cap, int* n_events);
+/* 1 while any request is waiting or in flight, else 0. */
+int mk_engine_busy(const mk_engine* e, int* busy);
+/* Ends the request at its next emitted token (a waiting one at the next step) with MK_FINISH_CANCELLED. */
+int mk_engine_cancel(mk_engine* e, int32_t request_id);
+int mk_engine_stats(const mk_engine* e, int32_t request_id, mk_gen_stats* out);
+/* Engine::perplexity (engine.cpp:525-559) over token ids: mean negative log-likelihood of the second half of each
+ * window of `window` tokens (at most n_ctx); bos >= 0 replaces each window's first token (Tokenizer::add_bos).
+ * Uses sequence 0; no request may be in flight (MK_ERR_STATE). */
+int mk_engine_perplexity(mk_engine* e, const int32_t* tokens, int n, int window, int32_t bos, double* mean_nll,
+                         int* scored);
 
 /* Per-stage device time of the last forward, ms, in the 8 MALKIN_PROFILE stages (model.cpp:52-76):
  * norm+qkv, qk-norm/rope/kv, attention, wo+res+norm, gate+up, silu+quant, down, output. Enabled by

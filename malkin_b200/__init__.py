@@ -9,7 +9,7 @@ from __future__ import annotations
 
 import ctypes
 import os
-from typing import Iterable, List, Optional, Sequence
+from typing import Dict, Iterable, List, Optional, Sequence, Tuple
 
 import numpy as np
 
@@ -62,7 +62,7 @@ class SynthSpec(ctypes.Structure):
         ("rope_base", ctypes.c_float), ("rms_eps", ctypes.c_float), ("tied", ctypes.c_int32),
         ("type_default", ctypes.c_int32), ("type_attn_v", ctypes.c_int32), ("type_ffn_down", ctypes.c_int32),
         ("type_output", ctypes.c_int32), ("type_embd", ctypes.c_int32), ("sigma", ctypes.c_float),
-        ("seed", ctypes.c_uint64)]
+        ("seed", ctypes.c_uint64), ("has_eos", ctypes.c_int32), ("eos_token_id", ctypes.c_int32)]
 
 
 class BatchToken(ctypes.Structure):
@@ -202,7 +202,9 @@ EXPORTS = ("mk_last_error", "mk_version", "mk_synth_gguf", "mk_init", "mk_nccl_u
            "mk_load_gguf", "mk_alloc_kv", "mk_model_config_get", "mk_forward", "mk_move_kv", "mk_accept",
            "mk_rng_uniforms", "mk_verify_step", "mk_set_profile", "mk_stage_times", "mk_last_launch_count",
            "mk_stream", "mk_last_io_bytes", "mk_tp_shard_of", "mk_tp_exchange_check", "mk_weight_upload", "mk_weight_free", "mk_weight_device_bytes", "mk_quantize_q8",
-           "mk_matmul", "mk_matmul_noalloc", "mk_block_dots", "mk_quantize_i8", "mk_silu_mul", "mk_attention")
+           "mk_matmul", "mk_matmul_noalloc", "mk_block_dots", "mk_quantize_i8", "mk_silu_mul", "mk_attention",
+           "mk_engine_create", "mk_engine_destroy", "mk_engine_submit", "mk_engine_step", "mk_engine_events",
+           "mk_engine_busy", "mk_engine_cancel", "mk_engine_stats", "mk_engine_perplexity")
 
 
 def version() -> str:
@@ -213,13 +215,16 @@ def synth_gguf(path: str, n_layer: int, n_embd: int, n_ff: int, n_head: int, n_h
                n_vocab: int = 151936, n_ctx_train: int = 40960, rope_base: float = 1e6, rms_eps: float = 1e-6,
                tied: bool = False, type_default: int = TYPE_Q8_0, type_attn_v: Optional[int] = None,
                type_ffn_down: Optional[int] = None, type_output: Optional[int] = None,
-               type_embd: Optional[int] = None, sigma: float = 0.02, seed: int = 0, n_threads: int = 0) -> str:
-    """Writes a synthetic Qwen3 GGUF (seeded N(0, sigma) weights, norms 1.0) and returns its path."""
+               type_embd: Optional[int] = None, sigma: float = 0.02, seed: int = 0, n_threads: int = 0,
+               eos_token_id: Optional[int] = None) -> str:
+    """Writes a synthetic Qwen3 GGUF (seeded N(0, sigma) weights, norms 1.0) and returns its path. eos_token_id: an
+    end-of-generation token written as tokenizer.ggml.eos_token_id."""
     s = SynthSpec(n_layer, n_embd, n_ff, n_head, n_head_kv, head_dim, n_vocab, n_ctx_train, rope_base, rms_eps,
                   int(tied), type_default, type_attn_v if type_attn_v is not None else type_default,
                   type_ffn_down if type_ffn_down is not None else type_default,
                   type_output if type_output is not None else type_default,
-                  type_embd if type_embd is not None else type_default, sigma, seed)
+                  type_embd if type_embd is not None else type_default, sigma, seed,
+                  int(eos_token_id is not None), eos_token_id or 0)
     _check(lib.mk_synth_gguf(path.encode(), ctypes.byref(s), n_threads))
     return path
 
@@ -342,6 +347,111 @@ class Model:
     @property
     def stream(self) -> int:
         return int(lib.mk_stream(self._h) or 0)
+
+
+FINISH_STOP, FINISH_LENGTH, FINISH_CANCELLED = 1, 2, 3
+
+
+class GenRequest(ctypes.Structure):
+    """GenRequest (engine.h:29-34) with token ids."""
+    _fields_ = [("prompt", ctypes.c_void_p), ("n_prompt", ctypes.c_int32), ("max_tokens", ctypes.c_int32),
+                ("sampling", Sampling), ("seed", ctypes.c_uint64), ("eog", ctypes.c_void_p),
+                ("n_eog", ctypes.c_int32)]
+
+
+class GenEvent(ctypes.Structure):
+    _fields_ = [("request", ctypes.c_int32), ("token", ctypes.c_int32), ("finish", ctypes.c_int32)]
+
+
+class GenStats(ctypes.Structure):
+    """GenResult's counters (engine.h:36-42); finish 0 while running."""
+    _fields_ = [(n, ctypes.c_int32) for n in
+                ("prompt_tokens", "cached_tokens", "completion_tokens", "drafted", "accepted", "finish")]
+
+
+lib.mk_engine_create.argtypes = [_vp, _vp, ctypes.c_int, ctypes.POINTER(_vp)]
+lib.mk_engine_destroy.argtypes = [_vp]
+lib.mk_engine_submit.argtypes = [_vp, ctypes.POINTER(GenRequest), ctypes.POINTER(ctypes.c_int32)]
+lib.mk_engine_step.argtypes = [_vp, ctypes.POINTER(GenEvent), ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
+lib.mk_engine_events.argtypes = [_vp, ctypes.POINTER(GenEvent), ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
+lib.mk_engine_busy.argtypes = [_vp, ctypes.POINTER(ctypes.c_int)]
+lib.mk_engine_cancel.argtypes = [_vp, ctypes.c_int32]
+lib.mk_engine_stats.argtypes = [_vp, ctypes.c_int32, ctypes.POINTER(GenStats)]
+lib.mk_engine_perplexity.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int32,
+                                     ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int)]
+
+
+class Engine:
+    """malkin::Engine (engine.h:47-141) at the token level over a target Model and an optional draft Model."""
+
+    def __init__(self, target: "Model", draft: Optional["Model"] = None, n_draft: int = 0):
+        self._h = _vp()
+        self._keep = (target, draft)
+        _check(lib.mk_engine_create(target._h, draft._h if draft is not None else None, n_draft,
+                                    ctypes.byref(self._h)))
+        self._ev = (GenEvent * 4096)()
+
+    def close(self) -> None:
+        if self._h:
+            _check(lib.mk_engine_destroy(self._h))
+            self._h = _vp()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def submit(self, prompt: Sequence[int], max_tokens: int = 0, sampling: Optional[Sampling] = None, seed: int = 0,
+               eog: Sequence[int] = ()) -> int:
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        e = np.ascontiguousarray(eog, dtype=np.int32)
+        r = GenRequest(p.ctypes.data, len(p), max_tokens, sampling or Sampling(temperature=0.0), seed,
+                       e.ctypes.data if len(e) else None, len(e))
+        rid = ctypes.c_int32()
+        _check(lib.mk_engine_submit(self._h, ctypes.byref(r), ctypes.byref(rid)))
+        return rid.value
+
+    def step(self) -> List[Tuple[int, int, int]]:
+        """One Engine::step; returns (request, token, finish) events (token -1 with the finish code at the end)."""
+        out, n = [], ctypes.c_int()
+        _check(lib.mk_engine_step(self._h, self._ev, len(self._ev), ctypes.byref(n)))
+        while True:
+            out += [(e.request, e.token, e.finish) for e in self._ev[:n.value]]
+            if n.value < len(self._ev):
+                return out
+            _check(lib.mk_engine_events(self._h, self._ev, len(self._ev), ctypes.byref(n)))
+
+    def busy(self) -> bool:
+        b = ctypes.c_int()
+        _check(lib.mk_engine_busy(self._h, ctypes.byref(b)))
+        return bool(b.value)
+
+    def cancel(self, request: int) -> None:
+        _check(lib.mk_engine_cancel(self._h, request))
+
+    def stats(self, request: int) -> GenStats:
+        s = GenStats()
+        _check(lib.mk_engine_stats(self._h, request, ctypes.byref(s)))
+        return s
+
+    def run(self) -> Dict[int, List[int]]:
+        """Steps until every request finished; returns each request's tokens."""
+        toks: Dict[int, List[int]] = {}
+        while self.busy():
+            for r, t, f in self.step():
+                toks.setdefault(r, [])
+                if f == 0:
+                    toks[r].append(t)
+        return toks
+
+    def perplexity(self, tokens: Sequence[int], window: int, bos: int = -1) -> Tuple[float, int]:
+        """Engine::perplexity over token ids: (mean negative log-likelihood, tokens scored)."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        nll, n = ctypes.c_double(), ctypes.c_int()
+        _check(lib.mk_engine_perplexity(self._h, t.ctypes.data, len(t), window, bos, ctypes.byref(nll),
+                                        ctypes.byref(n)))
+        return nll.value, n.value
 
 
 class Weight:

@@ -10,6 +10,7 @@
 #include <vector>
 
 #include "../../../include/malkin_b200.h"
+#include "engine.hpp"
 #include "gguf.hpp"
 #include "layout.hpp"
 #include "model.hpp"
@@ -19,6 +20,12 @@
 
 struct mk_ctx {
   std::unique_ptr<mkb::Model> model;
+};
+
+struct mk_engine {
+  std::unique_ptr<mkb::Engine> engine;
+  std::vector<mk_gen_event> queue;  // events not yet handed out
+  size_t head = 0;
 };
 
 struct mk_weight {
@@ -116,7 +123,7 @@ int mk_synth_gguf(const char* path, const mk_synth_spec* spec, int n_threads) {
                      spec->rope_base, spec->rms_eps,   spec->tied,         static_cast<uint32_t>(spec->type_default),
                      static_cast<uint32_t>(spec->type_attn_v), static_cast<uint32_t>(spec->type_ffn_down),
                      static_cast<uint32_t>(spec->type_output), static_cast<uint32_t>(spec->type_embd), spec->sigma,
-                     spec->seed};
+                     spec->seed, spec->has_eos, spec->eos_token_id};
     mkb::write_synth_gguf(path, s, n_threads);
   });
 }
@@ -495,3 +502,82 @@ int mk_attention(const float* dev_q, int n, int H, int KV, int D, const int8_t* 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------------------------------
+// engine
+// ---------------------------------------------------------------------------------------------------------------
+namespace {
+
+void drain(mk_engine* e, mk_gen_event* events, int cap, int* n_events) {
+  int n = 0;
+  while (n < cap && e->head < e->queue.size()) events[n++] = e->queue[e->head++];
+  if (e->head == e->queue.size()) e->queue.clear(), e->head = 0;
+  if (n_events) *n_events = n;
+}
+
+}  // namespace
+
+int mk_engine_create(mk_ctx* target, mk_ctx* draft, int n_draft, mk_engine** out) {
+  return guard(MK_ERR_ARG, [&] {
+    if (!target || !out || n_draft < 0) throw mkb::ArgError("engine_create: bad argument");
+    auto e = std::make_unique<mk_engine>();
+    e->engine = std::make_unique<mkb::Engine>(&model_of(target), draft ? &model_of(draft) : nullptr, n_draft);
+    *out = e.release();
+  });
+}
+
+int mk_engine_destroy(mk_engine* e) {
+  return guard(MK_ERR_ARG, [&] { delete e; });
+}
+
+int mk_engine_submit(mk_engine* e, const mk_gen_request* r, int32_t* request_id) {
+  return guard(MK_ERR_ARG, [&] {
+    if (!e || !r) throw mkb::ArgError("engine_submit: bad argument");
+    const int id = e->engine->submit(*r);
+    if (request_id) *request_id = id;
+  });
+}
+
+int mk_engine_step(mk_engine* e, mk_gen_event* events, int cap, int* n_events) {
+  return guard(MK_ERR_ARG, [&] {
+    if (!e || cap < 0 || (cap > 0 && !events)) throw mkb::ArgError("engine_step: bad argument");
+    e->engine->step(&e->queue);
+    drain(e, events, cap, n_events);
+  });
+}
+
+int mk_engine_events(mk_engine* e, mk_gen_event* events, int cap, int* n_events) {
+  return guard(MK_ERR_ARG, [&] {
+    if (!e || cap < 0 || (cap > 0 && !events)) throw mkb::ArgError("engine_events: bad argument");
+    drain(e, events, cap, n_events);
+  });
+}
+
+int mk_engine_busy(const mk_engine* e, int* busy) {
+  return guard(MK_ERR_ARG, [&] {
+    if (!e || !busy) throw mkb::ArgError("engine_busy: bad argument");
+    *busy = e->engine->busy() ? 1 : 0;
+  });
+}
+
+int mk_engine_cancel(mk_engine* e, int32_t request_id) {
+  return guard(MK_ERR_ARG, [&] {
+    if (!e) throw mkb::ArgError("engine_cancel: bad argument");
+    e->engine->cancel(request_id);
+  });
+}
+
+int mk_engine_stats(const mk_engine* e, int32_t request_id, mk_gen_stats* out) {
+  return guard(MK_ERR_ARG, [&] {
+    if (!e || !out) throw mkb::ArgError("engine_stats: bad argument");
+    *out = e->engine->stats(request_id);
+  });
+}
+
+int mk_engine_perplexity(mk_engine* e, const int32_t* tokens, int n, int window, int32_t bos, double* mean_nll,
+                         int* scored) {
+  return guard(MK_ERR_ARG, [&] {
+    if (!e || !tokens || !mean_nll) throw mkb::ArgError("engine_perplexity: bad argument");
+    *mean_nll = e->engine->perplexity(tokens, n, window, bos, scored);
+  });
+}

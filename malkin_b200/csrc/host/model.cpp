@@ -862,6 +862,77 @@ void Model::check_status() {
   }
 }
 
+void Model::candidates(int k, std::vector<float>* v, std::vector<int32_t>* ids) {
+  if (last_n_ == 0) throw StateError("candidates before forward");
+  if (k < 1 || k > MK_MAX_TOPK) throw ArgError("candidates: k outside 1.." + std::to_string(MK_MAX_TOPK));
+  cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+  constexpr int kc = MK_TOPK_CAP;
+  const int m = last_m_;
+  v->assign(static_cast<size_t>(m) * k, 0.0f);
+  ids->assign(static_cast<size_t>(m) * k, 0);
+  if (m == 0) return;
+  const int K = static_cast<int>(std::min<int64_t>(k, Vl_));
+  if (K > 1)
+    launch_topk(logits_, Vl_, m, static_cast<int>(Vl_), static_cast<int>(V0_), K, kc, cand_v_, cand_i_, stream_);
+  else
+    launch_argmax_kc(logits_, Vl_, m, static_cast<int>(Vl_), static_cast<int>(V0_), kc, cand_v_, cand_i_, stream_);
+  if (tp_size_ > 1) {
+    auto comm = static_cast<ncclComm_t>(nccl_);
+    nccl_check(dl_group_start(), "group");
+    nccl_check(dl_all_gather(cand_v_, gath_v_, static_cast<size_t>(m) * kc, ncclFloat, comm, stream_), "allgather");
+    nccl_check(dl_all_gather(cand_i_, gath_i_, static_cast<size_t>(m) * kc, ncclInt32, comm, stream_), "allgather");
+    nccl_check(dl_group_end(), "group");
+    launch_merge_cand(gath_v_, gath_i_, tp_size_, m, k, kc, cand_v_, cand_i_, stream_);
+  }
+  std::vector<float> hv(static_cast<size_t>(m) * kc);
+  std::vector<int32_t> hi(static_cast<size_t>(m) * kc);
+  cuda_check(cudaMemcpyAsync(hv.data(), cand_v_, hv.size() * 4, cudaMemcpyDeviceToHost, stream_), "candidates");
+  cuda_check(cudaMemcpyAsync(hi.data(), cand_i_, hi.size() * 4, cudaMemcpyDeviceToHost, stream_), "candidates");
+  cuda_check(cudaStreamSynchronize(stream_), "candidates");
+  d2h_bytes_ += static_cast<int64_t>(hv.size() * 8);
+  for (int r = 0; r < m; ++r)
+    for (int j = 0; j < k; ++j) {
+      (*v)[static_cast<size_t>(r) * k + j] = hv[static_cast<size_t>(r) * kc + j];
+      (*ids)[static_cast<size_t>(r) * k + j] = hi[static_cast<size_t>(r) * kc + j];
+    }
+}
+
+void Model::row_nll(const int32_t* targets, double* nll) {
+  if (last_n_ == 0) throw StateError("row_nll before forward");
+  cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+  const int m = last_m_;
+  if (m == 0) return;
+  const size_t MB = static_cast<size_t>(max_batch_);
+  // scratch: row maxima and target logits in the candidate values, targets in the candidate ids, the argmax
+  // indices and the double sums in the gather buffers
+  float* mx = cand_v_;
+  float* tl = cand_v_ + MB * 32;
+  int32_t* tgt = cand_i_;
+  double* sum = reinterpret_cast<double*>(gath_v_);
+  cuda_check(cudaMemcpyAsync(tgt, targets, static_cast<size_t>(m) * 4, cudaMemcpyHostToDevice, stream_), "targets");
+  h2d_bytes_ += static_cast<int64_t>(m) * 4;
+  launch_argmax(logits_, Vl_, m, static_cast<int>(Vl_), static_cast<int>(V0_), mx, gath_i_, stream_);
+  auto comm = static_cast<ncclComm_t>(nccl_);
+  if (tp_size_ > 1) nccl_check(dl_all_reduce(mx, mx, m, ncclFloat, ncclMax, comm, stream_), "allreduce max");
+  launch_row_lse(logits_, Vl_, m, static_cast<int>(Vl_), static_cast<int>(V0_), mx, tgt, sum, tl, stream_);
+  if (tp_size_ > 1) {
+    nccl_check(dl_group_start(), "group");
+    nccl_check(dl_all_reduce(sum, sum, m, ncclDouble, ncclSum, comm, stream_), "allreduce sum");
+    nccl_check(dl_all_reduce(tl, tl, m, ncclFloat, ncclSum, comm, stream_), "allreduce logit");
+    nccl_check(dl_group_end(), "group");
+  }
+  std::vector<float> hmx(static_cast<size_t>(m)), htl(static_cast<size_t>(m));
+  std::vector<double> hs(static_cast<size_t>(m));
+  cuda_check(cudaMemcpyAsync(hmx.data(), mx, static_cast<size_t>(m) * 4, cudaMemcpyDeviceToHost, stream_), "nll");
+  cuda_check(cudaMemcpyAsync(htl.data(), tl, static_cast<size_t>(m) * 4, cudaMemcpyDeviceToHost, stream_), "nll");
+  cuda_check(cudaMemcpyAsync(hs.data(), sum, static_cast<size_t>(m) * 8, cudaMemcpyDeviceToHost, stream_), "nll");
+  cuda_check(cudaStreamSynchronize(stream_), "nll");
+  d2h_bytes_ += static_cast<int64_t>(m) * 16;
+  for (int r = 0; r < m; ++r)
+    nll[r] = targets[r] < 0 ? 0.0 : std::log(hs[static_cast<size_t>(r)]) + hmx[static_cast<size_t>(r)] -
+                                          htl[static_cast<size_t>(r)];
+}
+
 void Model::move_kv(int from, int to, int seq) {
   if (n_ctx_ == 0) throw StateError("move_kv before alloc_kv");
   if (seq < 0 || seq >= n_seq_ || from < 0 || from >= n_ctx_ || to < 0 || to >= n_ctx_) throw ArgError("move_kv: bad row");

@@ -92,6 +92,14 @@ class Model {
   void forward(const mk_batch_token* batch, int n, float* host_logits);
   void move_kv(int from, int to, int seq);
   void accept(const mk_proposal* props, int n_props, mk_accept_result* out);
+  // Top-k candidates (value desc, index asc; k <= MK_MAX_TOPK) of every logits row of the last forward, on the host:
+  // rows x k values and token ids (tensor parallel: merged over the vocabulary shards).
+  void candidates(int k, std::vector<float>* v, std::vector<int32_t>* ids);
+  // Per logits row r of the last forward with targets[r] >= 0: log(sum exp(l - mx)) + mx - l[targets[r]], the
+  // negative log-likelihood Engine::perplexity adds (engine.cpp:545-552); rows with targets[r] < 0 get 0.
+  void row_nll(const int32_t* targets, double* nll);
+  int max_batch() const { return max_batch_; }
+  int last_logit_rows() const { return last_m_; }
 
   const ModelCfg& cfg() const { return cfg_; }
   int n_ctx() const { return n_ctx_; }

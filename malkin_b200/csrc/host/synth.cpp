@@ -178,6 +178,10 @@ void write_synth_gguf(const std::string& path, const SynthSpec& s, int n_threads
     for (int i = 0; i < s.n_vocab; ++i) toks[static_cast<size_t>(i)] = "<t" + std::to_string(i) + ">";
     w.add_str_array("tokenizer.ggml.tokens", toks);
   }
+  if (s.has_eos) {
+    if (s.eos_token_id < 0 || s.eos_token_id >= s.n_vocab) throw std::runtime_error("synth: eos_token_id out of range");
+    w.add_u32("tokenizer.ggml.eos_token_id", static_cast<uint32_t>(s.eos_token_id));
+  }
   const int64_t E = s.n_embd, F = s.n_ff, HD = static_cast<int64_t>(s.n_head) * s.head_dim,
                 KD = static_cast<int64_t>(s.n_head_kv) * s.head_dim, V = s.n_vocab;
   struct Job {

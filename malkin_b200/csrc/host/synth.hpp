@@ -11,6 +11,7 @@ struct SynthSpec {
   uint32_t type_default, type_attn_v, type_ffn_down, type_output, type_embd;
   float sigma;
   uint64_t seed;
+  int has_eos = 0, eos_token_id = 0;  // tokenizer.ggml.eos_token_id when has_eos
 };
 
 // Writes a synthetic Qwen3 model (see synth.cpp) to path.

@@ -355,7 +355,40 @@ __global__ void k_accept(const AcceptReq* __restrict__ reqs, const float* __rest
   out[r] = o;
 }
 
+// ---------------- log-sum-exp for perplexity ----------------
+// Engine::perplexity (engine.cpp:545-552) per logits row: sum over the row of exp(double(l[v] - mx)) with the row's
+// maximum mx (over every vocabulary shard), and the row's logit of its target token when this shard holds it (else 0).
+// The double sum is a tree over the block, not malkin's sequential loop: the two agree to about 1e-15 relative.
+__global__ void k_row_lse(const float* __restrict__ logits, int64_t ld, int V, int vbase, const float* __restrict__ mx,
+                          const int32_t* __restrict__ tgt, double* __restrict__ sum, float* __restrict__ tl) {
+  __shared__ double part[32];
+  const int row = blockIdx.x, tid = threadIdx.x;
+  const float* l = logits + static_cast<size_t>(row) * ld;
+  const float m = mx[row];
+  double s = 0.0;
+  for (int i = tid; i < V; i += blockDim.x) s += exp(static_cast<double>(__fsub_rn(l[i], m)));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if ((tid & 31) == 0) part[tid >> 5] = s;
+  __syncthreads();
+  if (tid < 32) {
+    s = tid < static_cast<int>(blockDim.x >> 5) ? part[tid] : 0.0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (tid == 0) {
+      sum[row] = s;
+      const int t = tgt[row] - vbase;
+      tl[row] = t >= 0 && t < V ? l[t] : 0.0f;
+    }
+  }
+}
+
 }  // namespace
+
+void launch_row_lse(const float* logits, int64_t ld, int m, int V, int vbase, const float* mx, const int32_t* tgt,
+                    double* sum, float* tl, cudaStream_t s) {
+  if (m > 0) k_row_lse<<<m, 512, 0, s>>>(logits, ld, V, vbase, mx, tgt, sum, tl);
+}
 
 void launch_argmax(const float* logits, int64_t ld, int m, int V, int vbase, float* best_v, int32_t* best_i,
                    cudaStream_t s) {

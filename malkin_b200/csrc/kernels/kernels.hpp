@@ -198,6 +198,10 @@ void launch_argmax(const float* logits, int64_t ld, int m, int V, int vbase, flo
 // Same, written at row * kc (candidate-list layout).
 void launch_argmax_kc(const float* logits, int64_t ld, int m, int V, int vbase, int kc, float* best_v,
                       int32_t* best_i, cudaStream_t s);
+// Per logits row r: sum[r] = sum over this shard's V values of exp(double(l - mx[r])), tl[r] = the logit of token
+// tgt[r] if vbase <= tgt[r] < vbase + V, else 0 (perplexity).
+void launch_row_lse(const float* logits, int64_t ld, int m, int V, int vbase, const float* mx, const int32_t* tgt,
+                    double* sum, float* tl, cudaStream_t s);
 // Per logits row: top-k (value desc, index asc) candidates, stride kc per row; k <= 64.
 void launch_topk(const float* logits, int64_t ld, int m, int V, int vbase, int k, int kc, float* cand_v,
                  int32_t* cand_i, cudaStream_t s);

@@ -9,7 +9,7 @@ from __future__ import annotations
 import ctypes
 import os
 import subprocess
-from typing import List, Optional, Sequence, Tuple
+from typing import Dict, List, Optional, Sequence, Tuple
 
 import numpy as np
 
@@ -244,6 +244,14 @@ class Ref:
                                         _vp, _vp, ctypes.c_int]
         L.ref_accept_sampled.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                          ctypes.c_int]
+        L.ref_engine_open.argtypes = [ctypes.c_char_p, ctypes.c_char_p] + [ctypes.c_int] * 4 + [ctypes.c_char_p,
+                                                                                                ctypes.c_int]
+        L.ref_engine_open.restype = _vp
+        L.ref_engine_close.argtypes = [_vp]
+        L.ref_engine_generate.argtypes = [_vp, ctypes.c_int, ctypes.c_int] + [_vp] * 5 + [ctypes.c_int] + [_vp] * 3 + [
+            ctypes.c_char_p, ctypes.c_int]
+        L.ref_engine_perplexity.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp, _vp, ctypes.c_char_p,
+                                            ctypes.c_int]
 
     @staticmethod
     def available() -> Optional[str]:
@@ -387,3 +395,55 @@ class RefModel:
 
     def move_kv(self, frm: int, to: int, seq: int = 0) -> None:
         self.r.lib.ref_model_move_kv(self.h, frm, to, seq)
+
+
+class RefEngine:
+    """malkin::Engine (engine.cpp) through the reference library: continuous batching, the draft model's
+    speculative trees / chains, adaptive draft length, perplexity. Token i's text is "<ti>" (the synthetic models'
+    vocabulary), so generated text reads back as token ids."""
+
+    def __init__(self, ref: Ref, path: str, n_ctx: int, parallel: int = 1, draft: Optional[str] = None,
+                 n_draft: int = 0, threads: int = 0):
+        self.r = ref
+        err = ctypes.create_string_buffer(512)
+        self.h = ref.lib.ref_engine_open(path.encode(), draft.encode() if draft else None, n_ctx, parallel, n_draft,
+                                         threads, err, 512)
+        if not self.h:
+            raise RuntimeError(err.value.decode())
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            self.r.lib.ref_engine_close(self.h)
+            self.h = None
+
+    def generate(self, requests: Sequence[Dict], sequential: bool = False, cap: int = 4096):
+        """requests: dicts with prompt, max_tokens, and optionally temperature, top_p, top_k, min_p, seed (greedy
+        by default). Returns [(tokens, stats)] with stats = (prompt, cached, completion, drafted, accepted, finish)."""
+        n = len(requests)
+        prompts = np.concatenate([np.asarray(q["prompt"], dtype=np.int32) for q in requests])
+        plen = np.array([len(q["prompt"]) for q in requests], dtype=np.int32)
+        mt = np.array([q.get("max_tokens", 0) for q in requests], dtype=np.int32)
+        smp = np.array([[q.get("temperature", 0.0), q.get("top_p", 0.95), q.get("top_k", 40), q.get("min_p", 0.05)]
+                        for q in requests], dtype=np.float32)
+        seeds = np.array([q.get("seed", 1) for q in requests], dtype=np.uint64)
+        out = np.zeros((n, cap), dtype=np.int32)
+        out_n = np.zeros(n, dtype=np.int32)
+        st = np.zeros((n, 6), dtype=np.int32)
+        err = ctypes.create_string_buffer(512)
+        rc = self.r.lib.ref_engine_generate(self.h, n, int(sequential), prompts.ctypes.data, plen.ctypes.data,
+                                            mt.ctypes.data, smp.ctypes.data, seeds.ctypes.data, cap, out.ctypes.data,
+                                            out_n.ctypes.data, st.ctypes.data, err, 512)
+        if rc != 0:
+            raise RuntimeError(err.value.decode())
+        return [(out[i, :out_n[i]].tolist(), tuple(int(x) for x in st[i])) for i in range(n)]
+
+    def perplexity(self, tokens: Sequence[int], window: int):
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        nll = ctypes.c_double()
+        scored = ctypes.c_int()
+        err = ctypes.create_string_buffer(512)
+        rc = self.r.lib.ref_engine_perplexity(self.h, t.ctypes.data, len(t), window, ctypes.byref(nll),
+                                              ctypes.byref(scored), err, 512)
+        if rc != 0:
+            raise RuntimeError(err.value.decode())
+        return nll.value, scored.value

@@ -11,8 +11,10 @@
 //   attention  kern::attend_gqa (tree ancestors as extra keys)                                    kernels_avx512.cpp:282
 //   sampler    Sampler::distribution / draw / verify                                              sampler.cpp:22-97
 //   accept     Engine::accept_greedy / accept_sampled restated over Model::move_kv and Sampler,   engine.cpp:441-507
-//              because they are private members of Engine (whose tokenizer needs pcre2, absent
-//              here). emit() is taken as "continue" (no end-of-generation token, no stop string).
+//              because they are private members of Engine; emit() is taken as "continue" (no
+//              end-of-generation token, no stop string).
+//   engine     malkin's Engine itself (generate with continuous batching and a draft model, and      engine.cpp:100-559
+//              perplexity), compiled with ref_tokenizer.cpp standing in for the pcre2 tokenizer.
 #include <cstddef>
 #include <cstdint>
 #include <cstring>
@@ -24,7 +26,10 @@
 
 #include <omp.h>
 
+#include <thread>
+
 #include "cpu.h"
+#include "engine.h"
 #include "gguf.h"
 #include "kernels.h"
 #include "model.h"
@@ -318,6 +323,95 @@ int ref_accept_sampled(void* sampler, float* logits, int n_vocab, int kk, const 
   else if (2 * i < kk)
     *k = std::max(1, *k - 1);
   return acc;
+}
+
+// ---- Engine (engine.cpp) ----
+void* ref_engine_open(const char* model, const char* draft, int n_ctx, int parallel, int n_draft, int threads, char* err,
+                      int errlen) {
+  try {
+    EngineOptions o;
+    o.model_path = model;
+    o.n_ctx = n_ctx;
+    o.threads = threads;
+    o.threads_batch = threads;
+    o.draft_path = draft ? draft : "";
+    o.n_draft = n_draft;
+    o.parallel = parallel;
+    return new Engine(o);
+  } catch (const std::exception& e) {
+    put_err(err, errlen, e.what());
+    return nullptr;
+  }
+}
+
+void ref_engine_close(void* h) { delete static_cast<Engine*>(h); }
+
+// n requests through Engine::generate, each on its own thread started together (continuous batching) or one after
+// another (sequential). sampling: n x (temperature, top_p, top_k, min_p). Per request: its tokens (read back from
+// the generated text, at most cap) in out[i * cap ..], their count in out_n[i], and stats[i * 6 ..] = prompt,
+// cached, completion tokens, drafted, accepted, finish (1 stop, 2 length, 3 cancelled). 0 = ok, -1 = exception.
+int ref_engine_generate(void* h, int n, int sequential, const int32_t* prompts, const int32_t* plen,
+                        const int32_t* max_tokens, const float* sampling, const uint64_t* seeds, int cap, int32_t* out,
+                        int32_t* out_n, int32_t* stats, char* err, int errlen) {
+  Engine& e = *static_cast<Engine*>(h);
+  std::vector<GenRequest> reqs(static_cast<size_t>(n));
+  size_t off = 0;
+  for (int i = 0; i < n; ++i) {
+    GenRequest& r = reqs[static_cast<size_t>(i)];
+    r.prompt.assign(prompts + off, prompts + off + plen[i]);
+    off += static_cast<size_t>(plen[i]);
+    r.max_tokens = max_tokens[i];
+    r.sampling = params_of(sampling[4 * i], sampling[4 * i + 1], static_cast<int>(sampling[4 * i + 2]),
+                           sampling[4 * i + 3], 0.0f, 0.0f, seeds[i]);
+  }
+  std::vector<GenResult> res(static_cast<size_t>(n));
+  std::vector<std::string> errs(static_cast<size_t>(n));
+  auto run = [&](int i) {
+    try {
+      res[static_cast<size_t>(i)] = e.generate(reqs[static_cast<size_t>(i)], nullptr);
+    } catch (const std::exception& x) {
+      errs[static_cast<size_t>(i)] = x.what();
+    }
+  };
+  if (sequential) {
+    for (int i = 0; i < n; ++i) run(i);
+  } else {
+    std::vector<std::thread> th;
+    for (int i = 0; i < n; ++i) th.emplace_back(run, i);
+    for (auto& t : th) t.join();
+  }
+  for (int i = 0; i < n; ++i) {
+    if (!errs[static_cast<size_t>(i)].empty()) {
+      put_err(err, errlen, errs[static_cast<size_t>(i)].c_str());
+      return -1;
+    }
+    const GenResult& r = res[static_cast<size_t>(i)];
+    const auto ids = e.tokenizer().encode(r.text, false);
+    const int m = std::min<int>(cap, static_cast<int>(ids.size()));
+    std::copy(ids.begin(), ids.begin() + m, out + static_cast<size_t>(i) * cap);
+    out_n[i] = m;
+    int32_t* st = stats + 6 * i;
+    st[0] = r.prompt_tokens;
+    st[1] = r.cached_tokens;
+    st[2] = r.completion_tokens;
+    st[3] = r.drafted;
+    st[4] = r.accepted;
+    st[5] = r.finish_reason == "stop" ? 1 : (r.finish_reason == "length" ? 2 : 3);
+  }
+  return 0;
+}
+
+// Engine::perplexity over token ids (the text is their pieces, read back by the stand-in tokenizer).
+int ref_engine_perplexity(void* h, const int32_t* toks, int n, int window, double* nll, int* scored, char* err,
+                          int errlen) {
+  try {
+    Engine& e = *static_cast<Engine*>(h);
+    *nll = e.perplexity(e.tokenizer().decode(std::vector<int32_t>(toks, toks + n)), window, scored);
+    return 0;
+  } catch (const std::exception& x) {
+    put_err(err, errlen, x.what());
+    return -1;
+  }
 }
 
 }  // extern "C"
