@@ -199,6 +199,20 @@ def profiled_traffic(name: str):
     return None
 
 
+def fp32_floor(cfg: dict, world: int, n: int, gu_ms: float, clocks):
+    """The gate+up GEMM's other bound: malkin's exact block order needs a float epilogue per (row, token, 32-value
+    block) - float(dot), d_w * d_x, fma (Q8_0: 3 FMA-pipe lane operations) - at 128 FMA lanes per SM."""
+    s = spec_of(cfg)
+    if s["type_default"] != Q8_0 or gu_ms <= 0:
+        return None
+    rows = 2 * s["n_ff"] // world
+    ops = rows * n * (s["n_embd"] // 32) * 3
+    mhz = (clocks or {}).get("sm_mhz") or 1965.0
+    floor_us = ops / (148 * 128 * mhz * 1e6) * 1e6
+    launch_us = gu_ms * 1e3 / s["n_layer"]
+    return {"lane_ops_per_launch": ops, "floor_us": floor_us, "launch_us": launch_us, "frac": floor_us / launch_us}
+
+
 def reference_model(path: str, cfg: dict):
     """malkin's CPU path (oracle/_ref) with the configuration's weights loaded and KV for its requests, all physical
     cores; (ref, model, load seconds) or (None, reason, 0)."""
@@ -290,40 +304,56 @@ def config_json(args, cfg):
 # ---------------------------------------------------------------------------------------------------------------
 # Kernel probes (for ncu captures of one kernel at the 8B verify shapes; not part of the timed benchmark)
 # ---------------------------------------------------------------------------------------------------------------
-PROBE_GEMM_SHAPES = {"gate+up": (24576, 4096), "down": (4096, 12288), "qkv": (6144, 4096), "wo": (4096, 4096),
-                     "lm_head": (151936, 4096)}
+PROBE_GEMM_SHAPES = {  # name: (rows, cols, weight type); the 8B Q8_0 matrices, then the 4B and 14B K-quant ones
+    "gate+up": (24576, 4096, Q8_0), "down": (4096, 12288, Q8_0), "qkv": (6144, 4096, Q8_0), "wo": (4096, 4096, Q8_0),
+    "lm_head": (151936, 4096, Q8_0), "gate+up_q4k_4b": (19456, 2560, Q4_K), "down_q6k_4b": (2560, 9728, Q6_K),
+    "gate+up_q6k_14b": (34816, 5120, Q6_K), "down_q6k_14b": (5120, 17408, Q6_K)}
 
 
 def probe_gemm(shapes, layouts, n: int, reps: int) -> None:
-    """Q8_0 matmul (mk_matmul, automatic split) on seeded random weights of the 8B shapes, n tokens."""
+    """mk_matmul on seeded random weights of the named shapes, n tokens. The first call measures the kernel shapes
+    (gemm_tune); the reps after it run between cudaProfilerStart / Stop, so `ncu --profile-from-start off` sees only
+    the chosen kernel."""
     import torch
     import malkin_b200 as mk
     sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
     from make_golden import random_rows
     rng = np.random.default_rng(0)
     for name in shapes:
-        rows, cols = PROBE_GEMM_SHAPES[name]
-        w = random_rows(rng, Q8_0, rows, cols)
+        rows, cols, t = PROBE_GEMM_SHAPES[name]
+        w = random_rows(rng, t, min(rows, 4096), cols)
+        if rows > w.shape[0]:  # tile the seeded rows up to the full shape (the data does not change the timing)
+            w = np.tile(w, (rows // w.shape[0] + 1, 1))[:rows]
         x = torch.from_numpy(rng.uniform(-3, 3, (n, cols)).astype(np.float32)).cuda()
         y = torch.zeros((n, rows), device="cuda")
         for layout in layouts:
             os.environ.pop("MALKIN_B200_Q8_LAYOUT", None)
             if layout != "auto":
                 os.environ["MALKIN_B200_Q8_LAYOUT"] = layout
-            W = mk.Weight(Q8_0, w, rows, cols)
+            W = mk.Weight(t, w, rows, cols)
+            W.matmul(x.data_ptr(), n, y.data_ptr(), split_k=0)
+            torch.cuda.synchronize()
+            torch.cuda.profiler.start()
             for _ in range(reps):
                 W.matmul(x.data_ptr(), n, y.data_ptr(), split_k=0)
             torch.cuda.synchronize()
-            print(json.dumps({"probe": "gemm", "shape": name, "layout": layout, "rows": rows, "cols": cols, "n": n}))
+            torch.cuda.profiler.stop()
+            print(json.dumps({"probe": "gemm", "shape": name, "type": t, "layout": layout, "rows": rows, "cols": cols,
+                              "n": n}))
             del W
 
 
-def probe_attention(reps: int) -> None:
-    """Tree attention (mk_attention) at the 8B verify shape: 8 requests x 17 tree rows, 2049 contiguous keys plus
-    the node's ancestors, 32 q heads / 8 kv heads, D = 128, seeded int8 KV."""
+PROBE_ATTN_SHAPES = {  # name: (requests, rows per request, prefix keys, q heads, kv heads)
+    "8b": (8, 17, 2048, 32, 8), "0.6b": (1, 17, 512, 16, 8), "4b": (1, 17, 4096, 32, 8), "14b": (4, 33, 8192, 40, 8)}
+
+
+def probe_attention(reps: int, shape: str = "8b") -> None:
+    """Tree attention (mk_attention) at a configuration's verify shape: requests x tree rows, prefix + 1 contiguous
+    keys plus each node's ancestors, D = 128, seeded int8 KV. The reps run between cudaProfilerStart / Stop."""
     import torch
     import malkin_b200 as mk
-    reqs, tok, P, H, KV, D, n_ctx = 8, 17, 2048, 32, 8, 128, 2304
+    reqs, tok, P, H, KV = PROBE_ATTN_SHAPES[shape]
+    D, n_ctx = 128, P + 2 * tok + 8
     n_rows, n = reqs * n_ctx, reqs * tok
     rng = np.random.default_rng(0)
     q = torch.from_numpy(rng.standard_normal((n, H, D)).astype(np.float32)).cuda()
@@ -341,11 +371,14 @@ def probe_attention(reps: int) -> None:
     ti = lambda a: torch.tensor(a, dtype=torch.int32).cuda()  # noqa: E731
     kvb, nk, ao, an = ti(kv_base), ti(n_keys), ti(anc_off), ti(anc)
     out = torch.zeros((n, H, D), device="cuda")
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
     for _ in range(reps):
         mk.attention(q.data_ptr(), n, H, KV, D, k.data_ptr(), v.data_ptr(), ks.data_ptr(), vs.data_ptr(), n_rows,
                      kvb.data_ptr(), nk.data_ptr(), ao.data_ptr(), an.data_ptr(), out.data_ptr())
     torch.cuda.synchronize()
-    print(json.dumps({"probe": "attention", "n": n, "heads": H, "kv_heads": KV, "keys": P + 1}))
+    torch.cuda.profiler.stop()
+    print(json.dumps({"probe": "attention", "shape": shape, "n": n, "heads": H, "kv_heads": KV, "keys": P + 1}))
 
 
 PARITY_PREFIX = {"0.6b": 512, "4b": 256, "8b": 128, "14b": 64, "32b": 64, "8b-l2": 128, "tiny": 64}
@@ -401,7 +434,7 @@ def sampled_variant(mk, m, cfg, nexts, P, timed, steps):
                          uniforms=mk.rng_uniforms(77 + s, 2 * kk + 4)) for s in range(R)]
     for _ in range(3):
         m.verify_step(batch, props)
-    res, ms, launches = timed(batch, props)
+    res, ms, launches = timed(batch, props, profile_range=True)
     A = sum(r.n_accepted + 1 for r in res)
     ms_step = ms / steps
     return {"value": A / (ms_step / 1e3), "unit": "tok/s", "ms_per_step": ms_step, "accepted_per_step": A,
@@ -422,6 +455,7 @@ def main():
     ap.add_argument("--probe-layouts", default="auto", help="gemm probe: auto,tc,panels")
     ap.add_argument("--probe-n", type=int, default=136)
     ap.add_argument("--probe-reps", type=int, default=3)
+    ap.add_argument("--probe-attn", default="8b", choices=["8b", "0.6b", "4b", "14b"], help="attention probe shape")
     ap.add_argument("--no-parity", action="store_true", help="skip the parity leg against malkin's CPU path")
     ap.add_argument("--write-model", metavar="CONFIG", help="write the configuration's synthetic GGUF and exit")
     args = ap.parse_args()
@@ -431,7 +465,7 @@ def main():
     if args.probe == "gemm":
         return probe_gemm(args.probe_shapes.split(","), args.probe_layouts.split(","), args.probe_n, args.probe_reps)
     if args.probe == "attention":
-        return probe_attention(args.probe_reps)
+        return probe_attention(args.probe_reps, args.probe_attn)
     args.warmup = max(3, args.warmup)
     cfg = CONFIGS[args.config]
     if args.impl == "reference":
@@ -508,11 +542,14 @@ def main():
         m.verify_step(batch, props)
     stream = torch.cuda.ExternalStream(m.stream)
 
-    def timed(b, ps):
-        """K steps on the library's stream between device events, after a barrier; max over ranks."""
+    def timed(b, ps, profile_range=False):
+        """K steps on the library's stream between device events, after a barrier; max over ranks. profile_range:
+        the steps run between cudaProfilerStart / Stop (`ncu --profile-from-start off` lists only them)."""
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
+        if profile_range:
+            torch.cuda.profiler.start()
         n_launch = 0
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
@@ -522,6 +559,8 @@ def main():
         e1.record(stream)
         e1.synchronize()
         torch.cuda.synchronize()
+        if profile_range:
+            torch.cuda.profiler.stop()
         if world > 1:
             dist.barrier()
         t_ms = e0.elapsed_time(e1)
@@ -533,7 +572,7 @@ def main():
 
     # the clock sampler starts before the first barrier (its start-up must not delay one rank's first step)
     clk = clocks_start() if rank == 0 else (None, None)
-    res, ms, launches = timed(batch, props)
+    res, ms, launches = timed(batch, props, profile_range=True)
     clocks = clocks_stop(clk, list(range(world))) if rank == 0 else None
     A_step = sum(r.n_accepted + 1 for r in res)
     ms_step = ms / args.steps
@@ -580,12 +619,14 @@ def main():
         "e2e": {"value": A_step * args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": h2d // args.steps,
                 "d2h_bytes_per_step": d2h // args.steps},
         "gpu_launches": launches,
-        "roofline": {"kernel": "gate+up weight-streaming GEMM (k_gemm<Q8_0>, mma.sync panels)", "bound": "hbm",
+        "roofline": {"kernel": "gate+up weight-streaming GEMM (k_gemm<Q8_0>, mma.sync panels, tuned shape)",
+                     "bound": "hbm",
                      "achieved": gu_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": (gu_gbs / pk["hbm_gbs"]) if gu_gbs else None, "peak_source": pk_src,
                      "traffic": profiled_traffic("gemm_q8_gate_up_8b") if args.config == "8b" and world == 1 else None,
                      "traffic_source": "profiles/gemm_q8_gate_up_8b.md (ncu, one launch at the 8B gate+up shape)",
                      "algorithmic_bytes_per_launch": gu_bytes / spec_of(cfg)["n_layer"],
+                     "fp32_epilogue": fp32_floor(cfg, world, rows_per_step, st[4], clocks),
                      "stage_ms": {k: float(v) for k, v in zip(
                          ["norm+qkv", "qk-norm/rope/kv", "attention", "wo+res+norm", "gate+up", "silu+quant", "down",
                           "output"], st)}},

@@ -55,7 +55,7 @@ def test_matmul_bit_exact_split1(mk, golden, torch_cuda, monkeypatch, t):
     torch = torch_cuda
     w, x = golden[f"mm{t}_w"], golden[f"mm{t}_x"]
     W = mk.Weight(t, w, 35, 512)
-    quantum = 128 if t == 8 else 16  # Q8_0 streams in 128-row tensor-core tiles, K-quants in 16-row panels
+    quantum = 16  # every type streams in 16-row panels by default (HBM bytes = GGUF bytes of the padded rows)
     assert W.device_bytes == ((35 + quantum - 1) // quantum) * quantum * mk.row_bytes(t, 512)
     y = torch.full((x.shape[0], 35), np.nan, dtype=torch.float32, device="cuda")
     W.matmul(dev(torch, x).data_ptr(), x.shape[0], y.data_ptr(), split_k=1)
