@@ -117,7 +117,7 @@ constexpr int kScoreKeys = 128;   // keys per score CTA (and per chunk maximum)
 constexpr int kScoreParts = 2;    // score CTAs that split a sub-group's rows
 constexpr int kPvTile = 32;       // keys per P.V stage
 constexpr int kPvStages = 3;      // P.V ring depth
-constexpr int kPvSlice = 32;      // output values per P.V CTA
+constexpr int kPvSliceMax = 32;   // output values per P.V CTA (fewer when the grid would leave SMs idle)
 constexpr int kErrAttWait = 24;   // status code: a P.V stage never landed or was never released
 
 struct AttArgs {
@@ -367,20 +367,20 @@ __global__ void __launch_bounds__(512) k_att_softmax(AttArgs a) {
   }
 }
 
-// grid (n_sg, KV, D / kPvSlice), block 32 + rows x 8 (rows = kQMax / G). Warp 0 is the producer: lane 0 keeps
+// grid (n_sg, KV, D / S), block 32 + rows x S / 4 (rows = kQMax / G). Warp 0 is the producer: lane 0 keeps
 // kPvStages tiles of kPvTile keys in flight with TMA bulk copies (the ST rows and the raw int8 value rows), the warp
 // converts the slice of each landed value tile into floats held twice, (v, v), and signals `ready`. Consumer thread
 // (r, u) owns values 4u .. 4u + 3 of the slice for the G heads of row t0 + r: one f32x2 FMA advances the chains of
 // two heads (heads 2i, 2i + 1; for odd G the last pair's second lane is a padding slot whose result is discarded).
 // Each lane of the pair is its own IEEE fma in key order: malkin's acc = fma(p_j, v_j, acc). Converted value row:
-// (v0 v0 v1 v1) of every u in the first 128 bytes, (v2 v2 v3 v3) in the next, so each 16-byte load of a warp
-// reads 128 contiguous bytes.
-constexpr int kVfRow = 2 * kPvSlice;  // floats per converted value row
-template <int D, int G>
+// (v0 v0 v1 v1) of every u in the first 4 S bytes, (v2 v2 v3 v3) in the next, so a warp's 16-byte loads read
+// contiguous bytes. S (32, 16, 8 or 4 values per CTA) is picked per launch (pv_slice).
+template <int D, int G, int S>
 struct PvGeom {
-  static constexpr int ROWS = kQMax / G, CW = (ROWS * 8 + 31) / 32, NT = 32 * (1 + CW);
+  static constexpr int U = S / 4, VFROW = 2 * S;  // threads per row; floats per converted value row
+  static constexpr int ROWS = kQMax / G, CW = (ROWS * U + 31) / 32, NT = 32 * (1 + CW);
   static constexpr int GA = att_ga(G), NQP = att_nqp(ROWS, G);
-  static constexpr uint32_t PB = kPvTile * NQP * 4, VB = kPvTile * D, FB = kPvTile * kVfRow * 4;
+  static constexpr uint32_t PB = kPvTile * NQP * 4, VB = kPvTile * D, FB = kPvTile * VFROW * 4;
   static constexpr uint32_t STAGE = (PB + VB + FB + 127) / 128 * 128;  // P rows | raw values | converted values
   static constexpr uint32_t BAR = kPvStages * STAGE;
   static constexpr uint32_t SMEM = BAR + 3 * kPvStages * 8;
@@ -397,16 +397,17 @@ __device__ __forceinline__ void pv_issue(uint8_t* stg, uint32_t pb_off, uint64_t
   bulk_g2s(stg + pb_off, vsrc + static_cast<int64_t>(k0) * D, vb, bar);
 }
 
-template <int D, int G>
-__global__ void __launch_bounds__(PvGeom<D, G>::NT) k_att_pv(AttArgs a) {
-  using Gm = PvGeom<D, G>;
+template <int D, int G, int S>
+__global__ void __launch_bounds__(PvGeom<D, G, S>::NT) k_att_pv(AttArgs a) {
+  using Gm = PvGeom<D, G, S>;
+  constexpr int U = Gm::U, VFROW = Gm::VFROW;
   constexpr int GP = Gm::GA / 2;        // head pairs (the last one padded for odd G)
   constexpr int KB = G <= 4 ? 4 : 2;    // keys whose loads are issued together
   extern __shared__ __align__(128) uint8_t sm[];
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + Gm::BAR);
   uint64_t* ready = full + kPvStages;
   uint64_t* empty = ready + kPvStages;
-  const int sg = blockIdx.x, kvh = blockIdx.y, d0 = blockIdx.z * kPvSlice;
+  const int sg = blockIdx.x, kvh = blockIdx.y, d0 = blockIdx.z * S;
   const int t0 = a.p.sg_first[sg], nr = a.p.sg_first[sg + 1] - t0;
   const int maxk = a.p.sg_maxk[sg];
   const int nqp = att_nqp(nr, G);
@@ -414,7 +415,7 @@ __global__ void __launch_bounds__(PvGeom<D, G>::NT) k_att_pv(AttArgs a) {
   const size_t hb = static_cast<size_t>(kvh) * a.L.n_rows + a.p.kv_base[t0];
   const int ntiles = (maxk + kPvTile - 1) / kPvTile;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int cwarps = (nr * 8 + 31) / 32;  // consumer warps with at least one row
+  const int cwarps = (nr * U + 31) / 32;  // consumer warps with at least one row
   if (threadIdx.x == 0) {
     for (int s = 0; s < kPvStages; ++s) {
       mbar_init(&full[s], 1);
@@ -439,11 +440,11 @@ __global__ void __launch_bounds__(PvGeom<D, G>::NT) k_att_pv(AttArgs a) {
       const int8_t* vraw = reinterpret_cast<const int8_t*>(stg + Gm::PB);
       float4* vf = reinterpret_cast<float4*>(sm + s * Gm::STAGE + Gm::PB + Gm::VB);
       const int nkt = min(kPvTile, maxk - it * kPvTile);
-      for (int i = lane; i < nkt * 8; i += 32) {
-        const int jj = i >> 3, u = i & 7;
+      for (int i = lane; i < nkt * U; i += 32) {
+        const int jj = i / U, u = i % U;
         const char4 w = *reinterpret_cast<const char4*>(vraw + jj * D + d0 + 4 * u);
-        vf[jj * (kVfRow / 4) + u] = make_float4(i8f(w.x), i8f(w.x), i8f(w.y), i8f(w.y));
-        vf[jj * (kVfRow / 4) + 8 + u] = make_float4(i8f(w.z), i8f(w.z), i8f(w.w), i8f(w.w));
+        vf[jj * (VFROW / 4) + u] = make_float4(i8f(w.x), i8f(w.x), i8f(w.y), i8f(w.y));
+        vf[jj * (VFROW / 4) + U + u] = make_float4(i8f(w.z), i8f(w.z), i8f(w.w), i8f(w.w));
       }
       mbar_arrive(&ready[s]);  // every lane: its conversions happen before the consumers' reads
       // refill the stage of the previous tile once its consumers have released it
@@ -462,7 +463,7 @@ __global__ void __launch_bounds__(PvGeom<D, G>::NT) k_att_pv(AttArgs a) {
   }
   // ---------------- consumers ----------------
   if (warp - 1 >= cwarps) return;
-  const int ct = threadIdx.x - 32, r = ct >> 3, u = ct & 7;
+  const int ct = threadIdx.x - 32, r = ct / U, u = ct % U;
   const int t = t0 + r;
   const bool active = r < nr;
   const int n0 = active ? a.p.n_keys[t] : 0;
@@ -486,8 +487,8 @@ __global__ void __launch_bounds__(PvGeom<D, G>::NT) k_att_pv(AttArgs a) {
       f2 V[KB][4], P[KB][GP];
 #pragma unroll
       for (int b = 0; b < KB; ++b) {
-        const ulonglong2 va = *reinterpret_cast<const ulonglong2*>(vf + (jj + b) * kVfRow);
-        const ulonglong2 vb = *reinterpret_cast<const ulonglong2*>(vf + (jj + b) * kVfRow + 32);
+        const ulonglong2 va = *reinterpret_cast<const ulonglong2*>(vf + (jj + b) * VFROW);
+        const ulonglong2 vb = *reinterpret_cast<const ulonglong2*>(vf + (jj + b) * VFROW + S);
         V[b][0] = va.x, V[b][1] = va.y, V[b][2] = vb.x, V[b][3] = vb.y;
         const float* pp = pt + (jj + b) * nqp;
         if constexpr (Gm::GA % 4 == 0) {
@@ -509,8 +510,8 @@ __global__ void __launch_bounds__(PvGeom<D, G>::NT) k_att_pv(AttArgs a) {
           for (int e = 0; e < 4; ++e) acc[i][e] = f2_fma(P[b][i], V[b][e], acc[i][e]);
     }
     for (; jj < lim; ++jj) {
-      const ulonglong2 va = *reinterpret_cast<const ulonglong2*>(vf + jj * kVfRow);
-      const ulonglong2 vb = *reinterpret_cast<const ulonglong2*>(vf + jj * kVfRow + 32);
+      const ulonglong2 va = *reinterpret_cast<const ulonglong2*>(vf + jj * VFROW);
+      const ulonglong2 vb = *reinterpret_cast<const ulonglong2*>(vf + jj * VFROW + S);
       const f2 V[4] = {va.x, va.y, vb.x, vb.y};
       const f2* pp = reinterpret_cast<const f2*>(pt + jj * nqp);
 #pragma unroll
@@ -550,18 +551,46 @@ __global__ void __launch_bounds__(PvGeom<D, G>::NT) k_att_pv(AttArgs a) {
   }
 }
 
-template <int D, int G>
-void launch_pv(const AttArgs& a, cudaStream_t s) {
-  using Gm = PvGeom<D, G>;
+template <int D, int G, int S>
+void launch_pv_s(const AttArgs& a, cudaStream_t s) {
+  using Gm = PvGeom<D, G, S>;
   static bool attr[kMaxDevices] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < kMaxDevices && !attr[dev]) {
-    cudaFuncSetAttribute(k_att_pv<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(Gm::SMEM));
+    cudaFuncSetAttribute(k_att_pv<D, G, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(Gm::SMEM));
     attr[dev] = true;
   }
-  const dim3 g(a.p.n_sg, a.KV, D / kPvSlice);
-  k_att_pv<D, G><<<g, Gm::NT, Gm::SMEM, s>>>(a);
+  const dim3 g(a.p.n_sg, a.KV, D / S);
+  k_att_pv<D, G, S><<<g, Gm::NT, Gm::SMEM, s>>>(a);
+}
+
+// The value-slice width: 32 values per CTA unless that grid leaves SMs idle, then the widest that gives every SM a
+// CTA (measured at the configurations' shapes: 32 is fastest from 256 CTAs up, 8B 132 vs 185 us at 16; one request of
+// 17 rows, 32 CTAs at 32, runs 117 us at 4 vs 169 at 32); MALKIN_B200_PV_SLICE=<32|16|8|4> forces one.
+inline int pv_slice(int ctas_at_32, int sms) {
+  const char* e = std::getenv("MALKIN_B200_PV_SLICE");
+  const int v = e ? std::atoi(e) : 0;
+  const int forced = v == 32 || v == 16 || v == 8 || v == 4 ? v : 0;
+  if (forced) return forced;
+  int S = kPvSliceMax;
+  while (S > 4 && ctas_at_32 * (kPvSliceMax / S) < sms) S /= 2;
+  return S;
+}
+
+template <int D, int G>
+void launch_pv(const AttArgs& a, cudaStream_t s) {
+  static int sms[kMaxDevices] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < kMaxDevices && !sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+  const int S = pv_slice(a.p.n_sg * a.KV * (D / kPvSliceMax), dev < kMaxDevices && sms[dev] ? sms[dev] : 148);
+  switch (S) {
+    case 32: launch_pv_s<D, G, 32>(a, s); break;
+    case 16: launch_pv_s<D, G, 16>(a, s); break;
+    case 8: launch_pv_s<D, G, 8>(a, s); break;
+    default: launch_pv_s<D, G, 4>(a, s); break;
+  }
 }
 
 template <int D>
