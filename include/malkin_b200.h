@@ -113,12 +113,15 @@ int mk_alloc_kv(mk_ctx* ctx, int n_ctx, int n_seq, int max_batch);
 int mk_model_config_get(const mk_ctx* ctx, mk_model_config* out);
 
 /* The slice of a qwen3 GGUF that tensor-parallel rank tp_rank of tp_size holds (host only, no device; no counterpart
- * in malkin, which runs on one host): q heads [head0, head0 + heads) and kv heads [kv_head0, ...) of the column-split
- * q / k / v, ffn rows [ffn0, ffn0 + ffn) of gate / up (and the matching ffn_down columns) in whole ffn_down blocks,
- * vocabulary rows [vocab0, vocab0 + vocab) of the LM head. */
+ * in malkin, which runs on one host): q heads [head0, head0 + heads) and kv heads [kv_head0, ...) of the row-split
+ * q / k / v, ffn rows [ffn0, ffn0 + ffn) of gate / up in whole ffn_down blocks, output features [embd0, embd0 + embd)
+ * of attn_output and ffn_down (each over its whole input, so every sum keeps malkin's block order; the ranks
+ * all-gather the quantized inputs of those two and the output slices), vocabulary rows [vocab0, vocab0 + vocab) of
+ * the LM head. */
 typedef struct mk_tp_shard {
   int32_t head0, heads, kv_head0, kv_heads, ffn0, ffn;
   int64_t vocab0, vocab;
+  int32_t embd0, embd;
 } mk_tp_shard;
 int mk_tp_shard_of(const char* gguf_path, int tp_size, int tp_rank, mk_tp_shard* out);
 

@@ -179,7 +179,7 @@ class TpShard(ctypes.Structure):
     """mk_tp_shard: the slice of the model one tensor-parallel rank holds."""
     _fields_ = [("head0", ctypes.c_int32), ("heads", ctypes.c_int32), ("kv_head0", ctypes.c_int32),
                 ("kv_heads", ctypes.c_int32), ("ffn0", ctypes.c_int32), ("ffn", ctypes.c_int32),
-                ("vocab0", ctypes.c_int64), ("vocab", ctypes.c_int64)]
+                ("vocab0", ctypes.c_int64), ("vocab", ctypes.c_int64), ("embd0", ctypes.c_int32), ("embd", ctypes.c_int32)]
 
 
 lib.mk_tp_shard_of.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.POINTER(TpShard)]

@@ -172,7 +172,8 @@ int mk_tp_shard_of(const char* gguf_path, int tp_size, int tp_rank, mk_tp_shard*
     if (!down0) throw mkb::ArgError("model: tensor blk.0.ffn_down.weight missing");
     if (!mkb::repack_supported(down0->type)) throw mkb::UnsupportedError("tp_shard: unsupported ffn_down type");
     const mkb::TpShard sh = mkb::tp_shard(c, mkb::kunit_values(down0->type), tp_size, tp_rank);
-    *out = mk_tp_shard{sh.head0, sh.heads, sh.kv_head0, sh.kv_heads, sh.ffn0, sh.ffn, sh.vocab0, sh.vocab};
+    *out = mk_tp_shard{sh.head0, sh.heads, sh.kv_head0, sh.kv_heads, sh.ffn0, sh.ffn, sh.vocab0, sh.vocab, sh.embd0,
+                       sh.embd};
   });
 }
 

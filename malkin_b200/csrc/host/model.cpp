@@ -132,6 +132,10 @@ TpShard tp_shard(const ModelCfg& c, int ffn_unit, int tp, int rank) {
   s.ffn = (fu1 - fu0) * ffn_unit;
   s.vocab0 = static_cast<int64_t>(rank) * c.n_vocab / tp;
   s.vocab = static_cast<int64_t>(rank + 1) * c.n_vocab / tp - s.vocab0;
+  if (c.n_embd % (kPanelRows * tp))
+    throw ArgError("tensor parallel: " + std::to_string(tp) + " ranks do not divide n_embd in 16-row panels");
+  s.embd = c.n_embd / tp;
+  s.embd0 = rank * s.embd;
   return s;
 }
 
@@ -176,6 +180,24 @@ void Model::load(const std::string& path) {
   Fl_ = sh.ffn;
   V0_ = sh.vocab0;
   Vl_ = sh.vocab;
+  {
+    const char* e = std::getenv("MALKIN_B200_TP_SPLIT");
+    tp_rows_ = tp > 1 && e && std::string(e) == "rows";
+  }
+  const bool exact_tp = tp > 1 && !tp_rows_;
+  E0_ = exact_tp ? sh.embd0 : 0;
+  El_ = exact_tp ? sh.embd : E;
+  head_blk0_.assign(static_cast<size_t>(tp), 0);
+  head_blks_.assign(static_cast<size_t>(tp), 0);
+  ffn_blk0_.assign(static_cast<size_t>(tp), 0);
+  ffn_blks_.assign(static_cast<size_t>(tp), 0);
+  for (int rr = 0; rr < tp; ++rr) {
+    const TpShard o = tp_shard(c, kunit_values(down0->type), tp, rr);
+    head_blk0_[static_cast<size_t>(rr)] = static_cast<int64_t>(o.head0) * D / 32;
+    head_blks_[static_cast<size_t>(rr)] = static_cast<int64_t>(o.heads) * D / 32;
+    ffn_blk0_[static_cast<size_t>(rr)] = o.ffn0 / 32;
+    ffn_blks_[static_cast<size_t>(rr)] = o.ffn / 32;
+  }
   const int64_t HDl = static_cast<int64_t>(Hl_) * D, KDl = static_cast<int64_t>(KVl_) * D;
 
   // Device byte plan.
@@ -228,11 +250,14 @@ void Model::load(const std::string& path) {
     L.qkv[1] = static_cast<int>(add_piece(wk, r * KDl, KDl, 0, E));
     L.qkv[2] = static_cast<int>(add_piece(wv, r * KDl, KDl, 0, E));
     L.nqkv = 3;
-    L.wo = static_cast<int>(add_piece(wo, 0, E, r * HDl, HDl));
+    // attn_output / ffn_down: this rank's output features over the whole input (exact), or all features over this
+    // rank's input columns (row split)
+    L.wo = static_cast<int>(exact_tp ? add_piece(wo, E0_, El_, 0, static_cast<int64_t>(c.n_head) * D)
+                                     : add_piece(wo, 0, E, r * HDl, HDl));
     L.gu[0] = static_cast<int>(add_piece(wg, F0_, Fl_, 0, E));
     L.gu[1] = static_cast<int>(add_piece(wu, F0_, Fl_, 0, E));
     L.ngu = 2;
-    L.down = static_cast<int>(add_piece(wd, 0, E, F0_, Fl_));
+    L.down = static_cast<int>(exact_tp ? add_piece(wd, E0_, El_, 0, c.n_ff) : add_piece(wd, 0, E, F0_, Fl_));
   }
   const int lm_piece = static_cast<int>(add_piece(out, V0_, Vl_, 0, E));
   // Embedding table (GGUF rows, replicated) and norms (F32) after the matrices.
@@ -373,7 +398,10 @@ void Model::alloc_kv(int n_ctx, int n_seq, int max_batch) {
   const int NT8 = act_tiles(max_batch);
   const int NB = NT8 * 8;  // token rows of the activation buffers (whole GEMM passes)
   const int64_t HD = static_cast<int64_t>(Hl_) * D;
-  const int64_t kmax = std::max<int64_t>({E, HD, Fl_});
+  const bool exact_tp = tp_size_ > 1 && !tp_rows_;
+  // activation blocks: the widest GEMM input (exact tensor parallel: the whole attention output and ffn width)
+  const int64_t kmax = exact_tp ? std::max<int64_t>({E, static_cast<int64_t>(c.n_head) * D, c.n_ff})
+                                : std::max<int64_t>({E, HD, Fl_});
   const int64_t blocks = kmax / 32;
   int s_qkv = 1, s_gu = 1, s_part = 1;
   for (const Layer& L : layers_) {
@@ -400,7 +428,8 @@ void Model::alloc_kv(int n_ctx, int n_seq, int max_batch) {
                o_sh = take(static_cast<size_t>(blocks) * NB * 4),
                o_cv = take(static_cast<size_t>(NB) * MK_TOPK_CAP * 4), o_ci = take(static_cast<size_t>(NB) * MK_TOPK_CAP * 4),
                o_gv = take(static_cast<size_t>(tp_size_) * NB * MK_TOPK_CAP * 4),
-               o_gi = take(static_cast<size_t>(tp_size_) * NB * MK_TOPK_CAP * 4), o_st = take(256);
+               o_gi = take(static_cast<size_t>(tp_size_) * NB * MK_TOPK_CAP * 4), o_st = take(256),
+               o_tpg = take(exact_tp ? static_cast<size_t>(NB) * E * 4 : 0);
   scratch_ = DevBuf(off);
   cuda_check(cudaMemset(scratch_.get(), 0, off), "scratch memset");
   uint8_t* sb = scratch_.get<uint8_t>();
@@ -423,7 +452,8 @@ void Model::alloc_kv(int n_ctx, int n_seq, int max_batch) {
   gath_v_ = reinterpret_cast<float*>(sb + o_gv);
   gath_i_ = reinterpret_cast<int32_t*>(sb + o_gi);
   status_ = reinterpret_cast<int*>(sb + o_st);
-  setup_tp_exchange(static_cast<size_t>(NB) * E);
+  tpg_ = exact_tp ? reinterpret_cast<float*>(sb + o_tpg) : nullptr;
+  if (!exact_tp) setup_tp_exchange(static_cast<size_t>(NB) * E);
   // attention plan geometry
   const int G = c.n_head / c.n_head_kv;
   sg_rows_ = std::max(1, attn_qmax() / G);
@@ -580,6 +610,46 @@ void Model::tp_sum(Slices parts, int n) {
   }
 }
 
+ActQ Model::act_at(int64_t block) const {
+  ActQ v = act_;
+  const int64_t npad = static_cast<int64_t>(act_.nt8) * 8;
+  v.qx = act_.qx + block * npad * 32;
+  v.qc = act_.qc ? act_.qc + block * npad * 32 : nullptr;
+  v.dx = act_.dx + block * npad;
+  v.dsx = act_.dsx + block * npad;
+  v.sh = act_.sh + block * npad;
+  return v;
+}
+
+void Model::act_gather(const std::vector<int64_t>& start, const std::vector<int64_t>& count, const DevWeight& w) {
+  auto comm = static_cast<ncclComm_t>(nccl_);
+  const size_t npad = static_cast<size_t>(act_.nt8) * 8;
+  nccl_check(dl_group_start(), "group");
+  for (int rr = 0; rr < tp_size_; ++rr) {  // rank rr's blocks, broadcast in place (block-major: one range each)
+    const size_t b0 = static_cast<size_t>(start[static_cast<size_t>(rr)]);
+    const size_t nb = static_cast<size_t>(count[static_cast<size_t>(rr)]);
+    if (nb == 0) continue;
+    uint8_t* q = (w.layout == kLayoutTc ? act_.qc : act_.qx) + b0 * npad * 32;
+    nccl_check(dl_broadcast(q, q, nb * npad * 32, ncclUint8, rr, comm, stream_), "broadcast");
+    nccl_check(dl_broadcast(act_.dx + b0 * npad, act_.dx + b0 * npad, nb * npad, ncclFloat, rr, comm, stream_),
+               "broadcast");
+    if (w.type == kQ4_K)
+      nccl_check(dl_broadcast(act_.dsx + b0 * npad, act_.dsx + b0 * npad, nb * npad, ncclFloat, rr, comm, stream_),
+                 "broadcast");
+    if (w.type == kQ6_K)
+      nccl_check(dl_broadcast(act_.sh + b0 * npad, act_.sh + b0 * npad, nb * npad, ncclUint32, rr, comm, stream_),
+                 "broadcast");
+  }
+  nccl_check(dl_group_end(), "group");
+}
+
+void Model::out_gather(int n) {
+  nccl_check(dl_all_gather(part_, tpg_, static_cast<size_t>(n) * El_, ncclFloat, static_cast<ncclComm_t>(nccl_),
+                           stream_),
+             "allgather");
+  launch_tp_concat(tpg_, tp_size_, n, El_, p_, stream_);
+}
+
 void Model::allreduce(float* buf, size_t count) {
   nccl_check(dl_all_reduce(buf, buf, count, ncclFloat, ncclSum, static_cast<ncclComm_t>(nccl_), stream_),
              "allreduce");
@@ -591,15 +661,14 @@ void Model::gemm(const DevWeight& w, int split, int n, float* y, int64_t ldy, in
 
 void Model::tune_gemms(int n, int m) {
   const Layer& L = layers_[0];  // every layer has the same shapes
-  const int E = cfg_.n_embd;
   act_.nt8 = act_tiles(n);
   for (int i = 0; i < L.n_qkv; ++i)
     if (L.qkv_split[i] == 1) gemm_tune(L.qkv[i], act_, n, yqkv_ + L.qkv_col[i], qkv_ld_, status_, stream_);
-  if (L.wo_split == 1) gemm_tune(L.wo, act_, n, part_, E, status_, stream_);
+  if (L.wo_split == 1) gemm_tune(L.wo, act_, n, part_, El_, status_, stream_);
   for (int i = 0; i < L.n_gu; ++i)
     if (L.gu_split[i] == 1)
       gemm_tune(L.gu[i], act_, n, ygu_ + L.gu_col[i], 2 * static_cast<int64_t>(Fl_), status_, stream_);
-  if (L.down_split == 1) gemm_tune(L.down, act_, n, part_, E, status_, stream_);
+  if (L.down_split == 1) gemm_tune(L.down, act_, n, part_, El_, status_, stream_);
   if (m > 0) {
     act_.nt8 = act_tiles(m);
     gemm_tune(lm_head_, act_, m, logits_, Vl_, status_, stream_);
@@ -616,7 +685,7 @@ void Model::run_forward(int n, int m) {
     stage(-1);
   }
   launch_embed(embd_, embd_type_, embd_row_bytes_, E, d_ids_, n, x_, stream_);
-  const bool tp = tp_size_ > 1;
+  const bool tp = tp_size_ > 1, gx = tp && !tp_rows_;  // gx: exact split (gathered inputs and output slices)
   Slices pending;  // residual contributions not yet added into x (the previous down projection)
   for (int il = 0; il < c.n_layer; ++il) {
     const Layer& L = layers_[static_cast<size_t>(il)];
@@ -632,11 +701,17 @@ void Model::run_forward(int n, int m) {
                     stream_);
     stage(1);
     act_.nt8 = nt8;
-    launch_attention(q_, Hl_, KVl_, D, scale, kv_layers_[static_cast<size_t>(il)], plan_, nullptr, act_, stream_);
+    const size_t rk = static_cast<size_t>(tp_rank_);
+    launch_attention(q_, Hl_, KVl_, D, scale, kv_layers_[static_cast<size_t>(il)], plan_, nullptr,
+                     gx ? act_at(head_blk0_[rk]) : act_, stream_);
+    if (gx) act_gather(head_blk0_, head_blks_, L.wo);
     stage(2);
-    gemm(L.wo, L.wo_split, n, part_, E, part_slice_);
+    gemm(L.wo, L.wo_split, n, part_, El_, part_slice_);
     Slices wo_add{part_, L.wo_split, part_slice_};
-    if (tp) {
+    if (gx) {
+      out_gather(n);
+      wo_add = Slices{p_, 1, 0};
+    } else if (tp) {
       tp_sum(wo_add, n);
       wo_add = Slices{p_, 1, 0};
     }
@@ -644,11 +719,16 @@ void Model::run_forward(int n, int m) {
     stage(3);
     for (int i = 0; i < L.n_gu; ++i) gemm(L.gu[i], L.gu_split[i], n, ygu_ + L.gu_col[i], 2 * static_cast<int64_t>(Fl_), gu_slice_);
     stage(4);
-    launch_silu_quant(Slices{ygu_, L.gu_split[0], gu_slice_}, 2 * static_cast<int64_t>(Fl_), Fl_, n, act_, stream_);
+    launch_silu_quant(Slices{ygu_, L.gu_split[0], gu_slice_}, 2 * static_cast<int64_t>(Fl_), Fl_, n,
+                      gx ? act_at(ffn_blk0_[rk]) : act_, stream_);
+    if (gx) act_gather(ffn_blk0_, ffn_blks_, L.down);
     stage(5);
-    gemm(L.down, L.down_split, n, part_, E, part_slice_);
+    gemm(L.down, L.down_split, n, part_, El_, part_slice_);
     pending = Slices{part_, L.down_split, part_slice_};
-    if (tp) {
+    if (gx) {
+      out_gather(n);
+      pending = Slices{p_, 1, 0};
+    } else if (tp) {
       tp_sum(pending, n);
       pending = Slices{p_, 1, 0};
     }

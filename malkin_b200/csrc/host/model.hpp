@@ -79,6 +79,7 @@ void tp_exchange_check(int size, bool twoshot, int n, int cols, int n_calls, con
 struct TpShard {
   int head0 = 0, heads = 0, kv_head0 = 0, kv_heads = 0, ffn0 = 0, ffn = 0;
   int64_t vocab0 = 0, vocab = 0;
+  int embd0 = 0, embd = 0;  // output features of attn_output / ffn_down
 };
 TpShard tp_shard(const ModelCfg& c, int ffn_unit, int tp, int rank);
 
@@ -143,6 +144,11 @@ class Model {
   // The rank sum of row-split partials (split-K slices) into p_: peer-memory kernels when the exchange is set up,
   // else slice sum + ncclAllReduce.
   void tp_sum(Slices parts, int n);
+  // Exact tensor parallel: the activation blocks [start[r], start[r] + count[r]) that rank r quantized, from every
+  // rank to every rank (what weight w reads), and the gathered output slices part_ [n][El_] -> p_ [n][E].
+  void act_gather(const std::vector<int64_t>& start, const std::vector<int64_t>& count, const DevWeight& w);
+  void out_gather(int n);
+  ActQ act_at(int64_t block) const;  // act_ from 32-value block `block` on
   void setup_tp_exchange(size_t floats);
   void close_tp_exchange();
   void stage(int i);                             // profile lap
@@ -158,6 +164,13 @@ class Model {
   TpExchange tpx_args_;
   bool tpx_on_ = false;
   bool tpx_twoshot_ = false;
+  // tensor-parallel split of attn_output / ffn_down: by output features over the whole input (exact, default), or
+  // by input columns with the rank sum of partials (MALKIN_B200_TP_SPLIT=rows: not malkin's block order)
+  bool tp_rows_ = false;
+  int E0_ = 0, El_ = 0;                           // this rank's output features of attn_output / ffn_down
+  std::vector<int64_t> head_blk0_, head_blks_;   // every rank's 32-value blocks of the attention output
+  std::vector<int64_t> ffn_blk0_, ffn_blks_;     // every rank's 32-value blocks of the ffn activations
+  float* tpg_ = nullptr;                          // [tp][n][El_] gathered output slices
   cudaStream_t stream_ = nullptr;
   bool loaded_ = false;
 

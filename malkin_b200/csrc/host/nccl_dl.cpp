@@ -19,6 +19,7 @@ struct Api {
   decltype(&ncclCommDestroy) comm_destroy = nullptr;
   decltype(&ncclAllReduce) all_reduce = nullptr;
   decltype(&ncclAllGather) all_gather = nullptr;
+  decltype(&ncclBroadcast) broadcast = nullptr;
   decltype(&ncclGroupStart) group_start = nullptr;
   decltype(&ncclGroupEnd) group_end = nullptr;
   decltype(&ncclGetErrorString) error_string = nullptr;
@@ -47,6 +48,7 @@ void load() {
     sym(h, "ncclCommDestroy", g_api.comm_destroy);
     sym(h, "ncclAllReduce", g_api.all_reduce);
     sym(h, "ncclAllGather", g_api.all_gather);
+    sym(h, "ncclBroadcast", g_api.broadcast);
     sym(h, "ncclGroupStart", g_api.group_start);
     sym(h, "ncclGroupEnd", g_api.group_end);
     sym(h, "ncclGetErrorString", g_api.error_string);
@@ -73,6 +75,10 @@ ncclResult_t dl_all_reduce(const void* s, void* r, size_t n, ncclDataType_t t, n
 }
 ncclResult_t dl_all_gather(const void* s, void* r, size_t n, ncclDataType_t t, ncclComm_t c, cudaStream_t st) {
   return api().all_gather(s, r, n, t, c, st);
+}
+ncclResult_t dl_broadcast(const void* s, void* r, size_t n, ncclDataType_t t, int root, ncclComm_t c,
+                          cudaStream_t st) {
+  return api().broadcast(s, r, n, t, root, c, st);
 }
 ncclResult_t dl_group_start() { return api().group_start(); }
 ncclResult_t dl_group_end() { return api().group_end(); }

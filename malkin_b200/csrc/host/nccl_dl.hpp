@@ -12,6 +12,8 @@ ncclResult_t dl_all_reduce(const void* send, void* recv, size_t count, ncclDataT
                            ncclComm_t comm, cudaStream_t stream);
 ncclResult_t dl_all_gather(const void* send, void* recv, size_t count, ncclDataType_t type, ncclComm_t comm,
                            cudaStream_t stream);
+ncclResult_t dl_broadcast(const void* send, void* recv, size_t count, ncclDataType_t type, int root, ncclComm_t comm,
+                          cudaStream_t stream);
 ncclResult_t dl_group_start();
 ncclResult_t dl_group_end();
 const char* dl_error_string(ncclResult_t r);

@@ -118,6 +118,8 @@ struct TpExchange {
 // publish: this rank's split-K slices, summed in slice order, into its half of the exchange; gather: the sum over
 // ranks in rank order into dst (n x cols, cols % 4 == 0). Run both, in this order, on every rank.
 void launch_tp_publish(const TpExchange& x, Slices src, int64_t ld, int n, int cols, cudaStream_t s);
+// Exact tensor parallel: dst[t][r * el + e] = src[r][t][e] (the all-gathered output-feature slices of tp ranks).
+void launch_tp_concat(const float* src, int tp, int n, int el, float* dst, cudaStream_t s);
 void launch_tp_gather(const TpExchange& x, int n, int cols, float* dst, int* status, cudaStream_t s);
 // Two-shot alternative to gather (after publish): reduce sums this rank's 1/size of the rows over the ranks (rank
 // order) into its red half; allgather copies every rank's reduced rows into dst. Same sums, bit for bit; each rank

@@ -19,6 +19,8 @@
 // red half of a call is rewritten two calls later, after every rank published the next call (after its allgather).
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "kernels.hpp"
 
 namespace mkb {
@@ -199,6 +201,26 @@ void launch_tp_reduce(const TpExchange& x, int n, int cols, int* status, cudaStr
 void launch_tp_allgather(const TpExchange& x, int n, int cols, float* dst, int* status, cudaStream_t s) {
   if (n <= 0) return;
   k_tp_allgather<<<tp_grid(static_cast<int64_t>(n) * cols / 4, 256), 256, 0, s>>>(x, n, cols, dst, status);
+}
+
+namespace {
+// float4 per thread: el % 4 == 0 (whole 16-row panels per rank).
+__global__ void k_tp_concat(const float4* __restrict__ src, int tp, int n, int el4, float4* __restrict__ dst) {
+  const int64_t e4 = static_cast<int64_t>(tp) * el4, total = static_cast<int64_t>(n) * e4;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = i / e4, e = i % e4, r = e / el4;
+    dst[i] = src[(r * n + t) * el4 + (e - r * el4)];
+  }
+}
+}  // namespace
+
+void launch_tp_concat(const float* src, int tp, int n, int el, float* dst, cudaStream_t s) {
+  const int64_t total = static_cast<int64_t>(n) * tp * el / 4;
+  if (total <= 0) return;
+  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 148 * 8));
+  k_tp_concat<<<blocks, 256, 0, s>>>(reinterpret_cast<const float4*>(src), tp, n, el / 4,
+                                     reinterpret_cast<float4*>(dst));
 }
 
 }  // namespace mkb

@@ -1,9 +1,11 @@
 """Tensor parallel on 2 / 4 / 8 GPUs (skipped with fewer): one process per GPU over NCCL, q / k / v / gate / up
-column-split, wo / down row-split with a rank sum (peer-memory one-shot or two-shot exchange, or NCCL allreduce),
-vocabulary-split LM head with gathered candidates. Logits and greedy accepts must match the single-GPU path (2e-2
-max-abs logits; identical accepted paths where the top-1 margin exceeds 1e-2). On one GPU: the exchange kernels
-against host-emulated peers, including a peer that never arrives (the bounded wait must reach the caller as
-MK_ERR_TIMEOUT and leave the next calls correct)."""
+split by heads / ffn rows, vocabulary-split LM head with gathered candidates. Default (exact) split: attn_output /
+ffn_down by output features over the whole gathered input, so the logits and greedy accepts are bit-identical to the
+single-GPU path (and so to malkin). Opt-in row split (MALKIN_B200_TP_SPLIT=rows): wo / down by input columns with a
+rank sum (peer-memory one-shot or two-shot exchange, or NCCL allreduce) - 2e-2 max-abs logits, identical accepted
+paths where the top-1 margin exceeds 1e-2. On one GPU: the exchange kernels against host-emulated peers, including
+a peer that never arrives (the bounded wait must reach the caller as MK_ERR_TIMEOUT and leave the next calls
+correct)."""
 import numpy as np
 import pytest
 
@@ -46,7 +48,9 @@ def _run(mk, path, device, rank, world, nccl_id, seed):
 def _child(rank, world, nccl_id, path, seed, q, mode):
     import os
     import sys
-    os.environ["MALKIN_B200_TP_REDUCE"] = mode
+    if mode != "exact":
+        os.environ["MALKIN_B200_TP_SPLIT"] = "rows"
+        os.environ["MALKIN_B200_TP_REDUCE"] = mode
     sys.path[:0] = ["tests", "tests/golden"]
     import malkin_b200 as mk
     try:
@@ -56,7 +60,7 @@ def _child(rank, world, nccl_id, path, seed, q, mode):
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
-@pytest.mark.parametrize("mode", ["oneshot", "twoshot", "nccl"])
+@pytest.mark.parametrize("mode", ["exact", "oneshot", "twoshot", "nccl"])
 def test_tp_matches_single_gpu(mk, model_paths, torch_cuda, world, mode):
     torch = torch_cuda
     if torch.cuda.device_count() < world:
@@ -80,6 +84,10 @@ def test_tp_matches_single_gpu(mk, model_paths, torch_cuda, world, mode):
         assert p.exitcode == 0
     for rank in range(world):  # every rank returns the full logits and the same accepts
         pl, tl, acc = out[rank]
+        if mode == "exact":
+            assert np.array_equal(pl, ref_pl) and np.array_equal(tl, ref_tl)
+            assert acc == ref_acc
+            continue
         assert np.abs(pl - ref_pl).max() < TOL
         assert np.abs(tl - ref_tl).max() < TOL
         s = np.sort(ref_tl, axis=-1)

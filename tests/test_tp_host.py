@@ -31,7 +31,7 @@ def _models(mk, tmp_path):
 def _check_partition(shards, spec, unit):
     n_head, n_kv, n_ff, n_vocab = spec["n_head"], spec["n_head_kv"], spec["n_ff"], spec["n_vocab"]
     for field0, field, total in (("head0", "heads", n_head), ("kv_head0", "kv_heads", n_kv), ("ffn0", "ffn", n_ff),
-                                 ("vocab0", "vocab", n_vocab)):
+                                 ("vocab0", "vocab", n_vocab), ("embd0", "embd", spec["n_embd"])):
         pos = 0
         for s in shards:
             assert s[field0] == pos, (field0, shards)
@@ -40,6 +40,7 @@ def _check_partition(shards, spec, unit):
     for s in shards:
         assert s["ffn0"] % unit == 0 and s["ffn"] % unit == 0
         assert s["heads"] == n_head // len(shards) and s["kv_heads"] == n_kv // len(shards)
+        assert s["embd"] == spec["n_embd"] // len(shards) and s["embd"] % 16 == 0  # whole 16-row panels
     sizes = [s["ffn"] // unit for s in shards]
     assert max(sizes) - min(sizes) <= 1  # as even as whole blocks allow
 
