@@ -30,12 +30,13 @@ MK_ERR_STATE = -5
 MK_ERR_IO = -6
 MK_ERR_TIMEOUT = -7
 
-TYPE_F32, TYPE_F16, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K = 0, 1, 8, 12, 14
+TYPE_F32, TYPE_F16, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K, TYPE_BF16 = 0, 1, 8, 12, 14, 30
 MAX_DRAFT = 32
 MAX_TOPK = 64
 
 # ggml block geometry (elements, bytes) per type
-BLOCK = {TYPE_F32: (1, 4), TYPE_F16: (1, 2), TYPE_Q8_0: (32, 34), TYPE_Q4_K: (256, 144), TYPE_Q6_K: (256, 210)}
+BLOCK = {TYPE_F32: (1, 4), TYPE_F16: (1, 2), TYPE_BF16: (1, 2), TYPE_Q8_0: (32, 34), TYPE_Q4_K: (256, 144),
+         TYPE_Q6_K: (256, 210)}
 
 
 def row_bytes(t: int, n: int) -> int:

@@ -316,6 +316,8 @@ int mk_matmul(const mk_weight* w, const float* dev_x, int n, float* dev_y, int s
     mkb::cuda_check(cudaMemsetAsync(status.get(), 0, sizeof(int), s), "memset");
     TmpAct t(n, w->w.cols);
     mkb::launch_quant_rows(dev_x, w->w.cols, n, static_cast<int>(w->w.cols), t.act, s);
+    t.act.xf = const_cast<float*>(dev_x);  // F32 / F16 / BF16 weights read the floats themselves
+    t.act.ldxf = w->w.cols;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -379,6 +381,8 @@ int mk_matmul_noalloc(const mk_weight* w, const float* dev_x, int n, float* dev_
     act.dsx = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(act.dx) + f);
     act.sh = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(act.dsx) + f);
     act.nt8 = nt8;
+    act.xf = const_cast<float*>(dev_x);  // F32 / F16 / BF16 weights read the floats themselves
+    act.ldxf = w->w.cols;
     float* slices = reinterpret_cast<float*>(base + act_end);
     // the status word must start at zero; activations and slices are fully written before they are read
     mkb::cuda_check(cudaMemsetAsync(status, 0, sizeof(int), s), "matmul_noalloc: clear status");
@@ -397,6 +401,7 @@ int mk_matmul_noalloc(const mk_weight* w, const float* dev_x, int n, float* dev_
 int mk_block_dots(const mk_weight* w, const float* dev_x, int n, int32_t* dev_out, void* stream) {
   return guard(MK_ERR_ARG, [&] {
     if (!w || n <= 0) throw mkb::ArgError("block_dots: bad argument");
+    if (mkb::float_type(w->w.type)) throw mkb::UnsupportedError("block_dots: F32 / F16 / BF16 weights have no int8 dots");
     cudaStream_t s = as_stream(stream);
     mkb::DevBuf status(sizeof(int));
     mkb::cuda_check(cudaMemsetAsync(status.get(), 0, sizeof(int), s), "memset");

@@ -46,7 +46,9 @@ constexpr int kTcRows = 128;
 constexpr size_t kTcRecord = 4352;
 constexpr size_t kChunkQ8_0 = 544, kChunkQ4_K = 2304, kChunkQ6_K = 3360;
 
-inline constexpr int kunit_values(uint32_t type) { return type == 8 ? 32 : 256; }
+// F32 / F16 / BF16 weights stream as GGUF rows; their k-unit is a 32-value block like Q8_0's.
+inline constexpr bool float_type(uint32_t type) { return type == 0 || type == 1 || type == 30; }
+inline constexpr int kunit_values(uint32_t type) { return type == 8 || float_type(type) ? 32 : 256; }
 inline constexpr size_t chunk_bytes(uint32_t type) {
   return type == 8 ? kChunkQ8_0 : type == 12 ? kChunkQ4_K : type == 14 ? kChunkQ6_K : 0;
 }

@@ -165,10 +165,15 @@ void Model::load(const std::string& path) {
   const int tp = tp_size_, r = tp_rank_;
   const int D = c.head_dim, E = c.n_embd;
 
+  any_float_ = false;
   auto check_mat = [&](const TensorView* t) {
     if (!repack_supported(t->type))
       throw UnsupportedError(std::string("unsupported: tensor ") + t->name + " has type " + type_name(t->type) +
-                               " (this path streams Q8_0 Q4_K Q6_K)");
+                               " (this path streams F32 F16 BF16 Q8_0 Q4_K Q6_K)");
+    if (float_type(t->type)) {
+      if (tp > 1) throw UnsupportedError("unsupported: F32 / F16 / BF16 matrices under tensor parallelism");
+      any_float_ = true;
+    }
   };
   // shard geometry (tensor parallel): heads, ffn rows in whole k-units of ffn_down, vocabulary rows
   const TensorView* down0 = weight("blk.0.ffn_down.weight", true);
@@ -264,7 +269,7 @@ void Model::load(const std::string& path) {
   total = align_up(total, 256);
   const size_t embd_off = total;
   embd_type_ = tok->type;
-  if (type_size(embd_type_).block == 0 || (embd_type_ != kF32 && embd_type_ != kF16 && !repack_supported(embd_type_)))
+  if (type_size(embd_type_).block == 0 || !repack_supported(embd_type_))
     throw UnsupportedError(std::string("unsupported: token_embd type ") + type_name(embd_type_));
   embd_row_bytes_ = row_bytes(tok->type, tok->cols());
   if (tok->cols() != E) throw ArgError("model: token_embd width != n_embd");
@@ -429,7 +434,8 @@ void Model::alloc_kv(int n_ctx, int n_seq, int max_batch) {
                o_cv = take(static_cast<size_t>(NB) * MK_TOPK_CAP * 4), o_ci = take(static_cast<size_t>(NB) * MK_TOPK_CAP * 4),
                o_gv = take(static_cast<size_t>(tp_size_) * NB * MK_TOPK_CAP * 4),
                o_gi = take(static_cast<size_t>(tp_size_) * NB * MK_TOPK_CAP * 4), o_st = take(256),
-               o_tpg = take(exact_tp ? static_cast<size_t>(NB) * E * 4 : 0);
+               o_tpg = take(exact_tp ? static_cast<size_t>(NB) * E * 4 : 0),
+               o_xf = take(any_float_ ? static_cast<size_t>(NB) * kmax * 4 : 0);
   scratch_ = DevBuf(off);
   cuda_check(cudaMemset(scratch_.get(), 0, off), "scratch memset");
   uint8_t* sb = scratch_.get<uint8_t>();
@@ -453,6 +459,8 @@ void Model::alloc_kv(int n_ctx, int n_seq, int max_batch) {
   gath_i_ = reinterpret_cast<int32_t*>(sb + o_gi);
   status_ = reinterpret_cast<int*>(sb + o_st);
   tpg_ = exact_tp ? reinterpret_cast<float*>(sb + o_tpg) : nullptr;
+  act_.xf = any_float_ ? reinterpret_cast<float*>(sb + o_xf) : nullptr;  // F32 / F16 / BF16 matrices read the floats
+  act_.ldxf = kmax;
   if (!exact_tp) setup_tp_exchange(static_cast<size_t>(NB) * E);
   // attention plan geometry
   const int G = c.n_head / c.n_head_kv;

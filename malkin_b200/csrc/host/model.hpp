@@ -166,6 +166,7 @@ class Model {
   bool tpx_twoshot_ = false;
   // tensor-parallel split of attn_output / ffn_down: by output features over the whole input (exact, default), or
   // by input columns with the rank sum of partials (MALKIN_B200_TP_SPLIT=rows: not malkin's block order)
+  bool any_float_ = false;  // some matrix is F32 / F16 / BF16: the producers also keep the float activations
   bool tp_rows_ = false;
   int E0_ = 0, El_ = 0;                           // this rank's output features of attn_output / ffn_down
   std::vector<int64_t> head_blk0_, head_blks_;   // every rank's 32-value blocks of the attention output

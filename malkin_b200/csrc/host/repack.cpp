@@ -104,7 +104,9 @@ void pack_chunk(uint32_t type, const uint8_t* const rows[16], size_t unit_off, u
 
 }  // namespace
 
-bool repack_supported(uint32_t type) { return type == kQ8_0 || type == kQ4_K || type == kQ6_K; }
+bool repack_supported(uint32_t type) {
+  return type == kQ8_0 || type == kQ4_K || type == kQ6_K || float_type(type);
+}
 
 size_t repack_bytes(uint32_t type, int64_t rows, int64_t units) {
   const int64_t panels = (rows + kPanelRows - 1) / kPanelRows;
@@ -172,6 +174,7 @@ void repack_tc(const uint8_t* src, size_t src_stride, int64_t rows, int64_t bloc
 }
 
 int weight_layout(uint32_t type, int64_t rows, int64_t cols) {
+  if (float_type(type)) return kLayoutRows;
   if (type != kQ8_0) return kLayoutPanels;
   const char* e = std::getenv("MALKIN_B200_Q8_LAYOUT");
   if (e && std::string(e) == "panels") return kLayoutPanels;
@@ -185,14 +188,22 @@ int weight_layout(uint32_t type, int64_t rows, int64_t cols) {
   return kLayoutPanels;
 }
 
-int layout_row_quantum(int layout) { return layout == kLayoutTc ? kTcRows : kPanelRows; }
+int layout_row_quantum(int layout) { return layout == kLayoutTc ? kTcRows : (layout == kLayoutRows ? 1 : kPanelRows); }
 
 size_t repack_layout_bytes(uint32_t type, int layout, int64_t rows, int64_t units) {
+  if (layout == kLayoutRows) return static_cast<size_t>(rows) * units * 32 * (type == kF32 ? 4 : 2);
   return layout == kLayoutTc ? repack_tc_bytes(rows, units) : repack_bytes(type, rows, units);
 }
 
 void repack_layout(uint32_t type, int layout, const uint8_t* src, size_t src_stride, int64_t rows, int64_t unit0,
                    int64_t units, uint8_t* dst, int n_threads) {
+  if (layout == kLayoutRows) {  // the rows' values [32 unit0, 32 (unit0 + units)) as they are
+    const size_t elt = type == kF32 ? 4 : 2, nb = static_cast<size_t>(units) * 32 * elt;
+    parallel_for(rows, n_threads, [&](int64_t r) {
+      std::memcpy(dst + static_cast<size_t>(r) * nb, src + static_cast<size_t>(r) * src_stride + unit0 * 32 * elt, nb);
+    });
+    return;
+  }
   if (layout == kLayoutTc) {
     if (type != kQ8_0) throw std::runtime_error("repack: the tensor-core layout holds Q8_0 only");
     repack_tc(src, src_stride, rows, unit0, units, dst, n_threads);

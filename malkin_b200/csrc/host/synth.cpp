@@ -132,8 +132,54 @@ void quant_q6_k(const float* x, uint8_t* y, int64_t k) {
   }
 }
 
+// IEEE binary16 with round-to-nearest-even (subnormals kept; overflow to infinity).
+uint16_t to_f16(float f) {
+  uint32_t x;
+  std::memcpy(&x, &f, 4);
+  const uint32_t sign = (x >> 16) & 0x8000u, e8 = (x >> 23) & 0xFFu;
+  uint32_t mant = x & 0x7FFFFFu;
+  if (e8 == 0xFF) return static_cast<uint16_t>(sign | 0x7C00u | (mant ? 0x200u : 0u));
+  const int e = static_cast<int>(e8) - 127 + 15;
+  if (e >= 31) return static_cast<uint16_t>(sign | 0x7C00u);
+  uint32_t r, rem, half;
+  if (e <= 0) {  // subnormal half: shift the implicit-one mantissa right
+    if (e < -10) return static_cast<uint16_t>(sign);
+    mant |= 0x800000u;
+    const int shift = 14 - e;
+    r = mant >> shift;
+    rem = mant & ((1u << shift) - 1);
+    half = 1u << (shift - 1);
+  } else {
+    r = (static_cast<uint32_t>(e) << 10) | (mant >> 13);
+    rem = mant & 0x1FFFu;
+    half = 0x1000u;
+  }
+  if (rem > half || (rem == half && (r & 1u))) ++r;  // a carry may move into the exponent, as rounding does
+  return static_cast<uint16_t>(sign | r);
+}
+
+// bfloat16: the top 16 bits of the float, rounded to nearest even.
+uint16_t to_bf16(float f) {
+  uint32_t x;
+  std::memcpy(&x, &f, 4);
+  if ((x & 0x7F800000u) == 0x7F800000u) return static_cast<uint16_t>((x >> 16) | ((x & 0xFFFFu) ? 0x40u : 0u));
+  return static_cast<uint16_t>((x + 0x7FFFu + ((x >> 16) & 1u)) >> 16);
+}
+
 void quantize_row(uint32_t type, const float* x, uint8_t* y, int64_t k) {
   switch (type) {
+    case kF16:
+      for (int64_t i = 0; i < k; ++i) {
+        const uint16_t h = to_f16(x[i]);
+        std::memcpy(y + 2 * i, &h, 2);
+      }
+      return;
+    case kBF16:
+      for (int64_t i = 0; i < k; ++i) {
+        const uint16_t h = to_bf16(x[i]);
+        std::memcpy(y + 2 * i, &h, 2);
+      }
+      return;
     case kQ8_0:
       return quant_q8_0(x, y, k);
     case kQ4_K:

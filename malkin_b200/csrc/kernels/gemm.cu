@@ -23,6 +23,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
+#include <stdexcept>
 #include <string>
 #include <array>
 #include <utility>
@@ -688,6 +689,11 @@ int gemm_slices(const DevWeight& w, int split) {
 void launch_gemm(const DevWeight& w, const ActQ& act, int n, float* y, int64_t ldy, int64_t slice, int split,
                  int* status, cudaStream_t s) {
   if (n <= 0) return;
+  if (w.layout == kLayoutRows) {
+    if (!act.xf) throw std::runtime_error("gemm: F32 / F16 / BF16 weights need the float activations");
+    launch_gemm_rows(w, act, n, y, ldy, s);  // one slice: the row path has no split
+    return;
+  }
   if (w.layout == kLayoutTc) {
     launch_gemm_tc(w, act, n, y, ldy, slice, split, nullptr, status, s);
     return;

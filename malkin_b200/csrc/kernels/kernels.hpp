@@ -29,10 +29,12 @@ struct ActQ {
   float* dsx = nullptr;
   uint32_t* sh = nullptr;
   int nt8 = 0;
+  float* xf = nullptr;  // the float values before quantization, [token][ldxf] (nullable; F32/F16/BF16 weights read it)
+  int64_t ldxf = 0;
 };
 
 // Device weight in the panel layout, or (Q8_0) in the tensor-core tile layout.
-constexpr int kLayoutPanels = 0, kLayoutTc = 1;
+constexpr int kLayoutPanels = 0, kLayoutTc = 1, kLayoutRows = 2;  // rows: F32 / F16 / BF16 GGUF rows as they are
 struct DevWeight {
   uint32_t type = 0;
   const uint8_t* data = nullptr;
@@ -72,6 +74,8 @@ void launch_silu_mul(float* g, const float* u, int64_t n, cudaStream_t s);
 // (plain stores). split 1 keeps malkin's block order. status: device word for bounded-wait failures (nullable).
 void launch_gemm(const DevWeight& w, const ActQ& act, int n, float* y, int64_t ldy, int64_t slice, int split,
                  int* status, cudaStream_t s);
+// F32 / F16 / BF16 weights (kLayoutRows): y[t][r] = malkin's vec_dot row path on the float activations act.xf.
+void launch_gemm_rows(const DevWeight& w, const ActQ& act, int n, float* y, int64_t ldy, cudaStream_t s);
 // Split that fills the GPU for this weight (>= 1), and the slices a split request produces.
 int gemm_split_for(const DevWeight& w, int num_sms);
 int gemm_slices(const DevWeight& w, int split);

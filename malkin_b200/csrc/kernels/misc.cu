@@ -21,6 +21,8 @@ __device__ float dequant_at(uint32_t type, const uint8_t* row, int i) {
       return reinterpret_cast<const float*>(row)[i];
     case 1:
       return ld_h(row + 2 * i);
+    case 30:  // BF16
+      return __uint_as_float(static_cast<uint32_t>(reinterpret_cast<const uint16_t*>(row)[i]) << 16);
     case 8: {
       const uint8_t* b = row + (i / 32) * 34;
       return __fmul_rn(ld_h(b), static_cast<float>(static_cast<int8_t>(b[2 + i % 32])));

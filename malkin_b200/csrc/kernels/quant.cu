@@ -21,7 +21,7 @@ namespace {
 
 __device__ __forceinline__ void store_zero(const ActQ& a, int b, int t, int lane) {
   QBlock z{0, 0.0f, 0, 0};
-  store_act(a, b, t, z, lane);
+  store_act(a, b, t, z, lane, 0.0f);
 }
 
 // grid (ceil(nb / 8), npad), block 256: warp w quantizes block blockIdx.x * 8 + w of token blockIdx.y.
@@ -33,7 +33,7 @@ __global__ void k_quant_rows(const float* __restrict__ x, int64_t ldx, int n, in
     return;
   }
   const float v = x[static_cast<size_t>(t) * ldx + b * 32 + lane];
-  store_act(a, b, t, quant_block32(v, lane), lane);
+  store_act(a, b, t, quant_block32(v, lane), lane, v);
 }
 
 // grid (npad), block 256: one token row. y = x * s * w, s = 1 / sqrt(dot(x, x) / K + eps), the dot in malkin's
@@ -63,7 +63,7 @@ __global__ void k_rmsnorm_quant(float* __restrict__ x, int64_t ldx, Slices add, 
   for (int b = warp; b < nb; b += 8) {
     const int i = b * 32 + lane;
     const float v = __fmul_rn(__fmul_rn(xr[i], s), w[i]);
-    store_act(a, b, t, quant_block32(v, lane), lane);
+    store_act(a, b, t, quant_block32(v, lane), lane, v);
   }
 }
 
@@ -121,7 +121,10 @@ __global__ void __launch_bounds__(kNormThreads) k_rmsnorm_quant_wide(float* __re
 #pragma unroll
   for (int j = 0; j < kNormMaxJ; ++j) {
     const int b = warp + 32 * j;
-    if (b < nb) store_act(a, b, t, quant_block32(__fmul_rn(__fmul_rn(v[j], sc), wv[j]), lane), lane);
+    if (b < nb) {
+      const float y = __fmul_rn(__fmul_rn(v[j], sc), wv[j]);
+      store_act(a, b, t, quant_block32(y, lane), lane, y);
+    }
   }
 }
 
@@ -142,7 +145,7 @@ __global__ void k_silu_quant(Slices gu, int64_t ld, int F, int n, ActQ a) {
   const float u = sum_strided<NS>(gu.p + row + F + b * 32 + lane, gu.stride);
   const float e = exp_malkin(__fsub_rn(0.0f, g));
   const float h = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, e)), u);
-  store_act(a, b, t, quant_block32(h, lane), lane);
+  store_act(a, b, t, quant_block32(h, lane), lane, h);
 }
 
 // malkin BlockQ8 {float d; int16 s[2]; int8 qs[32]} output. grid (ceil(nb / 8), n), block 256.

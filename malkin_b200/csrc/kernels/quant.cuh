@@ -34,9 +34,11 @@ __device__ __forceinline__ QBlock quant_block32(float v, int lane) {
   return r;
 }
 
-// Writes block b of token t (this warp's lane values already quantized) into the GEMM layout.
-__device__ __forceinline__ void store_act(const ActQ& a, int b, int t, const QBlock& qb, int lane) {
+// Writes block b of token t (this warp's lane values already quantized; v: the lane's float value) into the GEMM
+// layout, and the float value into a.xf when float weights read it.
+__device__ __forceinline__ void store_act(const ActQ& a, int b, int t, const QBlock& qb, int lane, float v) {
   const int npad = a.nt8 * 8;
+  if (a.xf) a.xf[static_cast<size_t>(t) * a.ldxf + b * 32 + lane] = v;
   // Gather 4 consecutive lanes' bytes into one word at lane 4m.
   const uint32_t byte = static_cast<uint32_t>(qb.q) & 0xFFu;
   const uint32_t b1 = __shfl_down_sync(0xffffffffu, byte, 1);

@@ -170,3 +170,24 @@ def test_profile_and_launch_count(mk, model_paths, torch_cuda):
     m.forward(b)
     st = m.stage_times()
     assert len(st) == 8 and all(t >= 0 for t in st) and sum(st) > 0
+
+
+FLOAT_MODELS = {  # malkin's row path for F32 / F16 / BF16 matrices (quant.cpp:171-191, 330-351)
+    "f16": dict(type_default=1), "bf16": dict(type_default=30), "f32": dict(type_default=0),
+    "mixed": dict(type_default=8, type_attn_v=0, type_ffn_down=1, type_output=30),
+}
+
+
+@pytest.mark.parametrize("name", list(FLOAT_MODELS))
+def test_float_weight_models_match_malkin(mk, ref, torch_cuda, tmp_path, name):
+    """F32 / F16 / BF16 matrices (alone, and mixed with Q8_0): prefill and tree-verify logits bit-identical to malkin's
+    CPU Model, which runs them through vec_dot's dot_f32 / dot_f16 / dot_bf16 (16 fma lanes, then reduce_add)."""
+    from oracle import RefModel
+    path = mk.synth_gguf(str(tmp_path / f"{name}.gguf"), n_layer=2, n_embd=256, n_ff=512, n_head=4, n_head_kv=2,
+                         head_dim=64, n_vocab=1000, n_ctx_train=256, seed=6, **FLOAT_MODELS[name])
+    m = load(mk, path, n_ctx=64, n_seq=1)
+    rm = RefModel(ref, path, 64, 1)
+    pre = [(int(t), 0, i, 1, -1, -1) for i, t in enumerate(np.random.default_rng(3).integers(0, 1000, 12))]
+    assert np.array_equal(m.forward(batch_of(mk, pre)), rm.forward(pre))
+    tree = [(17, 0, 12, 1, -1, -1), (23, 0, 13, 1, 13, 0), (5, 0, 13, 1, 14, 0), (99, 0, 14, 1, 15, 1)]
+    assert np.array_equal(m.forward(batch_of(mk, tree)), rm.forward(tree))
