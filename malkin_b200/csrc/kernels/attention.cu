@@ -98,16 +98,17 @@ __global__ void k_qkv_post(Slices qk, int v_n, int64_t v_col0, int64_t ldy, int 
 //   e_j  = exp(s_j - max_j s_j)                      (malkin's exp)
 //   inv  = 1 / reduce16(sums), sum l adds e_j for j = l, l + 16, ... in order
 //   out  = (acc over j in order: acc = fma(e_j * v_scale_j, v_j, acc), from 0) * inv
-// Every float operation is malkin's, in malkin's order, so the output is bit-identical. Four kernels:
+// Every float operation is malkin's, in malkin's order, so the output is bit-identical. Five kernels:
 //   k_att_scores   a thread pair per two prefix keys of a (sub-group, KV head, half of its rows): each thread holds
 //                  eight of the 16 chains of both keys in registers, the query vectors come from shared memory; the
 //                  scores of 128 keys are staged in shared memory, written out as whole rows of the sub-group's
 //                  key-major table ST[j][slot] (slot = row * GA + head, GA = G rounded up to even), followed by
 //                  the chunk's maximum of every slot (a row after the table's maxk rows per 128 keys)
 //   k_att_extras   one warp per (t, h): the scores of the token's extra (ancestor) keys, as 16 chains on a half-warp
-//   k_att_softmax  one CTA per (sub-group, KV head, 32 slots): warp l runs malkin's vector lane l - the lane-striped
-//                  sum of every slot - with 32 slots side by side, the maximum from the chunk maxima; then
-//                  e_j * v_scale_j in place of s_j and 1 / sum
+//   k_att_exp      e_j = exp(s_j - max) in place, elementwise over (256-key chunk, sub-group, KV head) CTAs, the
+//                  maximum from the chunk maxima and the extras
+//   k_att_sum      one CTA per (sub-group, KV head, 32 slots): warp l runs malkin's vector lane l - the lane-striped
+//                  sum of every slot - with 32 slots side by side; e_j * v_scale_j in place and 1 / sum
 //   k_att_pv       one CTA per (sub-group, KV head, 32 of the D values): a producer warp keeps key tiles of the
 //                  probabilities (ST rows) and of the int8 values in flight with TMA bulk copies and converts each
 //                  landed value tile to floats; the consumer warps advance the chains of two heads in one f32x2 FMA
@@ -115,6 +116,8 @@ __global__ void k_qkv_post(Slices qk, int v_n, int64_t v_col0, int64_t ldy, int 
 constexpr int kQMax = 96;         // query vectors (rows x G) per sub-group
 constexpr int kScoreKeys = 128;   // keys per score CTA (and per chunk maximum)
 constexpr int kScoreParts = 2;    // score CTAs that split a sub-group's rows
+constexpr int kExpKeys = 256;     // prefix keys per exp CTA
+constexpr int kMaxSlots = 2 * kQMax;  // slots of a sub-group's table, at most (rows <= kQMax / G, GA <= G + 1)
 constexpr int kPvTile = 32;       // keys per P.V stage
 constexpr int kPvStages = 3;      // P.V ring depth
 constexpr int kPvSliceMax = 32;   // output values per P.V CTA (fewer when the grid would leave SMs idle)
@@ -296,19 +299,74 @@ __global__ void __launch_bounds__(128) k_att_extras(AttArgs a) {
   }
 }
 
+// grid (ceil(longest prefix / kExpKeys), n_sg, KV), block 256: e_j = exp(s_j - max) in place for the table rows
+// j0 .. j0 + kExpKeys - 1 of a (sub-group, KV head), at every slot whose token has key j in its prefix. Each slot's
+// maximum comes from the chunk maxima of the score kernel and the extras (fmaxf: any order gives the same maximum);
+// CTA x = 0 leaves it in inv[t][h] for the extras, which k_att_sum exponentiates. A thread owns 4 consecutive slots
+// (one 16-byte column of the table) and walks rows; elementwise, so the split over CTAs changes no result.
+__global__ void __launch_bounds__(256) k_att_exp(AttArgs a) {
+  __shared__ float smx[kMaxSlots];
+  __shared__ int sn0[kMaxSlots];
+  const int sg = blockIdx.y, kvh = blockIdx.z;
+  const int t0 = a.p.sg_first[sg], rows = a.p.sg_first[sg + 1] - t0;
+  const int maxk = a.p.sg_maxk[sg], nch = att_nch(maxk);
+  const int j0 = blockIdx.x * kExpKeys;
+  if (j0 >= maxk && blockIdx.x > 0) return;
+  const int G = a.G, ga = att_ga(G), nqp = att_nqp(rows, G);
+  float* st = st_of(a, sg, kvh, maxk, nqp);
+  const float* pm = st + static_cast<int64_t>(maxk) * nqp;
+  for (int sl = threadIdx.x; sl < nqp; sl += blockDim.x) {
+    const int r = sl / ga, g = sl - r * ga;
+    int n0 = 0;
+    float mx = -INFINITY;
+    if (r < rows && g < G) {
+      const int t = t0 + r, h = kvh * G + g;
+      n0 = a.p.n_keys[t];
+      const int e0 = a.p.anc_off[t], ne = a.p.anc_off[t + 1] - e0;
+      const float* er = a.p.ex + (static_cast<size_t>(t) * a.H + h) * a.p.ex_stride;
+      const int nc = min(nch, (n0 + kScoreKeys - 1) / kScoreKeys);
+      for (int cc = 0; cc < nc; ++cc) mx = fmaxf(mx, pm[static_cast<int64_t>(cc) * nqp + sl]);
+      for (int e = 0; e < ne; ++e) mx = fmaxf(mx, er[e]);
+      if (blockIdx.x == 0) a.p.inv[static_cast<size_t>(t) * a.H + h] = mx;
+    }
+    smx[sl] = mx;
+    sn0[sl] = n0;
+  }
+  __syncthreads();
+  const int q4 = nqp / 4, rpp = blockDim.x / q4;  // 16-byte columns per row, rows per pass
+  const int rr = threadIdx.x / q4, cq = threadIdx.x - rr * q4;
+  if (rr >= rpp) return;
+  float mx[4];
+  int n0[4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    mx[c] = smx[4 * cq + c];
+    n0[c] = sn0[4 * cq + c];
+  }
+  const int j1 = min(j0 + kExpKeys, maxk);
+  float4* col = reinterpret_cast<float4*>(st) + cq;
+  for (int j = j0 + rr; j < j1; j += rpp) {
+    float4 v = col[static_cast<int64_t>(j) * q4];
+    if (j < n0[0]) v.x = exp_malkin(__fsub_rn(v.x, mx[0]));
+    if (j < n0[1]) v.y = exp_malkin(__fsub_rn(v.y, mx[1]));
+    if (j < n0[2]) v.z = exp_malkin(__fsub_rn(v.z, mx[2]));
+    if (j < n0[3]) v.w = exp_malkin(__fsub_rn(v.w, mx[3]));
+    col[static_cast<int64_t>(j) * q4] = v;
+  }
+}
+
 // grid (n_sg, KV, slot groups of 32), block 512: warp l (0..15) plays malkin's vector lane l for the CTA's 32 slots
-// (lane = slot): the maximum over the slot's keys (any order: the chunk maxima of the score kernel and the extras),
-// then e_j = exp(s_j - max) and the lane-striped sum over keys j = l, l + 16, ... in order (prefix keys from ST,
-// extras from ex), p_j = e_j * v_scale_j written in place; then 1 / reduce16 of the 16 sums.
-__global__ void __launch_bounds__(512) k_att_softmax(AttArgs a) {
+// (lane = slot): the lane-striped sum over keys j = l, l + 16, ... in order (e_j of the prefix keys from the table,
+// of the extras exp(s - max) here from ex and the maximum in inv), p_j = e_j * v_scale_j written in place; then
+// 1 / reduce16 of the 16 sums into inv.
+__global__ void __launch_bounds__(512, 2) k_att_sum(AttArgs a) {
   __shared__ float red[16][33];
   const int sg = blockIdx.x, kvh = blockIdx.y;
   const int l = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = a.p.sg_first[sg], rows = a.p.sg_first[sg + 1] - t0;
-  const int maxk = a.p.sg_maxk[sg], nch = att_nch(maxk);
+  const int maxk = a.p.sg_maxk[sg];
   const int ga = att_ga(a.G), nqp = att_nqp(rows, a.G);
   float* st = st_of(a, sg, kvh, maxk, nqp);
-  const float* pm = st + static_cast<int64_t>(maxk) * nqp;
   const size_t hb = static_cast<size_t>(kvh) * a.L.n_rows + a.p.kv_base[t0];
   const int s0 = blockIdx.z * 32;
   if (s0 >= rows * ga) return;
@@ -318,19 +376,9 @@ __global__ void __launch_bounds__(512) k_att_softmax(AttArgs a) {
   const int n0 = valid ? a.p.n_keys[t] : 0;
   const int e0 = a.p.anc_off[t], ne = valid ? a.p.anc_off[t + 1] - e0 : 0, nk = n0 + ne;
   float* er = a.p.ex + (static_cast<size_t>(t) * a.H + h) * a.p.ex_stride;
-  // maximum: chunk maxima (chunks with keys below n0) and the extras, striped over the warps
-  float mx = -INFINITY;
-  const int nc = valid ? min(nch, (n0 + kScoreKeys - 1) / kScoreKeys) : 0;
-  for (int cc = l; cc < nc; cc += 16) mx = fmaxf(mx, pm[static_cast<int64_t>(cc) * nqp + slot]);
-  for (int e = l; e < ne; e += 16) mx = fmaxf(mx, er[e]);
-  red[l][lane] = mx;
-  __syncthreads();
-  mx = red[0][lane];
-#pragma unroll
-  for (int i = 1; i < 16; ++i) mx = fmaxf(mx, red[i][lane]);
-  __syncthreads();
-  // lane-striped sum in key order; sixteen keys of the stripe loaded at once, only the sum runs in sequence
-  constexpr int kU = 16;
+  const float mx = a.p.inv[static_cast<size_t>(t) * a.H + h];  // rewritten below only after the block barrier
+  // kU keys of the stripe loaded at once, only the sum runs in sequence
+  constexpr int kU = 8;
   float sum = 0.0f;
   for (int jb = l; jb < nk; jb += 16 * kU) {
     float sv[kU], vv[kU];
@@ -344,7 +392,7 @@ __global__ void __launch_bounds__(512) k_att_softmax(AttArgs a) {
     for (int u = 0; u < kU; ++u) {
       const int j = jb + 16 * u;
       if (j < nk) {
-        const float e = exp_malkin(__fsub_rn(sv[u], mx));
+        const float e = j < n0 ? sv[u] : exp_malkin(__fsub_rn(sv[u], mx));
         sum = __fadd_rn(sum, e);
         const float p = __fmul_rn(e, vv[u]);
         if (j < n0)
@@ -611,7 +659,11 @@ void run_attention(const float* q, int H, int KV, float scale, const AttnLayer& 
   if (p.n_sg > 0 && p.kchunks > 0)
     k_att_scores<D><<<dim3(p.kchunks, p.n_sg * kScoreParts, KV), 2 * kScoreKeys / KP, sc_smem(a.G, D), s>>>(a);
   k_att_extras<D><<<dim3(p.n, (H + 3) / 4), 128, 0, s>>>(a);
-  if (p.n_sg > 0) k_att_softmax<<<dim3(p.n_sg, KV, (kQMax / a.G * att_ga(a.G) + 31) / 32), 512, 0, s>>>(a);
+  if (p.n_sg > 0) {
+    const int xc = std::max(1, (p.kchunks * kScoreKeys + kExpKeys - 1) / kExpKeys);
+    k_att_exp<<<dim3(xc, p.n_sg, KV), 256, 0, s>>>(a);
+    k_att_sum<<<dim3(p.n_sg, KV, (kQMax / a.G * att_ga(a.G) + 31) / 32), 512, 0, s>>>(a);
+  }
   switch (a.G) {
     case 1: launch_pv<D, 1>(a, s); break;
     case 2: launch_pv<D, 2>(a, s); break;
