@@ -484,7 +484,7 @@ int mk_attention(const float* dev_q, int n, int H, int KV, int D, const int8_t* 
                     "attention");
     const int64_t exs = (maxex + 3) / 4 * 4;
     const size_t ws_floats = static_cast<size_t>(st_total) + static_cast<size_t>(n) * H * exs +
-                             static_cast<size_t>(n) * H + static_cast<size_t>(n) * H * D;
+                             static_cast<size_t>(n) * H * 2 + static_cast<size_t>(n) * H * D;
     mkb::DevBuf ws(ws_floats * 4);
     p.sg_first = tabs.get<int32_t>();
     p.tok_sg = tabs.get<int32_t>() + sgf.size();
@@ -498,7 +498,8 @@ int mk_attention(const float* dev_q, int n, int H, int KV, int D, const int8_t* 
     p.ex = p.st + st_total;
     p.ex_stride = static_cast<int>(exs);
     p.inv = p.ex + static_cast<size_t>(n) * H * exs;
-    p.att = p.inv + static_cast<size_t>(n) * H;
+    p.exmax = p.inv + static_cast<size_t>(n) * H;
+    p.att = p.exmax + static_cast<size_t>(n) * H;
     mkb::AttnLayer L{const_cast<int8_t*>(dev_k), const_cast<int8_t*>(dev_v), const_cast<float*>(dev_ks),
                      const_cast<float*>(dev_vs), n_rows};
     mkb::launch_attention(dev_q, H, KV, D, 1.0f / std::sqrt(static_cast<float>(D)), L, p, dev_out, mkb::ActQ{}, s);

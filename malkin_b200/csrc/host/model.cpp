@@ -472,8 +472,8 @@ void Model::alloc_kv(int n_ctx, int n_seq, int max_batch) {
     attn_st_cap_ = static_cast<int64_t>(KVl_) * (n_ctx + attn_key_chunks(n_ctx)) * max_batch * (GA + 4);
     attn_ex_stride_ = max_batch;
     const int64_t ex = static_cast<int64_t>(max_batch) * Hl_ * attn_ex_stride_;
-    const int64_t inv = static_cast<int64_t>(max_batch) * Hl_, att = static_cast<int64_t>(max_batch) * Hl_ * D;
-    attn_ws_ = DevBuf(static_cast<size_t>(attn_st_cap_ + ex + inv + att) * sizeof(float));
+    const int64_t inv = static_cast<int64_t>(max_batch) * Hl_ * 2, att = static_cast<int64_t>(max_batch) * Hl_ * D;
+    attn_ws_ = DevBuf(static_cast<size_t>(attn_st_cap_ + ex + inv + att) * sizeof(float));  // inv + exmax
   }
   meta_cap_ = 0;
   ensure_meta(static_cast<size_t>(max_batch) * 16);
@@ -850,7 +850,8 @@ void Model::forward(const mk_batch_token* batch, int n, float* host_logits) {
     plan_.ex = ws + attn_st_cap_;
     plan_.ex_stride = attn_ex_stride_;
     plan_.inv = plan_.ex + static_cast<size_t>(max_batch_) * Hl_ * attn_ex_stride_;
-    plan_.att = plan_.inv + static_cast<size_t>(max_batch_) * Hl_;
+    plan_.exmax = plan_.inv + static_cast<size_t>(max_batch_) * Hl_;
+    plan_.att = plan_.exmax + static_cast<size_t>(max_batch_) * Hl_;
   }
   plan_.status = status_;
 

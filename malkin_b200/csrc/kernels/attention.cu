@@ -98,17 +98,16 @@ __global__ void k_qkv_post(Slices qk, int v_n, int64_t v_col0, int64_t ldy, int 
 //   e_j  = exp(s_j - max_j s_j)                      (malkin's exp)
 //   inv  = 1 / reduce16(sums), sum l adds e_j for j = l, l + 16, ... in order
 //   out  = (acc over j in order: acc = fma(e_j * v_scale_j, v_j, acc), from 0) * inv
-// Every float operation is malkin's, in malkin's order, so the output is bit-identical. Five kernels:
+// Every float operation is malkin's, in malkin's order, so the output is bit-identical. Four kernels:
 //   k_att_scores   a thread pair per two prefix keys of a (sub-group, KV head, half of its rows): each thread holds
 //                  eight of the 16 chains of both keys in registers, the query vectors come from shared memory; the
 //                  scores of 128 keys are staged in shared memory, written out as whole rows of the sub-group's
 //                  key-major table ST[j][slot] (slot = row * GA + head, GA = G rounded up to even), followed by
 //                  the chunk's maximum of every slot (a row after the table's maxk rows per 128 keys)
 //   k_att_extras   one warp per (t, h): the scores of the token's extra (ancestor) keys, as 16 chains on a half-warp
-//   k_att_exp      e_j = exp(s_j - max) in place, elementwise over (256-key chunk, sub-group, KV head) CTAs, the
-//                  maximum from the chunk maxima and the extras
-//   k_att_sum      one CTA per (sub-group, KV head, 32 slots): warp l runs malkin's vector lane l - the lane-striped
-//                  sum of every slot - with 32 slots side by side; e_j * v_scale_j in place and 1 / sum
+//   k_att_softmax  a thread per (slot, malkin vector lane l), the table streamed through a cp.async ring: the maximum
+//                  from the chunk maxima and the extras, then the lane-striped sum over keys l, l + 16, ... in order
+//                  with e_j * v_scale_j in place of s_j
 //   k_att_pv       one CTA per (sub-group, KV head, 32 of the D values): a producer warp keeps key tiles of the
 //                  probabilities (ST rows) and of the int8 values in flight with TMA bulk copies and converts each
 //                  landed value tile to floats; the consumer warps advance the chains of two heads in one f32x2 FMA
@@ -116,8 +115,8 @@ __global__ void k_qkv_post(Slices qk, int v_n, int64_t v_col0, int64_t ldy, int 
 constexpr int kQMax = 96;         // query vectors (rows x G) per sub-group
 constexpr int kScoreKeys = 128;   // keys per score CTA (and per chunk maximum)
 constexpr int kScoreParts = 2;    // score CTAs that split a sub-group's rows
-constexpr int kExpKeys = 256;     // prefix keys per exp CTA
-constexpr int kMaxSlots = 2 * kQMax;  // slots of a sub-group's table, at most (rows <= kQMax / G, GA <= G + 1)
+constexpr int kSmStages = 4;      // softmax cp.async ring depth
+constexpr int kSmStageFloats = 2048;  // table floats per softmax stage (8 KB)
 constexpr int kPvTile = 32;       // keys per P.V stage
 constexpr int kPvStages = 3;      // P.V ring depth
 constexpr int kPvSliceMax = 32;   // output values per P.V CTA (fewer when the grid would leave SMs idle)
@@ -273,7 +272,8 @@ __global__ void __launch_bounds__(2 * kScoreKeys / sc_kp<D>(), D <= 128 ? 3 : 1)
 }
 
 // grid (n, ceil(H / 4)), block 128: warp w computes the extra keys' scores of (t = blockIdx.x, h = blockIdx.y * 4 + w)
-// into ex[t][h][e]: lane l < 16 runs chain l (the lanes of malkin's vector), reduce16 across the half-warp.
+// into ex[t][h][e] and their maximum into exmax[t][h]: lane l < 16 runs chain l (the lanes of malkin's vector),
+// reduce16 across the half-warp.
 template <int D>
 __global__ void __launch_bounds__(128) k_att_extras(AttArgs a) {
   constexpr int DC = D / 16;
@@ -288,6 +288,7 @@ __global__ void __launch_bounds__(128) k_att_extras(AttArgs a) {
 #pragma unroll
   for (int i = 0; i < DC; ++i) q[i] = qv[16 * i + (lane & 15)];
   float* er = a.p.ex + (static_cast<size_t>(t) * a.H + h) * a.p.ex_stride;
+  float mx = -INFINITY;
   for (int e = 0; e < ne; ++e) {
     const size_t row = hb + a.p.anc[e0 + e];
     const int8_t* kr = a.L.k + row * D;
@@ -295,119 +296,121 @@ __global__ void __launch_bounds__(128) k_att_extras(AttArgs a) {
 #pragma unroll
     for (int i = 1; i < DC; ++i) acc = __fmaf_rn(q[i], i8f(kr[16 * i + (lane & 15)]), acc);
     acc = reduce16(acc);
-    if (lane == 0) er[e] = __fmul_rn(acc, __fmul_rn(a.L.ks[row], a.scale));
+    const float sc = __fmul_rn(acc, __fmul_rn(a.L.ks[row], a.scale));
+    mx = fmaxf(mx, sc);
+    if (lane == 0) er[e] = sc;
   }
+  if (lane == 0) a.p.exmax[static_cast<size_t>(t) * a.H + h] = mx;
 }
 
-// grid (ceil(longest prefix / kExpKeys), n_sg, KV), block 256: e_j = exp(s_j - max) in place for the table rows
-// j0 .. j0 + kExpKeys - 1 of a (sub-group, KV head), at every slot whose token has key j in its prefix. Each slot's
-// maximum comes from the chunk maxima of the score kernel and the extras (fmaxf: any order gives the same maximum);
-// CTA x = 0 leaves it in inv[t][h] for the extras, which k_att_sum exponentiates. A thread owns 4 consecutive slots
-// (one 16-byte column of the table) and walks rows; elementwise, so the split over CTAs changes no result.
-__global__ void __launch_bounds__(256) k_att_exp(AttArgs a) {
-  __shared__ float smx[kMaxSlots];
-  __shared__ int sn0[kMaxSlots];
-  const int sg = blockIdx.y, kvh = blockIdx.z;
+__device__ __forceinline__ void cp_async16(void* sm, const void* g) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(sm))),
+               "l"(g)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* sm, const void* g) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(sm))),
+               "l"(g)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// Stage `it` of the softmax ring: table rows it * TK .. + TK - 1 at the CTA's SG slots (16-byte copies) and their
+// value scales (4-byte copies; the cache rows have no 16-byte alignment), one commit group.
+template <int SG>
+__device__ __forceinline__ void sm_issue(const AttArgs& a, const float* st, int nqp, int s0, int maxk, size_t hb,
+                                         int it, float* tile, float* vst) {
+  constexpr int TK = kSmStageFloats / SG, CPR = SG / 4;
+  const int jt = it * TK;
+  for (int i = threadIdx.x; i < TK * CPR; i += 16 * SG) {
+    const int rr = i / CPR, cc = i - rr * CPR, j = jt + rr;
+    if (j < maxk && s0 + 4 * cc < nqp) cp_async16(tile + rr * SG + 4 * cc, st + static_cast<int64_t>(j) * nqp + s0 + 4 * cc);
+  }
+  for (int i = threadIdx.x; i < TK; i += 16 * SG)
+    if (jt + i < maxk) cp_async4(vst + i, a.L.vs + hb + jt + i);
+  cp_async_commit();
+}
+
+// grid (slot groups of SG, n_sg, KV), block 16 x SG: thread (l, sl) = threadIdx.x / SG, % SG runs malkin's vector lane
+// l (0..15) of slot s0 + sl. The maximum over the slot's keys (any order: the chunk maxima of the score kernel, striped
+// over the lanes, and the extras' maximum), then the table streams through shared memory in a kSmStages-deep cp.async
+// ring of kSmStageFloats-float tiles, and each thread walks its keys j = l, l + 16, ... in order: e_j = exp(s_j - max),
+// sum += e_j, p_j = e_j * v_scale_j written in place; then the extras (keys n0 .. nk - 1 of the stripe, from ex),
+// and 1 / reduce16 of the slot's 16 lane sums into inv. SG (32, 16, 8 or 4 slots per CTA) is picked per launch so
+// the grid covers the SMs.
+template <int SG>
+__global__ void __launch_bounds__(16 * SG) k_att_softmax(AttArgs a) {
+  constexpr int TK = kSmStageFloats / SG;
+  __shared__ __align__(16) float tile[kSmStages][kSmStageFloats];
+  __shared__ float vst[kSmStages][TK];
+  __shared__ float red[16][SG + 1], rsum[16][SG + 1];
+  const int sg = blockIdx.y, kvh = blockIdx.z, s0 = blockIdx.x * SG;
   const int t0 = a.p.sg_first[sg], rows = a.p.sg_first[sg + 1] - t0;
   const int maxk = a.p.sg_maxk[sg], nch = att_nch(maxk);
-  const int j0 = blockIdx.x * kExpKeys;
-  if (j0 >= maxk && blockIdx.x > 0) return;
   const int G = a.G, ga = att_ga(G), nqp = att_nqp(rows, G);
-  float* st = st_of(a, sg, kvh, maxk, nqp);
-  const float* pm = st + static_cast<int64_t>(maxk) * nqp;
-  for (int sl = threadIdx.x; sl < nqp; sl += blockDim.x) {
-    const int r = sl / ga, g = sl - r * ga;
-    int n0 = 0;
-    float mx = -INFINITY;
-    if (r < rows && g < G) {
-      const int t = t0 + r, h = kvh * G + g;
-      n0 = a.p.n_keys[t];
-      const int e0 = a.p.anc_off[t], ne = a.p.anc_off[t + 1] - e0;
-      const float* er = a.p.ex + (static_cast<size_t>(t) * a.H + h) * a.p.ex_stride;
-      const int nc = min(nch, (n0 + kScoreKeys - 1) / kScoreKeys);
-      for (int cc = 0; cc < nc; ++cc) mx = fmaxf(mx, pm[static_cast<int64_t>(cc) * nqp + sl]);
-      for (int e = 0; e < ne; ++e) mx = fmaxf(mx, er[e]);
-      if (blockIdx.x == 0) a.p.inv[static_cast<size_t>(t) * a.H + h] = mx;
-    }
-    smx[sl] = mx;
-    sn0[sl] = n0;
-  }
-  __syncthreads();
-  const int q4 = nqp / 4, rpp = blockDim.x / q4;  // 16-byte columns per row, rows per pass
-  const int rr = threadIdx.x / q4, cq = threadIdx.x - rr * q4;
-  if (rr >= rpp) return;
-  float mx[4];
-  int n0[4];
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    mx[c] = smx[4 * cq + c];
-    n0[c] = sn0[4 * cq + c];
-  }
-  const int j1 = min(j0 + kExpKeys, maxk);
-  float4* col = reinterpret_cast<float4*>(st) + cq;
-  for (int j = j0 + rr; j < j1; j += rpp) {
-    float4 v = col[static_cast<int64_t>(j) * q4];
-    if (j < n0[0]) v.x = exp_malkin(__fsub_rn(v.x, mx[0]));
-    if (j < n0[1]) v.y = exp_malkin(__fsub_rn(v.y, mx[1]));
-    if (j < n0[2]) v.z = exp_malkin(__fsub_rn(v.z, mx[2]));
-    if (j < n0[3]) v.w = exp_malkin(__fsub_rn(v.w, mx[3]));
-    col[static_cast<int64_t>(j) * q4] = v;
-  }
-}
-
-// grid (n_sg, KV, slot groups of 32), block 512: warp l (0..15) plays malkin's vector lane l for the CTA's 32 slots
-// (lane = slot): the lane-striped sum over keys j = l, l + 16, ... in order (e_j of the prefix keys from the table,
-// of the extras exp(s - max) here from ex and the maximum in inv), p_j = e_j * v_scale_j written in place; then
-// 1 / reduce16 of the 16 sums into inv.
-__global__ void __launch_bounds__(512, 2) k_att_sum(AttArgs a) {
-  __shared__ float red[16][33];
-  const int sg = blockIdx.x, kvh = blockIdx.y;
-  const int l = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t0 = a.p.sg_first[sg], rows = a.p.sg_first[sg + 1] - t0;
-  const int maxk = a.p.sg_maxk[sg];
-  const int ga = att_ga(a.G), nqp = att_nqp(rows, a.G);
-  float* st = st_of(a, sg, kvh, maxk, nqp);
-  const size_t hb = static_cast<size_t>(kvh) * a.L.n_rows + a.p.kv_base[t0];
-  const int s0 = blockIdx.z * 32;
-  if (s0 >= rows * ga) return;
-  const int slot = s0 + lane, r = slot / ga, g = slot % ga;
-  const bool valid = r < rows && g < a.G;
-  const int t = t0 + (valid ? r : 0), h = kvh * a.G + (valid ? g : 0);
+  if (s0 >= nqp) return;
+  const int l = threadIdx.x / SG, sl = threadIdx.x - l * SG, slot = s0 + sl;
+  const int r = slot / ga, g = slot - r * ga;
+  const bool valid = slot < nqp && r < rows && g < G;
+  const int t = t0 + (valid ? r : 0), h = kvh * G + (valid ? g : 0);
   const int n0 = valid ? a.p.n_keys[t] : 0;
   const int e0 = a.p.anc_off[t], ne = valid ? a.p.anc_off[t + 1] - e0 : 0, nk = n0 + ne;
-  float* er = a.p.ex + (static_cast<size_t>(t) * a.H + h) * a.p.ex_stride;
-  const float mx = a.p.inv[static_cast<size_t>(t) * a.H + h];  // rewritten below only after the block barrier
-  // kU keys of the stripe loaded at once, only the sum runs in sequence
-  constexpr int kU = 8;
+  float* st = st_of(a, sg, kvh, maxk, nqp);
+  const float* pm = st + static_cast<int64_t>(maxk) * nqp;
+  const size_t hb = static_cast<size_t>(kvh) * a.L.n_rows + a.p.kv_base[t0];
+  const int ntiles = (maxk + TK - 1) / TK;
+  for (int it = 0; it < kSmStages - 1; ++it) {
+    if (it < ntiles)
+      sm_issue<SG>(a, st, nqp, s0, maxk, hb, it, tile[it], vst[it]);
+    else
+      cp_async_commit();
+  }
+  float mx = l == 0 && ne > 0 ? a.p.exmax[static_cast<size_t>(t) * a.H + h] : -INFINITY;
+  const int nc = valid ? min(nch, (n0 + kScoreKeys - 1) / kScoreKeys) : 0;
+  for (int cc = l; cc < nc; cc += 16) mx = fmaxf(mx, pm[static_cast<int64_t>(cc) * nqp + slot]);
+  red[l][sl] = mx;
+  __syncthreads();
+  mx = red[0][sl];
+#pragma unroll
+  for (int i = 1; i < 16; ++i) mx = fmaxf(mx, red[i][sl]);
   float sum = 0.0f;
-  for (int jb = l; jb < nk; jb += 16 * kU) {
-    float sv[kU], vv[kU];
-#pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      const int j = jb + 16 * u;
-      sv[u] = j < nk ? (j < n0 ? st[static_cast<int64_t>(j) * nqp + slot] : er[j - n0]) : 0.0f;
-      vv[u] = j < nk ? a.L.vs[j < n0 ? hb + j : hb + a.p.anc[e0 + j - n0]] : 0.0f;
-    }
-#pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      const int j = jb + 16 * u;
-      if (j < nk) {
-        const float e = j < n0 ? sv[u] : exp_malkin(__fsub_rn(sv[u], mx));
-        sum = __fadd_rn(sum, e);
-        const float p = __fmul_rn(e, vv[u]);
-        if (j < n0)
-          st[static_cast<int64_t>(j) * nqp + slot] = p;
-        else
-          er[j - n0] = p;
-      }
+  for (int it = 0; it < ntiles; ++it) {
+    cp_async_wait<kSmStages - 2>();
+    __syncthreads();  // tile `it` landed for every thread; the stage of tile it - 1 is free
+    const int nx = it + kSmStages - 1;
+    if (nx < ntiles)
+      sm_issue<SG>(a, st, nqp, s0, maxk, hb, nx, tile[nx % kSmStages], vst[nx % kSmStages]);
+    else
+      cp_async_commit();
+    const int jt = it * TK;
+    const float* tl = tile[it % kSmStages];
+    const float* vl = vst[it % kSmStages];
+    const int lim = min(TK, n0 - jt);
+#pragma unroll 4
+    for (int i = l; i < lim; i += 16) {
+      const float e = exp_malkin(__fsub_rn(tl[i * SG + sl], mx));
+      sum = __fadd_rn(sum, e);
+      st[static_cast<int64_t>(jt + i) * nqp + slot] = __fmul_rn(e, vl[i]);
     }
   }
-  red[l][lane] = sum;
+  cp_async_wait<0>();
+  float* er = a.p.ex + (static_cast<size_t>(t) * a.H + h) * a.p.ex_stride;
+  // the extras: from the first key >= n0 of lane l's stripe on
+  for (int j = n0 + ((l - n0 % 16) + 16) % 16; j < nk; j += 16) {
+    const float e = exp_malkin(__fsub_rn(er[j - n0], mx));
+    sum = __fadd_rn(sum, e);
+    er[j - n0] = __fmul_rn(e, a.L.vs[hb + a.p.anc[e0 + j - n0]]);
+  }
+  rsum[l][sl] = sum;
   __syncthreads();
-  if (l == 0 && valid) {
+  if (l == 0 && valid) {  // malkin's reduce_add of the 16 lane sums
     float b8[8], c4[4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) b8[i] = __fadd_rn(red[i + 8][lane], red[i][lane]);
+    for (int i = 0; i < 8; ++i) b8[i] = __fadd_rn(rsum[i + 8][sl], rsum[i][sl]);
 #pragma unroll
     for (int i = 0; i < 4; ++i) c4[i] = __fadd_rn(b8[i + 4], b8[i]);
     const float tot = __fadd_rn(__fadd_rn(c4[0], c4[2]), __fadd_rn(c4[1], c4[3]));
@@ -641,6 +644,35 @@ void launch_pv(const AttArgs& a, cudaStream_t s) {
   }
 }
 
+// Slots per softmax CTA: 32, halved while the grid (sub-groups x KV heads x slot groups of the largest sub-group)
+// would cover fewer than two CTAs per SM; MALKIN_B200_SM_SLOTS = 32 / 16 / 8 / 4 forces one.
+template <int SG>
+void launch_softmax_s(const AttArgs& a, int nqp, cudaStream_t s) {
+  k_att_softmax<SG><<<dim3((nqp + SG - 1) / SG, a.p.n_sg, a.KV), 16 * SG, 0, s>>>(a);
+}
+
+void launch_softmax(const AttArgs& a, cudaStream_t s) {
+  static int sms[kMaxDevices] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < kMaxDevices && !sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+  const int nsm = dev < kMaxDevices && sms[dev] ? sms[dev] : 148;
+  const int nqp = att_nqp(kQMax / a.G, a.G);  // the largest sub-group's slots; CTAs past a smaller one exit
+  const char* e = std::getenv("MALKIN_B200_SM_SLOTS");
+  const int v = e ? std::atoi(e) : 0;
+  int SG = v == 32 || v == 16 || v == 8 || v == 4 ? v : 0;
+  if (!SG) {
+    SG = 32;
+    while (SG > 4 && a.p.n_sg * a.KV * ((nqp + SG - 1) / SG) < 2 * nsm) SG /= 2;
+  }
+  switch (SG) {
+    case 32: launch_softmax_s<32>(a, nqp, s); break;
+    case 16: launch_softmax_s<16>(a, nqp, s); break;
+    case 8: launch_softmax_s<8>(a, nqp, s); break;
+    default: launch_softmax_s<4>(a, nqp, s); break;
+  }
+}
+
 template <int D>
 void run_attention(const float* q, int H, int KV, float scale, const AttnLayer& L, const AttnPlan& p, float* out,
                    const ActQ& act, cudaStream_t s) {
@@ -659,11 +691,7 @@ void run_attention(const float* q, int H, int KV, float scale, const AttnLayer& 
   if (p.n_sg > 0 && p.kchunks > 0)
     k_att_scores<D><<<dim3(p.kchunks, p.n_sg * kScoreParts, KV), 2 * kScoreKeys / KP, sc_smem(a.G, D), s>>>(a);
   k_att_extras<D><<<dim3(p.n, (H + 3) / 4), 128, 0, s>>>(a);
-  if (p.n_sg > 0) {
-    const int xc = std::max(1, (p.kchunks * kScoreKeys + kExpKeys - 1) / kExpKeys);
-    k_att_exp<<<dim3(xc, p.n_sg, KV), 256, 0, s>>>(a);
-    k_att_sum<<<dim3(p.n_sg, KV, (kQMax / a.G * att_ga(a.G) + 31) / 32), 512, 0, s>>>(a);
-  }
+  if (p.n_sg > 0) launch_softmax(a, s);
   switch (a.G) {
     case 1: launch_pv<D, 1>(a, s); break;
     case 2: launch_pv<D, 2>(a, s); break;

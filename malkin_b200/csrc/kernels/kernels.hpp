@@ -167,6 +167,7 @@ struct AttnPlan {
   float* ex = nullptr;                // [n][H][ex_stride] the extra keys' scores, then probabilities
   int ex_stride = 0;                  // >= the most extra keys of any token
   float* inv = nullptr;               // [n][H] 1 / sum of e_j
+  float* exmax = nullptr;             // [n][H] the largest extra-key score
   float* att = nullptr;               // [n][H][D] output when the caller passes none (workspace)
   int* status = nullptr;              // device word for bounded-wait failures (nullable)
 };

@@ -156,7 +156,20 @@ def test_attention_golden(mk, golden, torch_cuda):
 def test_attention_tree_batch_vs_oracle(mk, oracle, torch_cuda, H, KV, D):
     """Two sequences, a 9-node tree on one and a 5-token prompt chunk on the other, long prefix (several key chunks
     and P.V tiles): bit-identical to the oracle's restatement of attend_gqa for G = 1, 2, 3, 4, 5, 8 and D = 64, 128, 256."""
-    torch = torch_cuda
+    _tree_batch_check(mk, oracle, torch_cuda, H, KV, D)
+
+
+@pytest.mark.parametrize("width", [32, 16, 8, 4])
+@pytest.mark.parametrize("H,KV,D", [(8, 2, 128), (40, 8, 128), (4, 1, 256)])
+def test_attention_forced_widths(mk, oracle, torch_cuda, monkeypatch, H, KV, D, width):
+    """Every softmax CTA width (slots per CTA) and P.V value-slice width that the per-launch rule can pick, forced:
+    each bit-identical to the oracle."""
+    monkeypatch.setenv("MALKIN_B200_SM_SLOTS", str(width))
+    monkeypatch.setenv("MALKIN_B200_PV_SLICE", str(width))
+    _tree_batch_check(mk, oracle, torch_cuda, H, KV, D)
+
+
+def _tree_batch_check(mk, oracle, torch, H, KV, D):
     rng = np.random.default_rng(5 + H + D)
     n_ctx = 700
     G = H // KV
