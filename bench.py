@@ -295,9 +295,12 @@ def config_json(args, cfg):
            "prompt": cfg["prompt"], "parallelism": f"tp{args.gpus}",
            "q8_gemm": os.environ.get("MALKIN_B200_Q8_GEMM", "exact"),
            "l2": "inputs larger than L2 (weights stream from HBM every step)"}
-    if args.gpus > 1:
+    if args.gpus > 1 and os.environ.get("MALKIN_B200_TP_SPLIT", "") == "rows":
+        out["tp_split"] = "rows (wo / down by input columns, rank sum)"
         out["tp_reduce"] = {"nccl": "ncclAllReduce", "twoshot": "peer memory, two-shot"}.get(
             os.environ.get("MALKIN_B200_TP_REDUCE", ""), "peer memory, one-shot")
+    elif args.gpus > 1:
+        out["tp_split"] = "exact (wo / down by output features over gathered inputs, NCCL broadcasts + all-gather)"
     return out
 
 

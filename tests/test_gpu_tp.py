@@ -12,6 +12,13 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 TOL = 2e-2
+# a model every tensor-parallel size divides: heads, KV heads, E / (16 tp), ffn blocks and vocabulary panels
+TP_SPEC = dict(n_layer=2, n_embd=512, n_ff=1024, n_head=8, n_head_kv=8, head_dim=64, n_vocab=1024, seed=11)
+
+
+@pytest.fixture(scope="module")
+def tp_model(tmp_path_factory, mk):
+    return mk.synth_gguf(str(tmp_path_factory.mktemp("tp") / "tp.gguf"), type_default=mk.TYPE_Q8_0, **TP_SPEC)
 
 
 def _batches(rng):
@@ -61,12 +68,12 @@ def _child(rank, world, nccl_id, path, seed, q, mode):
 
 @pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("mode", ["exact", "oneshot", "twoshot", "nccl"])
-def test_tp_matches_single_gpu(mk, model_paths, torch_cuda, world, mode):
+def test_tp_matches_single_gpu(mk, tp_model, torch_cuda, world, mode):
     torch = torch_cuda
     if torch.cuda.device_count() < world:
         pytest.skip(f"tensor parallel over {world} ranks needs {world} GPUs")
     import torch.multiprocessing as mp
-    path, seed = model_paths["q8"], 7
+    path, seed = tp_model, 7
     ref_pl, ref_tl, ref_acc = _run(mk, path, 0, 0, 1, None, seed)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
