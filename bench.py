@@ -311,7 +311,9 @@ PROBE_GEMM_SHAPES = {  # name: (rows, cols, weight type); the 8B Q8_0 matrices, 
     "gate+up": (24576, 4096, Q8_0), "down": (4096, 12288, Q8_0), "qkv": (6144, 4096, Q8_0), "wo": (4096, 4096, Q8_0),
     "lm_head": (151936, 4096, Q8_0), "gate+up_q4k_4b": (19456, 2560, Q4_K), "down_q6k_4b": (2560, 9728, Q6_K),
     "gate+up_q6k_14b": (34816, 5120, Q6_K), "down_q6k_14b": (5120, 17408, Q6_K),
-    "down_tp2": (2048, 12288, Q8_0), "down_tp8": (512, 12288, Q8_0)}
+    "down_tp2": (2048, 12288, Q8_0), "down_tp8": (512, 12288, Q8_0),
+    "q_q4k_4b": (4096, 2560, Q4_K), "wo_q4k_4b": (2560, 4096, Q4_K), "v_q6k_4b": (1024, 2560, Q6_K),
+    "gate+up_06b": (6144, 1024, Q8_0), "down_06b": (1024, 3072, Q8_0), "qkv_06b": (4096, 1024, Q8_0)}
 
 
 def probe_gemm(shapes, layouts, n: int, reps: int) -> None:

@@ -303,22 +303,6 @@ __global__ void __launch_bounds__(128) k_att_extras(AttArgs a) {
   if (lane == 0) a.p.exmax[static_cast<size_t>(t) * a.H + h] = mx;
 }
 
-__device__ __forceinline__ void cp_async16(void* sm, const void* g) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(sm))),
-               "l"(g)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async4(void* sm, const void* g) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(sm))),
-               "l"(g)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
-}
-
 // Stage `it` of the softmax ring: table rows it * TK .. + TK - 1 at the CTA's SG slots (16-byte copies) and their
 // value scales (4-byte copies; the cache rows have no 16-byte alignment), one commit group.
 template <int SG>

@@ -167,6 +167,23 @@ __device__ __forceinline__ float sum_strided(const float* p, int64_t stride) {
 // e^x as malkin computes it for softmax and SiLU (kernels_avx512.cpp:186-203): clamp below at -87, Cody-Waite
 // reduction with ln 2 split in two, degree-6 Taylor polynomial in Horner form with fused multiply-adds, then
 // scaling by 2^n. (malkin's own algorithm, restated, so both sides exponentiate identically.)
+// cp.async (16-byte global -> shared copies, 4-byte for unaligned scalars), commit groups and bounded waits
+__device__ __forceinline__ void cp_async16(void* sm, const void* g) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(sm))),
+               "l"(g)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* sm, const void* g) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(sm))),
+               "l"(g)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
 __device__ __forceinline__ float exp_malkin(float x) {
   x = fmaxf(x, -87.0f);
   const float n = rintf(__fmul_rn(x, 1.44269504088896341f));

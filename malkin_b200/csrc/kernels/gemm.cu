@@ -361,6 +361,157 @@ __global__ void __launch_bounds__(kThreadsG, NTW <= 7 ? 2 : 1) k_gemm(GemmArgs a
   }
 }
 
+
+// ---------------- small-row regime: dp4a ----------------
+// A few tokens against a deep or narrow weight give the mma tiles few CTAs (rows / 32 at most) and leave most of
+// their warps without token tiles. Here a warp covers one whole panel (16 rows) x 2 tokens: lane L = 4 g + c reads
+// the panel chunk's 16-byte fragment L (rows g, g + 8, value quarter c of a 32-value block) with one coalesced
+// load, takes 4 dp4a per 16 values for the entries (row g, g + 8) x (token t0, t0 + 1), and a two-step shuffle
+// butterfly over the 4 lanes of the quad leaves lane c with the whole integer dot of entry c: row g + 8 (c / 2),
+// token t0 + c % 2. Integer sums are exact in any order, so each dot equals the mma's; the lane then runs malkin's
+// float chain for its (row, token) over the blocks in order with the same roundings as k_gemm: bit-identical.
+constexpr int kDpWarps = 4;  // warps per CTA: one panel x one 8-token tile
+
+// lanes c of a quad hold partial dots p0..p3 of entries 0..3; returns the quad's total of entry c
+__device__ __forceinline__ int quad_take(int p0, int p1, int p2, int p3, int c) {
+  const bool b0 = c & 1, b1 = (c >> 1) & 1;
+  const int k0 = b0 ? p1 : p0, s0 = b0 ? p0 : p1;  // keep entry b0, send the partner's
+  const int k1 = b0 ? p3 : p2, s1 = b0 ? p2 : p3;  // keep entry 2 + b0
+  const int r0 = k0 + __shfl_xor_sync(0xffffffffu, s0, 1);
+  const int r1 = k1 + __shfl_xor_sync(0xffffffffu, s1, 1);
+  const int k = b1 ? r1 : r0, sd = b1 ? r0 : r1;  // keep entry b0 + 2 b1
+  return k + __shfl_xor_sync(0xffffffffu, sd, 2);
+}
+
+// entries (row g, t0), (row g, t1), (row g + 8, t0), (row g + 8, t1) of one 16-value half: weight words wg, wg8,
+// activation words x0, x1 (4 values each)
+__device__ __forceinline__ int quad_dot(uint32_t wg, uint32_t wg8, uint32_t x0, uint32_t x1, int c) {
+  return quad_take(__dp4a(static_cast<int>(wg), static_cast<int>(x0), 0), __dp4a(static_cast<int>(wg), static_cast<int>(x1), 0),
+                   __dp4a(static_cast<int>(wg8), static_cast<int>(x0), 0), __dp4a(static_cast<int>(wg8), static_cast<int>(x1), 0), c);
+}
+
+// One stage of the dp4a ring: KU k-units of the panel's weight chunks, the token tile's activation blocks (int8
+// fragments), their d (and the Q4_K min term or the Q6_K half sums); every part a multiple of 16 bytes.
+template <uint32_t T>
+struct DpCfg {
+  using C = TypeCfg<T>;
+  static constexpr int KU = T == 8 ? 8 : 1;       // k-units per stage (8 blocks of 32 values)
+  static constexpr int BLK = KU * C::BPU;
+  static constexpr int WB = KU * C::UNIT, XB = BLK * 256, SB = BLK * 32;
+  static constexpr int EX = (C::kDsx || C::kSh) ? SB : 0;
+  static constexpr int BYTES = WB + XB + SB + EX;
+};
+constexpr int kDpStages = 4;
+
+template <uint32_t T>
+__device__ __forceinline__ void dp_issue(const GemmArgs& a, int64_t p, int tt, int u0, uint8_t* sm) {
+  using D = DpCfg<T>;
+  using C = TypeCfg<T>;
+  const int uk = min(D::KU, a.kunits - u0), nb = uk * C::BPU;
+  const uint8_t* wsrc = a.w + (static_cast<size_t>(p) * a.kunits + u0) * C::UNIT;
+  for (int i = threadIdx.x; i < uk * static_cast<int>(C::UNIT) / 16; i += blockDim.x) cp_async16(sm + 16 * i, wsrc + 16 * i);
+  const int64_t b0 = static_cast<int64_t>(u0) * C::BPU, npad = static_cast<int64_t>(a.nt8) * 8;
+  for (int i = threadIdx.x; i < nb * 16; i += blockDim.x) {
+    const int bb = i >> 4, q = i & 15;
+    cp_async16(sm + D::WB + bb * 256 + 16 * q, a.qx + ((b0 + bb) * a.nt8 + tt) * 256 + 16 * q);
+  }
+  for (int i = threadIdx.x; i < nb * 2; i += blockDim.x) {
+    const int bb = i >> 1, q = i & 1;
+    const int64_t off = (b0 + bb) * npad + tt * 8 + 4 * q;
+    cp_async16(sm + D::WB + D::XB + bb * 32 + 16 * q, a.dx + off);
+    if constexpr (C::kDsx) cp_async16(sm + D::WB + D::XB + D::SB + bb * 32 + 16 * q, a.dsx + off);
+    if constexpr (C::kSh) cp_async16(sm + D::WB + D::XB + D::SB + bb * 32 + 16 * q, a.sh + off);
+  }
+  cp_async_commit();
+}
+
+// grid (panels, token tiles), block 32 kDpWarps: warp w takes tokens 8 blockIdx.y + 2 w, + 1 of the panel; the CTA
+// streams the panel's chunks and the tile's activations through a kDpStages-deep cp.async ring.
+template <uint32_t T>
+__global__ void __launch_bounds__(32 * kDpWarps) k_gemm_dp4a(GemmArgs a) {
+  using C = TypeCfg<T>;
+  using D = DpCfg<T>;
+  __shared__ __align__(16) uint8_t sm[kDpStages][D::BYTES];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3, h = c >> 1;
+  const int64_t p = blockIdx.x;
+  const int tt = blockIdx.y, t0 = tt * 8 + 2 * warp;
+  const bool active = t0 < a.n;    // warps past the last token still copy and wait
+  const int tl = 2 * warp + (c & 1), t = tt * 8 + tl;  // this lane's token (in the tile, overall)
+  const int64_t row = p * 16 + g + 8 * h;
+  const int nst = (a.kunits + D::KU - 1) / D::KU;
+  for (int s = 0; s < kDpStages - 1; ++s) {
+    if (s < nst)
+      dp_issue<T>(a, p, tt, s * D::KU, sm[s]);
+    else
+      cp_async_commit();
+  }
+  float acc = 0.0f;
+  for (int it = 0; it < nst; ++it) {
+    cp_async_wait<kDpStages - 2>();
+    __syncthreads();  // stage `it` landed for every thread; the stage of it - 1 is free
+    const int nx = it + kDpStages - 1;
+    if (nx < nst)
+      dp_issue<T>(a, p, tt, nx * D::KU, sm[nx % kDpStages]);
+    else
+      cp_async_commit();
+    if (!active) continue;
+    const uint8_t* st = sm[it % kDpStages];
+    const uint8_t* xs = st + D::WB + 8 * (4 * (2 * warp) + c);  // token t0's quarter c; t0 + 1 at + 32
+    const float* dxs = reinterpret_cast<const float*>(st + D::WB + D::XB) + tl;
+    if constexpr (T == 8) {
+      const int uk = min(D::KU, a.kunits - it * D::KU);
+#pragma unroll 4
+      for (int uu = 0; uu < uk; ++uu) {
+        const uint8_t* ch = st + uu * C::UNIT;
+        const uint4 A = *reinterpret_cast<const uint4*>(ch + 16 * lane);  // (g lo, g+8 lo, g hi, g+8 hi)
+        const uint2 x0 = *reinterpret_cast<const uint2*>(xs + uu * 256), x1 = *reinterpret_cast<const uint2*>(xs + uu * 256 + 32);
+        const int lo = quad_dot(A.x, A.y, x0.x, x1.x, c), hi = quad_dot(A.z, A.w, x0.y, x1.y, c);
+        const float dw = __half2float(*reinterpret_cast<const __half*>(ch + 512 + 4 * g + 2 * h));
+        acc = __fmaf_rn(__int2float_rn(lo + hi), __fmul_rn(dw, dxs[uu * 8]), acc);
+      }
+    } else if constexpr (T == 12) {
+      const uint4 H = *reinterpret_cast<const uint4*>(st + 2048 + 32 * g + 16 * h);  // this lane's row's head
+      const float d = h2f_lo(H.x), dmin = h2f_hi(H.x);
+      const float* dss = reinterpret_cast<const float*>(st + D::WB + D::XB + D::SB) + tl;
+#pragma unroll 2
+      for (int j = 0; j < 8; ++j) {
+        const uint2 w = *reinterpret_cast<const uint2*>(st + 256 * j + 8 * lane);  // rows g, g + 8
+        const uint2 x0 = *reinterpret_cast<const uint2*>(xs + j * 256), x1 = *reinterpret_cast<const uint2*>(xs + j * 256 + 32);
+        const int lo = quad_dot(w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, x0.x, x1.x, c);
+        const int hi = quad_dot((w.x >> 4) & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu, x0.y, x1.y, c);
+        int sc, m;
+        q4k_scale_min(j, H.y, H.z, H.w, sc, m);
+        const float scg = __fmul_rn(d, static_cast<float>(sc)), mng = __fmul_rn(dmin, static_cast<float>(m));
+        acc = __fmaf_rn(-mng, dss[j * 8], __fmaf_rn(__int2float_rn(lo + hi), __fmul_rn(scg, dxs[j * 8]), acc));
+      }
+    } else {  // Q6_K: two 16-value halves per block, q stored +32 (the half sums s remove the offset)
+      const uint4 SG = *reinterpret_cast<const uint4*>(st + 3072 + 32 * g + 16 * h);  // this row's 16 scales
+      const float dd = __half2float(*reinterpret_cast<const __half*>(st + 3328 + 4 * g + 2 * h));
+      const uint32_t* shs = reinterpret_cast<const uint32_t*>(st + D::WB + D::XB + D::SB) + tl;
+#pragma unroll 2
+      for (int j = 0; j < 8; ++j) {
+        const uint2 w = *reinterpret_cast<const uint2*>(st + 256 * j + 8 * lane);
+        const uint32_t hb = *reinterpret_cast<const uint32_t*>(st + 2048 + 128 * j + 4 * lane);
+        const uint2 x0 = *reinterpret_cast<const uint2*>(xs + j * 256), x1 = *reinterpret_cast<const uint2*>(xs + j * 256 + 32);
+        const int lo = quad_dot((w.x & 0x0F0F0F0Fu) | ((hb << 4) & 0x30303030u),
+                                (w.y & 0x0F0F0F0Fu) | ((hb << 2) & 0x30303030u), x0.x, x1.x, c);
+        const int hi = quad_dot(((w.x >> 4) & 0x0F0F0F0Fu) | (hb & 0x30303030u),
+                                ((w.y >> 4) & 0x0F0F0F0Fu) | ((hb >> 2) & 0x30303030u), x0.y, x1.y, c);
+        const uint32_t sv = shs[j * 8];
+        const int dot0 = lo - 32 * static_cast<int16_t>(sv & 0xFFFF), dot1 = hi - 32 * static_cast<int16_t>(sv >> 16);
+        const uint32_t sw = j < 2 ? SG.x : (j < 4 ? SG.y : (j < 6 ? SG.z : SG.w));  // scales 2 j, 2 j + 1
+        const float s0 = static_cast<float>(static_cast<int8_t>((sw >> (16 * (j & 1))) & 0xFF));
+        const float s1 = static_cast<float>(static_cast<int8_t>((sw >> (16 * (j & 1) + 8)) & 0xFF));
+        const float dx = dxs[j * 8];
+        acc = __fmaf_rn(__int2float_rn(dot1), __fmul_rn(__fmul_rn(dd, s1), dx),
+                        __fmaf_rn(__int2float_rn(dot0), __fmul_rn(__fmul_rn(dd, s0), dx), acc));
+      }
+    }
+  }
+  cp_async_wait<0>();
+  if (active && t < a.n && row < a.rows) a.y[static_cast<int64_t>(t) * a.ldy + row] = acc;
+}
+
 // ---------------- exact block dots (parity tests) ----------------
 // grid (panels), block 32: one warp per panel, all tokens in tiles of 8, every block.
 __global__ void k_block_dots(uint32_t type, const uint8_t* __restrict__ w, int64_t panels, int kunits, int64_t rows,
@@ -509,6 +660,8 @@ int prepare(uint32_t type, int i) {
 struct Plan {
   int variant = 0, passes = 1;
 };
+constexpr int kDp4a = kVariants;       // plan value of the dp4a kernel (k_gemm_dp4a)
+constexpr int kDp4aMaxTiles = 4;       // token tiles (of 8) up to which the tuner times it
 
 // The kernel shape for a weight, n tokens (tiles of 8, at most nt8 readable) and split-K slices. With one slice the
 // SMs are filled by token passes and narrow tiles instead: the estimate is the busiest SM's share of the per-block
@@ -523,8 +676,9 @@ Plan plan_for(const DevWeight& w, int n, int nt8, int split) {
     best.passes = passes;
     return best;
   }
-  // MALKIN_B200_GEMM_PLAN=<wp>:<ntw> forces one kernel shape (tests and measurements), when it is valid here
+  // MALKIN_B200_GEMM_PLAN=<wp>:<ntw> (or dp4a) forces one kernel shape (tests and measurements), when it is valid here
   if (const char* e = std::getenv("MALKIN_B200_GEMM_PLAN")) {
+    if (std::string(e) == "dp4a") return Plan{kDp4a, 1};
     int wp = 0, ntw = 0;
     if (std::sscanf(e, "%d:%d", &wp, &ntw) == 2)
       for (int i = 0; i < kVariants; ++i)
@@ -534,6 +688,7 @@ Plan plan_for(const DevWeight& w, int n, int nt8, int split) {
         }
   }
   // the measured shape (gemm_tune)
+  if (const int ch = gemm_choice(w, n); ch == kDp4a) return Plan{kDp4a, 1};
   if (const int ch = gemm_choice(w, n); ch >= 0 && ch < kVariants) {
     const int nt = (kConsumers / tab[ch].wp) * tab[ch].ntw;
     return Plan{ch, (tiles + nt - 1) / nt};
@@ -624,6 +779,7 @@ void gemm_tune(const DevWeight& w, const ActQ& act, int n, float* y, int64_t ldy
     const auto& tab = table_of(w.type);
     for (int i = 0; i < kVariants; ++i)
       if ((kConsumers / tab[i].wp) * tab[i].ntw <= std::max(8, 2 * tiles + 1)) cand.push_back(i);
+    if (tiles <= kDp4aMaxTiles) cand.push_back(kDp4a);
   }
   if (cand.empty()) return;
   const TuneKey key = tune_key(w, n);
@@ -719,6 +875,15 @@ void launch_gemm(const DevWeight& w, const ActQ& act, int n, float* y, int64_t l
   a.status = status;
   if (w.type != 8 && w.type != 12 && w.type != 14) return;
   const Plan pl = plan_for(w, n, act.nt8, gy);
+  if (pl.variant == kDp4a && gy == 1) {
+    const dim3 grid(static_cast<unsigned>(w.panels), static_cast<unsigned>((n + 7) / 8));
+    switch (w.type) {
+      case 8: k_gemm_dp4a<8><<<grid, 32 * kDpWarps, 0, s>>>(a); break;
+      case 12: k_gemm_dp4a<12><<<grid, 32 * kDpWarps, 0, s>>>(a); break;
+      default: k_gemm_dp4a<14><<<grid, 32 * kDpWarps, 0, s>>>(a); break;
+    }
+    return;
+  }
   const Variant& v = table_of(w.type)[pl.variant];
   prepare(w.type, pl.variant);
   const dim3 grid(static_cast<unsigned>(pl.passes), static_cast<unsigned>(gy),

@@ -115,6 +115,26 @@ def test_matmul_every_kernel_shape(mk, oracle, torch_cuda, monkeypatch, t, wp, n
     assert np.array_equal(y.cpu().numpy(), oracle.matmul(t, w, rows, cols, x))
 
 
+@pytest.mark.parametrize("t", TYPES)
+@pytest.mark.parametrize("n", [1, 2, 7, 17, 32, 45])
+def test_matmul_dp4a_vs_oracle(mk, oracle, torch_cuda, monkeypatch, t, n):
+    """The small-row dp4a kernel (a warp per panel x 2 tokens, quad butterflies of exact integer dots), forced with
+    MALKIN_B200_GEMM_PLAN=dp4a: ragged rows, odd token counts, a partial last tile; bit-identical to malkin's
+    compact-panel arithmetic (the oracle)."""
+    torch = torch_cuda
+    from make_golden import random_rows
+    monkeypatch.setenv("MALKIN_B200_GEMM_PLAN", "dp4a")
+    monkeypatch.setenv("MALKIN_B200_Q8_LAYOUT", "panels")
+    rng = np.random.default_rng(n * 13 + t)
+    rows, cols = 200, 768 if t == 8 else 1536
+    w = random_rows(rng, t, rows, cols)
+    x = rng.uniform(-3, 3, (n, cols)).astype(np.float32)
+    W = mk.Weight(t, w, rows, cols)
+    y = torch.full((n, rows), np.nan, dtype=torch.float32, device="cuda")
+    W.matmul(dev(torch, x).data_ptr(), n, y.data_ptr(), split_k=1)
+    assert np.array_equal(y.cpu().numpy(), oracle.matmul(t, w, rows, cols, x))
+
+
 def test_silu(mk, golden, torch_cuda):
     torch = torch_cuda
     g = dev(torch, golden["silu_g"])
