@@ -146,6 +146,9 @@ def clocks_start():
                               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
                               "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "100"],
                              stdout=out, stderr=subprocess.DEVNULL)
+        t_end = time.time() + 3.0  # the sampler is running (its first line written) before the timed region starts
+        while time.time() < t_end and os.path.getsize(out.name) == 0 and p.poll() is None:
+            time.sleep(0.02)
         return p, out
     except Exception:
         return None, None
@@ -155,9 +158,22 @@ def clocks_stop(handle, devices):
     p, out = handle
     if p is None:
         return None
+    size_at_stop = os.path.getsize(out.name)
     p.terminate()
     p.wait()
     out.close()
+    note = None
+    if size_at_stop == 0:  # a region shorter than the sampling interval: one reading right after it
+        note = "timed region shorter than the 100 ms sampling interval: one reading right after it"
+        try:
+            with open(out.name, "w") as f:
+                subprocess.run(["nvidia-smi", "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,"
+                                "clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+                                "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                                "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits"],
+                               stdout=f, stderr=subprocess.DEVNULL, timeout=20)
+        except Exception:
+            pass
     sm, mx, reasons = [], 0.0, set()
     names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
     want = {str(d) for d in devices}
@@ -176,8 +192,11 @@ def clocks_stop(handle, devices):
     os.unlink(out.name)
     if not sm:
         return None
-    return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm),
-            "gpus": sorted(int(d) for d in want)}
+    res = {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm),
+           "gpus": sorted(int(d) for d in want)}
+    if note:
+        res["note"] = note
+    return res
 
 
 def peaks():

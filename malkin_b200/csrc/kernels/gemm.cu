@@ -364,13 +364,19 @@ __global__ void __launch_bounds__(kThreadsG, NTW <= 7 ? 2 : 1) k_gemm(GemmArgs a
 
 // ---------------- small-row regime: dp4a ----------------
 // A few tokens against a deep or narrow weight give the mma tiles few CTAs (rows / 32 at most) and leave most of
-// their warps without token tiles. Here a warp covers one whole panel (16 rows) x 2 tokens: lane L = 4 g + c reads
-// the panel chunk's 16-byte fragment L (rows g, g + 8, value quarter c of a 32-value block) with one coalesced
-// load, takes 4 dp4a per 16 values for the entries (row g, g + 8) x (token t0, t0 + 1), and a two-step shuffle
-// butterfly over the 4 lanes of the quad leaves lane c with the whole integer dot of entry c: row g + 8 (c / 2),
-// token t0 + c % 2. Integer sums are exact in any order, so each dot equals the mma's; the lane then runs malkin's
-// float chain for its (row, token) over the blocks in order with the same roundings as k_gemm: bit-identical.
+// their warps without token tiles. Here a warp covers one whole panel (16 rows) x 2 tokens, one (row, token) chain
+// per lane, from a shared-memory copy of the panel chunk and the token tile. Each 32-value block's integer dot comes
+// from dp4a: for Q8_0 and Q6_K lane 4 g + c reads fragment slot 4 g + c (rows g, g + 8, value quarter c), takes the
+// quarter's partial dots of (row g, g + 8) x (token t0, t0 + 1) and a two-step shuffle butterfly over the quad
+// leaves lane c with entry c's whole dot; for Q4_K a lane reads its own row's four quarters and its token's 32
+// values and needs no shuffle (the form measured faster per type). Integer sums are exact in any order, so each dot
+// equals the mma's; the lane then runs malkin's float chain for its (row, token) over the blocks in order with the
+// same roundings as k_gemm: bit-identical.
 constexpr int kDpWarps = 4;  // warps per CTA: one panel x one 8-token tile
+
+__device__ __forceinline__ int dp4(uint32_t a, uint32_t b, int c) {
+  return __dp4a(static_cast<int>(a), static_cast<int>(b), c);
+}
 
 // lanes c of a quad hold partial dots p0..p3 of entries 0..3; returns the quad's total of entry c
 __device__ __forceinline__ int quad_take(int p0, int p1, int p2, int p3, int c) {
@@ -432,11 +438,14 @@ __global__ void __launch_bounds__(32 * kDpWarps) k_gemm_dp4a(GemmArgs a) {
   using C = TypeCfg<T>;
   using D = DpCfg<T>;
   __shared__ __align__(16) uint8_t sm[kDpStages][D::BYTES];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3, h = c >> 1;
+  constexpr bool kQuad = T != 12;  // quad butterfly (Q8_0, Q6_K) or a lane's own row (Q4_K)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = kQuad ? lane >> 2 : lane & 7, c = lane & 3;
+  const int h = kQuad ? c >> 1 : (lane >> 3) & 1;
   const int64_t p = blockIdx.x;
   const int tt = blockIdx.y, t0 = tt * 8 + 2 * warp;
   const bool active = t0 < a.n;    // warps past the last token still copy and wait
-  const int tl = 2 * warp + (c & 1), t = tt * 8 + tl;  // this lane's token (in the tile, overall)
+  const int tl = 2 * warp + (kQuad ? (c & 1) : (lane >> 4)), t = tt * 8 + tl;  // this lane's token (tile, overall)
   const int64_t row = p * 16 + g + 8 * h;
   const int nst = (a.kunits + D::KU - 1) / D::KU;
   for (int s = 0; s < kDpStages - 1; ++s) {
@@ -456,7 +465,8 @@ __global__ void __launch_bounds__(32 * kDpWarps) k_gemm_dp4a(GemmArgs a) {
       cp_async_commit();
     if (!active) continue;
     const uint8_t* st = sm[it % kDpStages];
-    const uint8_t* xs = st + D::WB + 8 * (4 * (2 * warp) + c);  // token t0's quarter c; t0 + 1 at + 32
+    // quad: token t0's quarter c (t0 + 1 at + 32); lane: the token's 32 bytes, (low 4, high 4) per quarter
+    const uint8_t* xs = st + D::WB + (kQuad ? 8 * (4 * (2 * warp) + c) : 32 * tl);
     const float* dxs = reinterpret_cast<const float*>(st + D::WB + D::XB) + tl;
     if constexpr (T == 8) {
       const int uk = min(D::KU, a.kunits - it * D::KU);
@@ -475,14 +485,19 @@ __global__ void __launch_bounds__(32 * kDpWarps) k_gemm_dp4a(GemmArgs a) {
       const float* dss = reinterpret_cast<const float*>(st + D::WB + D::XB + D::SB) + tl;
 #pragma unroll 2
       for (int j = 0; j < 8; ++j) {
-        const uint2 w = *reinterpret_cast<const uint2*>(st + 256 * j + 8 * lane);  // rows g, g + 8
-        const uint2 x0 = *reinterpret_cast<const uint2*>(xs + j * 256), x1 = *reinterpret_cast<const uint2*>(xs + j * 256 + 32);
-        const int lo = quad_dot(w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, x0.x, x1.x, c);
-        const int hi = quad_dot((w.x >> 4) & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu, x0.y, x1.y, c);
+        const uint4 W0 = *reinterpret_cast<const uint4*>(st + 256 * j + 32 * g);  // slots 4g, 4g+1: (row g, row g+8)
+        const uint4 W1 = *reinterpret_cast<const uint4*>(st + 256 * j + 32 * g + 16);
+        const uint32_t wv[4] = {h ? W0.y : W0.x, h ? W0.w : W0.z, h ? W1.y : W1.x, h ? W1.w : W1.z};
+        const uint4 X0 = *reinterpret_cast<const uint4*>(xs + j * 256), X1 = *reinterpret_cast<const uint4*>(xs + j * 256 + 16);
+        const uint32_t xv[8] = {X0.x, X0.y, X0.z, X0.w, X1.x, X1.y, X1.z, X1.w};
+        int dot = 0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          dot = dp4((wv[q] >> 4) & 0x0F0F0F0Fu, xv[2 * q + 1], dp4(wv[q] & 0x0F0F0F0Fu, xv[2 * q], dot));
         int sc, m;
         q4k_scale_min(j, H.y, H.z, H.w, sc, m);
         const float scg = __fmul_rn(d, static_cast<float>(sc)), mng = __fmul_rn(dmin, static_cast<float>(m));
-        acc = __fmaf_rn(-mng, dss[j * 8], __fmaf_rn(__int2float_rn(lo + hi), __fmul_rn(scg, dxs[j * 8]), acc));
+        acc = __fmaf_rn(-mng, dss[j * 8], __fmaf_rn(__int2float_rn(dot), __fmul_rn(scg, dxs[j * 8]), acc));
       }
     } else {  // Q6_K: two 16-value halves per block, q stored +32 (the half sums s remove the offset)
       const uint4 SG = *reinterpret_cast<const uint4*>(st + 3072 + 32 * g + 16 * h);  // this row's 16 scales
