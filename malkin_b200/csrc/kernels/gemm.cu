@@ -401,7 +401,7 @@ __device__ __forceinline__ int quad_dot(uint32_t wg, uint32_t wg8, uint32_t x0, 
 template <uint32_t T>
 struct DpCfg {
   using C = TypeCfg<T>;
-  static constexpr int KU = T == 8 ? 8 : 1;       // k-units per stage (8 blocks of 32 values)
+  static constexpr int KU = T == 8 ? 8 : 2;       // k-units per stage (8 or 16 blocks of 32 values)
   static constexpr int BLK = KU * C::BPU;
   static constexpr int WB = KU * C::UNIT, XB = BLK * 256, SB = BLK * 32;
   static constexpr int EX = (C::kDsx || C::kSh) ? SB : 0;
@@ -480,15 +480,19 @@ __global__ void __launch_bounds__(32 * kDpWarps) k_gemm_dp4a(GemmArgs a) {
         acc = __fmaf_rn(__int2float_rn(lo + hi), __fmul_rn(dw, dxs[uu * 8]), acc);
       }
     } else if constexpr (T == 12) {
-      const uint4 H = *reinterpret_cast<const uint4*>(st + 2048 + 32 * g + 16 * h);  // this lane's row's head
+      const int uk = min(D::KU, a.kunits - it * D::KU);
+      for (int uu = 0; uu < uk; ++uu) {
+      const uint8_t* cu = st + uu * C::UNIT;
+      const uint4 H = *reinterpret_cast<const uint4*>(cu + 2048 + 32 * g + 16 * h);  // this lane's row's head
       const float d = h2f_lo(H.x), dmin = h2f_hi(H.x);
-      const float* dss = reinterpret_cast<const float*>(st + D::WB + D::XB + D::SB) + tl;
+      const float* dss = reinterpret_cast<const float*>(st + D::WB + D::XB + D::SB) + tl + 64 * uu;
 #pragma unroll 2
       for (int j = 0; j < 8; ++j) {
-        const uint4 W0 = *reinterpret_cast<const uint4*>(st + 256 * j + 32 * g);  // slots 4g, 4g+1: (row g, row g+8)
-        const uint4 W1 = *reinterpret_cast<const uint4*>(st + 256 * j + 32 * g + 16);
+        const int bj = 8 * uu + j;  // block in the stage
+        const uint4 W0 = *reinterpret_cast<const uint4*>(cu + 256 * j + 32 * g);  // slots 4g, 4g+1: (row g, row g+8)
+        const uint4 W1 = *reinterpret_cast<const uint4*>(cu + 256 * j + 32 * g + 16);
         const uint32_t wv[4] = {h ? W0.y : W0.x, h ? W0.w : W0.z, h ? W1.y : W1.x, h ? W1.w : W1.z};
-        const uint4 X0 = *reinterpret_cast<const uint4*>(xs + j * 256), X1 = *reinterpret_cast<const uint4*>(xs + j * 256 + 16);
+        const uint4 X0 = *reinterpret_cast<const uint4*>(xs + bj * 256), X1 = *reinterpret_cast<const uint4*>(xs + bj * 256 + 16);
         const uint32_t xv[8] = {X0.x, X0.y, X0.z, X0.w, X1.x, X1.y, X1.z, X1.w};
         int dot = 0;
 #pragma unroll
@@ -497,17 +501,22 @@ __global__ void __launch_bounds__(32 * kDpWarps) k_gemm_dp4a(GemmArgs a) {
         int sc, m;
         q4k_scale_min(j, H.y, H.z, H.w, sc, m);
         const float scg = __fmul_rn(d, static_cast<float>(sc)), mng = __fmul_rn(dmin, static_cast<float>(m));
-        acc = __fmaf_rn(-mng, dss[j * 8], __fmaf_rn(__int2float_rn(dot), __fmul_rn(scg, dxs[j * 8]), acc));
+        acc = __fmaf_rn(-mng, dss[j * 8], __fmaf_rn(__int2float_rn(dot), __fmul_rn(scg, dxs[bj * 8]), acc));
+      }
       }
     } else {  // Q6_K: two 16-value halves per block, q stored +32 (the half sums s remove the offset)
-      const uint4 SG = *reinterpret_cast<const uint4*>(st + 3072 + 32 * g + 16 * h);  // this row's 16 scales
-      const float dd = __half2float(*reinterpret_cast<const __half*>(st + 3328 + 4 * g + 2 * h));
-      const uint32_t* shs = reinterpret_cast<const uint32_t*>(st + D::WB + D::XB + D::SB) + tl;
+      const int uk = min(D::KU, a.kunits - it * D::KU);
+      for (int uu = 0; uu < uk; ++uu) {
+      const uint8_t* cu = st + uu * C::UNIT;
+      const uint4 SG = *reinterpret_cast<const uint4*>(cu + 3072 + 32 * g + 16 * h);  // this row's 16 scales
+      const float dd = __half2float(*reinterpret_cast<const __half*>(cu + 3328 + 4 * g + 2 * h));
+      const uint32_t* shs = reinterpret_cast<const uint32_t*>(st + D::WB + D::XB + D::SB) + tl + 64 * uu;
 #pragma unroll 2
       for (int j = 0; j < 8; ++j) {
-        const uint2 w = *reinterpret_cast<const uint2*>(st + 256 * j + 8 * lane);
-        const uint32_t hb = *reinterpret_cast<const uint32_t*>(st + 2048 + 128 * j + 4 * lane);
-        const uint2 x0 = *reinterpret_cast<const uint2*>(xs + j * 256), x1 = *reinterpret_cast<const uint2*>(xs + j * 256 + 32);
+        const int bj = 8 * uu + j;  // block in the stage
+        const uint2 w = *reinterpret_cast<const uint2*>(cu + 256 * j + 8 * lane);
+        const uint32_t hb = *reinterpret_cast<const uint32_t*>(cu + 2048 + 128 * j + 4 * lane);
+        const uint2 x0 = *reinterpret_cast<const uint2*>(xs + bj * 256), x1 = *reinterpret_cast<const uint2*>(xs + bj * 256 + 32);
         const int lo = quad_dot((w.x & 0x0F0F0F0Fu) | ((hb << 4) & 0x30303030u),
                                 (w.y & 0x0F0F0F0Fu) | ((hb << 2) & 0x30303030u), x0.x, x1.x, c);
         const int hi = quad_dot(((w.x >> 4) & 0x0F0F0F0Fu) | (hb & 0x30303030u),
@@ -517,9 +526,10 @@ __global__ void __launch_bounds__(32 * kDpWarps) k_gemm_dp4a(GemmArgs a) {
         const uint32_t sw = j < 2 ? SG.x : (j < 4 ? SG.y : (j < 6 ? SG.z : SG.w));  // scales 2 j, 2 j + 1
         const float s0 = static_cast<float>(static_cast<int8_t>((sw >> (16 * (j & 1))) & 0xFF));
         const float s1 = static_cast<float>(static_cast<int8_t>((sw >> (16 * (j & 1) + 8)) & 0xFF));
-        const float dx = dxs[j * 8];
+        const float dx = dxs[bj * 8];
         acc = __fmaf_rn(__int2float_rn(dot1), __fmul_rn(__fmul_rn(dd, s1), dx),
                         __fmaf_rn(__int2float_rn(dot0), __fmul_rn(__fmul_rn(dd, s0), dx), acc));
+      }
       }
     }
   }

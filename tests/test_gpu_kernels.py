@@ -117,16 +117,19 @@ def test_matmul_every_kernel_shape(mk, oracle, torch_cuda, monkeypatch, t, wp, n
 
 @pytest.mark.parametrize("t", TYPES)
 @pytest.mark.parametrize("n", [1, 2, 7, 17, 32, 45])
-def test_matmul_dp4a_vs_oracle(mk, oracle, torch_cuda, monkeypatch, t, n):
-    """The small-row dp4a kernel (a warp per panel x 2 tokens, quad butterflies of exact integer dots), forced with
-    MALKIN_B200_GEMM_PLAN=dp4a: ragged rows, odd token counts, a partial last tile; bit-identical to malkin's
-    compact-panel arithmetic (the oracle)."""
+@pytest.mark.parametrize("odd", [False, True])
+def test_matmul_dp4a_vs_oracle(mk, oracle, torch_cuda, monkeypatch, t, n, odd):
+    """The small-row dp4a kernel (a warp per panel x 2 tokens, exact integer dots by dp4a), forced with
+    MALKIN_B200_GEMM_PLAN=dp4a: ragged rows, odd token counts, a partial last tile, and k-unit counts that fill the
+    last shared-memory stage or leave it part empty (odd); bit-identical to malkin's compact-panel arithmetic (the
+    oracle)."""
     torch = torch_cuda
     from make_golden import random_rows
     monkeypatch.setenv("MALKIN_B200_GEMM_PLAN", "dp4a")
     monkeypatch.setenv("MALKIN_B200_Q8_LAYOUT", "panels")
-    rng = np.random.default_rng(n * 13 + t)
-    rows, cols = 200, 768 if t == 8 else 1536
+    rng = np.random.default_rng(n * 13 + t + 7 * odd)
+    rows = 200
+    cols = (736 if odd else 768) if t == 8 else (1280 if odd else 1536)  # Q8_0: 23 / 24 blocks; K-quants: 5 / 6
     w = random_rows(rng, t, rows, cols)
     x = rng.uniform(-3, 3, (n, cols)).astype(np.float32)
     W = mk.Weight(t, w, rows, cols)
